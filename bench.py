@@ -1,0 +1,368 @@
+"""GPT-2 prefill throughput on B200: tokens/s of the GPT-2 small BF16 forward,
+batch 64 x seq 1024 (global batch; sharded over the ranks), logits resident
+on each shard.
+
+  python bench.py [--gpus N --steps K --warmup W]        # this library
+  python bench.py --impl reference [...]                  # the CPU reference path
+  torchrun --nproc-per-node N bench.py --gpus N ...       # one process per GPU
+
+One step = one forward over this rank's B/N sequences (ids resident in HBM,
+FP32 logits written to HBM).  value = all ranks' tokens / max-over-ranks
+device time of the K timed steps (CUDA events on the launching stream).
+Every step reads and writes far more than the 126 MB L2 (the FP32 logits
+alone are 13.2 GB at N=1), so no separate L2 flush is done.
+
+Also reported: a per-kernel event breakdown with the roofline of the
+dominant kernel, the end-to-end rate through the host-buffer C ABI
+(gpt2_forward_host: ids host->device and FP32 logits device->host inside
+the timed region), the SM clocks sampled during the timed steps, and (rank 0,
+N=1) the CPU oracle timed on one sequence of the same workload.
+"""
+from __future__ import annotations
+
+import argparse
+import importlib.util
+import json
+import os
+import statistics
+import subprocess
+import sys
+import time
+
+import numpy as np
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+SEED = 1234
+D, FF, V, L, H, DH = 768, 3072, 50257, 12, 12, 64
+LD_LOGITS = 50304  # row stride of the resident logits (16-byte aligned rows)
+
+
+def _pkg():
+    name = "mlir_learning_b200"
+    if name in sys.modules:
+        return sys.modules[name]
+    path = os.path.join(ROOT, "mlir-learning_b200", "__init__.py")
+    spec = importlib.util.spec_from_file_location(name, path, submodule_search_locations=[os.path.dirname(path)])
+    mod = importlib.util.module_from_spec(spec)
+    sys.modules[name] = mod
+    spec.loader.exec_module(mod)
+    return mod
+
+
+def _oracle():
+    if ROOT not in sys.path:
+        sys.path.insert(0, ROOT)
+    from oracle import oracle as O
+    return O
+
+
+def _peaks():
+    try:
+        with open(os.path.join(ROOT, "MEASURED_PEAKS.json")) as f:
+            p = json.load(f)
+        return {"hbm_gbs": p["hbm_gbs"], "bf16": p["bf16_tflops"], "bf16_sus": p["bf16_tflops_sustained"],
+                "src": "measured"}
+    except Exception:
+        return {"hbm_gbs": 6650.0, "bf16": 1590.0, "bf16_sus": 1400.0, "src": "fallback"}
+
+
+def kernel_work(B, S):
+    """Algorithmic work of one launch of each kernel kind at B sequences of S tokens:
+    ('flop', F) for tensor-bound kernels, ('bytes', N) for the bandwidth-bound ones."""
+    T = B * S
+    return {
+        "gemm_qkv": ("flop", 2.0 * T * D * 3 * D),
+        "gemm_proj": ("flop", 2.0 * T * D * D),
+        "gemm_fc": ("flop", 2.0 * T * D * FF),
+        "gemm_mproj": ("flop", 2.0 * T * FF * D),
+        "lm_head": ("flop", 2.0 * T * D * V),
+        "attention": ("flop", 4.0 * B * H * DH * S * (S + 1) / 2),
+        "layernorm": ("bytes", T * D * (2 + 2) + 2 * D * 4),
+        "embed": ("bytes", T * 8 + 2 * T * D * 2 + T * D * 2),
+    }
+
+
+class ClockSampler:
+    """nvidia-smi clocks / throttle reasons sampled every 200 ms while running."""
+
+    FIELDS = ["index", "clocks.sm", "clocks.max.sm", "power.draw", "clocks_event_reasons.active",
+              "clocks_event_reasons.hw_slowdown", "clocks_event_reasons.hw_thermal_slowdown",
+              "clocks_event_reasons.sw_thermal_slowdown", "clocks_event_reasons.sw_power_cap"]
+
+    def __init__(self, gpu_index: int):
+        self.gpu = gpu_index
+        self.proc = None
+
+    def __enter__(self):
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", "-i", str(self.gpu), "--query-gpu=" + ",".join(self.FIELDS),
+                 "--format=csv,noheader,nounits", "-lms", "200"],
+                stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+        except Exception:
+            self.proc = None
+        return self
+
+    def __exit__(self, *exc):
+        self.out = ""
+        if self.proc is not None:
+            time.sleep(0.25)
+            self.proc.terminate()
+            try:
+                self.out, _ = self.proc.communicate(timeout=5)
+            except Exception:
+                self.proc.kill()
+        return False
+
+    def summary(self):
+        sm, mx, reasons = [], [], set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for line in (self.out or "").splitlines():
+            parts = [p.strip() for p in line.split(",")]
+            if len(parts) != len(self.FIELDS):
+                continue
+            try:
+                sm.append(float(parts[1]))
+                mx.append(float(parts[2]))
+            except ValueError:
+                continue
+            for n, v in zip(names, parts[5:9]):
+                if v.lower().startswith("active"):
+                    reasons.add(n)
+        if not sm:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": [], "samples": 0}
+        return {"sm_mhz": statistics.median(sm), "sm_max_mhz": max(mx), "reasons": sorted(reasons),
+                "samples": len(sm)}
+
+
+def cpu_reference_rate(S: int, n_seq: int = 1):
+    """The oracle (the reference's CPU lowering restated in C: OpenBLAS sgemm for the 2-D
+    matmuls on all cores, single-threaded loop nests for the rest) on n_seq sequences of S
+    tokens of the workload; returns (tokens/s, seconds, cores)."""
+    O = _oracle()
+    O.build()
+    O.set_loop_threads(1)
+    shape = O.GPT2_SMALL
+    blob = O.seeded_blob(shape, SEED, 0)
+    ids = O.token_ids(64, S, SEED, shape.vocab_size)[:n_seq]
+    out = np.empty((n_seq, S, shape.vocab_size), dtype=np.float32)
+    t0 = time.perf_counter()
+    O.forward(shape, blob, ids, out=out)
+    dt = time.perf_counter() - t0
+    return n_seq * S / dt, dt, os.cpu_count() or 1
+
+
+def run_reference(args, rank, world):
+    if rank != 0:
+        return
+    S = args.seq
+    rates = []
+    for i in range(args.warmup + args.steps):
+        r, dt, cores = cpu_reference_rate(S)
+        if i >= args.warmup:
+            rates.append((r, dt))
+    total_tokens = S * len(rates)
+    total_s = sum(dt for _, dt in rates)
+    value = total_tokens / total_s
+    O = _oracle()
+    line = {
+        "impl": "reference",
+        "metric": "GPT-2 prefill tokens/s (GPT-2 small, B64 x S1024)",
+        "value": value, "unit": "tokens/s", "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
+        "ms_per_step": 1000.0 * total_s / len(rates), "higher_is_better": True, "scaling": "strong",
+        "vs_baseline": None, "dtype": "f32", "data": "synthetic (seeded Philox weights N(0,0.02), uniform ids)",
+        "config": {"workload": "gpt2-small prefill B64xS1024 (config 2)", "global_batch": 64, "seq_len": S,
+                   "sample_per_step": f"1 sequence x {S} tokens"},
+        "cpu_baseline": {"value": value, "unit": "tokens/s", "cores": cores, "kind": "port",
+                         "sample": f"1 x {S} tokens per step; OpenBLAS sgemm ({O.blas_name().split('/')[-1]}) on "
+                                   f"all {cores} cores, loop nests single-threaded as the reference's CPU lowering"},
+        "e2e": {"value": value, "unit": "tokens/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }
+    print(json.dumps(line), flush=True)
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=10)
+    ap.add_argument("--warmup", type=int, default=3)
+    ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
+    ap.add_argument("--batch", type=int, default=64, help="global batch (sequences)")
+    ap.add_argument("--seq", type=int, default=1024)
+    ap.add_argument("--e2e-steps", type=int, default=2)
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    args = ap.parse_args()
+
+    rank = int(os.environ.get("RANK", "0"))
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    local_rank = int(os.environ.get("LOCAL_RANK", "0"))
+    if args.impl == "reference":
+        run_reference(args, rank, world)
+        return
+
+    import torch
+    import torch.distributed as dist
+    from datetime import timedelta
+
+    torch.cuda.set_device(local_rank)
+    if world > 1:
+        dist.init_process_group("nccl", timeout=timedelta(seconds=120), device_id=torch.device("cuda", local_rank))
+    pkg = _pkg()
+    if args.batch % world:
+        raise SystemExit(f"global batch {args.batch} does not split over {world} ranks")
+    B, S = args.batch // world, args.seq
+    T = B * S
+
+    pkg.init(pkg.gpt2_small(pkg.DTYPE_BF16), local_rank)
+    pkg.init_seeded(SEED, 0)
+    ids_all = pkg.seeded_ids(args.batch, S, SEED, V)
+    ids_h = np.ascontiguousarray(ids_all[rank * B:(rank + 1) * B])
+    ids = torch.from_numpy(ids_h).cuda()
+    logits = torch.empty(T, LD_LOGITS, device="cuda", dtype=torch.float32)
+    stream = torch.cuda.current_stream()
+    sp = stream.cuda_stream
+
+    def step():
+        pkg.forward_device(ids.data_ptr(), None, B, S, logits.data_ptr(), LD_LOGITS, sp)
+
+    def barrier():
+        if world > 1:
+            dist.barrier()
+
+    for _ in range(max(args.warmup, 3)):
+        step()
+    torch.cuda.synchronize()
+    if pkg.status() != 0:
+        raise SystemExit("device status word set during warm-up")
+    barrier()
+    torch.cuda.synchronize()
+    ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    with ClockSampler(local_rank) as clk:
+        ev0.record(stream)
+        for _ in range(args.steps):
+            step()
+        ev1.record(stream)
+        torch.cuda.synchronize()
+    barrier()
+    elapsed = ev0.elapsed_time(ev1) / 1000.0
+    t = torch.tensor([elapsed], device="cuda", dtype=torch.float64)
+    if world > 1:
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    t_max = float(t.item())
+    value = args.batch * S * args.steps / t_max
+
+    # Per-kernel breakdown (separate, profiled steps of the same workload).
+    pkg.profile_begin()
+    nprof = 2
+    for _ in range(nprof):
+        step()
+    prof = pkg.profile_end()
+    torch.cuda.synchronize()
+    work = kernel_work(B, S)
+    peaks = _peaks()
+    kernels = {}
+    for k, (ms, n) in prof.items():
+        if n == 0:
+            continue
+        ent = {"ms_per_step": ms / nprof, "launches_per_step": n // nprof, "avg_launch_ms": ms / n}
+        if k in work:
+            kind, amount = work[k]
+            per_launch_s = ms / n / 1000.0
+            if kind == "flop":
+                ent["tflops"] = amount / per_launch_s / 1e12
+            else:
+                ent["gbs"] = amount / per_launch_s / 1e9
+        kernels[k] = ent
+    step_ms = sum(e["ms_per_step"] for e in kernels.values())
+    for e in kernels.values():
+        e["share"] = e["ms_per_step"] / step_ms if step_ms else None
+    dom = max(kernels, key=lambda k: kernels[k]["ms_per_step"])
+    traffic = None
+    try:
+        with open(os.path.join(ROOT, "profiles", "traffic.json")) as f:
+            tr = json.load(f)
+        traffic = tr.get(dom, {}).get("bytes_per_launch_full")
+    except Exception:
+        pass
+    kind, amount = work.get(dom, ("flop", 0.0))
+    per_launch_s = kernels[dom]["avg_launch_ms"] / 1000.0
+    if kind == "flop":
+        achieved = amount / per_launch_s / 1e12
+        roof = {"bound": "tensor", "achieved": achieved, "peak": peaks["bf16_sus"], "unit": "TFLOP/s",
+                "frac": achieved / peaks["bf16_sus"], "traffic": traffic, "kernel": dom,
+                "peak_kind": f"bf16 sustained ({peaks['src']})",
+                "algorithmic_per_launch": amount}
+    else:
+        achieved = amount / per_launch_s / 1e9
+        roof = {"bound": "hbm", "achieved": achieved, "peak": peaks["hbm_gbs"], "unit": "GB/s",
+                "frac": achieved / peaks["hbm_gbs"], "traffic": traffic, "kernel": dom,
+                "peak_kind": f"hbm copy ({peaks['src']})", "algorithmic_per_launch": amount}
+    total_flop = (work["gemm_qkv"][1] + work["gemm_proj"][1] + work["gemm_fc"][1] + work["gemm_mproj"][1]) * L \
+        + work["lm_head"][1] + work["attention"][1] * L
+    fwd_tflops = total_flop / (t_max / args.steps) / 1e12
+
+    # End to end through the host-buffer C ABI: ids from pinned host memory in, FP32 logits out to
+    # pinned host memory, per step, synchronised.
+    e2e = None
+    if args.e2e_steps > 0:
+        host_ids = torch.from_numpy(ids_h).pin_memory()
+        host_logits = torch.empty((B, S, V), dtype=torch.float32).pin_memory()
+        ids_np, out_np = host_ids.numpy(), host_logits.numpy()
+        import ctypes
+        P = ctypes.POINTER
+        lib = pkg.lib()
+        ip = ids_np.ctypes.data_as(P(ctypes.c_int64))
+        op = out_np.ctypes.data_as(P(ctypes.c_float))
+        rc = lib.gpt2_forward_host(ip, None, B, S, op)  # warm-up (grows staging buffers)
+        if rc != 0:
+            raise SystemExit("gpt2_forward_host failed: " + pkg.last_error())
+        barrier()
+        t0 = time.perf_counter()
+        for _ in range(args.e2e_steps):
+            lib.gpt2_forward_host(ip, None, B, S, op)
+        et = time.perf_counter() - t0
+        tt = torch.tensor([et], device="cuda", dtype=torch.float64)
+        if world > 1:
+            dist.all_reduce(tt, op=dist.ReduceOp.MAX)
+        e2e = {"value": args.batch * S * args.e2e_steps / float(tt.item()), "unit": "tokens/s",
+               "h2d_bytes_per_step": int(ids_np.nbytes * world), "d2h_bytes_per_step": int(out_np.nbytes * world),
+               "steps": args.e2e_steps, "api": "gpt2_forward_host (C ABI, host buffers, synchronous)"}
+        del host_logits
+
+    cpu = None
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+        r, dt, cores = cpu_reference_rate(S)
+        O = _oracle()
+        cpu = {"value": r, "unit": "tokens/s", "cores": cores, "kind": "port",
+               "sample": f"1 sequence x {S} tokens ({dt:.1f} s); OpenBLAS sgemm "
+                         f"({O.blas_name().split('/')[-1]}) on all {cores} cores, loop nests single-threaded"}
+
+    clocks = clk.summary()
+    if world > 1:
+        dist.barrier()
+    if rank == 0:
+        line = {
+            "metric": "GPT-2 prefill tokens/s (GPT-2 small, B64 x S1024)",
+            "value": value, "unit": "tokens/s", "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
+            "ms_per_step": 1000.0 * t_max / args.steps, "higher_is_better": True, "scaling": "strong",
+            "vs_baseline": None, "dtype": "bf16",
+            "data": "synthetic (seeded Philox weights N(0,0.02), LN gain 1, biases 0; uniform token ids)",
+            "config": {"workload": "gpt2-small prefill B64xS1024 (config 2), logits FP32 resident per shard",
+                       "global_batch": args.batch, "seq_len": S, "per_rank_batch": B,
+                       "parallelism": f"batch-sharded dp{world}", "l2": "no flush: every step moves > 13 GB"},
+            "forward_tflops": fwd_tflops,
+            "roofline": roof,
+            "kernels": kernels,
+            "cpu_baseline": cpu,
+            "e2e": e2e,
+            "clocks": clocks,
+            "gpu_launches": pkg.forward_launches(B, S, False) * args.steps,
+        }
+        print(json.dumps(line), flush=True)
+    pkg.shutdown()
+    if world > 1:
+        dist.destroy_process_group()
+
+
+if __name__ == "__main__":
+    main()

@@ -1,0 +1,224 @@
+/*
+ * gpt2_b200.h -- C ABI of libgpt2_b200.so, a B200 (sm_100a) implementation of
+ * the GPT-2 forward (prefill) pass that drops in for the object file the
+ * reference compiles from its linalg MLIR.
+ *
+ * No function aborts the process.  Functions returning int return 0 on
+ * success and a negative GPT2_E* code on failure; gpt2_last_error() then
+ * describes the failure.  The decoder entry points return an all-zero
+ * descriptor on failure.
+ */
+#ifndef GPT2_B200_H
+#define GPT2_B200_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#if defined(__GNUC__)
+#pragma GCC visibility push(default)
+#endif
+
+/* ------------------------------------------------------------------------ */
+/* MLIR memref descriptors                                                   */
+/* ------------------------------------------------------------------------ */
+
+/* memref<?x?x?xf32>: the result struct of the reference's compiled
+ * gpt2_decoder (src/gpt/gpt2_call.cpp:23-29; layout of the MLIR C ABI,
+ * docs/Chapter4.md:97-106). */
+typedef struct MemRef3D {
+  float *allocated;
+  float *aligned;
+  int64_t offset;
+  int64_t sizes[3];
+  int64_t strides[3];
+} MemRef3D;
+
+/* memref<?x?xi64>: the token-id and attention-mask operands. */
+typedef struct MemRef2D_i64 {
+  int64_t *allocated;
+  int64_t *aligned;
+  int64_t offset;
+  int64_t sizes[2];
+  int64_t strides[2];
+} MemRef2D_i64;
+
+/* ------------------------------------------------------------------------ */
+/* Drop-in forward entry points                                              */
+/* ------------------------------------------------------------------------ */
+
+/* Replaces the compiled `gpt2_decoder` declared at src/gpt/gpt2_call.cpp:31-37
+ * (decomposed memref ABI: memref<1x?xi64> ids, memref<1x?xi64> mask ->
+ * memref<1x?x50257xf32> logits).
+ *
+ * ids / mask: int64 [B, S] with the given offset and strides (any strides);
+ * mask value != 0 means "attend" (all ones in the reference call,
+ * src/gpt/gpt2_call.cpp:55).  B >= 1 and 1 <= S <= n_positions (the
+ * reference's export fixes B = 1 and S <= 128).
+ *
+ * Returns FP32 logits [B, S, vocab] in host memory obtained from malloc(),
+ * contiguous, offset 0, strides {S*V, V, 1}; the caller frees `allocated`
+ * with free() as src/gpt/gpt2_call.cpp:94 does.  Synchronous.
+ *
+ * The model is the one loaded by gpt2_init / gpt2_load_weights /
+ * gpt2_init_seeded; when none is loaded, the first call creates GPT-2 small
+ * on the current CUDA device with seeded weights (env GPT2_SEED, default
+ * 1234; env GPT2_DTYPE = "f32" (default) | "bf16"). */
+MemRef3D gpt2_decoder(int64_t *in_alloc, int64_t *in_align, int64_t in_offs, int64_t in_s0, int64_t in_s1,
+                      int64_t in_str0, int64_t in_str1, int64_t *mask_alloc, int64_t *mask_align,
+                      int64_t mask_offs, int64_t mask_s0, int64_t mask_s1, int64_t mask_str0, int64_t mask_str1);
+
+/* The `-llvm-request-c-wrappers` form of the same function
+ * (src/gpt/run_mlir_pipeline.sh:7; convention of docs/Chapter4.md:78-112,
+ * e.g. src/bert-base-uncased/call_bert.cpp:46-53).  On failure *result is
+ * zeroed. */
+void _mlir_ciface_gpt2_decoder(MemRef3D *result, MemRef2D_i64 *input_ids, MemRef2D_i64 *attention_mask);
+
+/* ------------------------------------------------------------------------ */
+/* Model configuration and weights (companions; the reference bakes its    */
+/* weights into the object as constants, README.md:11, :30)                 */
+/* ------------------------------------------------------------------------ */
+
+enum {
+  GPT2_DTYPE_F32 = 0,  /* exact FP32 (SIMT FFMA); logits within 1e-4 of the CPU lowering */
+  GPT2_DTYPE_BF16 = 1  /* BF16 weights and activations, FP32 accumulate and statistics (tcgen05) */
+};
+
+typedef struct Gpt2Config {
+  int32_t n_layer;       /* 12 */
+  int32_t n_embd;        /* 768; multiple of 64 */
+  int32_t n_head;        /* 12; n_embd / n_head must be 64 */
+  int32_t n_inner;       /* 3072 */
+  int32_t vocab_size;    /* 50257 */
+  int32_t n_positions;   /* 1024 */
+  float layer_norm_eps;  /* 1e-5 */
+  int32_t dtype;         /* GPT2_DTYPE_* */
+} Gpt2Config;
+
+/* Error codes (negative returns). */
+enum {
+  GPT2_EINVAL = -1,   /* bad argument or shape */
+  GPT2_ECUDA = -2,    /* a CUDA call failed */
+  GPT2_ENOMODEL = -3, /* no model loaded */
+  GPT2_EDEVICE = -4,  /* a kernel reported an error in the status word */
+  GPT2_ENOMEM = -5
+};
+
+/* Creates (or replaces) the process-wide model on CUDA device `device`
+ * (-1: the current device).  No weights are loaded yet. */
+int gpt2_init(const Gpt2Config *cfg, int device);
+
+/* Number of floats of the canonical FP32 weight blob of `cfg`: tensors in
+ * the order wte [V,d], wpe [P,d], then per layer ln_1.{weight,bias},
+ * attn.c_attn.{weight [d,3d], bias}, attn.c_proj.{weight [d,d], bias},
+ * ln_2.{weight,bias}, mlp.c_fc.{weight [d,ff], bias},
+ * mlp.c_proj.{weight [ff,d], bias}, then ln_f.{weight,bias}; Conv1D weights
+ * are [in, out] as in HF GPT-2, lm_head is tied to wte. */
+int64_t gpt2_blob_floats(const Gpt2Config *cfg);
+
+/* Loads a canonical FP32 blob (bytes == 4 * gpt2_blob_floats).  manifest_json
+ * may be NULL, or a JSON object whose "layout" is "gpt2-canonical-f32-v1". */
+int gpt2_load_weights(const void *packed, size_t bytes, const char *manifest_json);
+
+/* Generates the seeded synthetic weights (Philox4x32-10 + Box-Muller) and
+ * loads them.  init_mode 0: matrices N(0, 0.02), LayerNorm gain 1, every
+ * bias 0.  init_mode 1: also gains 1 + N(0, 0.1) and biases N(0, 0.02). */
+int gpt2_init_seeded(uint64_t seed, int init_mode);
+
+/* Fills out[0 .. gpt2_blob_floats(cfg)) with the seeded blob on the host. */
+int gpt2_seeded_blob(const Gpt2Config *cfg, uint64_t seed, int init_mode, float *out);
+
+/* Seeded token ids: ids[i] = floor(w_i * vocab / 2^32), w_i a Philox word. */
+int gpt2_seeded_ids(int64_t *ids, int64_t n, uint64_t seed, uint32_t stream, int64_t vocab);
+
+/* Copies the loaded model's configuration into *out (GPT2_ENOMODEL if none). */
+int gpt2_get_config(Gpt2Config *out);
+
+/* Releases the model and every device buffer. */
+void gpt2_shutdown(void);
+
+/* Text of the last failure on this thread ("" if none). */
+const char *gpt2_last_error(void);
+
+/* Device status word of the model (0 = OK; 1 = token id out of range,
+ * 2 = a barrier wait timed out, 3 = bad launch); reading clears it. */
+int gpt2_status(void);
+
+/* ------------------------------------------------------------------------ */
+/* Device-resident forward (benchmarks and device callers)                  */
+/* ------------------------------------------------------------------------ */
+
+/* logits [B, S, vocab] (row stride ld_logits >= vocab floats) of the loaded
+ * model, everything on the model's device.  d_ids / d_mask: contiguous
+ * int64 [B, S] device arrays (d_mask may be NULL = all ones).  Enqueued on
+ * `stream` (a cudaStream_t; NULL = the model's own stream); returns when
+ * enqueued.  logits_dtype must be GPT2_DTYPE_F32. */
+int gpt2_forward_device(const int64_t *d_ids, const int64_t *d_mask, int B, int S, void *d_logits,
+                        int64_t ld_logits, int logits_dtype, void *stream);
+
+/* Forward with the host-side contract of gpt2_decoder but caller-owned host
+ * buffers: ids / mask contiguous int64 [B, S] (mask may be NULL), logits
+ * [B, S, vocab] FP32 host memory.  Copies in, runs, copies out, synchronises. */
+int gpt2_forward_host(const int64_t *ids, const int64_t *mask, int B, int S, float *logits);
+
+/* Number of kernel launches one forward of (B, S) enqueues. */
+int gpt2_forward_launches(int B, int S, int has_mask);
+
+/* Per-kernel timing: between gpt2_profile_begin() and gpt2_profile_end(),
+ * every launch of the forward is bracketed by CUDA events on its stream.
+ * gpt2_profile_end waits for them and writes, per kernel kind, the summed
+ * milliseconds and the launch count.  Kinds: 0 seq_info, 1 embed,
+ * 2 layernorm, 3 qkv GEMM, 4 attention, 5 masked-row fix-up, 6 attention
+ * out-proj GEMM, 7 MLP fc GEMM, 8 MLP proj GEMM, 9 lm_head GEMM. */
+enum { GPT2_KERNEL_KINDS = 10 };
+int gpt2_profile_begin(void);
+int gpt2_profile_end(double *ms_per_kind, int64_t *launches_per_kind, int n_kinds);
+
+/* ------------------------------------------------------------------------ */
+/* Kernel-level entry points (device pointers, enqueued on `stream`)         */
+/* ------------------------------------------------------------------------ */
+
+/* Epilogues fused into the GEMMs. */
+enum { GPT2_EPI_NONE = 0, GPT2_EPI_BIAS = 1, GPT2_EPI_BIAS_GELU = 2, GPT2_EPI_BIAS_RESID = 3 };
+
+/* Exact-FP32 SIMT GEMM: C[M,N] (row stride ldc) = epi(A[M,K] @ op(B)),
+ * op(B) = B[K,N] (b_nk = 0) or B[N,K]^T (b_nk = 1); resid row stride ldc. */
+int gpt2k_gemm_f32(const float *A, const float *B, int b_nk, float *C, int M, int N, int K, int ldc,
+                   const float *bias, const float *resid, int epi, void *stream);
+
+/* tcgen05 BF16 GEMM: C[M,N] = epi(A[M,K] @ B[N,K]^T), A and B bf16
+ * row-major; C bf16 (out_f32 = 0) or f32 (out_f32 = 1, EPI_NONE / EPI_BIAS);
+ * resid bf16 with row stride ldc; bn = 128 or 256 (output tile width). */
+int gpt2k_gemm_bf16(const void *A, const void *B, void *C, int M, int N, int K, int ldc, int out_f32,
+                    const float *bias, const void *resid, int epi, int bn, void *stream);
+
+/* LayerNorm over rows of width d (FP32 statistics): dtype GPT2_DTYPE_F32
+ * (x, y float) or GPT2_DTYPE_BF16 (x, y bf16); gain and shift are float. */
+int gpt2k_layernorm(const void *x, const float *gain, const float *shift, void *y, int T, int d, float eps,
+                    int dtype, void *stream);
+
+/* Causal attention of one layer, head dim 64: qkv [B*S, 3*H*64] (q | k | v),
+ * o [B*S, H*64], in dtype.  d_mask: contiguous int64 [B, S] or NULL.
+ * workspace: device memory of gpt2k_attention_workspace_bytes(B, S) bytes
+ * (unused, may be NULL, when d_mask is NULL). */
+size_t gpt2k_attention_workspace_bytes(int B, int S);
+int gpt2k_attention(const void *qkv, const int64_t *d_mask, void *o, int B, int S, int H, int dtype,
+                    void *workspace, void *stream);
+
+/* Token + position embedding: x[t] = wte[ids[t]] + wpe[t % S] in dtype;
+ * out-of-range ids set the model-independent status word *d_status to 1. */
+int gpt2k_embed(const int64_t *d_ids, const void *wte, const void *wpe, void *x, int T, int S, int d, int V,
+                int dtype, int *d_status, void *stream);
+
+#if defined(__GNUC__)
+#pragma GCC visibility pop
+#endif
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* GPT2_B200_H */

@@ -1,0 +1,332 @@
+"""Python host mirror of libgpt2_b200.so (the C ABI in include/gpt2_b200.h).
+
+The reference calls its compiled GPT-2 through the memref C ABI from C++
+(src/gpt/gpt2_call.cpp:31-64) and defines the operator in Python as
+GPT2Wrapper.forward(input_ids, attention_mask) -> logits
+(src/gpt/lower_gpt_model.py:20-50).  This module binds the same entry points
+with ctypes:
+
+  * `gpt2_decoder(ids, mask)` / `ciface_gpt2_decoder(ids, mask)`: the two
+    drop-in symbols, numpy int64 [B, S] in, FP32 logits [B, S, V] out;
+  * `GPT2Decoder(...).forward(input_ids, attention_mask)`: the wrapper's
+    operator shape over the same library;
+  * device-side entry points (`forward_device`, kernel-level `k_*`) taking raw
+    device pointers, used by the benchmark and the parity tests.
+
+There is no CPU fallback: every call goes to the CUDA library, and importing
+fails loudly when the library has not been built.
+"""
+from __future__ import annotations
+
+import ctypes
+import os
+import subprocess
+
+import numpy as np
+
+HERE = os.path.dirname(os.path.abspath(__file__))
+LIB_PATH = os.path.join(HERE, "libgpt2_b200.so")
+HEADER = os.path.join(os.path.dirname(HERE), "include", "gpt2_b200.h")
+
+DTYPE_F32, DTYPE_BF16 = 0, 1
+EPI_NONE, EPI_BIAS, EPI_BIAS_GELU, EPI_BIAS_RESID = 0, 1, 2, 3
+STATUS_NAMES = {0: "ok", 1: "token id out of range", 2: "barrier wait timed out", 3: "bad launch"}
+
+
+class Gpt2Config(ctypes.Structure):
+    _fields_ = [
+        ("n_layer", ctypes.c_int32),
+        ("n_embd", ctypes.c_int32),
+        ("n_head", ctypes.c_int32),
+        ("n_inner", ctypes.c_int32),
+        ("vocab_size", ctypes.c_int32),
+        ("n_positions", ctypes.c_int32),
+        ("layer_norm_eps", ctypes.c_float),
+        ("dtype", ctypes.c_int32),
+    ]
+
+
+def gpt2_small(dtype: int = DTYPE_F32) -> Gpt2Config:
+    """GPT-2 124M: 12 layers, d 768, 12 heads of 64, MLP 3072, vocab 50257, ctx 1024."""
+    return Gpt2Config(12, 768, 12, 3072, 50257, 1024, 1e-5, dtype)
+
+
+class MemRef3D(ctypes.Structure):
+    _fields_ = [
+        ("allocated", ctypes.POINTER(ctypes.c_float)),
+        ("aligned", ctypes.POINTER(ctypes.c_float)),
+        ("offset", ctypes.c_int64),
+        ("sizes", ctypes.c_int64 * 3),
+        ("strides", ctypes.c_int64 * 3),
+    ]
+
+
+class MemRef2D_i64(ctypes.Structure):
+    _fields_ = [
+        ("allocated", ctypes.POINTER(ctypes.c_int64)),
+        ("aligned", ctypes.POINTER(ctypes.c_int64)),
+        ("offset", ctypes.c_int64),
+        ("sizes", ctypes.c_int64 * 2),
+        ("strides", ctypes.c_int64 * 2),
+    ]
+
+
+class Gpt2Error(RuntimeError):
+    pass
+
+
+def build(verbose: bool = False) -> str:
+    """Compiles libgpt2_b200.so in-tree with nvcc for sm_100a (make -C this directory)."""
+    out = subprocess.run(["make", "-C", HERE, "-j8"], capture_output=True, text=True)
+    if out.returncode != 0:
+        raise Gpt2Error("libgpt2_b200.so build failed:\n" + out.stdout[-4000:] + out.stderr[-4000:])
+    if verbose:
+        print(out.stdout)
+    return LIB_PATH
+
+
+_lib = None
+_libc = ctypes.CDLL(None)
+_libc.free.argtypes = [ctypes.c_void_p]
+
+
+def lib() -> ctypes.CDLL:
+    """The loaded C library; raises if it has not been built (no fallback)."""
+    global _lib
+    if _lib is not None:
+        return _lib
+    if not os.path.exists(LIB_PATH):
+        raise Gpt2Error(f"{LIB_PATH} is missing: build it with __graft_entry__.build() or make -C {HERE}")
+    L = ctypes.CDLL(LIB_PATH)
+    P, i64, i32, vp = ctypes.POINTER, ctypes.c_int64, ctypes.c_int, ctypes.c_void_p
+    L.gpt2_decoder.restype = MemRef3D
+    L.gpt2_decoder.argtypes = [P(i64), P(i64), i64, i64, i64, i64, i64, P(i64), P(i64), i64, i64, i64, i64, i64]
+    L._mlir_ciface_gpt2_decoder.restype = None
+    L._mlir_ciface_gpt2_decoder.argtypes = [P(MemRef3D), P(MemRef2D_i64), P(MemRef2D_i64)]
+    L.gpt2_init.argtypes = [P(Gpt2Config), i32]
+    L.gpt2_blob_floats.argtypes = [P(Gpt2Config)]
+    L.gpt2_blob_floats.restype = i64
+    L.gpt2_load_weights.argtypes = [vp, ctypes.c_size_t, ctypes.c_char_p]
+    L.gpt2_init_seeded.argtypes = [ctypes.c_uint64, i32]
+    L.gpt2_seeded_blob.argtypes = [P(Gpt2Config), ctypes.c_uint64, i32, P(ctypes.c_float)]
+    L.gpt2_seeded_ids.argtypes = [P(i64), i64, ctypes.c_uint64, ctypes.c_uint32, i64]
+    L.gpt2_get_config.argtypes = [P(Gpt2Config)]
+    L.gpt2_shutdown.restype = None
+    L.gpt2_last_error.restype = ctypes.c_char_p
+    L.gpt2_forward_device.argtypes = [vp, vp, i32, i32, vp, i64, i32, vp]
+    L.gpt2_forward_host.argtypes = [P(i64), P(i64), i32, i32, P(ctypes.c_float)]
+    L.gpt2_forward_launches.argtypes = [i32, i32, i32]
+    L.gpt2_profile_end.argtypes = [P(ctypes.c_double), P(i64), i32]
+    L.gpt2k_gemm_f32.argtypes = [vp, vp, i32, vp, i32, i32, i32, i32, vp, vp, i32, vp]
+    L.gpt2k_gemm_bf16.argtypes = [vp, vp, vp, i32, i32, i32, i32, i32, vp, vp, i32, i32, vp]
+    L.gpt2k_layernorm.argtypes = [vp, vp, vp, vp, i32, i32, ctypes.c_float, i32, vp]
+    L.gpt2k_attention_workspace_bytes.argtypes = [i32, i32]
+    L.gpt2k_attention_workspace_bytes.restype = ctypes.c_size_t
+    L.gpt2k_attention.argtypes = [vp, vp, vp, i32, i32, i32, i32, vp, vp]
+    L.gpt2k_embed.argtypes = [vp, vp, vp, vp, i32, i32, i32, i32, i32, vp, vp]
+    _lib = L
+    return L
+
+
+def last_error() -> str:
+    return lib().gpt2_last_error().decode()
+
+
+def _check(rc: int, what: str) -> int:
+    if rc < 0:
+        raise Gpt2Error(f"{what} failed ({rc}): {last_error()}")
+    return rc
+
+
+def declared_functions() -> list[str]:
+    """Names of the functions include/gpt2_b200.h declares."""
+    import re
+    text = open(HEADER).read()
+    text = re.sub(r"/\*.*?\*/", "", text, flags=re.S)
+    text = "\n".join(line for line in text.splitlines() if not line.lstrip().startswith("#"))
+    return sorted(set(re.findall(r"\b([A-Za-z_][A-Za-z0-9_]*)\s*\(", text)))
+
+
+# ---------------------------------------------------------------------------
+# model management
+# ---------------------------------------------------------------------------
+def init(cfg: Gpt2Config, device: int = -1) -> None:
+    _check(lib().gpt2_init(ctypes.byref(cfg), device), "gpt2_init")
+
+
+def get_config() -> Gpt2Config:
+    cfg = Gpt2Config()
+    _check(lib().gpt2_get_config(ctypes.byref(cfg)), "gpt2_get_config")
+    return cfg
+
+
+def blob_floats(cfg: Gpt2Config) -> int:
+    return _check(lib().gpt2_blob_floats(ctypes.byref(cfg)), "gpt2_blob_floats")
+
+
+def seeded_blob(cfg: Gpt2Config, seed: int, init_mode: int = 0) -> np.ndarray:
+    out = np.empty(blob_floats(cfg), dtype=np.float32)
+    _check(lib().gpt2_seeded_blob(ctypes.byref(cfg), seed, init_mode,
+                                  out.ctypes.data_as(ctypes.POINTER(ctypes.c_float))), "gpt2_seeded_blob")
+    return out
+
+
+def seeded_ids(B: int, S: int, seed: int, vocab: int, stream: int = 0x10000) -> np.ndarray:
+    out = np.empty(B * S, dtype=np.int64)
+    _check(lib().gpt2_seeded_ids(out.ctypes.data_as(ctypes.POINTER(ctypes.c_int64)), B * S, seed, stream, vocab),
+           "gpt2_seeded_ids")
+    return out.reshape(B, S)
+
+
+def load_weights(blob: np.ndarray, manifest: str | None = None) -> None:
+    blob = np.ascontiguousarray(blob, dtype=np.float32)
+    _check(lib().gpt2_load_weights(blob.ctypes.data, blob.nbytes, manifest.encode() if manifest else None),
+           "gpt2_load_weights")
+
+
+def init_seeded(seed: int, init_mode: int = 0) -> None:
+    _check(lib().gpt2_init_seeded(seed, init_mode), "gpt2_init_seeded")
+
+
+def shutdown() -> None:
+    lib().gpt2_shutdown()
+
+
+def status() -> int:
+    return lib().gpt2_status()
+
+
+def forward_launches(B: int, S: int, has_mask: bool) -> int:
+    return _check(lib().gpt2_forward_launches(B, S, int(has_mask)), "gpt2_forward_launches")
+
+
+# ---------------------------------------------------------------------------
+# forward entry points
+# ---------------------------------------------------------------------------
+def _as_i64(a) -> np.ndarray:
+    a = np.asarray(a, dtype=np.int64)
+    if a.ndim != 2:
+        raise ValueError("ids and mask are [B, S]")
+    return a
+
+
+def _take_memref(m: MemRef3D) -> np.ndarray:
+    if not m.allocated:
+        raise Gpt2Error(f"gpt2_decoder failed: {last_error()}")
+    n = m.sizes[0] * m.sizes[1] * m.sizes[2]
+    view = np.ctypeslib.as_array(m.aligned, shape=(n,))
+    out = view.reshape(m.sizes[0], m.sizes[1], m.sizes[2]).copy()
+    _libc.free(ctypes.cast(m.allocated, ctypes.c_void_p))
+    return out
+
+
+def gpt2_decoder(input_ids, attention_mask=None) -> np.ndarray:
+    """Calls the decomposed-memref `gpt2_decoder` exactly as src/gpt/gpt2_call.cpp:62-64 does
+    (strides honoured, malloc'd result freed after copying)."""
+    ids = _as_i64(input_ids)
+    mask = _as_i64(attention_mask) if attention_mask is not None else np.ones_like(ids)
+    P = ctypes.POINTER(ctypes.c_int64)
+    ip, mp = ids.ctypes.data_as(P), mask.ctypes.data_as(P)
+    isz, msz = ids.itemsize, mask.itemsize
+    m = lib().gpt2_decoder(ip, ip, 0, ids.shape[0], ids.shape[1], ids.strides[0] // isz, ids.strides[1] // isz,
+                           mp, mp, 0, mask.shape[0], mask.shape[1], mask.strides[0] // msz, mask.strides[1] // msz)
+    return _take_memref(m)
+
+
+def ciface_gpt2_decoder(input_ids, attention_mask=None) -> np.ndarray:
+    """Calls `_mlir_ciface_gpt2_decoder` (descriptor pointers, result out-parameter)."""
+    ids = _as_i64(input_ids)
+    mask = _as_i64(attention_mask) if attention_mask is not None else np.ones_like(ids)
+
+    def desc(a):
+        p = a.ctypes.data_as(ctypes.POINTER(ctypes.c_int64))
+        return MemRef2D_i64(p, p, 0, (ctypes.c_int64 * 2)(*a.shape),
+                            (ctypes.c_int64 * 2)(a.strides[0] // a.itemsize, a.strides[1] // a.itemsize))
+
+    res = MemRef3D()
+    di, dm = desc(ids), desc(mask)
+    lib()._mlir_ciface_gpt2_decoder(ctypes.byref(res), ctypes.byref(di), ctypes.byref(dm))
+    return _take_memref(res)
+
+
+def forward_host(input_ids, attention_mask=None) -> np.ndarray:
+    ids = np.ascontiguousarray(_as_i64(input_ids))
+    B, S = ids.shape
+    mask_p = None
+    if attention_mask is not None:
+        mask = np.ascontiguousarray(_as_i64(attention_mask))
+        mask_p = mask.ctypes.data_as(ctypes.POINTER(ctypes.c_int64))
+    vocab = get_config().vocab_size
+    out = np.empty((B, S, vocab), dtype=np.float32)
+    _check(lib().gpt2_forward_host(ids.ctypes.data_as(ctypes.POINTER(ctypes.c_int64)), mask_p, B, S,
+                                   out.ctypes.data_as(ctypes.POINTER(ctypes.c_float))), "gpt2_forward_host")
+    return out
+
+
+def forward_device(ids_ptr: int, mask_ptr: int | None, B: int, S: int, logits_ptr: int, ld_logits: int,
+                   stream_ptr: int | None = None) -> None:
+    _check(lib().gpt2_forward_device(ids_ptr, mask_ptr, B, S, logits_ptr, ld_logits, DTYPE_F32, stream_ptr),
+           "gpt2_forward_device")
+
+
+KERNEL_KINDS = ["seq_info", "embed", "layernorm", "gemm_qkv", "attention", "masked_rows", "gemm_proj", "gemm_fc",
+                "gemm_mproj", "lm_head"]
+
+
+def profile_begin() -> None:
+    _check(lib().gpt2_profile_begin(), "gpt2_profile_begin")
+
+
+def profile_end() -> dict:
+    """{kind: (total ms, launches)} of the launches since profile_begin()."""
+    n = len(KERNEL_KINDS)
+    ms = (ctypes.c_double * n)()
+    cnt = (ctypes.c_int64 * n)()
+    _check(lib().gpt2_profile_end(ms, cnt, n), "gpt2_profile_end")
+    return {k: (ms[i], cnt[i]) for i, k in enumerate(KERNEL_KINDS)}
+
+
+class GPT2Decoder:
+    """Operator shape of the reference's GPT2Wrapper (src/gpt/lower_gpt_model.py:20-50): full logits
+    [B, S, V] for (input_ids, attention_mask), here backed by the B200 library."""
+
+    def __init__(self, cfg: Gpt2Config | None = None, seed: int = 1234, init_mode: int = 0,
+                 blob: np.ndarray | None = None, device: int = -1):
+        self.cfg = cfg or gpt2_small()
+        init(self.cfg, device)
+        if blob is not None:
+            load_weights(blob)
+        else:
+            init_seeded(seed, init_mode)
+
+    def forward(self, input_ids, attention_mask=None) -> np.ndarray:
+        return forward_host(input_ids, attention_mask)
+
+    __call__ = forward
+
+
+# ---------------------------------------------------------------------------
+# kernel-level entry points (device pointers as ints)
+# ---------------------------------------------------------------------------
+def k_gemm_f32(A, B, b_nk, C, M, N, K, ldc, bias=None, resid=None, epi=EPI_NONE, stream=None):
+    _check(lib().gpt2k_gemm_f32(A, B, b_nk, C, M, N, K, ldc, bias, resid, epi, stream), "gpt2k_gemm_f32")
+
+
+def k_gemm_bf16(A, B, C, M, N, K, ldc, out_f32=0, bias=None, resid=None, epi=EPI_NONE, bn=256, stream=None):
+    _check(lib().gpt2k_gemm_bf16(A, B, C, M, N, K, ldc, out_f32, bias, resid, epi, bn, stream), "gpt2k_gemm_bf16")
+
+
+def k_layernorm(x, gain, shift, y, T, d, eps, dtype, stream=None):
+    _check(lib().gpt2k_layernorm(x, gain, shift, y, T, d, eps, dtype, stream), "gpt2k_layernorm")
+
+
+def k_attention_workspace_bytes(B, S) -> int:
+    return int(lib().gpt2k_attention_workspace_bytes(B, S))
+
+
+def k_attention(qkv, mask, o, B, S, H, dtype, workspace=None, stream=None):
+    _check(lib().gpt2k_attention(qkv, mask, o, B, S, H, dtype, workspace, stream), "gpt2k_attention")
+
+
+def k_embed(ids, wte, wpe, x, T, S, d, V, dtype, status_ptr=None, stream=None):
+    _check(lib().gpt2k_embed(ids, wte, wpe, x, T, S, d, V, dtype, status_ptr, stream), "gpt2k_embed")

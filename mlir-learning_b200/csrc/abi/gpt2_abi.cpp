@@ -1,0 +1,472 @@
+// gpt2_abi.cpp -- the C ABI of libgpt2_b200.so (include/gpt2_b200.h).
+//
+// gpt2_decoder / _mlir_ciface_gpt2_decoder reproduce the entry points the
+// reference's host program links against (src/gpt/gpt2_call.cpp:17-38,
+// :62-64) and its CPU pipeline emits (src/gpt/run_mlir_pipeline.sh:7): ids and
+// mask memrefs in, a malloc'd FP32 logits memref out (freed by the caller,
+// src/gpt/gpt2_call.cpp:93-94).  Nothing here aborts: failures return a
+// zeroed descriptor or a negative code plus gpt2_last_error().
+#include <stdlib.h>
+#include <string.h>
+
+#include <string>
+#include <vector>
+
+#include "../../../include/gpt2_b200.h"
+#include "../runtime/runtime.h"
+
+namespace gpt2 {
+const char *last_error_text();
+void clear_error();
+}  // namespace gpt2
+
+using namespace gpt2;
+
+namespace {
+std::mutex g_api_mu;  // serialises every entry point that touches the model
+
+ModelDims dims_of(const Gpt2Config *c) {
+  ModelDims m;
+  m.n_layer = c->n_layer;
+  m.n_embd = c->n_embd;
+  m.n_head = c->n_head;
+  m.n_inner = c->n_inner;
+  m.vocab = c->vocab_size;
+  m.n_pos = c->n_positions;
+  m.eps = c->layer_norm_eps;
+  return m;
+}
+
+bool valid_dims(const Gpt2Config *c) {
+  return c && c->n_layer > 0 && c->n_embd > 0 && c->n_head > 0 && c->n_inner > 0 && c->vocab_size > 0 &&
+         c->n_positions > 0;
+}
+
+int load_seeded_locked(uint64_t seed, int init_mode) {
+  Context *c = context();
+  if (!c) {
+    set_error("no model: call gpt2_init first");
+    return GPT2_ENOMODEL;
+  }
+  std::vector<float> blob(static_cast<size_t>(blob_floats(c->dims)));
+  seeded_blob(c->dims, seed, init_mode, blob.data());
+  return load_blob(*c, blob.data());
+}
+
+// Creates GPT-2 small with seeded weights when no model exists (the
+// reference's object file carries its weights; this is the stand-in).
+int ensure_default_model_locked() {
+  Context *c = context();
+  if (c && c->loaded) return 0;
+  if (!c) {
+    int dtype = GPT2_DTYPE_F32;
+    if (const char *e = getenv("GPT2_DTYPE")) {
+      if (!strcmp(e, "bf16")) dtype = GPT2_DTYPE_BF16;
+      else if (strcmp(e, "f32") && strcmp(e, "fp32")) {
+        set_error("GPT2_DTYPE must be f32 or bf16, got '%s'", e);
+        return GPT2_EINVAL;
+      }
+    }
+    int r = create_context(ModelDims(), dtype, -1);
+    if (r) return r;
+  }
+  uint64_t seed = 1234;
+  if (const char *e = getenv("GPT2_SEED")) seed = strtoull(e, nullptr, 10);
+  return load_seeded_locked(seed, 0);
+}
+
+int read_status_locked(Context &c) {
+  int h = 0;
+  if (cudaMemcpy(&h, c.d_status, sizeof(int), cudaMemcpyDeviceToHost) != cudaSuccess) return -1;
+  if (h) cudaMemset(c.d_status, 0, sizeof(int));
+  return h;
+}
+
+// Gathers a strided memref<?x?xi64> into a contiguous [B, S] vector.
+void gather_i64(const int64_t *aligned, int64_t off, int64_t s0, int64_t s1, int64_t st0, int64_t st1,
+                std::vector<int64_t> &out) {
+  out.resize(static_cast<size_t>(s0 * s1));
+  for (int64_t i = 0; i < s0; ++i)
+    for (int64_t j = 0; j < s1; ++j) out[i * s1 + j] = aligned[off + i * st0 + j * st1];
+}
+
+int forward_host_locked(const int64_t *ids, const int64_t *mask, int B, int S, float *logits) {
+  int r = ensure_default_model_locked();
+  if (r) return r;
+  Context &c = *context();
+  if (cudaSetDevice(c.device) != cudaSuccess) {
+    set_error("cudaSetDevice(%d) failed", c.device);
+    return GPT2_ECUDA;
+  }
+  const int64_t T = (int64_t)B * S;
+  if (B < 1 || S < 1 || S > c.dims.n_pos) {
+    set_error("bad shape B=%d S=%d (n_positions %d)", B, S, c.dims.n_pos);
+    return GPT2_EINVAL;
+  }
+  // Host-side check of the ids gives the caller a precise error; the embed
+  // kernel also checks and reports through the status word.
+  for (int64_t i = 0; i < T; ++i)
+    if (ids[i] < 0 || ids[i] >= c.dims.vocab) {
+      set_error("token id %lld at position %lld outside [0, %d)", (long long)ids[i], (long long)i, c.dims.vocab);
+      return GPT2_EINVAL;
+    }
+  // Staging buffers and a device logits buffer, grown on demand.
+  Workspace &w = c.ws;
+  r = ensure_workspace(c, B, S);
+  if (r) return r;
+  const int64_t V = c.dims.vocab;
+  if (!w.logits || w.logits_T < T) {
+    if (w.logits) cudaFree(w.logits);
+    w.logits = nullptr;
+    w.logits_T = 0;
+    if (cudaMalloc(&w.logits, sizeof(float) * T * V) != cudaSuccess) {
+      set_error("cudaMalloc of %lld logits failed", (long long)(T * V));
+      return GPT2_ENOMEM;
+    }
+    w.logits_T = T;
+  }
+  cudaStream_t st = c.stream;
+  if (cudaMemcpyAsync(w.ids, ids, sizeof(int64_t) * T, cudaMemcpyHostToDevice, st) != cudaSuccess ||
+      (mask && cudaMemcpyAsync(w.mask, mask, sizeof(int64_t) * T, cudaMemcpyHostToDevice, st) != cudaSuccess)) {
+    set_error("host-to-device copy of ids/mask failed");
+    return GPT2_ECUDA;
+  }
+  r = forward_device(c, w.ids, mask ? w.mask : nullptr, B, S, w.logits, V, st);
+  if (r) return r;
+  cudaError_t e = cudaMemcpyAsync(logits, w.logits, sizeof(float) * T * V, cudaMemcpyDeviceToHost, st);
+  if (e == cudaSuccess) e = cudaStreamSynchronize(st);
+  if (e != cudaSuccess) {
+    set_error("forward failed: %s", cudaGetErrorString(e));
+    return GPT2_ECUDA;
+  }
+  const int s = read_status_locked(c);
+  if (s) {
+    set_error("device status %d after forward", s);
+    return GPT2_EDEVICE;
+  }
+  return 0;
+}
+
+MemRef3D decoder_impl(const int64_t *ids_aligned, int64_t ids_off, int64_t is0, int64_t is1, int64_t ist0,
+                      int64_t ist1, const int64_t *m_aligned, int64_t m_off, int64_t ms0, int64_t ms1, int64_t mst0,
+                      int64_t mst1) {
+  MemRef3D out;
+  memset(&out, 0, sizeof out);
+  std::lock_guard<std::mutex> lk(g_api_mu);
+  clear_error();
+  if (!ids_aligned || is0 < 1 || is1 < 1 || is0 > (1 << 20) || is1 > (1 << 20)) {
+    set_error("gpt2_decoder: bad input_ids memref (sizes %lld x %lld)", (long long)is0, (long long)is1);
+    return out;
+  }
+  std::vector<int64_t> ids, mask;
+  gather_i64(ids_aligned, ids_off, is0, is1, ist0, ist1, ids);
+  bool has_mask = false;
+  if (m_aligned) {
+    if (ms0 != is0 || ms1 != is1) {
+      set_error("gpt2_decoder: attention_mask sizes %lld x %lld differ from input_ids %lld x %lld", (long long)ms0,
+                (long long)ms1, (long long)is0, (long long)is1);
+      return out;
+    }
+    gather_i64(m_aligned, m_off, ms0, ms1, mst0, mst1, mask);
+    for (int64_t v : mask)
+      if (v == 0) {
+        has_mask = true;
+        break;
+      }
+  }
+  int r = ensure_default_model_locked();
+  if (r) return out;
+  const int64_t V = context()->dims.vocab;
+  const int64_t n = is0 * is1 * V;
+  float *buf = static_cast<float *>(malloc(sizeof(float) * n));
+  if (!buf) {
+    set_error("gpt2_decoder: malloc of %lld floats failed", (long long)n);
+    return out;
+  }
+  // An all-ones mask is the unmasked computation; skip its kernels.
+  r = forward_host_locked(ids.data(), has_mask ? mask.data() : nullptr, (int)is0, (int)is1, buf);
+  if (r) {
+    free(buf);
+    return out;
+  }
+  out.allocated = buf;
+  out.aligned = buf;
+  out.offset = 0;
+  out.sizes[0] = is0;
+  out.sizes[1] = is1;
+  out.sizes[2] = V;
+  out.strides[0] = is1 * V;
+  out.strides[1] = V;
+  out.strides[2] = 1;
+  return out;
+}
+}  // namespace
+
+extern "C" {
+
+MemRef3D gpt2_decoder(int64_t *in_alloc, int64_t *in_align, int64_t in_offs, int64_t in_s0, int64_t in_s1,
+                      int64_t in_str0, int64_t in_str1, int64_t *mask_alloc, int64_t *mask_align,
+                      int64_t mask_offs, int64_t mask_s0, int64_t mask_s1, int64_t mask_str0, int64_t mask_str1) {
+  (void)in_alloc;
+  (void)mask_alloc;
+  return decoder_impl(in_align, in_offs, in_s0, in_s1, in_str0, in_str1, mask_align, mask_offs, mask_s0, mask_s1,
+                      mask_str0, mask_str1);
+}
+
+void _mlir_ciface_gpt2_decoder(MemRef3D *result, MemRef2D_i64 *input_ids, MemRef2D_i64 *attention_mask) {
+  if (!result) return;
+  if (!input_ids) {
+    memset(result, 0, sizeof *result);
+    set_error("_mlir_ciface_gpt2_decoder: null input_ids");
+    return;
+  }
+  const MemRef2D_i64 *m = attention_mask;
+  *result = decoder_impl(input_ids->aligned, input_ids->offset, input_ids->sizes[0], input_ids->sizes[1],
+                         input_ids->strides[0], input_ids->strides[1], m ? m->aligned : nullptr, m ? m->offset : 0,
+                         m ? m->sizes[0] : 0, m ? m->sizes[1] : 0, m ? m->strides[0] : 0, m ? m->strides[1] : 0);
+}
+
+int gpt2_init(const Gpt2Config *cfg, int device) {
+  std::lock_guard<std::mutex> lk(g_api_mu);
+  clear_error();
+  if (!valid_dims(cfg)) {
+    set_error("gpt2_init: invalid configuration");
+    return GPT2_EINVAL;
+  }
+  return create_context(dims_of(cfg), cfg->dtype, device);
+}
+
+int64_t gpt2_blob_floats(const Gpt2Config *cfg) {
+  if (!valid_dims(cfg)) return GPT2_EINVAL;
+  return blob_floats(dims_of(cfg));
+}
+
+int gpt2_load_weights(const void *packed, size_t bytes, const char *manifest_json) {
+  std::lock_guard<std::mutex> lk(g_api_mu);
+  clear_error();
+  Context *c = context();
+  if (!c) {
+    set_error("gpt2_load_weights: no model, call gpt2_init first");
+    return GPT2_ENOMODEL;
+  }
+  if (!packed || bytes != sizeof(float) * static_cast<size_t>(blob_floats(c->dims))) {
+    set_error("gpt2_load_weights: expected %lld bytes of canonical FP32 blob, got %zu",
+              (long long)(sizeof(float) * blob_floats(c->dims)), bytes);
+    return GPT2_EINVAL;
+  }
+  if (manifest_json && !strstr(manifest_json, "gpt2-canonical-f32-v1")) {
+    set_error("gpt2_load_weights: manifest layout must be \"gpt2-canonical-f32-v1\"");
+    return GPT2_EINVAL;
+  }
+  return load_blob(*c, static_cast<const float *>(packed));
+}
+
+int gpt2_init_seeded(uint64_t seed, int init_mode) {
+  std::lock_guard<std::mutex> lk(g_api_mu);
+  clear_error();
+  if (init_mode != 0 && init_mode != 1) {
+    set_error("gpt2_init_seeded: init_mode must be 0 or 1");
+    return GPT2_EINVAL;
+  }
+  return load_seeded_locked(seed, init_mode);
+}
+
+int gpt2_seeded_blob(const Gpt2Config *cfg, uint64_t seed, int init_mode, float *out) {
+  if (!valid_dims(cfg) || !out || (init_mode != 0 && init_mode != 1)) return GPT2_EINVAL;
+  seeded_blob(dims_of(cfg), seed, init_mode, out);
+  return 0;
+}
+
+int gpt2_seeded_ids(int64_t *ids, int64_t n, uint64_t seed, uint32_t stream, int64_t vocab) {
+  if (!ids || n < 0 || vocab < 1) return GPT2_EINVAL;
+  seeded_ids(ids, n, seed, stream, vocab);
+  return 0;
+}
+
+int gpt2_get_config(Gpt2Config *out) {
+  std::lock_guard<std::mutex> lk(g_api_mu);
+  Context *c = context();
+  if (!c) {
+    set_error("gpt2_get_config: no model");
+    return GPT2_ENOMODEL;
+  }
+  if (!out) return GPT2_EINVAL;
+  out->n_layer = c->dims.n_layer;
+  out->n_embd = c->dims.n_embd;
+  out->n_head = c->dims.n_head;
+  out->n_inner = c->dims.n_inner;
+  out->vocab_size = c->dims.vocab;
+  out->n_positions = c->dims.n_pos;
+  out->layer_norm_eps = c->dims.eps;
+  out->dtype = c->dtype;
+  return 0;
+}
+
+void gpt2_shutdown(void) {
+  std::lock_guard<std::mutex> lk(g_api_mu);
+  destroy_context();
+}
+
+const char *gpt2_last_error(void) { return last_error_text(); }
+
+int gpt2_status(void) {
+  std::lock_guard<std::mutex> lk(g_api_mu);
+  Context *c = context();
+  if (!c) return GPT2_ENOMODEL;
+  cudaSetDevice(c->device);
+  return read_status_locked(*c);
+}
+
+int gpt2_forward_device(const int64_t *d_ids, const int64_t *d_mask, int B, int S, void *d_logits,
+                        int64_t ld_logits, int logits_dtype, void *stream) {
+  std::lock_guard<std::mutex> lk(g_api_mu);
+  clear_error();
+  Context *c = context();
+  if (!c || !c->loaded) {
+    set_error("gpt2_forward_device: no model loaded");
+    return GPT2_ENOMODEL;
+  }
+  if (logits_dtype != GPT2_DTYPE_F32 || !d_ids || !d_logits) {
+    set_error("gpt2_forward_device: need ids, logits and logits_dtype GPT2_DTYPE_F32");
+    return GPT2_EINVAL;
+  }
+  cudaSetDevice(c->device);
+  cudaStream_t st = stream ? static_cast<cudaStream_t>(stream) : c->stream;
+  return forward_device(*c, d_ids, d_mask, B, S, static_cast<float *>(d_logits), ld_logits, st);
+}
+
+int gpt2_forward_host(const int64_t *ids, const int64_t *mask, int B, int S, float *logits) {
+  std::lock_guard<std::mutex> lk(g_api_mu);
+  clear_error();
+  if (!ids || !logits) {
+    set_error("gpt2_forward_host: null ids or logits");
+    return GPT2_EINVAL;
+  }
+  return forward_host_locked(ids, mask, B, S, logits);
+}
+
+int gpt2_forward_launches(int B, int S, int has_mask) {
+  (void)B;
+  (void)S;
+  Context *c = context();
+  if (!c) return GPT2_ENOMODEL;
+  return forward_launch_count(*c, has_mask);
+}
+
+int gpt2_profile_begin(void) {
+  std::lock_guard<std::mutex> lk(g_api_mu);
+  Context *c = context();
+  if (!c) return GPT2_ENOMODEL;
+  return profile_begin(*c);
+}
+
+int gpt2_profile_end(double *ms_per_kind, int64_t *launches_per_kind, int n_kinds) {
+  std::lock_guard<std::mutex> lk(g_api_mu);
+  Context *c = context();
+  if (!c) return GPT2_ENOMODEL;
+  if (!ms_per_kind || !launches_per_kind || n_kinds < 0) return GPT2_EINVAL;
+  cudaSetDevice(c->device);
+  return profile_end(*c, ms_per_kind, launches_per_kind, n_kinds < K_NUM_KINDS ? n_kinds : K_NUM_KINDS);
+}
+
+// ---------------------------------------------------------------------------
+// Kernel-level entry points
+// ---------------------------------------------------------------------------
+static int ck(cudaError_t e, const char *what) {
+  if (e == cudaSuccess) return 0;
+  set_error("%s: %s", what, cudaGetErrorString(e));
+  return e == cudaErrorInvalidValue ? GPT2_EINVAL : GPT2_ECUDA;
+}
+
+int gpt2k_gemm_f32(const float *A, const float *B, int b_nk, float *C, int M, int N, int K, int ldc,
+                   const float *bias, const float *resid, int epi, void *stream) {
+  return ck(launch_gemm_f32(A, B, b_nk, C, M, N, K, ldc, bias, resid, epi, static_cast<cudaStream_t>(stream)),
+            "gpt2k_gemm_f32");
+}
+
+int gpt2k_gemm_bf16(const void *A, const void *B, void *C, int M, int N, int K, int ldc, int out_f32,
+                    const float *bias, const void *resid, int epi, int bn, void *stream) {
+  TcGemmPlan plan;
+  const int r = tc_gemm_plan(&plan, static_cast<const bf16 *>(A), static_cast<const bf16 *>(B), M, N, K, bn);
+  if (r) {
+    set_error("gpt2k_gemm_bf16: TMA descriptor creation failed (%d)", r);
+    return GPT2_EINVAL;
+  }
+  int dev = 0, sms = 148;
+  cudaGetDevice(&dev);
+  cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+  return ck(launch_gemm_tc(plan, C, ldc, out_f32, bias, static_cast<const bf16 *>(resid), epi, nullptr, sms,
+                           static_cast<cudaStream_t>(stream)),
+            "gpt2k_gemm_bf16");
+}
+
+int gpt2k_layernorm(const void *x, const float *gain, const float *shift, void *y, int T, int d, float eps,
+                    int dtype, void *stream) {
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  if (dtype == GPT2_DTYPE_F32)
+    return ck(launch_layernorm_f32(static_cast<const float *>(x), gain, shift, static_cast<float *>(y), T, d, eps, st),
+              "gpt2k_layernorm");
+  if (dtype == GPT2_DTYPE_BF16)
+    return ck(launch_layernorm_bf16(static_cast<const bf16 *>(x), gain, shift, static_cast<bf16 *>(y), T, d, eps, st),
+              "gpt2k_layernorm");
+  set_error("gpt2k_layernorm: bad dtype");
+  return GPT2_EINVAL;
+}
+
+size_t gpt2k_attention_workspace_bytes(int B, int S) {
+  return 256 + sizeof(int) * (size_t)B + (size_t)B * S;
+}
+
+int gpt2k_attention(const void *qkv, const int64_t *d_mask, void *o, int B, int S, int H, int dtype, void *workspace,
+                    void *stream) {
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  int *first_valid = nullptr;
+  uint8_t *key_valid = nullptr;
+  if (d_mask) {
+    if (!workspace) {
+      set_error("gpt2k_attention: a mask needs a workspace");
+      return GPT2_EINVAL;
+    }
+    first_valid = static_cast<int *>(workspace);
+    key_valid = static_cast<uint8_t *>(workspace) + 256 + sizeof(int) * (size_t)B;
+    int r = ck(launch_seq_info(d_mask, B, S, first_valid, key_valid, st), "gpt2k_attention");
+    if (r) return r;
+  }
+  int r;
+  if (dtype == GPT2_DTYPE_F32) {
+    r = ck(launch_attention_f32(static_cast<const float *>(qkv), key_valid, static_cast<float *>(o), B, S, H, st),
+           "gpt2k_attention");
+    if (!r && d_mask)
+      r = ck(launch_attn_masked_rows_f32(static_cast<const float *>(qkv), first_valid, static_cast<float *>(o), B, S,
+                                         H, st),
+             "gpt2k_attention");
+  } else if (dtype == GPT2_DTYPE_BF16) {
+    r = ck(launch_attention_bf16(static_cast<const bf16 *>(qkv), key_valid, static_cast<bf16 *>(o), B, S, H, st),
+           "gpt2k_attention");
+    if (!r && d_mask)
+      r = ck(launch_attn_masked_rows_bf16(static_cast<const bf16 *>(qkv), first_valid, static_cast<bf16 *>(o), B, S,
+                                          H, st),
+             "gpt2k_attention");
+  } else {
+    set_error("gpt2k_attention: bad dtype");
+    return GPT2_EINVAL;
+  }
+  return r;
+}
+
+int gpt2k_embed(const int64_t *d_ids, const void *wte, const void *wpe, void *x, int T, int S, int d, int V, int dtype,
+                int *d_status, void *stream) {
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  if (dtype == GPT2_DTYPE_F32)
+    return ck(launch_embed_f32(d_ids, static_cast<const float *>(wte), static_cast<const float *>(wpe),
+                               static_cast<float *>(x), T, S, d, V, d_status, st),
+              "gpt2k_embed");
+  if (dtype == GPT2_DTYPE_BF16)
+    return ck(launch_embed_bf16(d_ids, static_cast<const bf16 *>(wte), static_cast<const bf16 *>(wpe),
+                                static_cast<bf16 *>(x), T, S, d, V, d_status, st),
+              "gpt2k_embed");
+  set_error("gpt2k_embed: bad dtype");
+  return GPT2_EINVAL;
+}
+
+}  // extern "C"

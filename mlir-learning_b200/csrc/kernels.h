@@ -1,0 +1,94 @@
+// kernels.h -- host launchers of the GPT-2 device kernels (internal API of
+// libgpt2_b200.so; the public C ABI is include/gpt2_b200.h).
+#pragma once
+
+#include <cuda.h>
+#include <cuda_bf16.h>
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+#include <atomic>
+
+namespace gpt2 {
+
+typedef __nv_bfloat16 bf16;
+
+// Raises a kernel's dynamic shared-memory limit once per device (the
+// attribute is per device; `done` holds one bit per device ordinal).
+template <typename Kernel>
+inline cudaError_t set_smem_once(Kernel kernel, int bytes, std::atomic<uint64_t> &done) {
+  int dev = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) return e;
+  const uint64_t bit = 1ull << (dev & 63);
+  if (done.load() & bit) return cudaSuccess;
+  e = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes);
+  if (e == cudaSuccess) done.fetch_or(bit);
+  return e;
+}
+
+// Epilogue applied to C = A @ B (+ ...), fused into every GEMM:
+//   EPI_NONE       C = acc
+//   EPI_BIAS       C = acc + bias[col]
+//   EPI_BIAS_GELU  C = gelu_new(acc + bias[col])
+//   EPI_BIAS_RESID C = resid[row, col] + (acc + bias[col])   (resid may alias C)
+enum Epilogue : int { EPI_NONE = 0, EPI_BIAS = 1, EPI_BIAS_GELU = 2, EPI_BIAS_RESID = 3 };
+
+// ---- sequence / mask preparation -------------------------------------------
+// first_valid[b] = smallest k with mask[b, k] != 0 (S if none);
+// key_valid[b*S + k] = mask[b, k] != 0.  mask is contiguous [B, S] int64.
+cudaError_t launch_seq_info(const int64_t *mask, int B, int S, int *first_valid, uint8_t *key_valid,
+                            cudaStream_t st);
+
+// ---- embedding: x[t] = wte[ids[t]] + wpe[t % S] -------------------------------
+cudaError_t launch_embed_f32(const int64_t *ids, const float *wte, const float *wpe, float *x, int T, int S, int d,
+                             int V, int *status, cudaStream_t st);
+cudaError_t launch_embed_bf16(const int64_t *ids, const bf16 *wte, const bf16 *wpe, bf16 *x, int T, int S, int d,
+                              int V, int *status, cudaStream_t st);
+
+// ---- LayerNorm (biased variance, FP32 statistics) ----------------------------
+cudaError_t launch_layernorm_f32(const float *x, const float *g, const float *b, float *y, int T, int d, float eps,
+                                 cudaStream_t st);
+cudaError_t launch_layernorm_bf16(const bf16 *x, const float *g, const float *b, bf16 *y, int T, int d, float eps,
+                                  cudaStream_t st);
+
+// ---- exact-FP32 SIMT GEMM ----------------------------------------------------
+// C[M, N] (row stride ldc) = epilogue(A[M, K] @ op(B)), op(B) = B[K, N] when
+// b_nk == 0 (Conv1D weight) or B[N, K]^T when b_nk == 1 (tied lm_head).
+// resid has row stride ldc.
+cudaError_t launch_gemm_f32(const float *A, const float *B, int b_nk, float *C, int M, int N, int K, int ldc,
+                            const float *bias, const float *resid, int epi, cudaStream_t st);
+
+// ---- tcgen05 BF16 GEMM -------------------------------------------------------
+// C[M, N] = epilogue(A[M, K] @ B[N, K]^T), A and B bf16 K-major, f32 accumulate
+// in TMEM.  out_f32 selects an FP32 output (lm_head logits) instead of bf16.
+struct TcGemmPlan {
+  CUtensorMap map_a;
+  CUtensorMap map_b;
+  int M, N, K;
+  int bn;  // 128 or 256
+};
+// Builds the TMA descriptors; returns 0 or a negative error.
+int tc_gemm_plan(TcGemmPlan *plan, const bf16 *A, const bf16 *B, int M, int N, int K, int bn);
+cudaError_t launch_gemm_tc(const TcGemmPlan &plan, void *C, int ldc, int out_f32, const float *bias,
+                           const bf16 *resid, int epi, int *status, int num_sms, cudaStream_t st);
+
+// ---- attention ----------------------------------------------------------------
+// qkv [B*S, 3*H*64] (q | k | v, head h at columns h*64), o [B*S, H*64].
+// key_valid may be null (all keys valid); a query row with no attendable key
+// is written by launch_attn_masked_rows afterwards.
+cudaError_t launch_attention_f32(const float *qkv, const uint8_t *key_valid, float *o, int B, int S, int H,
+                                 cudaStream_t st);
+cudaError_t launch_attention_bf16(const bf16 *qkv, const uint8_t *key_valid, bf16 *o, int B, int S, int H,
+                                  cudaStream_t st);
+// Rows q < first_valid[b] (no attendable key) get the mean of V over all S keys.
+cudaError_t launch_attn_masked_rows_f32(const float *qkv, const int *first_valid, float *o, int B, int S, int H,
+                                        cudaStream_t st);
+cudaError_t launch_attn_masked_rows_bf16(const bf16 *qkv, const int *first_valid, bf16 *o, int B, int S, int H,
+                                         cudaStream_t st);
+
+// ---- weight packing --------------------------------------------------------
+// dst[N, K] (bf16) = transpose(src[K, N] fp32); dst[r, c] = bf16(src[r, c]) when transpose == 0.
+cudaError_t launch_pack_bf16(const float *src, bf16 *dst, int rows, int cols, int transpose, cudaStream_t st);
+
+}  // namespace gpt2

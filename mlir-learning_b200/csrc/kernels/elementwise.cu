@@ -1,0 +1,286 @@
+// elementwise.cu -- the bandwidth-bound kernels of the GPT-2 forward:
+// mask preparation, token + position embedding, LayerNorm, weight packing.
+//
+// These replace the reference's gather / reduction / elementwise
+// linalg.generic launches (README.md:11, :49; LayerNorm mean/var over 768
+// columns, the wte[id] + wpe[pos] gathers) with one launch per op, 128-bit
+// accesses and warp-shuffle reductions.
+#include "../common.cuh"
+#include "../kernels.h"
+
+namespace gpt2 {
+
+// ---------------------------------------------------------------------------
+// Mask preparation: one block per sequence.
+// ---------------------------------------------------------------------------
+__global__ void seq_info_kernel(const int64_t *__restrict__ mask, int S, int *__restrict__ first_valid,
+                                uint8_t *__restrict__ key_valid) {
+  const int b = blockIdx.x;
+  __shared__ int first;
+  if (threadIdx.x == 0) first = S;
+  __syncthreads();
+  int local = S;
+  for (int k = threadIdx.x; k < S; k += blockDim.x) {
+    const bool v = mask[(int64_t)b * S + k] != 0;
+    key_valid[(int64_t)b * S + k] = v ? 1 : 0;
+    if (v && k < local) local = k;
+  }
+  if (local < S) atomicMin(&first, local);
+  __syncthreads();
+  if (threadIdx.x == 0) first_valid[b] = first;
+}
+
+cudaError_t launch_seq_info(const int64_t *mask, int B, int S, int *first_valid, uint8_t *key_valid,
+                            cudaStream_t st) {
+  seq_info_kernel<<<B, 256, 0, st>>>(mask, S, first_valid, key_valid);
+  return cudaGetLastError();
+}
+
+// ---------------------------------------------------------------------------
+// Embedding.  One warp per token row; d % 4 == 0 (f32) / d % 8 == 0 (bf16).
+// ---------------------------------------------------------------------------
+__global__ void embed_f32_kernel(const int64_t *__restrict__ ids, const float *__restrict__ wte,
+                                 const float *__restrict__ wpe, float *__restrict__ x, int T, int S, int d, int V,
+                                 int *status) {
+  const int warp = (blockIdx.x * blockDim.x + threadIdx.x) >> 5;
+  const int lane = threadIdx.x & 31;
+  if (warp >= T) return;
+  const int64_t id = ids[warp];
+  const bool ok = id >= 0 && id < V;
+  if (!ok && lane == 0) set_status(status, GPT2_ERR_TOKEN_RANGE);
+  const float4 *e = reinterpret_cast<const float4 *>(wte + (ok ? id : 0) * (int64_t)d);
+  const float4 *p = reinterpret_cast<const float4 *>(wpe + (int64_t)(warp % S) * d);
+  float4 *o = reinterpret_cast<float4 *>(x + (int64_t)warp * d);
+  for (int i = lane; i < d / 4; i += 32) {
+    const float4 a = ok ? e[i] : make_float4(0.f, 0.f, 0.f, 0.f), b = p[i];
+    o[i] = make_float4(a.x + b.x, a.y + b.y, a.z + b.z, a.w + b.w);
+  }
+}
+
+__global__ void embed_bf16_kernel(const int64_t *__restrict__ ids, const bf16 *__restrict__ wte,
+                                  const bf16 *__restrict__ wpe, bf16 *__restrict__ x, int T, int S, int d, int V,
+                                  int *status) {
+  const int warp = (blockIdx.x * blockDim.x + threadIdx.x) >> 5;
+  const int lane = threadIdx.x & 31;
+  if (warp >= T) return;
+  const int64_t id = ids[warp];
+  const bool ok = id >= 0 && id < V;
+  if (!ok && lane == 0) set_status(status, GPT2_ERR_TOKEN_RANGE);
+  const uint4 *e = reinterpret_cast<const uint4 *>(wte + (ok ? id : 0) * (int64_t)d);
+  const uint4 *p = reinterpret_cast<const uint4 *>(wpe + (int64_t)(warp % S) * d);
+  uint4 *o = reinterpret_cast<uint4 *>(x + (int64_t)warp * d);
+  for (int i = lane; i < d / 8; i += 32) {
+    uint4 a = ok ? e[i] : make_uint4(0, 0, 0, 0);
+    const uint4 b = p[i];
+    const __nv_bfloat162 *a2 = reinterpret_cast<const __nv_bfloat162 *>(&a);
+    const __nv_bfloat162 *b2 = reinterpret_cast<const __nv_bfloat162 *>(&b);
+    uint4 r;
+    uint32_t *r2 = reinterpret_cast<uint32_t *>(&r);
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      const float2 fa = __bfloat1622float2(a2[j]), fb = __bfloat1622float2(b2[j]);
+      r2[j] = pack_bf16x2(fa.x + fb.x, fa.y + fb.y);
+    }
+    o[i] = r;
+  }
+}
+
+cudaError_t launch_embed_f32(const int64_t *ids, const float *wte, const float *wpe, float *x, int T, int S, int d,
+                             int V, int *status, cudaStream_t st) {
+  if (d % 4) return cudaErrorInvalidValue;
+  const int threads = 256, rows = threads / 32;
+  embed_f32_kernel<<<(T + rows - 1) / rows, threads, 0, st>>>(ids, wte, wpe, x, T, S, d, V, status);
+  return cudaGetLastError();
+}
+
+cudaError_t launch_embed_bf16(const int64_t *ids, const bf16 *wte, const bf16 *wpe, bf16 *x, int T, int S, int d,
+                              int V, int *status, cudaStream_t st) {
+  if (d % 8) return cudaErrorInvalidValue;
+  const int threads = 256, rows = threads / 32;
+  embed_bf16_kernel<<<(T + rows - 1) / rows, threads, 0, st>>>(ids, wte, wpe, x, T, S, d, V, status);
+  return cudaGetLastError();
+}
+
+// ---------------------------------------------------------------------------
+// LayerNorm: one warp per row, the row held in registers (VPT 128-bit vectors
+// per lane), mean then centred variance from the registers, FP32 throughout.
+// ---------------------------------------------------------------------------
+template <int VPT>
+__global__ void layernorm_f32_kernel(const float *__restrict__ x, const float *__restrict__ g,
+                                     const float *__restrict__ b, float *__restrict__ y, int T, int d, float eps) {
+  const int row = (blockIdx.x * blockDim.x + threadIdx.x) >> 5;
+  const int lane = threadIdx.x & 31;
+  if (row >= T) return;
+  const int nv = d / 4;
+  const float4 *xr = reinterpret_cast<const float4 *>(x + (int64_t)row * d);
+  float4 v[VPT];
+  float s = 0.f;
+#pragma unroll
+  for (int i = 0; i < VPT; ++i) {
+    const int c = lane + 32 * i;
+    v[i] = c < nv ? xr[c] : make_float4(0.f, 0.f, 0.f, 0.f);
+    s += (v[i].x + v[i].y) + (v[i].z + v[i].w);
+  }
+  const float mean = warp_sum(s) / d;
+  float q = 0.f;
+#pragma unroll
+  for (int i = 0; i < VPT; ++i) {
+    const int c = lane + 32 * i;
+    if (c < nv) {
+      const float a = v[i].x - mean, bb = v[i].y - mean, cc = v[i].z - mean, dd = v[i].w - mean;
+      q += (a * a + bb * bb) + (cc * cc + dd * dd);
+    }
+  }
+  const float rstd = rsqrtf(warp_sum(q) / d + eps);
+  const float4 *g4 = reinterpret_cast<const float4 *>(g);
+  const float4 *b4 = reinterpret_cast<const float4 *>(b);
+  float4 *yr = reinterpret_cast<float4 *>(y + (int64_t)row * d);
+#pragma unroll
+  for (int i = 0; i < VPT; ++i) {
+    const int c = lane + 32 * i;
+    if (c < nv) {
+      const float4 gg = g4[c], bb = b4[c];
+      yr[c] = make_float4((v[i].x - mean) * rstd * gg.x + bb.x, (v[i].y - mean) * rstd * gg.y + bb.y,
+                          (v[i].z - mean) * rstd * gg.z + bb.z, (v[i].w - mean) * rstd * gg.w + bb.w);
+    }
+  }
+}
+
+template <int VPT>
+__global__ void layernorm_bf16_kernel(const bf16 *__restrict__ x, const float *__restrict__ g,
+                                      const float *__restrict__ b, bf16 *__restrict__ y, int T, int d, float eps) {
+  const int row = (blockIdx.x * blockDim.x + threadIdx.x) >> 5;
+  const int lane = threadIdx.x & 31;
+  if (row >= T) return;
+  const int nv = d / 8;
+  const uint4 *xr = reinterpret_cast<const uint4 *>(x + (int64_t)row * d);
+  float v[VPT][8];
+  float s = 0.f;
+#pragma unroll
+  for (int i = 0; i < VPT; ++i) {
+    const int c = lane + 32 * i;
+    uint4 raw = c < nv ? xr[c] : make_uint4(0, 0, 0, 0);
+    const __nv_bfloat162 *h = reinterpret_cast<const __nv_bfloat162 *>(&raw);
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      const float2 f = __bfloat1622float2(h[j]);
+      v[i][2 * j] = f.x;
+      v[i][2 * j + 1] = f.y;
+      s += f.x + f.y;
+    }
+  }
+  const float mean = warp_sum(s) / d;
+  float q = 0.f;
+#pragma unroll
+  for (int i = 0; i < VPT; ++i) {
+    const int c = lane + 32 * i;
+    if (c < nv) {
+#pragma unroll
+      for (int j = 0; j < 8; ++j) {
+        const float e = v[i][j] - mean;
+        q += e * e;
+      }
+    }
+  }
+  const float rstd = rsqrtf(warp_sum(q) / d + eps);
+  uint4 *yr = reinterpret_cast<uint4 *>(y + (int64_t)row * d);
+#pragma unroll
+  for (int i = 0; i < VPT; ++i) {
+    const int c = lane + 32 * i;
+    if (c < nv) {
+      const float4 g0 = reinterpret_cast<const float4 *>(g)[2 * c], g1 = reinterpret_cast<const float4 *>(g)[2 * c + 1];
+      const float4 b0 = reinterpret_cast<const float4 *>(b)[2 * c], b1 = reinterpret_cast<const float4 *>(b)[2 * c + 1];
+      const float gg[8] = {g0.x, g0.y, g0.z, g0.w, g1.x, g1.y, g1.z, g1.w};
+      const float bb[8] = {b0.x, b0.y, b0.z, b0.w, b1.x, b1.y, b1.z, b1.w};
+      uint4 r;
+      uint32_t *r2 = reinterpret_cast<uint32_t *>(&r);
+#pragma unroll
+      for (int j = 0; j < 4; ++j)
+        r2[j] = pack_bf16x2((v[i][2 * j] - mean) * rstd * gg[2 * j] + bb[2 * j],
+                            (v[i][2 * j + 1] - mean) * rstd * gg[2 * j + 1] + bb[2 * j + 1]);
+      yr[c] = r;
+    }
+  }
+}
+
+#define LN_CASE(V, KERNEL, ...)                                              \
+  case V:                                                                    \
+    KERNEL<V><<<(T + rows - 1) / rows, threads, 0, st>>>(__VA_ARGS__);       \
+    break;
+
+cudaError_t launch_layernorm_f32(const float *x, const float *g, const float *b, float *y, int T, int d, float eps,
+                                 cudaStream_t st) {
+  if (d % 4 || d > 128 * 16) return cudaErrorInvalidValue;
+  const int threads = 256, rows = threads / 32;
+  switch ((d + 127) / 128) {
+    LN_CASE(1, layernorm_f32_kernel, x, g, b, y, T, d, eps)
+    LN_CASE(2, layernorm_f32_kernel, x, g, b, y, T, d, eps)
+    LN_CASE(3, layernorm_f32_kernel, x, g, b, y, T, d, eps)
+    LN_CASE(4, layernorm_f32_kernel, x, g, b, y, T, d, eps)
+    LN_CASE(5, layernorm_f32_kernel, x, g, b, y, T, d, eps)
+    LN_CASE(6, layernorm_f32_kernel, x, g, b, y, T, d, eps)
+    LN_CASE(7, layernorm_f32_kernel, x, g, b, y, T, d, eps)
+    LN_CASE(8, layernorm_f32_kernel, x, g, b, y, T, d, eps)
+    LN_CASE(10, layernorm_f32_kernel, x, g, b, y, T, d, eps)
+    LN_CASE(13, layernorm_f32_kernel, x, g, b, y, T, d, eps)
+    LN_CASE(16, layernorm_f32_kernel, x, g, b, y, T, d, eps)
+    default:
+      if (d <= 128 * 10) layernorm_f32_kernel<10><<<(T + rows - 1) / rows, threads, 0, st>>>(x, g, b, y, T, d, eps);
+      else if (d <= 128 * 13) layernorm_f32_kernel<13><<<(T + rows - 1) / rows, threads, 0, st>>>(x, g, b, y, T, d, eps);
+      else layernorm_f32_kernel<16><<<(T + rows - 1) / rows, threads, 0, st>>>(x, g, b, y, T, d, eps);
+  }
+  return cudaGetLastError();
+}
+
+cudaError_t launch_layernorm_bf16(const bf16 *x, const float *g, const float *b, bf16 *y, int T, int d, float eps,
+                                  cudaStream_t st) {
+  if (d % 8 || d > 256 * 8) return cudaErrorInvalidValue;
+  const int threads = 256, rows = threads / 32;
+  switch ((d + 255) / 256) {
+    LN_CASE(1, layernorm_bf16_kernel, x, g, b, y, T, d, eps)
+    LN_CASE(2, layernorm_bf16_kernel, x, g, b, y, T, d, eps)
+    LN_CASE(3, layernorm_bf16_kernel, x, g, b, y, T, d, eps)
+    LN_CASE(4, layernorm_bf16_kernel, x, g, b, y, T, d, eps)
+    LN_CASE(5, layernorm_bf16_kernel, x, g, b, y, T, d, eps)
+    LN_CASE(6, layernorm_bf16_kernel, x, g, b, y, T, d, eps)
+    LN_CASE(7, layernorm_bf16_kernel, x, g, b, y, T, d, eps)
+    LN_CASE(8, layernorm_bf16_kernel, x, g, b, y, T, d, eps)
+    default:
+      return cudaErrorInvalidValue;
+  }
+  return cudaGetLastError();
+}
+
+// ---------------------------------------------------------------------------
+// Weight packing (run once per weight load).
+// ---------------------------------------------------------------------------
+__global__ void pack_bf16_kernel(const float *__restrict__ src, bf16 *__restrict__ dst, int rows, int cols,
+                                 int transpose) {
+  __shared__ float tile[32][33];
+  const int bx = blockIdx.x * 32, by = blockIdx.y * 32;
+  if (!transpose) {
+    for (int i = threadIdx.y; i < 32; i += blockDim.y) {
+      const int r = by + i, c = bx + threadIdx.x;
+      if (r < rows && c < cols) dst[(int64_t)r * cols + c] = __float2bfloat16_rn(src[(int64_t)r * cols + c]);
+    }
+    return;
+  }
+  // dst[cols, rows] = src[rows, cols]^T
+  for (int i = threadIdx.y; i < 32; i += blockDim.y) {
+    const int r = by + i, c = bx + threadIdx.x;
+    tile[i][threadIdx.x] = (r < rows && c < cols) ? src[(int64_t)r * cols + c] : 0.f;
+  }
+  __syncthreads();
+  for (int i = threadIdx.y; i < 32; i += blockDim.y) {
+    const int c = bx + i, r = by + threadIdx.x;
+    if (c < cols && r < rows) dst[(int64_t)c * rows + r] = __float2bfloat16_rn(tile[threadIdx.x][i]);
+  }
+}
+
+cudaError_t launch_pack_bf16(const float *src, bf16 *dst, int rows, int cols, int transpose, cudaStream_t st) {
+  dim3 grid((cols + 31) / 32, (rows + 31) / 32), block(32, 8);
+  pack_bf16_kernel<<<grid, block, 0, st>>>(src, dst, rows, cols, transpose);
+  return cudaGetLastError();
+}
+
+}  // namespace gpt2

@@ -1,0 +1,347 @@
+// gemm_tc.cu -- BF16 GEMM on the 5th-generation tensor cores (tcgen05,
+// accumulators in TMEM, operands staged by TMA) with fused epilogues.
+//
+// Replaces the reference's linalg.matmul launches (QKV, attention out-proj,
+// MLP fc and proj, the tied lm_head; README.md:11) and the bias / GELU /
+// residual generics fused around them (lib/ElementwiseFusion.cpp:43-109), in
+// the BF16 configuration.
+//
+//   C[M, N] = epilogue(A[M, K] @ B[N, K]^T)
+//   A: activations, bf16, row-major (K-major); B: weights packed [N, K]
+//   (K-major) at load time; f32 accumulation in TMEM; bf16 or f32 output.
+//
+// Structure (one CTA per SM, persistent, 192 threads):
+//   warp 0      TMA producer: 128 x 64 A and BN x 64 B tiles, 128-byte
+//               swizzle, into a STAGES-deep shared-memory ring (mbarrier
+//               full/empty pairs, transaction-count completion);
+//   warp 1      TMEM allocator and MMA issuer: one thread issues
+//               tcgen05.mma.cta_group::1.kind::f16 (M=128, N=BN, K=16) four
+//               times per stage and tcgen05.commit's the stage back to the
+//               producer; accumulators are double-buffered in TMEM (2 x BN
+//               columns) so the epilogue of tile i overlaps the MMAs of i+1;
+//   warps 2..5  epilogue: tcgen05.ld 32 rows x 32 columns per warp, bias /
+//               gelu_new / residual in registers, 16-byte global stores.
+// Tiles are walked in groups of 16 M-blocks so that the A rows and B columns
+// live in L2 while they are reused.  No cluster multicast anywhere.
+//
+// Every mbarrier wait is bounded (common.cuh); on a timeout the kernel
+// records GPT2_ERR_WAIT_TIMEOUT, stops issuing, drains what it issued and
+// frees its TMEM before returning.
+#include <atomic>
+
+#include "../common.cuh"
+#include "../kernels.h"
+
+namespace gpt2 {
+
+namespace {
+constexpr int BM = 128, BK = 64, NTHREADS = 192, GROUP_M = 16;
+
+template <int BN>
+struct TcCfg {
+  static constexpr int STAGES = BN == 256 ? 4 : 6;
+  static constexpr int A_BYTES = BM * BK * 2;
+  static constexpr int B_BYTES = BN * BK * 2;
+  static constexpr int STAGE_BYTES = A_BYTES + B_BYTES;
+  static constexpr int TMEM_COLS = 2 * BN;
+  static constexpr int SMEM_BYTES = 1024 /*align slack*/ + STAGES * STAGE_BYTES + 256;
+};
+
+__device__ __forceinline__ void tile_coords(int t, int num_m, int num_n, int &mb, int &nb) {
+  const int per_group = GROUP_M * num_n;
+  const int group = t / per_group;
+  const int first_m = group * GROUP_M;
+  const int gsize = min(num_m - first_m, GROUP_M);
+  const int in = t - group * per_group;
+  mb = first_m + in % gsize;
+  nb = in / gsize;
+}
+
+template <int BN, int EPI, int OUT_F32>
+__global__ void __launch_bounds__(NTHREADS, 1)
+    gemm_tc_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constant__ CUtensorMap map_b, void *C,
+                   int ldc, int M, int N, int K, const float *__restrict__ bias, const bf16 *resid, int *status) {
+  using Cfg = TcCfg<BN>;
+  constexpr int STAGES = Cfg::STAGES;
+  extern __shared__ unsigned char smem_raw[];
+  unsigned char *smem = reinterpret_cast<unsigned char *>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  unsigned char *sa = smem;
+  unsigned char *sb = smem + STAGES * Cfg::A_BYTES;
+  uint64_t *bars = reinterpret_cast<uint64_t *>(smem + STAGES * Cfg::STAGE_BYTES);
+  uint64_t *full = bars, *empty = bars + STAGES, *tfull = bars + 2 * STAGES, *tempty = bars + 2 * STAGES + 2;
+  uint64_t *drain = bars + 2 * STAGES + 4;
+  uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(bars + 2 * STAGES + 5);
+  volatile int *abort_flag = reinterpret_cast<volatile int *>(tmem_slot + 1);
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int num_m = (M + BM - 1) / BM, num_n = (N + BN - 1) / BN, num_k = (K + BK - 1) / BK;
+  const int total = num_m * num_n;
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < STAGES; ++s) {
+      mbar_init(&full[s], 1);
+      mbar_init(&empty[s], 1);
+    }
+    for (int a = 0; a < 2; ++a) {
+      mbar_init(&tfull[a], 1);
+      mbar_init(&tempty[a], 128);
+    }
+    mbar_init(drain, 1);
+    *abort_flag = 0;
+    fence_mbar_init();
+  }
+  if (warp == 1) {
+    tmem_alloc(tmem_slot, Cfg::TMEM_COLS);
+    tc_fence_before();
+  }
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem_base = *tmem_slot;
+
+  if (warp == 0 && lane == 0) {
+    // ---------------- TMA producer ----------------
+    prefetch_tmap(&map_a);
+    prefetch_tmap(&map_b);
+    uint32_t issued[STAGES];
+#pragma unroll
+    for (int s = 0; s < STAGES; ++s) issued[s] = 0;
+    int it = 0;
+    bool ok = true;
+    for (int t = blockIdx.x; t < total && ok; t += gridDim.x) {
+      int mb, nb;
+      tile_coords(t, num_m, num_n, mb, nb);
+      for (int kb = 0; kb < num_k; ++kb, ++it) {
+        const int s = it % STAGES;
+        const uint32_t ph = (it / STAGES) & 1;
+        if (!mbar_wait(&empty[s], ph ^ 1, abort_flag)) { ok = false; break; }
+        mbar_arrive_expect_tx(&full[s], Cfg::STAGE_BYTES);
+        tma_load_2d(sa + s * Cfg::A_BYTES, &map_a, &full[s], kb * BK, mb * BM);
+        tma_load_2d(sb + s * Cfg::B_BYTES, &map_b, &full[s], kb * BK, nb * BN);
+        ++issued[s];
+      }
+    }
+    if (!ok) {
+      set_status(status, GPT2_ERR_WAIT_TIMEOUT);
+      *abort_flag = 1;
+      // Let the copies already in flight land before the CTA's shared memory goes away.
+      for (int s = 0; s < STAGES; ++s)
+        if (issued[s]) mbar_wait(&full[s], (issued[s] - 1) & 1, nullptr);
+    }
+  } else if (warp == 1 && lane == 0) {
+    // ---------------- MMA issuer ----------------
+    constexpr uint32_t idesc = idesc_bf16_f32(BM, BN);
+    int it = 0, local = 0;
+    bool ok = true;
+    for (int t = blockIdx.x; t < total && ok; t += gridDim.x, ++local) {
+      const int acc = local & 1;
+      const uint32_t aph = (local >> 1) & 1;
+      if (!mbar_wait(&tempty[acc], aph ^ 1, abort_flag)) { ok = false; break; }
+      tc_fence_after();
+      const uint32_t d_tmem = tmem_base + acc * BN;
+      for (int kb = 0; kb < num_k; ++kb, ++it) {
+        const int s = it % STAGES;
+        const uint32_t ph = (it / STAGES) & 1;
+        if (!mbar_wait(&full[s], ph, abort_flag)) { ok = false; break; }
+        tc_fence_after();
+        const uint32_t a0 = smem_u32(sa + s * Cfg::A_BYTES), b0 = smem_u32(sb + s * Cfg::B_BYTES);
+#pragma unroll
+        for (int k = 0; k < BK / 16; ++k)
+          tc_mma_f16(d_tmem, sdesc_kmajor_sw128(a0 + k * 32), sdesc_kmajor_sw128(b0 + k * 32), idesc,
+                     (kb | k) != 0);
+        tc_commit(&empty[s]);
+      }
+      if (!ok) break;
+      tc_commit(&tfull[acc]);
+    }
+    if (!ok) {
+      set_status(status, GPT2_ERR_WAIT_TIMEOUT);
+      *abort_flag = 1;
+    }
+    // Drain: every MMA this thread issued has completed once this arrives.
+    tc_commit(drain);
+    mbar_wait(drain, 0, nullptr);
+  } else if (warp >= 2) {
+    // ---------------- epilogue ----------------
+    const int q = warp & 3;  // TMEM lane quarter this warp may access
+    const int row_in_tile = q * 32 + lane;
+    int local = 0;
+    for (int t = blockIdx.x; t < total; t += gridDim.x, ++local) {
+      int mb, nb;
+      tile_coords(t, num_m, num_n, mb, nb);
+      const int acc = local & 1;
+      const uint32_t aph = (local >> 1) & 1;
+      if (!mbar_wait(&tfull[acc], aph, abort_flag)) {
+        set_status(status, GPT2_ERR_WAIT_TIMEOUT);
+        *abort_flag = 1;
+        break;
+      }
+      tc_fence_after();
+      const int row = mb * BM + row_in_tile;
+      const bool row_ok = row < M;
+#pragma unroll 1
+      for (int c = 0; c < BN / 32; ++c) {
+        uint32_t r[32];
+        tmem_ld_32x32b_x32(tmem_base + (static_cast<uint32_t>(q * 32) << 16) + acc * BN + c * 32, r);
+        tc_wait_ld();
+        if (c == BN / 32 - 1) {
+          tc_fence_before();
+          mbar_arrive(&tempty[acc]);
+        }
+        const int col0 = nb * BN + c * 32;
+        float v[32];
+        float bias_lane = 0.f;
+        if (EPI != EPI_NONE) bias_lane = (col0 + lane < N) ? bias[col0 + lane] : 0.f;
+#pragma unroll
+        for (int j = 0; j < 32; ++j) {
+          float x = __uint_as_float(r[j]);
+          if (EPI != EPI_NONE) x += __shfl_sync(0xffffffffu, bias_lane, j);
+          if (EPI == EPI_BIAS_GELU) x = gelu_new_fast(x);
+          v[j] = x;
+        }
+        if (!row_ok) continue;
+        const bool full_chunk = col0 + 32 <= N;
+        const int64_t off = (int64_t)row * ldc + col0;
+        if (EPI == EPI_BIAS_RESID) {
+          if (full_chunk) {
+            const uint4 *rp = reinterpret_cast<const uint4 *>(resid + off);
+#pragma unroll
+            for (int g = 0; g < 4; ++g) {
+              uint4 raw = rp[g];
+              const __nv_bfloat162 *h = reinterpret_cast<const __nv_bfloat162 *>(&raw);
+#pragma unroll
+              for (int j = 0; j < 4; ++j) {
+                const float2 f = __bfloat1622float2(h[j]);
+                v[g * 8 + 2 * j] += f.x;
+                v[g * 8 + 2 * j + 1] += f.y;
+              }
+            }
+          } else {
+            for (int j = 0; j < 32; ++j)
+              if (col0 + j < N) v[j] += __bfloat162float(resid[off + j]);
+          }
+        }
+        if (OUT_F32) {
+          float *cp = reinterpret_cast<float *>(C) + off;
+          if (full_chunk && (ldc & 3) == 0) {
+#pragma unroll
+            for (int g = 0; g < 8; ++g)
+              reinterpret_cast<float4 *>(cp)[g] = make_float4(v[4 * g], v[4 * g + 1], v[4 * g + 2], v[4 * g + 3]);
+          } else {
+            for (int j = 0; j < 32; ++j)
+              if (col0 + j < N) cp[j] = v[j];
+          }
+        } else {
+          bf16 *cp = reinterpret_cast<bf16 *>(C) + off;
+          if (full_chunk) {
+#pragma unroll
+            for (int g = 0; g < 4; ++g) {
+              uint4 w;
+              w.x = pack_bf16x2(v[8 * g + 0], v[8 * g + 1]);
+              w.y = pack_bf16x2(v[8 * g + 2], v[8 * g + 3]);
+              w.z = pack_bf16x2(v[8 * g + 4], v[8 * g + 5]);
+              w.w = pack_bf16x2(v[8 * g + 6], v[8 * g + 7]);
+              reinterpret_cast<uint4 *>(cp)[g] = w;
+            }
+          } else {
+            for (int j = 0; j < 32; ++j)
+              if (col0 + j < N) cp[j] = __float2bfloat16_rn(v[j]);
+          }
+        }
+      }
+    }
+  }
+
+  __syncthreads();
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc(tmem_base, Cfg::TMEM_COLS);
+  }
+}
+
+typedef CUresult (*EncodeTiledFn)(CUtensorMap *, CUtensorMapDataType, cuuint32_t, void *, const cuuint64_t *,
+                                  const cuuint64_t *, const cuuint32_t *, const cuuint32_t *, CUtensorMapInterleave,
+                                  CUtensorMapSwizzle, CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+
+EncodeTiledFn encode_fn() {
+  static std::atomic<EncodeTiledFn> fn{nullptr};
+  EncodeTiledFn f = fn.load();
+  if (f) return f;
+  void *p = nullptr;
+  cudaDriverEntryPointQueryResult q;
+  if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) != cudaSuccess ||
+      q != cudaDriverEntryPointSuccess || !p)
+    return nullptr;
+  f = reinterpret_cast<EncodeTiledFn>(p);
+  fn.store(f);
+  return f;
+}
+
+// 2-D bf16 tensor [rows, cols] row-major, box [box_rows, 64 cols], 128-byte swizzle.
+int make_map_2d(CUtensorMap *map, const void *base, int64_t rows, int64_t cols, int box_rows) {
+  EncodeTiledFn f = encode_fn();
+  if (!f) return -1;
+  if ((reinterpret_cast<uintptr_t>(base) & 15) || (cols * 2) % 16) return -2;
+  const cuuint64_t dims[2] = {static_cast<cuuint64_t>(cols), static_cast<cuuint64_t>(rows)};
+  const cuuint64_t strides[1] = {static_cast<cuuint64_t>(cols * 2)};
+  const cuuint32_t box[2] = {static_cast<cuuint32_t>(BK), static_cast<cuuint32_t>(box_rows)};
+  const cuuint32_t estr[2] = {1, 1};
+  CUresult r = f(map, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, const_cast<void *>(base), dims, strides, box, estr,
+                 CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                 CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  return r == CUDA_SUCCESS ? 0 : -3;
+}
+
+template <int BN, int EPI, int OUT_F32>
+cudaError_t launch_variant(const TcGemmPlan &p, void *C, int ldc, const float *bias, const bf16 *resid, int *status,
+                           int num_sms, cudaStream_t st) {
+  using Cfg = TcCfg<BN>;
+  static std::atomic<uint64_t> attr_done{0};
+  cudaError_t e = set_smem_once(gemm_tc_kernel<BN, EPI, OUT_F32>, Cfg::SMEM_BYTES, attr_done);
+  if (e != cudaSuccess) return e;
+  const int tiles = ((p.M + BM - 1) / BM) * ((p.N + BN - 1) / BN);
+  const int grid = tiles < num_sms ? tiles : num_sms;
+  gemm_tc_kernel<BN, EPI, OUT_F32><<<grid, NTHREADS, Cfg::SMEM_BYTES, st>>>(p.map_a, p.map_b, C, ldc, p.M, p.N, p.K,
+                                                                              bias, resid, status);
+  return cudaGetLastError();
+}
+
+template <int BN>
+cudaError_t dispatch_epi(const TcGemmPlan &p, void *C, int ldc, int out_f32, const float *bias, const bf16 *resid,
+                         int epi, int *status, int num_sms, cudaStream_t st) {
+  if (out_f32) {
+    if (epi == EPI_NONE) return launch_variant<BN, EPI_NONE, 1>(p, C, ldc, bias, resid, status, num_sms, st);
+    if (epi == EPI_BIAS) return launch_variant<BN, EPI_BIAS, 1>(p, C, ldc, bias, resid, status, num_sms, st);
+    return cudaErrorInvalidValue;
+  }
+  switch (epi) {
+    case EPI_NONE: return launch_variant<BN, EPI_NONE, 0>(p, C, ldc, bias, resid, status, num_sms, st);
+    case EPI_BIAS: return launch_variant<BN, EPI_BIAS, 0>(p, C, ldc, bias, resid, status, num_sms, st);
+    case EPI_BIAS_GELU: return launch_variant<BN, EPI_BIAS_GELU, 0>(p, C, ldc, bias, resid, status, num_sms, st);
+    case EPI_BIAS_RESID: return launch_variant<BN, EPI_BIAS_RESID, 0>(p, C, ldc, bias, resid, status, num_sms, st);
+  }
+  return cudaErrorInvalidValue;
+}
+}  // namespace
+
+int tc_gemm_plan(TcGemmPlan *plan, const bf16 *A, const bf16 *B, int M, int N, int K, int bn) {
+  if (!plan || M <= 0 || N <= 0 || K <= 0 || K % 8 || (bn != 128 && bn != 256)) return -10;
+  plan->M = M;
+  plan->N = N;
+  plan->K = K;
+  plan->bn = bn;
+  int r = make_map_2d(&plan->map_a, A, M, K, BM);
+  if (r) return r;
+  return make_map_2d(&plan->map_b, B, N, K, bn);
+}
+
+cudaError_t launch_gemm_tc(const TcGemmPlan &plan, void *C, int ldc, int out_f32, const float *bias,
+                           const bf16 *resid, int epi, int *status, int num_sms, cudaStream_t st) {
+  if (ldc < plan.N || num_sms <= 0) return cudaErrorInvalidValue;
+  if (!out_f32 && ldc % 8) return cudaErrorInvalidValue;
+  if (epi != EPI_NONE && !bias) return cudaErrorInvalidValue;
+  if (epi == EPI_BIAS_RESID && !resid) return cudaErrorInvalidValue;
+  if (plan.bn == 256) return dispatch_epi<256>(plan, C, ldc, out_f32, bias, resid, epi, status, num_sms, st);
+  return dispatch_epi<128>(plan, C, ldc, out_f32, bias, resid, epi, status, num_sms, st);
+}
+
+}  // namespace gpt2

@@ -1,0 +1,396 @@
+// context.cu -- model context, weight upload and packing, workspace and the
+// forward schedule of the GPT-2 prefill.
+//
+// The schedule is the layer structure of HF GPT-2 as exported by the
+// reference (src/gpt/lower_gpt_model.py:20-50, full logits, use_cache=False):
+//   x = wte[ids] + wpe[pos]
+//   per layer: a = ln_1(x); qkv = a @ W_attn + b; o = attention(qkv, mask);
+//              x = x + (o @ W_proj + b); a = ln_2(x);
+//              u = gelu_new(a @ W_fc + b); x = x + (u @ W_mproj + b)
+//   logits = ln_f(x) @ wte^T
+// as 3 + 7 L launches (+ 1 + L when a mask is given) instead of
+// the reference's ~797 (README.md:96).
+#include <stdarg.h>
+#include <stdio.h>
+#include <string.h>
+
+#include <algorithm>
+
+#include "runtime.h"
+
+namespace gpt2 {
+
+namespace {
+thread_local std::string g_err;
+Context *g_ctx = nullptr;
+
+int cuda_fail(cudaError_t e, const char *what) {
+  set_error("%s: %s", what, cudaGetErrorString(e));
+  return -2;
+}
+#define CK(call)                                   \
+  do {                                             \
+    cudaError_t e_ = (call);                       \
+    if (e_ != cudaSuccess) return cuda_fail(e_, #call); \
+  } while (0)
+
+// A kernel launch of kind K on stream `st`, bracketed by profiler events when
+// profiling is on.
+#define CKP(K, call)                                                          \
+  do {                                                                        \
+    cudaEvent_t pa_ = nullptr, pb_ = nullptr;                                 \
+    if (c.prof.on) {                                                          \
+      pa_ = prof_event(c.prof);                                               \
+      pb_ = prof_event(c.prof);                                               \
+      if (pa_ && pb_) cudaEventRecord(pa_, st);                               \
+    }                                                                         \
+    cudaError_t e_ = (call);                                                  \
+    if (e_ != cudaSuccess) return cuda_fail(e_, #call);                       \
+    if (pa_ && pb_) {                                                         \
+      cudaEventRecord(pb_, st);                                               \
+      c.prof.kinds.push_back(K);                                              \
+    }                                                                         \
+  } while (0)
+
+void free_ws(Workspace &w) {
+  void *ptrs[] = {w.x, w.a, w.qkv, w.o, w.u, w.first_valid, w.key_valid, w.ids, w.mask};
+  for (void *p : ptrs)
+    if (p) cudaFree(p);
+  if (w.logits) cudaFree(w.logits);
+  w = Workspace();
+}
+}  // namespace
+
+void set_error(const char *fmt, ...) {
+  char buf[1024];
+  va_list ap;
+  va_start(ap, fmt);
+  vsnprintf(buf, sizeof buf, fmt, ap);
+  va_end(ap);
+  g_err = buf;
+}
+
+const char *last_error_text() { return g_err.c_str(); }
+void clear_error() { g_err.clear(); }
+
+std::vector<TensorSpec> blob_specs(const ModelDims &m) {
+  std::vector<TensorSpec> s;
+  int64_t off = 0;
+  auto add = [&](int64_t n, TensorSpec::Kind k) {
+    s.push_back({off, n, k});
+    off += n;
+  };
+  const int64_t d = m.n_embd, ff = m.n_inner;
+  add((int64_t)m.vocab * d, TensorSpec::kMatrix);
+  add((int64_t)m.n_pos * d, TensorSpec::kMatrix);
+  for (int l = 0; l < m.n_layer; ++l) {
+    add(d, TensorSpec::kGain);
+    add(d, TensorSpec::kBias);
+    add(d * 3 * d, TensorSpec::kMatrix);
+    add(3 * d, TensorSpec::kBias);
+    add(d * d, TensorSpec::kMatrix);
+    add(d, TensorSpec::kBias);
+    add(d, TensorSpec::kGain);
+    add(d, TensorSpec::kBias);
+    add(d * ff, TensorSpec::kMatrix);
+    add(ff, TensorSpec::kBias);
+    add(ff * d, TensorSpec::kMatrix);
+    add(d, TensorSpec::kBias);
+  }
+  add(d, TensorSpec::kGain);
+  add(d, TensorSpec::kBias);
+  return s;
+}
+
+int64_t blob_floats(const ModelDims &m) {
+  const auto s = blob_specs(m);
+  return s.back().offset + s.back().numel;
+}
+
+Context *context() { return g_ctx; }
+
+void destroy_context() {
+  if (!g_ctx) return;
+  Context *c = g_ctx;
+  g_ctx = nullptr;
+  int prev = 0;
+  cudaGetDevice(&prev);
+  cudaSetDevice(c->device);
+  cudaDeviceSynchronize();
+  free_ws(c->ws);
+  if (c->d_blob) cudaFree(c->d_blob);
+  if (c->wte_h) cudaFree(c->wte_h);
+  if (c->wpe_h) cudaFree(c->wpe_h);
+  for (auto &l : c->layers) {
+    bf16 *p[] = {l.qkv_wt, l.proj_wt, l.fc_wt, l.mproj_wt};
+    for (bf16 *q : p)
+      if (q) cudaFree(q);
+  }
+  if (c->d_status) cudaFree(c->d_status);
+  if (c->stream) cudaStreamDestroy(c->stream);
+  delete c;
+  cudaSetDevice(prev);
+}
+
+int create_context(const ModelDims &m, int dtype, int device) {
+  if (m.n_layer < 1 || m.n_embd < 64 || m.n_embd % 64 || m.n_head < 1 || m.n_embd / m.n_head != 64 ||
+      m.n_embd % m.n_head || m.n_inner < 64 || m.n_inner % 64 || m.vocab < 1 || m.n_pos < 1 || !(m.eps > 0.f)) {
+    set_error("unsupported GPT-2 configuration (need n_embd %% 64 == 0, head dim 64, n_inner %% 64 == 0)");
+    return -1;
+  }
+  if (dtype != 0 && dtype != 1) {
+    set_error("unsupported dtype %d", dtype);
+    return -1;
+  }
+  destroy_context();
+  if (device < 0) CK(cudaGetDevice(&device));
+  CK(cudaSetDevice(device));
+  Context *c = new Context();
+  c->dims = m;
+  c->dtype = dtype;
+  c->device = device;
+  cudaError_t e = cudaDeviceGetAttribute(&c->num_sms, cudaDevAttrMultiProcessorCount, device);
+  if (e == cudaSuccess) e = cudaStreamCreateWithFlags(&c->stream, cudaStreamNonBlocking);
+  if (e == cudaSuccess) e = cudaMalloc(&c->d_status, sizeof(int));
+  if (e == cudaSuccess) e = cudaMemset(c->d_status, 0, sizeof(int));
+  if (e != cudaSuccess) {
+    g_ctx = c;
+    destroy_context();
+    return cuda_fail(e, "context setup");
+  }
+  c->specs = blob_specs(m);
+  g_ctx = c;
+  return 0;
+}
+
+int load_blob(Context &c, const float *host_blob) {
+  CK(cudaSetDevice(c.device));
+  const ModelDims &m = c.dims;
+  const int64_t n = blob_floats(m);
+  if (!c.d_blob) CK(cudaMalloc(&c.d_blob, sizeof(float) * n));
+  CK(cudaMemcpy(c.d_blob, host_blob, sizeof(float) * n, cudaMemcpyHostToDevice));
+  const auto &s = c.specs;
+  auto at = [&](size_t i) -> float * { return c.d_blob + s[i].offset; };
+  c.wte = at(0);
+  c.wpe = at(1);
+  c.lnf_g = at(2 + PER_LAYER * m.n_layer);
+  c.lnf_b = at(3 + PER_LAYER * m.n_layer);
+  c.layers.resize(m.n_layer);
+  const int d = m.n_embd, ff = m.n_inner;
+  for (int l = 0; l < m.n_layer; ++l) {
+    LayerWeights &w = c.layers[l];
+    const size_t b = 2 + PER_LAYER * l;
+    w.ln1_g = at(b + LN1_G);
+    w.ln1_b = at(b + LN1_B);
+    w.qkv_w = at(b + QKV_W);
+    w.qkv_b = at(b + QKV_B);
+    w.proj_w = at(b + PROJ_W);
+    w.proj_b = at(b + PROJ_B);
+    w.ln2_g = at(b + LN2_G);
+    w.ln2_b = at(b + LN2_B);
+    w.fc_w = at(b + FC_W);
+    w.fc_b = at(b + FC_B);
+    w.mproj_w = at(b + MPROJ_W);
+    w.mproj_b = at(b + MPROJ_B);
+  }
+  if (c.dtype == 1) {
+    // BF16 copies: wte / wpe as stored ([V, d] is already the K-major B of the
+    // lm_head), Conv1D weights transposed to [out, in] (K-major B operands).
+    if (!c.wte_h) CK(cudaMalloc(&c.wte_h, sizeof(bf16) * (size_t)m.vocab * d));
+    if (!c.wpe_h) CK(cudaMalloc(&c.wpe_h, sizeof(bf16) * (size_t)m.n_pos * d));
+    CK(launch_pack_bf16(c.wte, c.wte_h, m.vocab, d, 0, c.stream));
+    CK(launch_pack_bf16(c.wpe, c.wpe_h, m.n_pos, d, 0, c.stream));
+    for (int l = 0; l < m.n_layer; ++l) {
+      LayerWeights &w = c.layers[l];
+      if (!w.qkv_wt) CK(cudaMalloc(&w.qkv_wt, sizeof(bf16) * (size_t)d * 3 * d));
+      if (!w.proj_wt) CK(cudaMalloc(&w.proj_wt, sizeof(bf16) * (size_t)d * d));
+      if (!w.fc_wt) CK(cudaMalloc(&w.fc_wt, sizeof(bf16) * (size_t)d * ff));
+      if (!w.mproj_wt) CK(cudaMalloc(&w.mproj_wt, sizeof(bf16) * (size_t)ff * d));
+      CK(launch_pack_bf16(w.qkv_w, w.qkv_wt, d, 3 * d, 1, c.stream));
+      CK(launch_pack_bf16(w.proj_w, w.proj_wt, d, d, 1, c.stream));
+      CK(launch_pack_bf16(w.fc_w, w.fc_wt, d, ff, 1, c.stream));
+      CK(launch_pack_bf16(w.mproj_w, w.mproj_wt, ff, d, 1, c.stream));
+    }
+    CK(cudaStreamSynchronize(c.stream));
+  }
+  c.loaded = true;
+  c.plans_T = -1;  // weights moved: rebuild TMA descriptors
+  return 0;
+}
+
+int ensure_workspace(Context &c, int B, int S) {
+  const int64_t T = (int64_t)B * S;
+  Workspace &w = c.ws;
+  if (T <= w.T && B <= w.B) return 0;
+  const int64_t Tn = std::max(T, w.T);
+  const int Bn = std::max(B, w.B);
+  CK(cudaDeviceSynchronize());  // earlier forwards may still read the buffers on any stream
+  Workspace keep_logits;
+  keep_logits.logits = w.logits;
+  keep_logits.logits_T = w.logits_T;
+  w.logits = nullptr;
+  free_ws(w);
+  w.logits = keep_logits.logits;
+  w.logits_T = keep_logits.logits_T;
+  const size_t es = c.dtype == 1 ? 2 : 4;
+  const int64_t d = c.dims.n_embd, ff = c.dims.n_inner;
+  CK(cudaMalloc(&w.x, es * Tn * d));
+  CK(cudaMalloc(&w.a, es * Tn * d));
+  CK(cudaMalloc(&w.qkv, es * Tn * 3 * d));
+  CK(cudaMalloc(&w.o, es * Tn * d));
+  CK(cudaMalloc(&w.u, es * Tn * ff));
+  CK(cudaMalloc(&w.first_valid, sizeof(int) * Bn));
+  CK(cudaMalloc(&w.key_valid, Tn));
+  CK(cudaMalloc(&w.ids, sizeof(int64_t) * Tn));
+  CK(cudaMalloc(&w.mask, sizeof(int64_t) * Tn));
+  w.T = Tn;
+  w.B = Bn;
+  c.plans_T = -1;
+  return 0;
+}
+
+namespace {
+// TMA descriptors of every BF16 GEMM for M = T tokens over the current
+// workspace: per layer qkv, proj, fc, mproj, then the lm_head.
+int ensure_plans(Context &c, int64_t T) {
+  if (c.plans_T == T) return 0;
+  const ModelDims &m = c.dims;
+  const int d = m.n_embd, ff = m.n_inner;
+  c.plans.resize(4 * m.n_layer + 1);
+  const bf16 *a = static_cast<const bf16 *>(c.ws.a), *o = static_cast<const bf16 *>(c.ws.o),
+             *u = static_cast<const bf16 *>(c.ws.u);
+  auto pick_bn = [&](int N) {
+    const int64_t tiles256 = ((T + 127) / 128) * ((N + 255) / 256);
+    return tiles256 >= 2 * c.num_sms ? 256 : 128;
+  };
+  for (int l = 0; l < m.n_layer; ++l) {
+    const LayerWeights &w = c.layers[l];
+    int r = tc_gemm_plan(&c.plans[4 * l + 0], a, w.qkv_wt, (int)T, 3 * d, d, pick_bn(3 * d));
+    if (!r) r = tc_gemm_plan(&c.plans[4 * l + 1], o, w.proj_wt, (int)T, d, d, pick_bn(d));
+    if (!r) r = tc_gemm_plan(&c.plans[4 * l + 2], a, w.fc_wt, (int)T, ff, d, pick_bn(ff));
+    if (!r) r = tc_gemm_plan(&c.plans[4 * l + 3], u, w.mproj_wt, (int)T, d, ff, pick_bn(d));
+    if (r) {
+      set_error("TMA descriptor creation failed (%d)", r);
+      return -2;
+    }
+  }
+  if (tc_gemm_plan(&c.plans[4 * m.n_layer], a, c.wte_h, (int)T, m.vocab, d, pick_bn(m.vocab))) {
+    set_error("TMA descriptor creation failed (lm_head)");
+    return -2;
+  }
+  c.plans_T = T;
+  return 0;
+}
+}  // namespace
+
+namespace {
+cudaEvent_t prof_event(Profiler &p) {
+  if (p.used == p.pool.size()) {
+    cudaEvent_t e;
+    if (cudaEventCreate(&e) != cudaSuccess) return nullptr;
+    p.pool.push_back(e);
+  }
+  return p.pool[p.used++];
+}
+}  // namespace
+
+int profile_begin(Context &c) {
+  c.prof.on = true;
+  c.prof.used = 0;
+  c.prof.kinds.clear();
+  return 0;
+}
+
+int profile_end(Context &c, double *ms, int64_t *count, int n) {
+  Profiler &p = c.prof;
+  p.on = false;
+  for (int k = 0; k < n; ++k) {
+    ms[k] = 0.0;
+    count[k] = 0;
+  }
+  for (size_t i = 0; i < p.kinds.size(); ++i) {
+    cudaEvent_t a = p.pool[2 * i], b = p.pool[2 * i + 1];
+    CK(cudaEventSynchronize(b));
+    float t = 0.f;
+    CK(cudaEventElapsedTime(&t, a, b));
+    const int k = p.kinds[i];
+    if (k < n) {
+      ms[k] += t;
+      count[k] += 1;
+    }
+  }
+  p.kinds.clear();
+  p.used = 0;
+  return 0;
+}
+
+int forward_launch_count(const Context &c, int has_mask) {
+  // embed + 7 per layer + ln_f + lm_head; with a mask, seq_info + 1 per layer
+  return 3 + 7 * c.dims.n_layer + (has_mask ? 1 + c.dims.n_layer : 0);
+}
+
+int forward_device(Context &c, const int64_t *d_ids, const int64_t *d_mask, int B, int S, float *d_logits,
+                   int64_t ld_logits, cudaStream_t st) {
+  const ModelDims &m = c.dims;
+  if (!c.loaded) {
+    set_error("no weights loaded");
+    return -3;
+  }
+  if (B < 1 || S < 1 || S > m.n_pos || (int64_t)B * S > (int64_t)1 << 30 || ld_logits < m.vocab) {
+    set_error("bad forward shape B=%d S=%d (n_positions %d) ld_logits=%lld", B, S, m.n_pos, (long long)ld_logits);
+    return -1;
+  }
+  int r = ensure_workspace(c, B, S);
+  if (r) return r;
+  const int64_t T = (int64_t)B * S;
+  const int d = m.n_embd, ff = m.n_inner, H = m.n_head, V = m.vocab;
+  Workspace &w = c.ws;
+  const uint8_t *kv = nullptr;
+  if (d_mask) {
+    CKP(K_SEQ_INFO, launch_seq_info(d_mask, B, S, w.first_valid, w.key_valid, st));
+    kv = w.key_valid;
+  }
+  if (c.dtype == 0) {
+    float *x = static_cast<float *>(w.x), *a = static_cast<float *>(w.a), *qkv = static_cast<float *>(w.qkv),
+          *o = static_cast<float *>(w.o), *u = static_cast<float *>(w.u);
+    CKP(K_EMBED, launch_embed_f32(d_ids, c.wte, c.wpe, x, (int)T, S, d, V, c.d_status, st));
+    for (int l = 0; l < m.n_layer; ++l) {
+      const LayerWeights &lw = c.layers[l];
+      CKP(K_LAYERNORM, launch_layernorm_f32(x, lw.ln1_g, lw.ln1_b, a, (int)T, d, m.eps, st));
+      CKP(K_GEMM_QKV, launch_gemm_f32(a, lw.qkv_w, 0, qkv, (int)T, 3 * d, d, 3 * d, lw.qkv_b, nullptr, EPI_BIAS, st));
+      CKP(K_ATTENTION, launch_attention_f32(qkv, kv, o, B, S, H, st));
+      if (d_mask) CKP(K_MASKED_ROWS, launch_attn_masked_rows_f32(qkv, w.first_valid, o, B, S, H, st));
+      CKP(K_GEMM_PROJ, launch_gemm_f32(o, lw.proj_w, 0, x, (int)T, d, d, d, lw.proj_b, x, EPI_BIAS_RESID, st));
+      CKP(K_LAYERNORM, launch_layernorm_f32(x, lw.ln2_g, lw.ln2_b, a, (int)T, d, m.eps, st));
+      CKP(K_GEMM_FC, launch_gemm_f32(a, lw.fc_w, 0, u, (int)T, ff, d, ff, lw.fc_b, nullptr, EPI_BIAS_GELU, st));
+      CKP(K_GEMM_MPROJ, launch_gemm_f32(u, lw.mproj_w, 0, x, (int)T, d, ff, d, lw.mproj_b, x, EPI_BIAS_RESID, st));
+    }
+    CKP(K_LAYERNORM, launch_layernorm_f32(x, c.lnf_g, c.lnf_b, a, (int)T, d, m.eps, st));
+    CKP(K_LM_HEAD, launch_gemm_f32(a, c.wte, 1, d_logits, (int)T, V, d, (int)ld_logits, nullptr, nullptr, EPI_NONE, st));
+    return 0;
+  }
+  r = ensure_plans(c, T);
+  if (r) return r;
+  bf16 *x = static_cast<bf16 *>(w.x), *a = static_cast<bf16 *>(w.a), *qkv = static_cast<bf16 *>(w.qkv),
+       *o = static_cast<bf16 *>(w.o), *u = static_cast<bf16 *>(w.u);
+  const int ns = c.num_sms;
+  CKP(K_EMBED, launch_embed_bf16(d_ids, c.wte_h, c.wpe_h, x, (int)T, S, d, V, c.d_status, st));
+  for (int l = 0; l < m.n_layer; ++l) {
+    const LayerWeights &lw = c.layers[l];
+    const TcGemmPlan *p = &c.plans[4 * l];
+    CKP(K_LAYERNORM, launch_layernorm_bf16(x, lw.ln1_g, lw.ln1_b, a, (int)T, d, m.eps, st));
+    CKP(K_GEMM_QKV, launch_gemm_tc(p[0], qkv, 3 * d, 0, lw.qkv_b, nullptr, EPI_BIAS, c.d_status, ns, st));
+    CKP(K_ATTENTION, launch_attention_bf16(qkv, kv, o, B, S, H, st));
+    if (d_mask) CKP(K_MASKED_ROWS, launch_attn_masked_rows_bf16(qkv, w.first_valid, o, B, S, H, st));
+    CKP(K_GEMM_PROJ, launch_gemm_tc(p[1], x, d, 0, lw.proj_b, x, EPI_BIAS_RESID, c.d_status, ns, st));
+    CKP(K_LAYERNORM, launch_layernorm_bf16(x, lw.ln2_g, lw.ln2_b, a, (int)T, d, m.eps, st));
+    CKP(K_GEMM_FC, launch_gemm_tc(p[2], u, ff, 0, lw.fc_b, nullptr, EPI_BIAS_GELU, c.d_status, ns, st));
+    CKP(K_GEMM_MPROJ, launch_gemm_tc(p[3], x, d, 0, lw.mproj_b, x, EPI_BIAS_RESID, c.d_status, ns, st));
+  }
+  CKP(K_LAYERNORM, launch_layernorm_bf16(x, c.lnf_g, c.lnf_b, a, (int)T, d, m.eps, st));
+  CKP(K_LM_HEAD, launch_gemm_tc(c.plans[4 * m.n_layer], d_logits, (int)ld_logits, 1, nullptr, nullptr, EPI_NONE, c.d_status, ns,
+                    st));
+  return 0;
+}
+
+}  // namespace gpt2

@@ -1,0 +1,113 @@
+// runtime.h -- host runtime of libgpt2_b200.so: model dimensions, the
+// canonical weight blob, the per-process model context and the forward
+// schedule.
+#pragma once
+
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+#include <mutex>
+#include <string>
+#include <vector>
+
+#include "../kernels.h"
+
+namespace gpt2 {
+
+struct ModelDims {
+  int n_layer = 12, n_embd = 768, n_head = 12, n_inner = 3072, vocab = 50257, n_pos = 1024;
+  float eps = 1e-5f;
+};
+
+// One tensor of the canonical FP32 blob.
+struct TensorSpec {
+  enum Kind { kMatrix = 0, kGain = 1, kBias = 2 };
+  int64_t offset, numel;
+  Kind kind;
+};
+
+// Per-layer tensor order inside the blob.
+enum LayerTensor { LN1_G, LN1_B, QKV_W, QKV_B, PROJ_W, PROJ_B, LN2_G, LN2_B, FC_W, FC_B, MPROJ_W, MPROJ_B, PER_LAYER };
+
+std::vector<TensorSpec> blob_specs(const ModelDims &m);
+int64_t blob_floats(const ModelDims &m);
+
+void seeded_normal(float *out, int64_t n, uint64_t seed, uint32_t stream, double mean, double stdv);
+void seeded_ids(int64_t *ids, int64_t n, uint64_t seed, uint32_t stream, int64_t vocab);
+void seeded_blob(const ModelDims &m, uint64_t seed, int init_mode, float *blob);
+
+// Device copies of the weights, in the layouts the kernels read.
+struct LayerWeights {
+  const float *ln1_g, *ln1_b, *qkv_b, *proj_b, *ln2_g, *ln2_b, *fc_b, *mproj_b;  // FP32, in blob
+  const float *qkv_w, *proj_w, *fc_w, *mproj_w;                                  // FP32 [in, out], in blob
+  bf16 *qkv_wt, *proj_wt, *fc_wt, *mproj_wt;                                     // BF16 [out, in]
+};
+
+// Activation buffers of one forward, grown on demand.
+struct Workspace {
+  int64_t T = 0;  // tokens the buffers hold
+  int B = 0;
+  int S = 0;
+  void *x = nullptr, *a = nullptr, *qkv = nullptr, *o = nullptr, *u = nullptr;
+  int *first_valid = nullptr;
+  uint8_t *key_valid = nullptr;
+  int64_t *ids = nullptr, *mask = nullptr;  // staging for host-side entry points
+  float *logits = nullptr;                  // for host-side entry points
+  int64_t logits_T = 0;
+};
+
+// Kernel kinds of the forward, for the per-kernel event profiler.
+enum KernelKind : int {
+  K_SEQ_INFO = 0, K_EMBED, K_LAYERNORM, K_GEMM_QKV, K_ATTENTION, K_MASKED_ROWS, K_GEMM_PROJ, K_GEMM_FC,
+  K_GEMM_MPROJ, K_LM_HEAD, K_NUM_KINDS
+};
+
+// Optional CUDA-event pair around every launch of the forward (off by default).
+struct Profiler {
+  bool on = false;
+  std::vector<cudaEvent_t> pool;
+  size_t used = 0;
+  std::vector<int> kinds;  // kind of record i; events 2i, 2i+1
+};
+
+struct Context {
+  ModelDims dims;
+  int dtype = 0;
+  int device = 0;
+  int num_sms = 148;
+  cudaStream_t stream = nullptr;
+  int *d_status = nullptr;
+  bool loaded = false;
+
+  float *d_blob = nullptr;  // canonical FP32 blob
+  std::vector<TensorSpec> specs;
+  const float *wte = nullptr, *wpe = nullptr, *lnf_g = nullptr, *lnf_b = nullptr;
+  bf16 *wte_h = nullptr, *wpe_h = nullptr;  // BF16 copies
+  std::vector<LayerWeights> layers;
+
+  Workspace ws;
+  // tcgen05 GEMM plans for the current workspace: 4 per layer + lm_head.
+  std::vector<TcGemmPlan> plans;
+  int64_t plans_T = -1;
+
+  Profiler prof;
+  std::mutex mu;
+};
+
+Context *context();  // the process-wide model (null if none)
+int create_context(const ModelDims &dims, int dtype, int device);
+void destroy_context();
+int load_blob(Context &c, const float *host_blob);
+// Grows the activation / staging buffers to hold B sequences of S tokens.
+int ensure_workspace(Context &c, int B, int S);
+
+// Enqueues the forward on `st`; ids / mask are contiguous device arrays.
+int forward_device(Context &c, const int64_t *d_ids, const int64_t *d_mask, int B, int S, float *d_logits,
+                   int64_t ld_logits, cudaStream_t st);
+int forward_launch_count(const Context &c, int has_mask);
+int profile_begin(Context &c);
+int profile_end(Context &c, double *ms, int64_t *count, int n);
+
+void set_error(const char *fmt, ...);
+
+}  // namespace gpt2

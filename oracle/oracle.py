@@ -1,0 +1,202 @@
+"""ctypes wrapper around the CPU oracle (oracle/gpt2_oracle.c).
+
+TEST INFRASTRUCTURE ONLY: tests/, the smoke() entry and bench.py's
+cpu_baseline / reference legs import this module to check or time the
+product; the product path never does.
+
+The oracle restates the reference's GPT-2 forward (HF GPT-2 as wrapped by
+src/gpt/lower_gpt_model.py:20-50 and lowered for the CPU by
+src/gpt/run_mlir_pipeline.sh:5-10, matmuls through cblas_sgemm as
+lib/ConvertMatMulToBlas.cpp:156-160 emits them).  It is pinned against
+transformers' GPT2LMHeadModel by the fixtures in tests/golden/.
+"""
+from __future__ import annotations
+
+import ctypes
+import glob
+import os
+import subprocess
+import sys
+from dataclasses import dataclass
+
+import numpy as np
+
+HERE = os.path.dirname(os.path.abspath(__file__))
+LIB_PATH = os.path.join(HERE, "_build", "libgpt2_oracle.so")
+
+# Philox stream used for the seeded token ids (weights use streams 0..4+12L).
+IDS_STREAM = 0x10000
+
+
+class OracleCfg(ctypes.Structure):
+    _fields_ = [
+        ("n_layer", ctypes.c_int32),
+        ("n_embd", ctypes.c_int32),
+        ("n_head", ctypes.c_int32),
+        ("n_inner", ctypes.c_int32),
+        ("vocab_size", ctypes.c_int32),
+        ("n_positions", ctypes.c_int32),
+        ("layer_norm_eps", ctypes.c_float),
+        ("dtype", ctypes.c_int32),
+    ]
+
+
+@dataclass(frozen=True)
+class ModelShape:
+    n_layer: int = 12
+    n_embd: int = 768
+    n_head: int = 12
+    n_inner: int = 3072
+    vocab_size: int = 50257
+    n_positions: int = 1024
+    layer_norm_eps: float = 1e-5
+
+    def c(self) -> OracleCfg:
+        return OracleCfg(self.n_layer, self.n_embd, self.n_head, self.n_inner,
+                         self.vocab_size, self.n_positions, self.layer_norm_eps, 0)
+
+
+GPT2_SMALL = ModelShape()
+# A small model of the same family for fast, mask-heavy parity cases.
+GPT2_TINY = ModelShape(n_layer=2, n_embd=128, n_head=2, n_inner=512, vocab_size=1000, n_positions=64)
+
+_lib = None
+
+
+def build(quiet: bool = True) -> str:
+    """Compiles the oracle with its Makefile; returns the library path."""
+    out = subprocess.run(["make", "-C", HERE], capture_output=True, text=True)
+    if out.returncode != 0:
+        raise RuntimeError("oracle build failed:\n" + out.stdout + out.stderr)
+    if not quiet:
+        sys.stdout.write(out.stdout)
+    return LIB_PATH
+
+
+def find_openblas() -> str | None:
+    """The OpenBLAS that scipy bundles (LP64 `scipy_cblas_sgemm`), else numpy's (ILP64)."""
+    try:
+        import scipy  # noqa: F401
+        base = os.path.dirname(os.path.dirname(scipy.__file__))
+        hits = sorted(glob.glob(os.path.join(base, "scipy.libs", "libscipy_openblas-*.so")))
+        if hits:
+            return hits[0]
+    except ImportError:
+        pass
+    base = os.path.dirname(os.path.dirname(np.__file__))
+    hits = sorted(glob.glob(os.path.join(base, "numpy.libs", "libscipy_openblas64_*.so")))
+    return hits[0] if hits else None
+
+
+def lib():
+    global _lib
+    if _lib is not None:
+        return _lib
+    if not os.path.exists(LIB_PATH):
+        build()
+    L = ctypes.CDLL(LIB_PATH)
+    P = ctypes.POINTER
+    L.oracle_num_tensors.argtypes = [P(OracleCfg)]
+    L.oracle_num_tensors.restype = ctypes.c_int
+    L.oracle_blob_layout.argtypes = [P(OracleCfg), P(ctypes.c_int64)]
+    L.oracle_blob_layout.restype = ctypes.c_int64
+    L.oracle_philox4x32_10.argtypes = [P(ctypes.c_uint32), P(ctypes.c_uint32), P(ctypes.c_uint32)]
+    L.oracle_normal_fill.argtypes = [P(ctypes.c_float), ctypes.c_int64, ctypes.c_uint64, ctypes.c_uint32,
+                                     ctypes.c_double, ctypes.c_double]
+    L.oracle_token_ids.argtypes = [P(ctypes.c_int64), ctypes.c_int64, ctypes.c_uint64, ctypes.c_uint32,
+                                   ctypes.c_int64]
+    L.oracle_seeded_blob.argtypes = [P(OracleCfg), ctypes.c_uint64, ctypes.c_int, P(ctypes.c_float)]
+    L.oracle_seeded_blob.restype = ctypes.c_int
+    L.oracle_set_blas.argtypes = [ctypes.c_char_p]
+    L.oracle_set_blas.restype = ctypes.c_int
+    L.oracle_blas_name.restype = ctypes.c_char_p
+    L.oracle_set_loop_threads.argtypes = [ctypes.c_int]
+    L.oracle_gpt2_forward.argtypes = [P(OracleCfg), P(ctypes.c_float), P(ctypes.c_int64), P(ctypes.c_int64),
+                                      ctypes.c_int, ctypes.c_int, P(ctypes.c_float)]
+    L.oracle_gpt2_forward.restype = ctypes.c_int
+    blas = os.environ.get("ORACLE_BLAS", None)
+    if blas is None:
+        blas = find_openblas() or ""
+    if blas and L.oracle_set_blas(blas.encode()) != 0:
+        L.oracle_set_blas(b"")
+    _lib = L
+    return L
+
+
+def _ptr(a: np.ndarray, ct):
+    return a.ctypes.data_as(ctypes.POINTER(ct))
+
+
+def blas_name() -> str:
+    return lib().oracle_blas_name().decode()
+
+
+def set_loop_threads(n: int) -> None:
+    lib().oracle_set_loop_threads(int(n))
+
+
+def philox(ctr, key) -> np.ndarray:
+    c = np.asarray(ctr, dtype=np.uint32)
+    k = np.asarray(key, dtype=np.uint32)
+    out = np.zeros(4, dtype=np.uint32)
+    lib().oracle_philox4x32_10(_ptr(c, ctypes.c_uint32), _ptr(k, ctypes.c_uint32), _ptr(out, ctypes.c_uint32))
+    return out
+
+
+def normal_fill(n: int, seed: int, stream: int, mean: float = 0.0, std: float = 1.0) -> np.ndarray:
+    out = np.empty(n, dtype=np.float32)
+    lib().oracle_normal_fill(_ptr(out, ctypes.c_float), n, seed, stream, mean, std)
+    return out
+
+
+def token_ids(B: int, S: int, seed: int, vocab: int, stream: int = IDS_STREAM) -> np.ndarray:
+    out = np.empty(B * S, dtype=np.int64)
+    lib().oracle_token_ids(_ptr(out, ctypes.c_int64), B * S, seed, stream, vocab)
+    return out.reshape(B, S)
+
+
+def blob_layout(shape: ModelShape) -> np.ndarray:
+    c = shape.c()
+    n = lib().oracle_num_tensors(ctypes.byref(c))
+    off = np.zeros(n + 1, dtype=np.int64)
+    lib().oracle_blob_layout(ctypes.byref(c), _ptr(off, ctypes.c_int64))
+    return off
+
+
+def seeded_blob(shape: ModelShape, seed: int, init_mode: int = 0) -> np.ndarray:
+    c = shape.c()
+    total = int(lib().oracle_blob_layout(ctypes.byref(c), None))
+    blob = np.empty(total, dtype=np.float32)
+    rc = lib().oracle_seeded_blob(ctypes.byref(c), seed, init_mode, _ptr(blob, ctypes.c_float))
+    assert rc == 0
+    return blob
+
+
+def tensor_names(shape: ModelShape) -> list[str]:
+    names = ["transformer.wte.weight", "transformer.wpe.weight"]
+    per = ["ln_1.weight", "ln_1.bias", "attn.c_attn.weight", "attn.c_attn.bias", "attn.c_proj.weight",
+           "attn.c_proj.bias", "ln_2.weight", "ln_2.bias", "mlp.c_fc.weight", "mlp.c_fc.bias",
+           "mlp.c_proj.weight", "mlp.c_proj.bias"]
+    for l in range(shape.n_layer):
+        names += [f"transformer.h.{l}.{p}" for p in per]
+    names += ["transformer.ln_f.weight", "transformer.ln_f.bias"]
+    return names
+
+
+def forward(shape: ModelShape, blob: np.ndarray, ids: np.ndarray, mask: np.ndarray | None = None,
+            out: np.ndarray | None = None) -> np.ndarray:
+    """FP32 logits [B, S, V] of the GPT-2 forward on (ids, mask)."""
+    ids = np.ascontiguousarray(ids, dtype=np.int64)
+    B, S = ids.shape
+    if out is None:
+        out = np.empty((B, S, shape.vocab_size), dtype=np.float32)
+    m = None
+    if mask is not None:
+        mask = np.ascontiguousarray(mask, dtype=np.int64)
+        m = _ptr(mask, ctypes.c_int64)
+    c = shape.c()
+    rc = lib().oracle_gpt2_forward(ctypes.byref(c), _ptr(blob, ctypes.c_float), _ptr(ids, ctypes.c_int64), m,
+                                   B, S, _ptr(out, ctypes.c_float))
+    if rc != 0:
+        raise ValueError(f"oracle_gpt2_forward failed with code {rc}")
+    return out

@@ -1,0 +1,189 @@
+"""End-to-end parity of the GPT-2 forward on the GPU, through the drop-in C ABI
+(gpt2_decoder / _mlir_ciface_gpt2_decoder) and the device entry point.
+
+FP32 path: within 1e-4 absolute of the golden fixtures (HF GPT2LMHeadModel)
+and of the oracle, the reference's own tolerance (src/compare_outputs.py:17).
+BF16 path: relative error bound BF16_RTOL on the logits (max |diff| over
+max |logit|) and top-5 identity wherever the oracle's top-5 is separated by
+more than twice that bound."""
+import numpy as np
+import pytest
+
+from helpers import attendable_rows, golden_files, load_golden, load_oracle, load_pkg, shape_to_cfg, top5_agreement
+
+pytestmark = pytest.mark.gpu
+pkg = load_pkg()
+O = load_oracle()
+
+FP32_ATOL = 1e-4
+BF16_RTOL = 0.03
+
+
+@pytest.fixture(scope="module")
+def torch():
+    import torch as t
+    assert t.cuda.is_available(), "GPU tests need a CUDA device"
+    t.cuda.set_device(0)
+    return t
+
+
+def _model(shape, blob, dtype):
+    pkg.init(shape_to_cfg(pkg, shape, dtype), 0)
+    pkg.load_weights(blob)
+
+
+def _bf16_check(ref, got, label):
+    scale = float(np.abs(ref).max())
+    err = float(np.abs(got - ref).max())
+    bound = BF16_RTOL * scale
+    checked, agree, total = top5_agreement(ref, got, bound)
+    print(f"{label}: max|diff| {err:.4g} (scale {scale:.3g}, rel {err / scale:.4g}); top-5 checked {checked}/{total}, "
+          f"identical {agree}")
+    assert err <= bound, (err, bound)
+    assert agree == checked
+
+
+@pytest.mark.parametrize("path", golden_files(), ids=lambda p: p.split("/")[-1])
+def test_fp32_matches_golden(torch, path):
+    shape, z = load_golden(path)
+    blob = O.seeded_blob(shape, int(z["seed"]), int(z["init_mode"]))
+    _model(shape, blob, pkg.DTYPE_F32)
+    got = pkg.gpt2_decoder(z["ids"], z["mask"])
+    if "cols" in z:
+        got = got[..., z["cols"]]
+    err = np.abs(got - z["logits"])
+    assert err.max() <= FP32_ATOL, err.max()
+    # the top-5 of every position with an attendable key matches HF's
+    rows = attendable_rows(z["mask"])
+    if "cols" not in z:
+        gi = np.argsort(-got, axis=-1, kind="stable")[..., :5]
+        assert np.array_equal(gi[rows], z["top5_idx"][rows])
+
+
+@pytest.mark.parametrize("path", golden_files(), ids=lambda p: p.split("/")[-1])
+def test_bf16_matches_golden(torch, path):
+    shape, z = load_golden(path)
+    blob = O.seeded_blob(shape, int(z["seed"]), int(z["init_mode"]))
+    _model(shape, blob, pkg.DTYPE_BF16)
+    got = pkg.ciface_gpt2_decoder(z["ids"], z["mask"])
+    ref = z["logits"]
+    if "cols" in z:
+        got = got[..., z["cols"]]
+    rows = attendable_rows(z["mask"])
+    _bf16_check(ref[rows], got[rows], path.split("/")[-1])
+
+
+def test_refcall_through_both_symbols_and_strides(torch):
+    """The reference host program's call (src/gpt/gpt2_call.cpp:54-64): ids [464, 3139, 286, 4881, 318],
+    all-ones mask; both ABI symbols agree, and a strided view gives the same logits."""
+    shape, z = load_golden(next(p for p in golden_files() if "refcall" in p))
+    blob = O.seeded_blob(shape, int(z["seed"]), int(z["init_mode"]))
+    _model(shape, blob, pkg.DTYPE_F32)
+    a = pkg.gpt2_decoder(z["ids"], z["mask"])
+    b = pkg.ciface_gpt2_decoder(z["ids"], z["mask"])
+    assert np.array_equal(a, b)
+    wide = np.zeros((1, 10), dtype=np.int64)
+    wide[0, ::2] = z["ids"][0]
+    c = pkg.gpt2_decoder(wide[:, ::2], np.ones((1, 5), dtype=np.int64))
+    assert np.array_equal(a, c)
+    assert np.abs(a - z["logits"]).max() <= FP32_ATOL
+
+
+def test_fp32_full_context_vs_oracle(torch):
+    """GPT-2 small, B=2 x S=1024 (the config-1 sequence length) against the oracle."""
+    shape = O.GPT2_SMALL
+    blob = O.seeded_blob(shape, 1234, 0)
+    ids = O.token_ids(2, 1024, 1234, shape.vocab_size)
+    O.set_loop_threads(8)
+    ref = O.forward(shape, blob, ids)
+    O.set_loop_threads(1)
+    _model(shape, blob, pkg.DTYPE_F32)
+    got = pkg.forward_host(ids)
+    err = float(np.abs(got - ref).max())
+    print(f"fp32 B2 S1024: max|diff| {err:.3g}")
+    assert err <= FP32_ATOL
+
+
+def test_fp32_batch_invariance_config1(torch):
+    """Config 1 (B=8 x S=1024, FP32): each sequence's logits equal those of the same sequence run
+    alone, bit for bit (rows never mix), so the B=2 oracle check covers all 8."""
+    shape = O.GPT2_SMALL
+    blob = O.seeded_blob(shape, 1234, 0)
+    _model(shape, blob, pkg.DTYPE_F32)
+    ids = O.token_ids(8, 1024, 1234, shape.vocab_size)
+    full = pkg.forward_host(ids)
+    for b in (0, 5, 7):
+        one = pkg.forward_host(ids[b:b + 1])
+        assert np.array_equal(full[b:b + 1], one)
+    assert np.isfinite(full).all()
+
+
+def test_bf16_vs_oracle_and_batch_invariance_config2(torch):
+    """Config 2 (B=64 x S=1024, BF16) on the device entry point: sequences are independent and
+    bit-identical to single-sequence runs; two of them are checked against the oracle."""
+    shape = O.GPT2_SMALL
+    blob = O.seeded_blob(shape, 1234, 0)
+    _model(shape, blob, pkg.DTYPE_BF16)
+    B, S, V = 64, 1024, shape.vocab_size
+    ids_h = O.token_ids(B, S, 1234, V)
+    ids = torch.from_numpy(ids_h).cuda()
+    logits = torch.empty(B * S, 50304, device="cuda")
+    pkg.forward_device(ids.data_ptr(), None, B, S, logits.data_ptr(), 50304,
+                       torch.cuda.current_stream().cuda_stream)
+    torch.cuda.synchronize()
+    assert pkg.status() == 0
+    one = torch.empty(S, 50304, device="cuda")
+    O.set_loop_threads(8)
+    for b in (0, 63):
+        pkg.forward_device(ids[b:b + 1].contiguous().data_ptr(), None, 1, S, one.data_ptr(), 50304,
+                           torch.cuda.current_stream().cuda_stream)
+        torch.cuda.synchronize()
+        assert torch.equal(logits[b * S:(b + 1) * S, :V], one[:, :V])
+        ref = O.forward(shape, blob, ids_h[b:b + 1])
+        _bf16_check(ref[0], one[:, :V].cpu().numpy(), f"bf16 config-2 seq {b}")
+    O.set_loop_threads(1)
+    assert torch.isfinite(logits[:, :V]).all()
+
+
+@pytest.mark.parametrize("dtype", [0, 1])
+def test_all_ones_mask_equals_no_mask_and_edge_lengths(torch, dtype):
+    shape = O.GPT2_TINY
+    blob = O.seeded_blob(shape, 8, 1)
+    _model(shape, blob, dtype)
+    V = shape.vocab_size
+    for S in (1, 2, 63, 64):
+        ids = torch.from_numpy(O.token_ids(3, S, S, V)).cuda()
+        ones = torch.ones_like(ids)
+        a = torch.empty(3 * S, V, device="cuda")
+        b = torch.empty(3 * S, V, device="cuda")
+        st = torch.cuda.current_stream().cuda_stream
+        pkg.forward_device(ids.data_ptr(), None, 3, S, a.data_ptr(), V, st)
+        pkg.forward_device(ids.data_ptr(), ones.data_ptr(), 3, S, b.data_ptr(), V, st)
+        torch.cuda.synchronize()
+        assert torch.equal(a, b)
+        ref = O.forward(shape, blob, ids.cpu().numpy())
+        got = a.view(3, S, V).cpu().numpy()
+        if dtype == 0:
+            assert np.abs(got - ref).max() <= FP32_ATOL
+        else:
+            _bf16_check(ref, got, f"tiny bf16 S={S}")
+
+
+def test_errors_are_reported_not_fatal(torch):
+    shape = O.GPT2_TINY
+    blob = O.seeded_blob(shape, 8, 0)
+    _model(shape, blob, pkg.DTYPE_F32)
+    V = shape.vocab_size
+    with pytest.raises(pkg.Gpt2Error, match="outside"):
+        pkg.gpt2_decoder(np.array([[1, V]]))
+    with pytest.raises(pkg.Gpt2Error):
+        pkg.gpt2_decoder(np.zeros((1, shape.n_positions + 1), dtype=np.int64))
+    # out-of-range id on the device path: recorded in the status word, the context stays usable
+    ids = torch.tensor([[1, 2, V + 5]], device="cuda")
+    out = torch.empty(3, V, device="cuda")
+    pkg.forward_device(ids.data_ptr(), None, 1, 3, out.data_ptr(), V, torch.cuda.current_stream().cuda_stream)
+    torch.cuda.synchronize()
+    assert pkg.status() == 1
+    assert pkg.status() == 0
+    good = pkg.gpt2_decoder(np.array([[1, 2, 3]]))
+    assert np.isfinite(good).all()

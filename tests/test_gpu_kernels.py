@@ -1,0 +1,180 @@
+"""Kernel-level parity on the GPU through the C ABI (gpt2k_* entry points).
+
+FP32 kernels are held to FP32 rounding against float64 references; BF16
+kernels to bf16 output rounding (the products of bf16 inputs are exact in
+FP32, so only the accumulation order and the final rounding differ)."""
+import numpy as np
+import pytest
+
+from helpers import load_pkg
+
+pytestmark = pytest.mark.gpu
+pkg = load_pkg()
+
+
+@pytest.fixture(scope="module")
+def torch():
+    import torch as t
+    assert t.cuda.is_available(), "GPU tests need a CUDA device"
+    t.cuda.set_device(0)
+    return t
+
+
+def _stream(torch):
+    return torch.cuda.current_stream().cuda_stream
+
+
+def _epi_ref(torch, acc, bias, resid, epi):
+    if epi == pkg.EPI_NONE:
+        return acc
+    v = acc + bias.double()
+    if epi == pkg.EPI_BIAS_GELU:
+        v = 0.5 * v * (1.0 + torch.tanh(0.7978845608028654 * (v + 0.044715 * v ** 3)))
+    if epi == pkg.EPI_BIAS_RESID:
+        v = resid.double() + v
+    return v
+
+
+@pytest.mark.parametrize("M,N,K,b_nk,epi,ldc", [
+    (5, 2304, 768, 0, pkg.EPI_BIAS, 2304),
+    (130, 768, 3072, 0, pkg.EPI_BIAS_RESID, 768),
+    (257, 3072, 768, 0, pkg.EPI_BIAS_GELU, 3072),
+    (77, 50257, 768, 1, pkg.EPI_NONE, 50257),
+    (64, 1000, 128, 1, pkg.EPI_NONE, 1008),
+])
+def test_gemm_f32(torch, M, N, K, b_nk, epi, ldc):
+    g = torch.Generator(device="cuda").manual_seed(M * 7 + N)
+    A = torch.randn(M, K, device="cuda", generator=g)
+    B = (torch.randn(N, K, device="cuda", generator=g) if b_nk else torch.randn(K, N, device="cuda", generator=g)) * 0.05
+    bias = torch.randn(N, device="cuda", generator=g)
+    C = torch.randn(M, ldc, device="cuda", generator=g)
+    resid = C[:, :N].clone()
+    pkg.k_gemm_f32(A.data_ptr(), B.data_ptr(), b_nk, C.data_ptr(), M, N, K, ldc, bias.data_ptr(), C.data_ptr(), epi,
+                   _stream(torch))
+    torch.cuda.synchronize()
+    acc = A.double() @ (B.double().T if b_nk else B.double())
+    ref = _epi_ref(torch, acc, bias, resid, epi)
+    err = (C[:, :N].double() - ref).abs().max().item()
+    assert err <= 2e-5 * ref.abs().max().item() + 1e-6, err
+
+
+@pytest.mark.parametrize("M,N,K,epi,out_f32,bn,ldc", [
+    (128, 256, 64, pkg.EPI_NONE, 0, 256, 256),
+    (1000, 2304, 768, pkg.EPI_BIAS, 0, 256, 2304),
+    (300, 768, 3072, pkg.EPI_BIAS_RESID, 0, 128, 768),
+    (513, 3072, 768, pkg.EPI_BIAS_GELU, 0, 256, 3072),
+    (200, 50257, 768, pkg.EPI_NONE, 1, 256, 50304),
+    (200, 50257, 768, pkg.EPI_NONE, 1, 128, 50257),
+    (64, 1000, 128, pkg.EPI_BIAS, 1, 128, 1000),
+    (4096, 768, 768, pkg.EPI_BIAS_RESID, 0, 256, 768),
+])
+def test_gemm_bf16_tcgen05(torch, M, N, K, epi, out_f32, bn, ldc):
+    g = torch.Generator(device="cuda").manual_seed(M + N + K)
+    A = torch.randn(M, K, device="cuda", generator=g).bfloat16()
+    B = (torch.randn(N, K, device="cuda", generator=g) * 0.05).bfloat16()
+    bias = torch.randn(N, device="cuda", generator=g)
+    if out_f32:
+        C = torch.full((M, ldc), 7.0, device="cuda")
+    else:
+        C = torch.randn(M, ldc, device="cuda", generator=g).bfloat16()
+    resid = C[:, :N].clone()
+    pkg.k_gemm_bf16(A.data_ptr(), B.data_ptr(), C.data_ptr(), M, N, K, ldc, out_f32, bias.data_ptr(),
+                    C.data_ptr(), epi, bn, _stream(torch))
+    torch.cuda.synchronize()
+    acc = A.double() @ B.double().T
+    ref = _epi_ref(torch, acc, bias, resid, epi)
+    got = C[:, :N].double()
+    scale = ref.abs().max().item()
+    err = (got - ref).abs().max().item()
+    if out_f32:
+        assert err <= 1e-5 * scale, (err, scale)
+        if ldc > N:  # padding columns untouched
+            assert torch.all(C[:, N:] == 7.0)
+    else:
+        assert err <= 8e-3 * scale, (err, scale)
+
+
+@pytest.mark.parametrize("T,d,dtype", [(1000, 768, 0), (33, 1600, 0), (1000, 768, 1), (5, 128, 1), (7, 1600, 1)])
+def test_layernorm(torch, T, d, dtype):
+    g = torch.Generator(device="cuda").manual_seed(T + d)
+    x = torch.randn(T, d, device="cuda", generator=g) * 3 + 0.5
+    gain = 1 + 0.1 * torch.randn(d, device="cuda", generator=g)
+    shift = 0.1 * torch.randn(d, device="cuda", generator=g)
+    if dtype == 1:
+        x = x.bfloat16()
+    y = torch.empty_like(x)
+    pkg.k_layernorm(x.data_ptr(), gain.data_ptr(), shift.data_ptr(), y.data_ptr(), T, d, 1e-5, dtype, _stream(torch))
+    torch.cuda.synchronize()
+    ref = torch.nn.functional.layer_norm(x.double(), (d,), gain.double(), shift.double(), 1e-5)
+    err = (y.double() - ref).abs().max().item()
+    assert err <= (1e-5 if dtype == 0 else 2e-2 * ref.abs().max().item()), err
+
+
+def attention_ref(torch, qkv, mask, B, S, H):
+    """float64 restatement of the oracle's attention semantics."""
+    D = H * 64
+    x = qkv.double().view(B, S, 3, H, 64)
+    q, k, v = x[:, :, 0].transpose(1, 2), x[:, :, 1].transpose(1, 2), x[:, :, 2].transpose(1, 2)
+    s = q @ k.transpose(-1, -2) * 0.125
+    causal = torch.ones(S, S, dtype=torch.bool, device=qkv.device).tril()
+    ok = causal[None, None]
+    if mask is not None:
+        ok = ok & (mask != 0)[:, None, None, :]
+    s = s.masked_fill(~ok, float("-inf"))
+    p = torch.softmax(s, dim=-1)
+    o = p @ v
+    none = ~ok.any(-1)  # [B,1|H,S]
+    mean_v = v.mean(dim=2, keepdim=True).expand_as(o)
+    o = torch.where(none[..., None].expand_as(o), mean_v, o)
+    return o.transpose(1, 2).reshape(B * S, D)
+
+
+@pytest.mark.parametrize("dtype", [0, 1])
+@pytest.mark.parametrize("B,S,H,masked", [(2, 1, 12, False), (3, 77, 2, True), (1, 1024, 12, False),
+                                          (2, 128, 2, True), (2, 200, 12, True)])
+def test_attention(torch, dtype, B, S, H, masked):
+    g = torch.Generator(device="cuda").manual_seed(B * 1000 + S)
+    qkv = torch.randn(B * S, 3 * H * 64, device="cuda", generator=g)
+    mask = None
+    if masked:
+        mask = torch.ones(B, S, dtype=torch.int64, device="cuda")
+        mask[0, : min(5, S)] = 0                 # left padding
+        if B > 1:
+            mask[1, S // 3: S // 2] = 0          # a hole
+            mask[1, -1] = 0                      # right padding
+        if B > 2:
+            mask[2, :] = 0                       # nothing attendable
+    if dtype == 1:
+        qkv = qkv.bfloat16()
+    o = torch.full((B * S, H * 64), 3.0, device="cuda", dtype=qkv.dtype)
+    ws = torch.empty(pkg.k_attention_workspace_bytes(B, S), dtype=torch.uint8, device="cuda")
+    pkg.k_attention(qkv.data_ptr(), mask.data_ptr() if mask is not None else None, o.data_ptr(), B, S, H, dtype,
+                    ws.data_ptr(), _stream(torch))
+    torch.cuda.synchronize()
+    ref = attention_ref(torch, qkv, mask, B, S, H)
+    err = (o.double() - ref).abs().max().item()
+    assert err <= (2e-5 if dtype == 0 else 3e-2), err
+
+
+@pytest.mark.parametrize("dtype", [0, 1])
+def test_embed_and_bad_ids(torch, dtype):
+    V, P, d, S = 1000, 64, 128, 10
+    g = torch.Generator(device="cuda").manual_seed(5)
+    wte = torch.randn(V, d, device="cuda", generator=g)
+    wpe = torch.randn(P, d, device="cuda", generator=g)
+    if dtype == 1:
+        wte, wpe = wte.bfloat16(), wpe.bfloat16()
+    ids = torch.randint(0, V, (2, S), device="cuda", generator=g)
+    ids[1, 3] = V  # out of range
+    x = torch.empty(2 * S, d, device="cuda", dtype=wte.dtype)
+    status = torch.zeros(1, dtype=torch.int32, device="cuda")
+    pkg.k_embed(ids.data_ptr(), wte.data_ptr(), wpe.data_ptr(), x.data_ptr(), 2 * S, S, d, V, dtype,
+                status.data_ptr(), _stream(torch))
+    torch.cuda.synchronize()
+    assert status.item() == 1
+    ref = wte.double()[ids.clamp(max=V - 1)].reshape(2 * S, d) + wpe.double()[torch.arange(S, device="cuda").repeat(2)]
+    good = torch.ones(2 * S, dtype=torch.bool, device="cuda")
+    good[S + 3] = False
+    err = (x.double()[good] - ref[good]).abs().max().item()
+    assert err <= (1e-6 if dtype == 0 else 3e-2), err
+    assert torch.all(x[S + 3].double() == wpe.double()[3])
