@@ -184,7 +184,7 @@ def run_reference(args, rank, world):
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
-    ap.add_argument("--steps", type=int, default=10)
+    ap.add_argument("--steps", type=int, default=50)
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--batch", type=int, default=64, help="global batch (sequences)")
@@ -219,7 +219,8 @@ def main():
     ids_h = np.ascontiguousarray(ids_all[rank * B:(rank + 1) * B])
     ids = torch.from_numpy(ids_h).cuda()
     logits = torch.empty(T, LD_LOGITS, device="cuda", dtype=torch.float32)
-    stream = torch.cuda.current_stream()
+    stream = torch.cuda.Stream()
+    torch.cuda.set_stream(stream)
     sp = stream.cuda_stream
 
     def step():

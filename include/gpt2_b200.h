@@ -154,7 +154,7 @@ int gpt2_status(void);
 /* logits [B, S, vocab] (row stride ld_logits >= vocab floats) of the loaded
  * model, everything on the model's device.  d_ids / d_mask: contiguous
  * int64 [B, S] device arrays (d_mask may be NULL = all ones).  Enqueued on
- * `stream` (a cudaStream_t; NULL = the model's own stream); returns when
+ * `stream` (a cudaStream_t; NULL = the CUDA default stream); returns when
  * enqueued.  logits_dtype must be GPT2_DTYPE_F32. */
 int gpt2_forward_device(const int64_t *d_ids, const int64_t *d_mask, int B, int S, void *d_logits,
                         int64_t ld_logits, int logits_dtype, void *stream);

@@ -115,12 +115,15 @@ int forward_host_locked(const int64_t *ids, const int64_t *mask, int B, int S, f
   r = ensure_workspace(c, B, S);
   if (r) return r;
   const int64_t V = c.dims.vocab;
+  // Device logits rows padded to a multiple of 4 floats (16 bytes) so the
+  // lm_head epilogue can store them with TMA; the copy-out strips the pad.
+  const int64_t ldl = (V + 3) / 4 * 4;
   if (!w.logits || w.logits_T < T) {
     if (w.logits) cudaFree(w.logits);
     w.logits = nullptr;
     w.logits_T = 0;
-    if (cudaMalloc(&w.logits, sizeof(float) * T * V) != cudaSuccess) {
-      set_error("cudaMalloc of %lld logits failed", (long long)(T * V));
+    if (cudaMalloc(&w.logits, sizeof(float) * T * ldl) != cudaSuccess) {
+      set_error("cudaMalloc of %lld logits failed", (long long)(T * ldl));
       return GPT2_ENOMEM;
     }
     w.logits_T = T;
@@ -131,9 +134,10 @@ int forward_host_locked(const int64_t *ids, const int64_t *mask, int B, int S, f
     set_error("host-to-device copy of ids/mask failed");
     return GPT2_ECUDA;
   }
-  r = forward_device(c, w.ids, mask ? w.mask : nullptr, B, S, w.logits, V, st);
+  r = forward_device(c, w.ids, mask ? w.mask : nullptr, B, S, w.logits, ldl, st);
   if (r) return r;
-  cudaError_t e = cudaMemcpyAsync(logits, w.logits, sizeof(float) * T * V, cudaMemcpyDeviceToHost, st);
+  cudaError_t e = cudaMemcpy2DAsync(logits, sizeof(float) * V, w.logits, sizeof(float) * ldl, sizeof(float) * V, T,
+                                    cudaMemcpyDeviceToHost, st);
   if (e == cudaSuccess) e = cudaStreamSynchronize(st);
   if (e != cudaSuccess) {
     set_error("forward failed: %s", cudaGetErrorString(e));
@@ -331,8 +335,8 @@ int gpt2_forward_device(const int64_t *d_ids, const int64_t *d_mask, int B, int 
     return GPT2_EINVAL;
   }
   cudaSetDevice(c->device);
-  cudaStream_t st = stream ? static_cast<cudaStream_t>(stream) : c->stream;
-  return forward_device(*c, d_ids, d_mask, B, S, static_cast<float *>(d_logits), ld_logits, st);
+  return forward_device(*c, d_ids, d_mask, B, S, static_cast<float *>(d_logits), ld_logits,
+                        static_cast<cudaStream_t>(stream));
 }
 
 int gpt2_forward_host(const int64_t *ids, const int64_t *mask, int B, int S, float *logits) {
@@ -392,6 +396,7 @@ int gpt2k_gemm_bf16(const void *A, const void *B, void *C, int M, int N, int K, 
     set_error("gpt2k_gemm_bf16: TMA descriptor creation failed (%d)", r);
     return GPT2_EINVAL;
   }
+  tc_gemm_set_output(&plan, C, ldc, out_f32);
   int dev = 0, sms = 148;
   cudaGetDevice(&dev);
   cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);

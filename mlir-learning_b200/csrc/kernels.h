@@ -65,11 +65,18 @@ cudaError_t launch_gemm_f32(const float *A, const float *B, int b_nk, float *C, 
 struct TcGemmPlan {
   CUtensorMap map_a;
   CUtensorMap map_b;
+  CUtensorMap map_c;  // output, when the output can be stored by TMA
   int M, N, K;
   int bn;  // 128 or 256
+  const void *c_ptr = nullptr;
+  int c_ld = 0, c_f32 = 0, has_c = 0;
 };
-// Builds the TMA descriptors; returns 0 or a negative error.
+// Builds the TMA descriptors of A and B; returns 0 or a negative error.
 int tc_gemm_plan(TcGemmPlan *plan, const bf16 *A, const bf16 *B, int M, int N, int K, int bn);
+// Builds the output descriptor for C (row stride ldc elements, f32 or bf16)
+// when C is 16-byte aligned and ldc * element size is a multiple of 16;
+// otherwise the kernel falls back to direct stores.  Returns has_c.
+int tc_gemm_set_output(TcGemmPlan *plan, const void *C, int ldc, int out_f32);
 cudaError_t launch_gemm_tc(const TcGemmPlan &plan, void *C, int ldc, int out_f32, const float *bias,
                            const bf16 *resid, int epi, int *status, int num_sms, cudaStream_t st);
 

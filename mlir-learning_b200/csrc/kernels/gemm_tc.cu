@@ -44,7 +44,9 @@ struct TcCfg {
   static constexpr int B_BYTES = BN * BK * 2;
   static constexpr int STAGE_BYTES = A_BYTES + B_BYTES;
   static constexpr int TMEM_COLS = 2 * BN;
-  static constexpr int SMEM_BYTES = 1024 /*align slack*/ + STAGES * STAGE_BYTES + 256;
+  // Epilogue staging: 4 warps x 2 buffers x (32 rows x 128 bytes).
+  static constexpr int STAGING_BYTES = 4 * 2 * 4096;
+  static constexpr int SMEM_BYTES = 1024 /*align slack*/ + STAGES * STAGE_BYTES + STAGING_BYTES + 256;
 };
 
 __device__ __forceinline__ void tile_coords(int t, int num_m, int num_n, int &mb, int &nb) {
@@ -57,17 +59,19 @@ __device__ __forceinline__ void tile_coords(int t, int num_m, int num_n, int &mb
   nb = in / gsize;
 }
 
-template <int BN, int EPI, int OUT_F32>
+template <int BN, int EPI, int OUT_F32, int TMA_STORE>
 __global__ void __launch_bounds__(NTHREADS, 1)
-    gemm_tc_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constant__ CUtensorMap map_b, void *C,
-                   int ldc, int M, int N, int K, const float *__restrict__ bias, const bf16 *resid, int *status) {
+    gemm_tc_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constant__ CUtensorMap map_b,
+                   const __grid_constant__ CUtensorMap map_c, void *C, int ldc, int M, int N, int K,
+                   const float *__restrict__ bias, const bf16 *resid, int *status) {
   using Cfg = TcCfg<BN>;
   constexpr int STAGES = Cfg::STAGES;
   extern __shared__ unsigned char smem_raw[];
   unsigned char *smem = reinterpret_cast<unsigned char *>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   unsigned char *sa = smem;
   unsigned char *sb = smem + STAGES * Cfg::A_BYTES;
-  uint64_t *bars = reinterpret_cast<uint64_t *>(smem + STAGES * Cfg::STAGE_BYTES);
+  unsigned char *staging = smem + STAGES * Cfg::STAGE_BYTES;
+  uint64_t *bars = reinterpret_cast<uint64_t *>(staging + Cfg::STAGING_BYTES);
   uint64_t *full = bars, *empty = bars + STAGES, *tfull = bars + 2 * STAGES, *tempty = bars + 2 * STAGES + 2;
   uint64_t *drain = bars + 2 * STAGES + 4;
   uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(bars + 2 * STAGES + 5);
@@ -162,8 +166,17 @@ __global__ void __launch_bounds__(NTHREADS, 1)
     mbar_wait(drain, 0, nullptr);
   } else if (warp >= 2) {
     // ---------------- epilogue ----------------
+    // Chunks of 128 bytes per row: 32 f32 or 64 bf16 columns.  Thread i of
+    // the warp owns row (q*32 + i) of the tile.  With TMA_STORE the chunk is
+    // written to a 128-byte-swizzled staging buffer (16-byte piece j of row r
+    // at piece j ^ (r & 7): conflict-free) and stored by one bulk tensor copy
+    // that the hardware clips at the ragged M / N edges.
+    constexpr int CH = OUT_F32 ? 32 : 64;
+    constexpr int NCH = BN / CH;
     const int q = warp & 3;  // TMEM lane quarter this warp may access
     const int row_in_tile = q * 32 + lane;
+    unsigned char *stage_buf = staging + (warp - 2) * 2 * 4096;
+    uint32_t chunk_count = 0;
     int local = 0;
     for (int t = blockIdx.x; t < total; t += gridDim.x, ++local) {
       int mb, nb;
@@ -178,36 +191,48 @@ __global__ void __launch_bounds__(NTHREADS, 1)
       tc_fence_after();
       const int row = mb * BM + row_in_tile;
       const bool row_ok = row < M;
+      const int64_t row_off = (int64_t)row * ldc;
+      uint4 res_cur[8], res_nxt[8];
+      auto load_res = [&](uint4 (&dst)[8], int col0) {
+        if (EPI == EPI_BIAS_RESID && !OUT_F32 && row_ok && col0 + CH <= N) {
+          const uint4 *rp = reinterpret_cast<const uint4 *>(resid + row_off + col0);
+#pragma unroll
+          for (int g = 0; g < 8; ++g) dst[g] = rp[g];
+        }
+      };
+      load_res(res_cur, nb * BN);
 #pragma unroll 1
-      for (int c = 0; c < BN / 32; ++c) {
-        uint32_t r[32];
-        tmem_ld_32x32b_x32(tmem_base + (static_cast<uint32_t>(q * 32) << 16) + acc * BN + c * 32, r);
+      for (int c = 0; c < NCH; ++c) {
+        const int col0 = nb * BN + c * CH;
+        if (c + 1 < NCH) load_res(res_nxt, col0 + CH);
+        uint32_t r[CH];
+        const uint32_t taddr = tmem_base + (static_cast<uint32_t>(q * 32) << 16) + acc * BN + c * CH;
+        tmem_ld_32x32b_x32(taddr, *reinterpret_cast<uint32_t(*)[32]>(&r[0]));
+        if (CH == 64) tmem_ld_32x32b_x32(taddr + 32, *reinterpret_cast<uint32_t(*)[32]>(&r[CH == 64 ? 32 : 0]));
         tc_wait_ld();
-        if (c == BN / 32 - 1) {
+        if (c == NCH - 1) {
           tc_fence_before();
           mbar_arrive(&tempty[acc]);
         }
-        const int col0 = nb * BN + c * 32;
-        float v[32];
-        float bias_lane = 0.f;
-        if (EPI != EPI_NONE) bias_lane = (col0 + lane < N) ? bias[col0 + lane] : 0.f;
+        float *v = reinterpret_cast<float *>(r);  // epilogue in place
+        float bias_lo = 0.f, bias_hi = 0.f;
+        if (EPI != EPI_NONE) {
+          bias_lo = (col0 + lane < N) ? bias[col0 + lane] : 0.f;
+          if (CH == 64) bias_hi = (col0 + 32 + lane < N) ? bias[col0 + 32 + lane] : 0.f;
+        }
 #pragma unroll
-        for (int j = 0; j < 32; ++j) {
+        for (int j = 0; j < CH; ++j) {
           float x = __uint_as_float(r[j]);
-          if (EPI != EPI_NONE) x += __shfl_sync(0xffffffffu, bias_lane, j);
+          if (EPI != EPI_NONE) x += __shfl_sync(0xffffffffu, j < 32 ? bias_lo : bias_hi, j & 31);
           if (EPI == EPI_BIAS_GELU) x = gelu_new_fast(x);
           v[j] = x;
         }
-        if (!row_ok) continue;
-        const bool full_chunk = col0 + 32 <= N;
-        const int64_t off = (int64_t)row * ldc + col0;
-        if (EPI == EPI_BIAS_RESID) {
+        const bool full_chunk = col0 + CH <= N;
+        if (EPI == EPI_BIAS_RESID && !OUT_F32 && row_ok) {
           if (full_chunk) {
-            const uint4 *rp = reinterpret_cast<const uint4 *>(resid + off);
 #pragma unroll
-            for (int g = 0; g < 4; ++g) {
-              uint4 raw = rp[g];
-              const __nv_bfloat162 *h = reinterpret_cast<const __nv_bfloat162 *>(&raw);
+            for (int g = 0; g < 8; ++g) {
+              const __nv_bfloat162 *h = reinterpret_cast<const __nv_bfloat162 *>(&res_cur[g]);
 #pragma unroll
               for (int j = 0; j < 4; ++j) {
                 const float2 f = __bfloat1622float2(h[j]);
@@ -216,39 +241,57 @@ __global__ void __launch_bounds__(NTHREADS, 1)
               }
             }
           } else {
-            for (int j = 0; j < 32; ++j)
-              if (col0 + j < N) v[j] += __bfloat162float(resid[off + j]);
+            for (int j = 0; j < CH; ++j)
+              if (col0 + j < N) v[j] += __bfloat162float(resid[row_off + col0 + j]);
+          }
+          if (c + 1 < NCH) {
+#pragma unroll
+            for (int g = 0; g < 8; ++g) res_cur[g] = res_nxt[g];
           }
         }
-        if (OUT_F32) {
-          float *cp = reinterpret_cast<float *>(C) + off;
-          if (full_chunk && (ldc & 3) == 0) {
-#pragma unroll
-            for (int g = 0; g < 8; ++g)
-              reinterpret_cast<float4 *>(cp)[g] = make_float4(v[4 * g], v[4 * g + 1], v[4 * g + 2], v[4 * g + 3]);
-          } else {
-            for (int j = 0; j < 32; ++j)
-              if (col0 + j < N) cp[j] = v[j];
+        // 16-byte piece g of this row: 4 f32 or 8 bf16 values
+        auto piece = [&](int g) -> uint4 {
+          if (OUT_F32)
+            return make_uint4(__float_as_uint(v[4 * g]), __float_as_uint(v[4 * g + 1]), __float_as_uint(v[4 * g + 2]),
+                              __float_as_uint(v[4 * g + 3]));
+          return make_uint4(pack_bf16x2(v[8 * g], v[8 * g + 1]), pack_bf16x2(v[8 * g + 2], v[8 * g + 3]),
+                            pack_bf16x2(v[8 * g + 4], v[8 * g + 5]), pack_bf16x2(v[8 * g + 6], v[8 * g + 7]));
+        };
+        if (TMA_STORE) {
+          unsigned char *buf = stage_buf + (chunk_count & 1) * 4096;
+          if (chunk_count >= 2) {
+            if (lane == 0) bulk_wait_read<1>();
+            __syncwarp();
           }
-        } else {
-          bf16 *cp = reinterpret_cast<bf16 *>(C) + off;
-          if (full_chunk) {
 #pragma unroll
-            for (int g = 0; g < 4; ++g) {
-              uint4 w;
-              w.x = pack_bf16x2(v[8 * g + 0], v[8 * g + 1]);
-              w.y = pack_bf16x2(v[8 * g + 2], v[8 * g + 3]);
-              w.z = pack_bf16x2(v[8 * g + 4], v[8 * g + 5]);
-              w.w = pack_bf16x2(v[8 * g + 6], v[8 * g + 7]);
-              reinterpret_cast<uint4 *>(cp)[g] = w;
-            }
+          for (int g = 0; g < 8; ++g)
+            *reinterpret_cast<uint4 *>(buf + lane * 128 + ((g ^ (lane & 7)) << 4)) = piece(g);
+          fence_proxy_async_smem();
+          __syncwarp();
+          if (lane == 0) {
+            tma_store_2d(&map_c, buf, col0, mb * BM + q * 32);
+            bulk_commit();
+          }
+          ++chunk_count;
+        } else if (row_ok) {
+          if (full_chunk && (!OUT_F32 || (ldc & 3) == 0)) {
+            uint4 *cp = reinterpret_cast<uint4 *>(reinterpret_cast<unsigned char *>(C) +
+                                                  (row_off + col0) * (OUT_F32 ? 4 : 2));
+#pragma unroll
+            for (int g = 0; g < 8; ++g) cp[g] = piece(g);
+          } else if (OUT_F32) {
+            float *cp = reinterpret_cast<float *>(C) + row_off + col0;
+            for (int j = 0; j < CH; ++j)
+              if (col0 + j < N) cp[j] = v[j];
           } else {
-            for (int j = 0; j < 32; ++j)
+            bf16 *cp = reinterpret_cast<bf16 *>(C) + row_off + col0;
+            for (int j = 0; j < CH; ++j)
               if (col0 + j < N) cp[j] = __float2bfloat16_rn(v[j]);
           }
         }
       }
     }
+    if (TMA_STORE && lane == 0) bulk_wait_all();
   }
 
   __syncthreads();
@@ -291,33 +334,58 @@ int make_map_2d(CUtensorMap *map, const void *base, int64_t rows, int64_t cols, 
   return r == CUDA_SUCCESS ? 0 : -3;
 }
 
-template <int BN, int EPI, int OUT_F32>
+// Output [rows, cols] (row stride ld elements) in boxes of 32 rows x 128
+// bytes with the 128-byte swizzle of the staging buffers.
+int make_map_out(CUtensorMap *map, const void *base, int64_t rows, int64_t cols, int64_t ld, int f32) {
+  EncodeTiledFn f = encode_fn();
+  if (!f) return -1;
+  const int es = f32 ? 4 : 2;
+  if ((reinterpret_cast<uintptr_t>(base) & 15) || (ld * es) % 16) return -2;
+  const cuuint64_t dims[2] = {static_cast<cuuint64_t>(cols), static_cast<cuuint64_t>(rows)};
+  const cuuint64_t strides[1] = {static_cast<cuuint64_t>(ld * es)};
+  const cuuint32_t box[2] = {static_cast<cuuint32_t>(128 / es), 32};
+  const cuuint32_t estr[2] = {1, 1};
+  CUresult r = f(map, f32 ? CU_TENSOR_MAP_DATA_TYPE_FLOAT32 : CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2,
+                 const_cast<void *>(base), dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
+                 CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_NONE, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  return r == CUDA_SUCCESS ? 0 : -3;
+}
+
+template <int BN, int EPI, int OUT_F32, int TMA_STORE>
 cudaError_t launch_variant(const TcGemmPlan &p, void *C, int ldc, const float *bias, const bf16 *resid, int *status,
                            int num_sms, cudaStream_t st) {
   using Cfg = TcCfg<BN>;
   static std::atomic<uint64_t> attr_done{0};
-  cudaError_t e = set_smem_once(gemm_tc_kernel<BN, EPI, OUT_F32>, Cfg::SMEM_BYTES, attr_done);
+  cudaError_t e = set_smem_once(gemm_tc_kernel<BN, EPI, OUT_F32, TMA_STORE>, Cfg::SMEM_BYTES, attr_done);
   if (e != cudaSuccess) return e;
   const int tiles = ((p.M + BM - 1) / BM) * ((p.N + BN - 1) / BN);
   const int grid = tiles < num_sms ? tiles : num_sms;
-  gemm_tc_kernel<BN, EPI, OUT_F32><<<grid, NTHREADS, Cfg::SMEM_BYTES, st>>>(p.map_a, p.map_b, C, ldc, p.M, p.N, p.K,
-                                                                              bias, resid, status);
+  gemm_tc_kernel<BN, EPI, OUT_F32, TMA_STORE><<<grid, NTHREADS, Cfg::SMEM_BYTES, st>>>(
+      p.map_a, p.map_b, p.map_c, C, ldc, p.M, p.N, p.K, bias, resid, status);
   return cudaGetLastError();
+}
+
+template <int BN, int EPI, int OUT_F32>
+cudaError_t launch_store(const TcGemmPlan &p, void *C, int ldc, const float *bias, const bf16 *resid, int *status,
+                         int num_sms, cudaStream_t st) {
+  const bool tma = p.has_c && p.c_ptr == C && p.c_ld == ldc && p.c_f32 == OUT_F32;
+  if (tma) return launch_variant<BN, EPI, OUT_F32, 1>(p, C, ldc, bias, resid, status, num_sms, st);
+  return launch_variant<BN, EPI, OUT_F32, 0>(p, C, ldc, bias, resid, status, num_sms, st);
 }
 
 template <int BN>
 cudaError_t dispatch_epi(const TcGemmPlan &p, void *C, int ldc, int out_f32, const float *bias, const bf16 *resid,
                          int epi, int *status, int num_sms, cudaStream_t st) {
   if (out_f32) {
-    if (epi == EPI_NONE) return launch_variant<BN, EPI_NONE, 1>(p, C, ldc, bias, resid, status, num_sms, st);
-    if (epi == EPI_BIAS) return launch_variant<BN, EPI_BIAS, 1>(p, C, ldc, bias, resid, status, num_sms, st);
+    if (epi == EPI_NONE) return launch_store<BN, EPI_NONE, 1>(p, C, ldc, bias, resid, status, num_sms, st);
+    if (epi == EPI_BIAS) return launch_store<BN, EPI_BIAS, 1>(p, C, ldc, bias, resid, status, num_sms, st);
     return cudaErrorInvalidValue;
   }
   switch (epi) {
-    case EPI_NONE: return launch_variant<BN, EPI_NONE, 0>(p, C, ldc, bias, resid, status, num_sms, st);
-    case EPI_BIAS: return launch_variant<BN, EPI_BIAS, 0>(p, C, ldc, bias, resid, status, num_sms, st);
-    case EPI_BIAS_GELU: return launch_variant<BN, EPI_BIAS_GELU, 0>(p, C, ldc, bias, resid, status, num_sms, st);
-    case EPI_BIAS_RESID: return launch_variant<BN, EPI_BIAS_RESID, 0>(p, C, ldc, bias, resid, status, num_sms, st);
+    case EPI_NONE: return launch_store<BN, EPI_NONE, 0>(p, C, ldc, bias, resid, status, num_sms, st);
+    case EPI_BIAS: return launch_store<BN, EPI_BIAS, 0>(p, C, ldc, bias, resid, status, num_sms, st);
+    case EPI_BIAS_GELU: return launch_store<BN, EPI_BIAS_GELU, 0>(p, C, ldc, bias, resid, status, num_sms, st);
+    case EPI_BIAS_RESID: return launch_store<BN, EPI_BIAS_RESID, 0>(p, C, ldc, bias, resid, status, num_sms, st);
   }
   return cudaErrorInvalidValue;
 }
@@ -325,6 +393,8 @@ cudaError_t dispatch_epi(const TcGemmPlan &p, void *C, int ldc, int out_f32, con
 
 int tc_gemm_plan(TcGemmPlan *plan, const bf16 *A, const bf16 *B, int M, int N, int K, int bn) {
   if (!plan || M <= 0 || N <= 0 || K <= 0 || K % 8 || (bn != 128 && bn != 256)) return -10;
+  plan->has_c = 0;
+  plan->c_ptr = nullptr;
   plan->M = M;
   plan->N = N;
   plan->K = K;
@@ -332,6 +402,14 @@ int tc_gemm_plan(TcGemmPlan *plan, const bf16 *A, const bf16 *B, int M, int N, i
   int r = make_map_2d(&plan->map_a, A, M, K, BM);
   if (r) return r;
   return make_map_2d(&plan->map_b, B, N, K, bn);
+}
+
+int tc_gemm_set_output(TcGemmPlan *plan, const void *C, int ldc, int out_f32) {
+  plan->c_ptr = C;
+  plan->c_ld = ldc;
+  plan->c_f32 = out_f32;
+  plan->has_c = make_map_out(&plan->map_c, C, plan->M, plan->N, ldc, out_f32) == 0;
+  return plan->has_c;
 }
 
 cudaError_t launch_gemm_tc(const TcGemmPlan &plan, void *C, int ldc, int out_f32, const float *bias,

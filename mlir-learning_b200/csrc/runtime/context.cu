@@ -265,14 +265,19 @@ int ensure_plans(Context &c, int64_t T) {
   };
   for (int l = 0; l < m.n_layer; ++l) {
     const LayerWeights &w = c.layers[l];
-    int r = tc_gemm_plan(&c.plans[4 * l + 0], a, w.qkv_wt, (int)T, 3 * d, d, pick_bn(3 * d));
-    if (!r) r = tc_gemm_plan(&c.plans[4 * l + 1], o, w.proj_wt, (int)T, d, d, pick_bn(d));
-    if (!r) r = tc_gemm_plan(&c.plans[4 * l + 2], a, w.fc_wt, (int)T, ff, d, pick_bn(ff));
-    if (!r) r = tc_gemm_plan(&c.plans[4 * l + 3], u, w.mproj_wt, (int)T, d, ff, pick_bn(d));
+    TcGemmPlan *p = &c.plans[4 * l];
+    int r = tc_gemm_plan(&p[0], a, w.qkv_wt, (int)T, 3 * d, d, pick_bn(3 * d));
+    if (!r) r = tc_gemm_plan(&p[1], o, w.proj_wt, (int)T, d, d, pick_bn(d));
+    if (!r) r = tc_gemm_plan(&p[2], a, w.fc_wt, (int)T, ff, d, pick_bn(ff));
+    if (!r) r = tc_gemm_plan(&p[3], u, w.mproj_wt, (int)T, d, ff, pick_bn(d));
     if (r) {
       set_error("TMA descriptor creation failed (%d)", r);
       return -2;
     }
+    tc_gemm_set_output(&p[0], c.ws.qkv, 3 * d, 0);
+    tc_gemm_set_output(&p[1], c.ws.x, d, 0);
+    tc_gemm_set_output(&p[2], c.ws.u, ff, 0);
+    tc_gemm_set_output(&p[3], c.ws.x, d, 0);
   }
   if (tc_gemm_plan(&c.plans[4 * m.n_layer], a, c.wte_h, (int)T, m.vocab, d, pick_bn(m.vocab))) {
     set_error("TMA descriptor creation failed (lm_head)");
@@ -388,7 +393,10 @@ int forward_device(Context &c, const int64_t *d_ids, const int64_t *d_mask, int 
     CKP(K_GEMM_MPROJ, launch_gemm_tc(p[3], x, d, 0, lw.mproj_b, x, EPI_BIAS_RESID, c.d_status, ns, st));
   }
   CKP(K_LAYERNORM, launch_layernorm_bf16(x, c.lnf_g, c.lnf_b, a, (int)T, d, m.eps, st));
-  CKP(K_LM_HEAD, launch_gemm_tc(c.plans[4 * m.n_layer], d_logits, (int)ld_logits, 1, nullptr, nullptr, EPI_NONE, c.d_status, ns,
+  TcGemmPlan &head = c.plans[4 * m.n_layer];
+  if (head.c_ptr != d_logits || head.c_ld != (int)ld_logits || !head.c_f32)
+    tc_gemm_set_output(&head, d_logits, (int)ld_logits, 1);
+  CKP(K_LM_HEAD, launch_gemm_tc(head, d_logits, (int)ld_logits, 1, nullptr, nullptr, EPI_NONE, c.d_status, ns,
                     st));
   return 0;
 }
