@@ -152,7 +152,8 @@ int gpt2_status(void);
 /* ------------------------------------------------------------------------ */
 
 /* logits [B, S, vocab] (row stride ld_logits >= vocab floats) of the loaded
- * model, everything on the model's device.  d_ids / d_mask: contiguous
+ * model, everything on the model's device.  Columns [vocab, ld_logits) of a
+ * row may be overwritten up to the next 16-byte boundary.  d_ids / d_mask: contiguous
  * int64 [B, S] device arrays (d_mask may be NULL = all ones).  Enqueued on
  * `stream` (a cudaStream_t; NULL = the CUDA default stream); returns when
  * enqueued.  logits_dtype must be GPT2_DTYPE_F32. */
@@ -201,9 +202,12 @@ int gpt2k_layernorm(const void *x, const float *gain, const float *shift, void *
                     int dtype, void *stream);
 
 /* Causal attention of one layer, head dim 64: qkv [B*S, 3*H*64] (q | k | v),
- * o [B*S, H*64], in dtype.  d_mask: contiguous int64 [B, S] or NULL.
+ * o [B*S, H*64], in dtype: GPT2_DTYPE_F32 (SIMT), GPT2_DTYPE_BF16 (tcgen05)
+ * or GPT2K_ATTN_BF16_MMA_SYNC (a second, warp-level mma.sync BF16 kernel kept
+ * as an independent cross-check).  d_mask: contiguous int64 [B, S] or NULL.
  * workspace: device memory of gpt2k_attention_workspace_bytes(B, S) bytes
  * (unused, may be NULL, when d_mask is NULL). */
+enum { GPT2K_ATTN_BF16_MMA_SYNC = 2 };
 size_t gpt2k_attention_workspace_bytes(int B, int S);
 int gpt2k_attention(const void *qkv, const int64_t *d_mask, void *o, int B, int S, int H, int dtype,
                     void *workspace, void *stream);

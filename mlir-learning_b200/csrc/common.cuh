@@ -70,15 +70,18 @@ __device__ __forceinline__ bool mbar_try_wait(uint64_t *bar, uint32_t parity) {
 }
 
 // Waits for the phase with the given parity to complete.  Gives up (returns
-// false) when *abort is set by another role of the CTA or after
+// false) when *abort is set by another role of the CTA, when the grid-wide
+// status word *gstatus is non-zero (another CTA gave up), or after
 // GPT2_WAIT_TIMEOUT_NS; the caller then records the timeout and unwinds.
-__device__ __forceinline__ bool mbar_wait(uint64_t *bar, uint32_t parity, volatile int *abort) {
+__device__ __forceinline__ bool mbar_wait(uint64_t *bar, uint32_t parity, volatile int *abort,
+                                          const volatile int *gstatus = nullptr) {
   if (mbar_try_wait(bar, parity)) return true;
   const uint64_t t0 = globaltimer_ns();
   for (uint32_t i = 1;; ++i) {
     if (mbar_try_wait(bar, parity)) return true;
     if ((i & 255u) == 0) {
       if (abort && *abort) return false;
+      if (gstatus && *gstatus == GPT2_ERR_WAIT_TIMEOUT) return false;
       if (globaltimer_ns() - t0 > GPT2_WAIT_TIMEOUT_NS) return false;
     }
   }

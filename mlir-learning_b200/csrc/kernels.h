@@ -88,6 +88,15 @@ cudaError_t launch_attention_f32(const float *qkv, const uint8_t *key_valid, flo
                                  cudaStream_t st);
 cudaError_t launch_attention_bf16(const bf16 *qkv, const uint8_t *key_valid, bf16 *o, int B, int S, int H,
                                   cudaStream_t st);
+// tcgen05 attention: TMA descriptor over qkv viewed as [B][S][3*H*64].
+struct AttnTcPlan {
+  CUtensorMap map_qkv;
+  const bf16 *qkv = nullptr;
+  int B = 0, S = 0, H = 0;
+};
+int attention_tc_plan(AttnTcPlan *plan, const bf16 *qkv, int B, int S, int H);
+cudaError_t launch_attention_tc(const AttnTcPlan &plan, const uint8_t *key_valid, bf16 *o, int *status,
+                                cudaStream_t st);
 // Rows q < first_valid[b] (no attendable key) get the mean of V over all S keys.
 cudaError_t launch_attn_masked_rows_f32(const float *qkv, const int *first_valid, float *o, int B, int S, int H,
                                         cudaStream_t st);

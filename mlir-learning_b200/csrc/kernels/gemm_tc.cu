@@ -117,7 +117,7 @@ __global__ void __launch_bounds__(NTHREADS, 1)
       for (int kb = 0; kb < num_k; ++kb, ++it) {
         const int s = it % STAGES;
         const uint32_t ph = (it / STAGES) & 1;
-        if (!mbar_wait(&empty[s], ph ^ 1, abort_flag)) { ok = false; break; }
+        if (!mbar_wait(&empty[s], ph ^ 1, abort_flag, status)) { ok = false; break; }
         mbar_arrive_expect_tx(&full[s], Cfg::STAGE_BYTES);
         tma_load_2d(sa + s * Cfg::A_BYTES, &map_a, &full[s], kb * BK, mb * BM);
         tma_load_2d(sb + s * Cfg::B_BYTES, &map_b, &full[s], kb * BK, nb * BN);
@@ -139,13 +139,13 @@ __global__ void __launch_bounds__(NTHREADS, 1)
     for (int t = blockIdx.x; t < total && ok; t += gridDim.x, ++local) {
       const int acc = local & 1;
       const uint32_t aph = (local >> 1) & 1;
-      if (!mbar_wait(&tempty[acc], aph ^ 1, abort_flag)) { ok = false; break; }
+      if (!mbar_wait(&tempty[acc], aph ^ 1, abort_flag, status)) { ok = false; break; }
       tc_fence_after();
       const uint32_t d_tmem = tmem_base + acc * BN;
       for (int kb = 0; kb < num_k; ++kb, ++it) {
         const int s = it % STAGES;
         const uint32_t ph = (it / STAGES) & 1;
-        if (!mbar_wait(&full[s], ph, abort_flag)) { ok = false; break; }
+        if (!mbar_wait(&full[s], ph, abort_flag, status)) { ok = false; break; }
         tc_fence_after();
         const uint32_t a0 = smem_u32(sa + s * Cfg::A_BYTES), b0 = smem_u32(sb + s * Cfg::B_BYTES);
 #pragma unroll
@@ -183,7 +183,7 @@ __global__ void __launch_bounds__(NTHREADS, 1)
       tile_coords(t, num_m, num_n, mb, nb);
       const int acc = local & 1;
       const uint32_t aph = (local >> 1) & 1;
-      if (!mbar_wait(&tfull[acc], aph, abort_flag)) {
+      if (!mbar_wait(&tfull[acc], aph, abort_flag, status)) {
         set_status(status, GPT2_ERR_WAIT_TIMEOUT);
         *abort_flag = 1;
         break;

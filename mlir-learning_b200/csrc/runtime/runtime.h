@@ -89,6 +89,7 @@ struct Context {
   // tcgen05 GEMM plans for the current workspace: 4 per layer + lm_head.
   std::vector<TcGemmPlan> plans;
   int64_t plans_T = -1;
+  AttnTcPlan attn_plan;  // tcgen05 attention descriptor for (ws.qkv, B, S)
 
   Profiler prof;
   std::mutex mu;
