@@ -282,6 +282,11 @@ __device__ __forceinline__ float gelu_new_fast(float x) {
   return 0.5f * x * (1.0f + tanh_approx(k * (x + 0.044715f * x * x * x)));
 }
 
+// Named barrier `id` (1..15) over `count` threads (a multiple of 32).
+__device__ __forceinline__ void named_bar_sync(int id, int count) {
+  asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(count) : "memory");
+}
+
 __device__ __forceinline__ float warp_sum(float v) {
 #pragma unroll
   for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
