@@ -212,6 +212,20 @@ size_t gpt2k_attention_workspace_bytes(int B, int S);
 int gpt2k_attention(const void *qkv, const int64_t *d_mask, void *o, int B, int S, int H, int dtype,
                     void *workspace, void *stream);
 
+/* Attention without a workspace argument, for callers that cannot allocate
+ * device memory at call time: hosts whose device memory is reserved up front
+ * by another allocator, generated code with no allocation hook at this call,
+ * real-time loops that must not pay for an allocation.  (No counterpart in
+ * the reference.)  Same arguments and results as gpt2k_attention; the mask
+ * scratch comes from a fixed 4 MiB array in the library's device image,
+ * present on every GPU that loads the library until the process exits, so
+ * 256 + 4*B + B*S must not exceed 4 MiB (a larger shape returns GPT2_EINVAL
+ * with a message).  The first call on a device looks up the array's address
+ * (make it before any stream capture).  Calls share the array: calls that
+ * overlap on the GPU race; each call rewrites the bytes it reads. */
+int gpt2k_attention_noalloc(const void *qkv, const int64_t *d_mask, void *o, int B, int S, int H, int dtype,
+                            void *stream);
+
 /* Token + position embedding: x[t] = wte[ids[t]] + wpe[t % S] in dtype;
  * out-of-range ids set the model-independent status word *d_status to 1. */
 int gpt2k_embed(const int64_t *d_ids, const void *wte, const void *wpe, void *x, int T, int S, int d, int V,

@@ -123,6 +123,7 @@ def lib() -> ctypes.CDLL:
     L.gpt2k_attention_workspace_bytes.argtypes = [i32, i32]
     L.gpt2k_attention_workspace_bytes.restype = ctypes.c_size_t
     L.gpt2k_attention.argtypes = [vp, vp, vp, i32, i32, i32, i32, vp, vp]
+    L.gpt2k_attention_noalloc.argtypes = [vp, vp, vp, i32, i32, i32, i32, vp]
     L.gpt2k_embed.argtypes = [vp, vp, vp, vp, i32, i32, i32, i32, i32, vp, vp]
     _lib = L
     return L
@@ -326,6 +327,10 @@ def k_attention_workspace_bytes(B, S) -> int:
 
 def k_attention(qkv, mask, o, B, S, H, dtype, workspace=None, stream=None):
     _check(lib().gpt2k_attention(qkv, mask, o, B, S, H, dtype, workspace, stream), "gpt2k_attention")
+
+
+def k_attention_noalloc(qkv, mask, o, B, S, H, dtype, stream=None):
+    _check(lib().gpt2k_attention_noalloc(qkv, mask, o, B, S, H, dtype, stream), "gpt2k_attention_noalloc")
 
 
 def k_embed(ids, wte, wpe, x, T, S, d, V, dtype, status_ptr=None, stream=None):
