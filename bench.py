@@ -66,6 +66,25 @@ def _peaks():
         return {"hbm_gbs": 6650.0, "bf16": 1590.0, "bf16_sus": 1400.0, "src": "fallback"}
 
 
+def shard_rows(global_batch: int, world: int, rank: int) -> tuple[int, int]:
+    """Rows [start, stop) of the global batch that `rank` of `world` processes.  Sequences are
+    independent, so the batch splits with no data-path collective; the global batch must divide."""
+    if world < 1 or not 0 <= rank < world or global_batch % world:
+        raise ValueError(f"global batch {global_batch} does not split over {world} ranks")
+    per = global_batch // world
+    return rank * per, (rank + 1) * per
+
+
+def max_over_ranks(seconds: float, dist=None, device=None) -> float:
+    """The slowest rank's time (the job's time); identity on one rank."""
+    if dist is None or not dist.is_initialized() or dist.get_world_size() == 1:
+        return seconds
+    import torch
+    t = torch.tensor([seconds], dtype=torch.float64, device=device)
+    dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    return float(t.item())
+
+
 def kernel_work(B, S):
     """Algorithmic work of one launch of each kernel kind at B sequences of S tokens:
     ('flop', F) for tensor-bound kernels, ('bytes', N) for the bandwidth-bound ones."""
@@ -191,6 +210,7 @@ def main():
     ap.add_argument("--seq", type=int, default=1024)
     ap.add_argument("--e2e-steps", type=int, default=2)
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--no-gather", action="store_true", help="skip the NCCL logits gather (N > 1)")
     args = ap.parse_args()
 
     rank = int(os.environ.get("RANK", "0"))
@@ -208,15 +228,14 @@ def main():
     if world > 1:
         dist.init_process_group("nccl", timeout=timedelta(seconds=120), device_id=torch.device("cuda", local_rank))
     pkg = _pkg()
-    if args.batch % world:
-        raise SystemExit(f"global batch {args.batch} does not split over {world} ranks")
-    B, S = args.batch // world, args.seq
+    row0, row1 = shard_rows(args.batch, world, rank)
+    B, S = row1 - row0, args.seq
     T = B * S
 
     pkg.init(pkg.gpt2_small(pkg.DTYPE_BF16), local_rank)
     pkg.init_seeded(SEED, 0)
     ids_all = pkg.seeded_ids(args.batch, S, SEED, V)
-    ids_h = np.ascontiguousarray(ids_all[rank * B:(rank + 1) * B])
+    ids_h = np.ascontiguousarray(ids_all[row0:row1])
     ids = torch.from_numpy(ids_h).cuda()
     logits = torch.empty(T, LD_LOGITS, device="cuda", dtype=torch.float32)
     stream = torch.cuda.Stream()
@@ -246,11 +265,28 @@ def main():
         torch.cuda.synchronize()
     barrier()
     elapsed = ev0.elapsed_time(ev1) / 1000.0
-    t = torch.tensor([elapsed], device="cuda", dtype=torch.float64)
-    if world > 1:
-        dist.all_reduce(t, op=dist.ReduceOp.MAX)
-    t_max = float(t.item())
+    t_max = max_over_ranks(elapsed, dist, "cuda")
     value = args.batch * S * args.steps / t_max
+
+    # The output step after the forward: gather every shard's FP32 logits to rank 0 with NCCL
+    # over NVLink (one collective; reported beside `value`, not inside it).
+    gather = None
+    if world > 1 and not args.no_gather:
+        glist = [torch.empty_like(logits) for _ in range(world)] if rank == 0 else None
+        for _ in range(2):
+            dist.gather(logits, glist, dst=0)
+        torch.cuda.synchronize()
+        dist.barrier()
+        g0, g1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        g0.record(stream)
+        dist.gather(logits, glist, dst=0)
+        g1.record(stream)
+        torch.cuda.synchronize()
+        gt = max_over_ranks(g0.elapsed_time(g1) / 1000.0, dist, "cuda")
+        gather = {"ms": 1000.0 * gt, "bytes_to_rank0": int(logits.numel() * 4 * (world - 1)),
+                  "gbs_into_rank0": logits.numel() * 4 * (world - 1) / gt / 1e9,
+                  "tokens_per_s_forward_plus_gather": args.batch * S / (t_max / args.steps + gt)}
+        del glist
 
     # Per-kernel breakdown (separate, profiled steps of the same workload).
     pkg.profile_begin()
@@ -322,10 +358,7 @@ def main():
         for _ in range(args.e2e_steps):
             lib.gpt2_forward_host(ip, None, B, S, op)
         et = time.perf_counter() - t0
-        tt = torch.tensor([et], device="cuda", dtype=torch.float64)
-        if world > 1:
-            dist.all_reduce(tt, op=dist.ReduceOp.MAX)
-        e2e = {"value": args.batch * S * args.e2e_steps / float(tt.item()), "unit": "tokens/s",
+        e2e = {"value": args.batch * S * args.e2e_steps / max_over_ranks(et, dist, "cuda"), "unit": "tokens/s",
                "h2d_bytes_per_step": int(ids_np.nbytes * world), "d2h_bytes_per_step": int(out_np.nbytes * world),
                "steps": args.e2e_steps, "api": "gpt2_forward_host (C ABI, host buffers, synchronous)"}
         del host_logits
@@ -356,6 +389,7 @@ def main():
             "kernels": kernels,
             "cpu_baseline": cpu,
             "e2e": e2e,
+            "logits_gather": gather,
             "clocks": clocks,
             "gpu_launches": pkg.forward_launches(B, S, False) * args.steps,
         }
