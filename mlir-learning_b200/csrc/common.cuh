@@ -87,6 +87,38 @@ __device__ __forceinline__ bool mbar_wait(uint64_t *bar, uint32_t parity, volati
   }
 }
 
+// Warp-uniform form of mbar_wait, for roles run by a whole warp: every lane
+// polls, and the warp leaves together as soon as any lane has seen the phase
+// complete (a completed phase stays complete until the barrier is re-armed,
+// which needs this warp's own later actions).  Same bounds as mbar_wait.
+__device__ __forceinline__ bool mbar_wait_warp(uint64_t *bar, uint32_t parity, volatile int *abort,
+                                               const volatile int *gstatus = nullptr) {
+  if (__any_sync(0xffffffffu, mbar_try_wait(bar, parity))) return true;
+  const uint64_t t0 = globaltimer_ns();
+  for (uint32_t i = 1;; ++i) {
+    if (__any_sync(0xffffffffu, mbar_try_wait(bar, parity))) return true;
+    if ((i & 255u) == 0) {
+      int give_up = 0;
+      if ((threadIdx.x & 31) == 0)
+        give_up = (abort && *abort) || (gstatus && *gstatus == GPT2_ERR_WAIT_TIMEOUT) ||
+                  (globaltimer_ns() - t0 > GPT2_WAIT_TIMEOUT_NS);
+      if (__shfl_sync(0xffffffffu, give_up, 0)) return false;
+    }
+  }
+}
+
+// True in exactly one lane of the (converged) warp.
+__device__ __forceinline__ bool elect_one_sync() {
+  uint32_t pred = 0;
+  asm volatile(
+      "{\n\t.reg .pred P;\n\t"
+      "elect.sync _|P, %1;\n\t"
+      "selp.u32 %0, 1, 0, P;\n\t}"
+      : "=r"(pred)
+      : "r"(0xffffffffu));
+  return pred != 0;
+}
+
 // ---------------------------------------------------------------------------
 // TMA (tiled, no multicast)
 // ---------------------------------------------------------------------------

@@ -51,8 +51,9 @@ struct AttnTcSmem {
   static constexpr int V = K + ST * TILE_BYTES;
   static constexpr int P = V + ST * TILE_BYTES;
   static constexpr int BARS = P + 2 * P_BYTES;
-  // q_full[2], q_empty[2], k_full[ST], v_full[ST], kv_empty[ST], s_full[2], s_free[2], p_full[2], o_done[2], drain
-  static constexpr int NBARS = 4 + 3 * ST + 8 + 1;
+  // q_full[2], q_empty[2], k_full[ST], v_full[ST], k_empty[ST], v_empty[ST], s_full[2], s_free[2], p_full[2],
+  // o_done[2], drain
+  static constexpr int NBARS = 4 + 4 * ST + 8 + 1;
   static constexpr int XM = BARS + NBARS * 8;          // row max exchange [2 parity][2 tiles][2 halves][128]
   static constexpr int XL = XM + 2 * 2 * 2 * 128 * 4;  // row sum exchange [2 tiles][2 halves][128]
   static constexpr int MISC = XL + 2 * 2 * 128 * 4;
@@ -64,6 +65,31 @@ __device__ __forceinline__ float ex2(float x) {
   float y;
   asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
   return y;
+}
+
+// Packed FP32 pairs (sm_100 f32x2 instructions): two elements per FMA / ADD.
+__device__ __forceinline__ uint64_t pk2(float lo, float hi) {
+  uint64_t r;
+  asm("mov.b64 %0, {%1, %2};" : "=l"(r) : "f"(lo), "f"(hi));
+  return r;
+}
+__device__ __forceinline__ void up2(uint64_t v, float &lo, float &hi) {
+  asm("mov.b64 {%0, %1}, %2;" : "=f"(lo), "=f"(hi) : "l"(v));
+}
+__device__ __forceinline__ uint64_t fma2(uint64_t a, uint64_t b, uint64_t c) {
+  uint64_t d;
+  asm("fma.rn.f32x2 %0, %1, %2, %3;" : "=l"(d) : "l"(a), "l"(b), "l"(c));
+  return d;
+}
+__device__ __forceinline__ uint64_t add2(uint64_t a, uint64_t b) {
+  uint64_t d;
+  asm("add.rn.f32x2 %0, %1, %2;" : "=l"(d) : "l"(a), "l"(b));
+  return d;
+}
+__device__ __forceinline__ float max3(float a, float b, float c) {
+  float d;
+  asm("max.f32 %0, %1, %2, %3;" : "=f"(d) : "f"(a), "f"(b), "f"(c));
+  return d;
 }
 
 // Work item w: (query-tile pair, batch, head), heaviest pairs first.
@@ -96,8 +122,8 @@ __global__ void __launch_bounds__(NTHREADS, 1)
       reinterpret_cast<unsigned char *>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint64_t *bars = reinterpret_cast<uint64_t *>(sm + AttnTcSmem::BARS);
   uint64_t *q_full = bars, *q_empty = bars + 2;
-  uint64_t *k_full = bars + 4, *v_full = k_full + ST, *kv_empty = v_full + ST;
-  uint64_t *s_full = kv_empty + ST, *s_free = s_full + 2, *p_full = s_free + 2, *o_done = p_full + 2;
+  uint64_t *k_full = bars + 4, *v_full = k_full + ST, *k_empty = v_full + ST, *v_empty = k_empty + ST;
+  uint64_t *s_full = v_empty + ST, *s_free = s_full + 2, *p_full = s_free + 2, *o_done = p_full + 2;
   uint64_t *drain = o_done + 2;
   uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(sm + AttnTcSmem::MISC);
   volatile int *abort_flag = reinterpret_cast<volatile int *>(sm + AttnTcSmem::MISC + 4);
@@ -114,12 +140,13 @@ __global__ void __launch_bounds__(NTHREADS, 1)
     for (int s = 0; s < ST; ++s) {
       mbar_init(&k_full[s], 1);
       mbar_init(&v_full[s], 1);
-      mbar_init(&kv_empty[s], 1);
+      mbar_init(&k_empty[s], 1);
+      mbar_init(&v_empty[s], 1);
     }
     for (int t = 0; t < 2; ++t) {
       mbar_init(&s_full[t], 1);
-      mbar_init(&s_free[t], SOFTMAX_THREADS);
-      mbar_init(&p_full[t], SOFTMAX_THREADS);
+      mbar_init(&s_free[t], SOFTMAX_THREADS / 32);  // one arrival per softmax warp
+      mbar_init(&p_full[t], SOFTMAX_THREADS / 32);
       mbar_init(&o_done[t], 1);
     }
     mbar_init(drain, 1);
@@ -134,28 +161,39 @@ __global__ void __launch_bounds__(NTHREADS, 1)
   tc_fence_after();
   const uint32_t tmem = *tmem_slot;
 
-  if (warp == 0 && lane == 0) {
-    // ---------------- TMA producer ----------------
-    prefetch_tmap(&map_qkv);
+  if (warp == 0) {
+    // ---------------- TMA producer (whole warp, one elected lane issues) ----------------
+    const bool leader = elect_one_sync();
+    if (leader) prefetch_tmap(&map_qkv);
     uint32_t q_issued[2] = {0, 0}, kv_issued[ST] = {};
     int qi = 0, kvi = 0;
     bool ok = true;
     for (int w = blockIdx.x; w < n_items && ok; w += gridDim.x, ++qi) {
       const AttnItem it = attn_item(w, S, B, H);
       const int qb = qi & 1;
-      if (!mbar_wait(&q_empty[qb], ((qi >> 1) & 1) ^ 1, abort_flag, status)) { ok = false; break; }
-      mbar_arrive_expect_tx(&q_full[qb], 2 * TILE_BYTES);
-      tma_load_3d(sm + AttnTcSmem::Q + qb * 2 * TILE_BYTES, &map_qkv, &q_full[qb], it.h * DH, it.q0, it.b);
-      tma_load_3d(sm + AttnTcSmem::Q + qb * 2 * TILE_BYTES + TILE_BYTES, &map_qkv, &q_full[qb], it.h * DH,
-                  it.q0 + BQ, it.b);
+      if (!mbar_wait_warp(&q_empty[qb], ((qi >> 1) & 1) ^ 1, abort_flag, status)) { ok = false; break; }
+      if (leader) {
+        mbar_arrive_expect_tx(&q_full[qb], 2 * TILE_BYTES);
+        tma_load_3d(sm + AttnTcSmem::Q + qb * 2 * TILE_BYTES, &map_qkv, &q_full[qb], it.h * DH, it.q0, it.b);
+        tma_load_3d(sm + AttnTcSmem::Q + qb * 2 * TILE_BYTES + TILE_BYTES, &map_qkv, &q_full[qb], it.h * DH,
+                    it.q0 + BQ, it.b);
+      }
       ++q_issued[qb];
       for (int j = 0; j < it.n_kv_max; ++j, ++kvi) {
         const int s = kvi % ST;
-        if (!mbar_wait(&kv_empty[s], ((kvi / ST) & 1) ^ 1, abort_flag, status)) { ok = false; break; }
-        mbar_arrive_expect_tx(&k_full[s], TILE_BYTES);
-        tma_load_3d(sm + AttnTcSmem::K + s * TILE_BYTES, &map_qkv, &k_full[s], D + it.h * DH, j * BKV, it.b);
-        mbar_arrive_expect_tx(&v_full[s], TILE_BYTES);
-        tma_load_3d(sm + AttnTcSmem::V + s * TILE_BYTES, &map_qkv, &v_full[s], 2 * D + it.h * DH, j * BKV, it.b);
+        // K slots free up once the S MMAs that read them complete, V slots
+        // once the P V MMAs do, so K runs a full iteration ahead of V.
+        if (!mbar_wait_warp(&k_empty[s], ((kvi / ST) & 1) ^ 1, abort_flag, status)) { ok = false; break; }
+        if (leader) {
+          mbar_arrive_expect_tx(&k_full[s], TILE_BYTES);
+          tma_load_3d(sm + AttnTcSmem::K + s * TILE_BYTES, &map_qkv, &k_full[s], D + it.h * DH, j * BKV, it.b);
+        }
+        if (!mbar_wait_warp(&v_empty[s], ((kvi / ST) & 1) ^ 1, abort_flag, status)) { ok = false; break; }
+        if (leader) {
+          mbar_arrive_expect_tx(&v_full[s], TILE_BYTES);
+          tma_load_3d(sm + AttnTcSmem::V + s * TILE_BYTES, &map_qkv, &v_full[s], 2 * D + it.h * DH, j * BKV,
+                      it.b);
+        }
         ++kv_issued[s];
       }
     }
@@ -165,56 +203,72 @@ __global__ void __launch_bounds__(NTHREADS, 1)
     }
     // Let every copy issued land before the CTA can exit.
     for (int i = 0; i < 2; ++i)
-      if (q_issued[i]) mbar_wait(&q_full[i], (q_issued[i] - 1) & 1, nullptr);
+      if (q_issued[i]) mbar_wait_warp(&q_full[i], (q_issued[i] - 1) & 1, nullptr);
     for (int s = 0; s < ST; ++s)
       if (kv_issued[s]) {
-        mbar_wait(&k_full[s], (kv_issued[s] - 1) & 1, nullptr);
-        mbar_wait(&v_full[s], (kv_issued[s] - 1) & 1, nullptr);
+        mbar_wait_warp(&k_full[s], (kv_issued[s] - 1) & 1, nullptr);
+        mbar_wait_warp(&v_full[s], (kv_issued[s] - 1) & 1, nullptr);
       }
-  } else if (warp == 1 && lane == 0) {
-    // ---------------- MMA issuer ----------------
+  } else if (warp == 1) {
+    // ---------------- MMA issuer (whole warp, one elected lane issues) ----------------
+    // The whole warp runs the schedule so that its state stays warp-uniform
+    // (uniform registers); only the elected lane issues tcgen05 instructions.
+    const bool leader = elect_one_sync();
     constexpr uint32_t idesc_s = idesc_bf16_f32(128, 128, 0);  // Q K^T: both K-major
     constexpr uint32_t idesc_o = idesc_bf16_f32(128, 64, 1);   // P V: V is MN-major
-    const uint32_t qa = smem_u32(sm + AttnTcSmem::Q), ka = smem_u32(sm + AttnTcSmem::K),
-                   va = smem_u32(sm + AttnTcSmem::V), pa = smem_u32(sm + AttnTcSmem::P);
+    // Base descriptors, computed once: the MMA thread shares its SM sub-partition
+    // with four busy softmax warps, so each MMA issue must cost only an add
+    // per operand (start addresses are in 16-byte units in the low bits).
+    const uint64_t dq0 = sdesc_kmajor_sw128(smem_u32(sm + AttnTcSmem::Q));
+    const uint64_t dk0 = sdesc_kmajor_sw128(smem_u32(sm + AttnTcSmem::K));
+    const uint64_t dp0 = sdesc_kmajor_sw128(smem_u32(sm + AttnTcSmem::P));
+    const uint64_t dv0 = sdesc_mnmajor_sw128(smem_u32(sm + AttnTcSmem::V), TILE_BYTES, 1024);
+    constexpr uint64_t kTile16 = TILE_BYTES >> 4;
     int g_base[2] = {0, 0};  // running per-tile iteration count (barrier phases)
     int qi = 0, kv_base = 0;
     bool ok = true;
     for (int w = blockIdx.x; w < n_items && ok; w += gridDim.x, ++qi) {
       const AttnItem it = attn_item(w, S, B, H);
       const int qb = qi & 1;
-      const uint32_t qbuf = qa + qb * 2 * TILE_BYTES;
-      if (!mbar_wait(&q_full[qb], (qi >> 1) & 1, abort_flag, status)) { ok = false; break; }
+      const uint64_t dq = dq0 + qb * 2 * kTile16;
+      if (!mbar_wait_warp(&q_full[qb], (qi >> 1) & 1, abort_flag, status)) { ok = false; break; }
       // S_t(j) = Q_t K_j^T into TMEM columns [t*128, t*128+128)
       auto issue_s = [&](int t, int j) -> bool {
         const int g = g_base[t] + j;
         const int s = (kv_base + j) % ST;
-        if (g > 0 && !mbar_wait(&s_free[t], (g - 1) & 1, abort_flag, status)) return false;
+        if (g > 0 && !mbar_wait_warp(&s_free[t], (g - 1) & 1, abort_flag, status)) return false;
         tc_fence_after();
+        const uint64_t a = dq + t * kTile16, b = dk0 + s * kTile16;
+        if (leader) {
 #pragma unroll
-        for (int k = 0; k < DH / 16; ++k)
-          tc_mma_f16(tmem + t * 128, sdesc_kmajor_sw128(qbuf + t * TILE_BYTES + k * 32),
-                     sdesc_kmajor_sw128(ka + s * TILE_BYTES + k * 32), idesc_s, k != 0);
-        tc_commit(&s_full[t]);
+          for (int k = 0; k < DH / 16; ++k) tc_mma_f16(tmem + t * 128, a + 2 * k, b + 2 * k, idesc_s, k != 0);
+          tc_commit(&s_full[t]);
+        }
+        __syncwarp();
         return true;
       };
       // O_t (+)= P_t V_j into TMEM columns [256 + t*64, 256 + t*64 + 64)
       auto issue_pv = [&](int t, int j) -> bool {
         const int g = g_base[t] + j;
         const int s = (kv_base + j) % ST;
-        if (!mbar_wait(&p_full[t], g & 1, abort_flag, status)) return false;
+        if (!mbar_wait_warp(&p_full[t], g & 1, abort_flag, status)) return false;
         tc_fence_after();
+        const uint64_t a = dp0 + t * 2 * kTile16, b = dv0 + s * kTile16;
+        const uint32_t first = j == 0;
+        if (leader) {
 #pragma unroll
-        for (int k = 0; k < BKV / 16; ++k)
-          tc_mma_f16(tmem + 256 + t * 64,
-                     sdesc_kmajor_sw128(pa + t * P_BYTES + (k >> 2) * TILE_BYTES + (k & 3) * 32),
-                     sdesc_mnmajor_sw128(va + s * TILE_BYTES + k * 2048, TILE_BYTES, 1024), idesc_o, (j | k) != 0);
-        tc_commit(&o_done[t]);
+          for (int k = 0; k < BKV / 16; ++k)
+            tc_mma_f16(tmem + 256 + t * 64, a + (k >> 2) * kTile16 + (k & 3) * 2, b + k * (2048 >> 4), idesc_o,
+                       !(first && k == 0));
+          tc_commit(&o_done[t]);
+        }
+        __syncwarp();
         return true;
       };
-      ok = mbar_wait(&k_full[kv_base % ST], (kv_base / ST) & 1, abort_flag, status);
+      ok = mbar_wait_warp(&k_full[kv_base % ST], (kv_base / ST) & 1, abort_flag, status);
       for (int t = 0; t < 2 && ok; ++t)
         if (it.n_kv[t] > 0) ok = issue_s(t, 0);
+      if (ok && leader) tc_commit(&k_empty[kv_base % ST]);
       for (int j = 0; j < it.n_kv_max && ok; ++j) {
         const int kv = kv_base + j;
         // S_t(j+1) as soon as the softmax holds S_t(j) in registers, so the
@@ -223,20 +277,21 @@ __global__ void __launch_bounds__(NTHREADS, 1)
         for (int t = 0; t < 2 && ok; ++t) {
           if (j + 1 < it.n_kv[t]) {
             if (!k_ready) {
-              ok = mbar_wait(&k_full[(kv + 1) % ST], ((kv + 1) / ST) & 1, abort_flag, status);
+              ok = mbar_wait_warp(&k_full[(kv + 1) % ST], ((kv + 1) / ST) & 1, abort_flag, status);
               k_ready = true;
             }
             if (ok) ok = issue_s(t, j + 1);
           }
         }
         if (!ok) break;
-        if (!mbar_wait(&v_full[kv % ST], (kv / ST) & 1, abort_flag, status)) { ok = false; break; }
+        if (k_ready && leader) tc_commit(&k_empty[(kv + 1) % ST]);
+        if (!mbar_wait_warp(&v_full[kv % ST], (kv / ST) & 1, abort_flag, status)) { ok = false; break; }
         for (int t = 0; t < 2 && ok; ++t)
           if (j < it.n_kv[t]) ok = issue_pv(t, j);
-        tc_commit(&kv_empty[kv % ST]);
+        if (leader) tc_commit(&v_empty[kv % ST]);
       }
       if (!ok) break;
-      tc_commit(&q_empty[qb]);  // this item's Q tiles are free once its MMAs complete
+      if (leader) tc_commit(&q_empty[qb]);  // this item's Q tiles are free once its MMAs complete
       g_base[0] += it.n_kv[0];
       g_base[1] += it.n_kv[1];
       kv_base += it.n_kv_max;
@@ -245,8 +300,8 @@ __global__ void __launch_bounds__(NTHREADS, 1)
       set_status(status, GPT2_ERR_WAIT_TIMEOUT);
       *abort_flag = 1;
     }
-    tc_commit(drain);
-    mbar_wait(drain, 0, nullptr);
+    if (leader) tc_commit(drain);
+    mbar_wait_warp(drain, 0, nullptr);
   } else if (warp >= 2) {
     // ---------------- softmax: two threads per query row ----------------
     // Warps 2-9 serve tile 0, warps 10-17 tile 1.  Within a tile, warps
@@ -269,11 +324,19 @@ __global__ void __launch_bounds__(NTHREADS, 1)
     // A failed wait raises the abort flag but never changes the control flow:
     // the two threads of a row must execute the same named barriers, and
     // once the flag is up every later wait returns at once.
+    // One lane per warp polls the barrier (keeping shared-memory barrier
+    // traffic low for the MMA warp); the warp then proceeds together.
     auto wait = [&](uint64_t *bar, uint32_t parity) {
-      if (!mbar_wait(bar, parity, abort_flag, status)) {
+      if (lane == 0 && !mbar_wait(bar, parity, abort_flag, status)) {
         set_status(status, GPT2_ERR_WAIT_TIMEOUT);
         *abort_flag = 1;
       }
+      __syncwarp();
+    };
+    // All lanes' tcgen05 / shared-memory work is done (each lane fenced) before one lane arrives.
+    auto arrive = [&](uint64_t *bar) {
+      __syncwarp();
+      if (lane == 0) mbar_arrive(bar);
     };
     int g_base = 0;
     for (int w = blockIdx.x; w < n_items; w += gridDim.x) {
@@ -295,7 +358,7 @@ __global__ void __launch_bounds__(NTHREADS, 1)
         tmem_ld_32x32b_x32(s_tmem + 32, *reinterpret_cast<uint32_t(*)[32]>(&sv[32]));
         tc_wait_ld();
         tc_fence_before();
-        mbar_arrive(&s_free[t]);  // S is in registers: the next Q K^T may overwrite it
+        arrive(&s_free[t]);  // S is in registers: the next Q K^T may overwrite it
         // Pass 1: masking (raw scores -> -inf) and the partial row max, 8 chains.
         float mx[8];
 #pragma unroll
@@ -336,7 +399,8 @@ __global__ void __launch_bounds__(NTHREADS, 1)
           }
         } else {
 #pragma unroll
-          for (int c = 0; c < 64; ++c) mx[c & 7] = fmaxf(mx[c & 7], __uint_as_float(sv[c]));
+          for (int c = 0; c < 64; c += 2)
+            mx[(c >> 1) & 7] = max3(mx[(c >> 1) & 7], __uint_as_float(sv[c]), __uint_as_float(sv[c + 1]));
         }
         float mraw = fmaxf(fmaxf(fmaxf(mx[0], mx[1]), fmaxf(mx[2], mx[3])),
                            fmaxf(fmaxf(mx[4], mx[5]), fmaxf(mx[6], mx[7])));
@@ -371,26 +435,34 @@ __global__ void __launch_bounds__(NTHREADS, 1)
           tc_wait_st();
         }
         l_run *= alpha;
-        // Pass 2: p = 2^(s * scale * log2e - m), bf16 P (this half's 64-key block), 8 partial sums.
-        float rs[8];
-#pragma unroll
-        for (int e = 0; e < 8; ++e) rs[e] = 0.f;
+        // Pass 2: p = 2^(s * scale * log2e - m), bf16 P (this half's 64-key block); the scale
+        // and the sums run on packed pairs.
+        const uint64_t sl2x2 = pk2(sl2, sl2), negm2 = pk2(neg_m, neg_m);
+        uint64_t rs2[4] = {0, 0, 0, 0};
 #pragma unroll
         for (int gi = 0; gi < 8; ++gi) {
-          float p[8];
+          uint32_t wv[4];
 #pragma unroll
-          for (int e = 0; e < 8; ++e) {
-            p[e] = ex2(fmaf(__uint_as_float(sv[gi * 8 + e]), sl2, neg_m));
-            rs[e] += p[e];
+          for (int e2 = 0; e2 < 4; ++e2) {
+            const uint64_t x2 = fma2(pk2(__uint_as_float(sv[gi * 8 + 2 * e2]), __uint_as_float(sv[gi * 8 + 2 * e2 + 1])),
+                                     sl2x2, negm2);
+            float x0, x1;
+            up2(x2, x0, x1);
+            const float p0 = ex2(x0), p1 = ex2(x1);
+            rs2[e2] = add2(rs2[e2], pk2(p0, p1));
+            wv[e2] = pack_bf16x2(p0, p1);
           }
-          const uint4 wv = make_uint4(pack_bf16x2(p[0], p[1]), pack_bf16x2(p[2], p[3]), pack_bf16x2(p[4], p[5]),
-                                      pack_bf16x2(p[6], p[7]));
-          *reinterpret_cast<uint4 *>(p_row + ((gi ^ (r & 7)) << 4)) = wv;
+          *reinterpret_cast<uint4 *>(p_row + ((gi ^ (r & 7)) << 4)) = make_uint4(wv[0], wv[1], wv[2], wv[3]);
         }
-        l_run += ((rs[0] + rs[1]) + (rs[2] + rs[3])) + ((rs[4] + rs[5]) + (rs[6] + rs[7]));
+        {
+          const uint64_t s01 = add2(rs2[0], rs2[1]), s23 = add2(rs2[2], rs2[3]);
+          float a0, a1;
+          up2(add2(s01, s23), a0, a1);
+          l_run += a0 + a1;
+        }
         fence_proxy_async_smem();
         tc_fence_before();
-        mbar_arrive(&p_full[t]);
+        arrive(&p_full[t]);
       }
       // Epilogue: O / l (l = sum of both halves), bf16; each half stores 32 columns.
       xl[(t * 2 + half) * 128 + r] = l_run;
