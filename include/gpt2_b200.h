@@ -84,7 +84,9 @@ void _mlir_ciface_gpt2_decoder(MemRef3D *result, MemRef2D_i64 *input_ids, MemRef
 
 enum {
   GPT2_DTYPE_F32 = 0,  /* exact FP32 (SIMT FFMA); logits within 1e-4 of the CPU lowering */
-  GPT2_DTYPE_BF16 = 1  /* BF16 weights and activations, FP32 accumulate and statistics (tcgen05) */
+  GPT2_DTYPE_BF16 = 1, /* BF16 weights and activations, FP32 accumulate and statistics (tcgen05) */
+  GPT2_DTYPE_FP8W = 2  /* as BF16, but the Conv1D weights are E4M3 with a per-output-channel FP32
+                          scale (weight-only FP8); embeddings and the tied lm_head stay BF16 */
 };
 
 typedef struct Gpt2Config {
@@ -130,6 +132,13 @@ int gpt2_init_seeded(uint64_t seed, int init_mode);
 
 /* Fills out[0 .. gpt2_blob_floats(cfg)) with the seeded blob on the host. */
 int gpt2_seeded_blob(const Gpt2Config *cfg, uint64_t seed, int init_mode, float *out);
+
+/* Weight-only FP8 quantization of one Conv1D weight w [K in, N out]:
+ * scale[n] = max_k |w[k,n]| / 448, q[n*K + k] = E4M3(w[k,n] / scale[n])
+ * (round to nearest even, saturating), codes packed [N, K].  The model does
+ * this itself at load time for GPT2_DTYPE_FP8W; exported for callers that
+ * store quantized checkpoints. */
+int gpt2_fp8_quantize(const float *w, int K, int N, uint8_t *q, float *scale);
 
 /* Seeded token ids: ids[i] = floor(w_i * vocab / 2^32), w_i a Philox word. */
 int gpt2_seeded_ids(int64_t *ids, int64_t n, uint64_t seed, uint32_t stream, int64_t vocab);

@@ -28,7 +28,7 @@ HERE = os.path.dirname(os.path.abspath(__file__))
 LIB_PATH = os.path.join(HERE, "libgpt2_b200.so")
 HEADER = os.path.join(os.path.dirname(HERE), "include", "gpt2_b200.h")
 
-DTYPE_F32, DTYPE_BF16 = 0, 1
+DTYPE_F32, DTYPE_BF16, DTYPE_FP8W = 0, 1, 2
 EPI_NONE, EPI_BIAS, EPI_BIAS_GELU, EPI_BIAS_RESID = 0, 1, 2, 3
 STATUS_NAMES = {0: "ok", 1: "token id out of range", 2: "barrier wait timed out", 3: "bad launch"}
 
@@ -111,6 +111,7 @@ def lib() -> ctypes.CDLL:
     L.gpt2_seeded_blob.argtypes = [P(Gpt2Config), ctypes.c_uint64, i32, P(ctypes.c_float)]
     L.gpt2_seeded_ids.argtypes = [P(i64), i64, ctypes.c_uint64, ctypes.c_uint32, i64]
     L.gpt2_get_config.argtypes = [P(Gpt2Config)]
+    L.gpt2_fp8_quantize.argtypes = [P(ctypes.c_float), i32, i32, P(ctypes.c_uint8), P(ctypes.c_float)]
     L.gpt2_shutdown.restype = None
     L.gpt2_last_error.restype = ctypes.c_char_p
     L.gpt2_forward_device.argtypes = [vp, vp, i32, i32, vp, i64, i32, vp]
@@ -177,6 +178,23 @@ def seeded_ids(B: int, S: int, seed: int, vocab: int, stream: int = 0x10000) -> 
     _check(lib().gpt2_seeded_ids(out.ctypes.data_as(ctypes.POINTER(ctypes.c_int64)), B * S, seed, stream, vocab),
            "gpt2_seeded_ids")
     return out.reshape(B, S)
+
+
+def fp8_quantize(w: np.ndarray):
+    """Conv1D weight w [K, N] -> (q [N, K] E4M3 codes, scale [N]) as the model quantizes it."""
+    w = np.ascontiguousarray(w, dtype=np.float32)
+    K, N = w.shape
+    q = np.empty((N, K), dtype=np.uint8)
+    sc = np.empty(N, dtype=np.float32)
+    _check(lib().gpt2_fp8_quantize(w.ctypes.data_as(ctypes.POINTER(ctypes.c_float)), K, N,
+                                   q.ctypes.data_as(ctypes.POINTER(ctypes.c_uint8)),
+                                   sc.ctypes.data_as(ctypes.POINTER(ctypes.c_float))), "gpt2_fp8_quantize")
+    return q, sc
+
+
+def gpt2_xl(dtype: int = DTYPE_FP8W) -> Gpt2Config:
+    """GPT-2 XL shape: 48 layers, d 1600, 25 heads of 64, MLP 6400, vocab 50257, ctx 1024."""
+    return Gpt2Config(48, 1600, 25, 6400, 50257, 1024, 1e-5, dtype)
 
 
 def load_weights(blob: np.ndarray, manifest: str | None = None) -> None:

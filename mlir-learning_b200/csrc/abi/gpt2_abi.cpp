@@ -62,6 +62,7 @@ int ensure_default_model_locked() {
     int dtype = GPT2_DTYPE_F32;
     if (const char *e = getenv("GPT2_DTYPE")) {
       if (!strcmp(e, "bf16")) dtype = GPT2_DTYPE_BF16;
+      else if (!strcmp(e, "fp8w")) dtype = GPT2_DTYPE_FP8W;
       else if (strcmp(e, "f32") && strcmp(e, "fp32")) {
         set_error("GPT2_DTYPE must be f32 or bf16, got '%s'", e);
         return GPT2_EINVAL;
@@ -278,6 +279,12 @@ int gpt2_init_seeded(uint64_t seed, int init_mode) {
 int gpt2_seeded_blob(const Gpt2Config *cfg, uint64_t seed, int init_mode, float *out) {
   if (!valid_dims(cfg) || !out || (init_mode != 0 && init_mode != 1)) return GPT2_EINVAL;
   seeded_blob(dims_of(cfg), seed, init_mode, out);
+  return 0;
+}
+
+int gpt2_fp8_quantize(const float *w, int K, int N, uint8_t *q, float *scale) {
+  if (!w || !q || !scale || K < 1 || N < 1) return GPT2_EINVAL;
+  fp8_quantize(w, K, N, q, scale);
   return 0;
 }
 

@@ -77,8 +77,11 @@ int tc_gemm_plan(TcGemmPlan *plan, const bf16 *A, const bf16 *B, int M, int N, i
 // when C is 16-byte aligned and ldc * element size is a multiple of 16;
 // otherwise the kernel falls back to direct stores.  Returns has_c.
 int tc_gemm_set_output(TcGemmPlan *plan, const void *C, int ldc, int out_f32);
+// scale (optional, [N]): per-output-column factor applied to the accumulator
+// before the epilogue (weight-only FP8 dequantization).
 cudaError_t launch_gemm_tc(const TcGemmPlan &plan, void *C, int ldc, int out_f32, const float *bias,
-                           const bf16 *resid, int epi, int *status, int num_sms, cudaStream_t st);
+                           const bf16 *resid, int epi, int *status, int num_sms, cudaStream_t st,
+                           const float *scale = nullptr);
 
 // ---- attention ----------------------------------------------------------------
 // qkv [B*S, 3*H*64] (q | k | v, head h at columns h*64), o [B*S, H*64].
@@ -104,6 +107,8 @@ cudaError_t launch_attn_masked_rows_bf16(const bf16 *qkv, const int *first_valid
                                          cudaStream_t st);
 
 // ---- weight packing --------------------------------------------------------
+// dst[i] = bf16(decode_e4m3(src[i])), exact (every E4M3 value is a BF16 value).
+cudaError_t launch_e4m3_to_bf16(const uint8_t *src, bf16 *dst, int64_t n, cudaStream_t st);
 // dst[N, K] (bf16) = transpose(src[K, N] fp32); dst[r, c] = bf16(src[r, c]) when transpose == 0.
 cudaError_t launch_pack_bf16(const float *src, bf16 *dst, int rows, int cols, int transpose, cudaStream_t st);
 

@@ -277,6 +277,21 @@ __global__ void pack_bf16_kernel(const float *__restrict__ src, bf16 *__restrict
   }
 }
 
+__global__ void e4m3_to_bf16_kernel(const uint8_t *__restrict__ src, bf16 *__restrict__ dst, int64_t n) {
+  for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < n; i += (int64_t)gridDim.x * blockDim.x) {
+    const uint32_t q = src[i];
+    const int e = (q >> 3) & 0xF, m = q & 7;
+    // E4M3 value: m * 2^-9 (e == 0) or (1 + m/8) * 2^(e-7); both exact in float and bf16
+    const float v = e == 0 ? m * (1.0f / 512.0f) : __int_as_float(((e + 120) << 23) | (m << 20));
+    dst[i] = __float2bfloat16_rn((q & 0x80) ? -v : v);
+  }
+}
+
+cudaError_t launch_e4m3_to_bf16(const uint8_t *src, bf16 *dst, int64_t n, cudaStream_t st) {
+  e4m3_to_bf16_kernel<<<1184, 256, 0, st>>>(src, dst, n);
+  return cudaGetLastError();
+}
+
 cudaError_t launch_pack_bf16(const float *src, bf16 *dst, int rows, int cols, int transpose, cudaStream_t st) {
   dim3 grid((cols + 31) / 32, (rows + 31) / 32), block(32, 8);
   pack_bf16_kernel<<<grid, block, 0, st>>>(src, dst, rows, cols, transpose);

@@ -63,7 +63,8 @@ template <int BN, int EPI, int OUT_F32, int TMA_STORE>
 __global__ void __launch_bounds__(NTHREADS, 1)
     gemm_tc_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constant__ CUtensorMap map_b,
                    const __grid_constant__ CUtensorMap map_c, void *C, int ldc, int M, int N, int K,
-                   const float *__restrict__ bias, const bf16 *resid, int *status) {
+                   const float *__restrict__ bias, const bf16 *resid, int *status,
+                   const float *__restrict__ scale) {
   using Cfg = TcCfg<BN>;
   constexpr int STAGES = Cfg::STAGES;
   extern __shared__ unsigned char smem_raw[];
@@ -215,6 +216,13 @@ __global__ void __launch_bounds__(NTHREADS, 1)
           mbar_arrive(&tempty[acc]);
         }
         float *v = reinterpret_cast<float *>(r);  // epilogue in place
+        if (scale) {  // weight-only FP8: per-output-column dequantization scale
+          const float s_lo = (col0 + lane < N) ? scale[col0 + lane] : 0.f;
+          const float s_hi = (CH == 64 && col0 + 32 + lane < N) ? scale[col0 + 32 + lane] : 0.f;
+#pragma unroll
+          for (int j = 0; j < CH; ++j)
+            r[j] = __float_as_uint(__uint_as_float(r[j]) * __shfl_sync(0xffffffffu, j < 32 ? s_lo : s_hi, j & 31));
+        }
         float bias_lo = 0.f, bias_hi = 0.f;
         if (EPI != EPI_NONE) {
           bias_lo = (col0 + lane < N) ? bias[col0 + lane] : 0.f;
@@ -353,7 +361,7 @@ int make_map_out(CUtensorMap *map, const void *base, int64_t rows, int64_t cols,
 
 template <int BN, int EPI, int OUT_F32, int TMA_STORE>
 cudaError_t launch_variant(const TcGemmPlan &p, void *C, int ldc, const float *bias, const bf16 *resid, int *status,
-                           int num_sms, cudaStream_t st) {
+                           int num_sms, cudaStream_t st, const float *scale) {
   using Cfg = TcCfg<BN>;
   static std::atomic<uint64_t> attr_done{0};
   cudaError_t e = set_smem_once(gemm_tc_kernel<BN, EPI, OUT_F32, TMA_STORE>, Cfg::SMEM_BYTES, attr_done);
@@ -361,31 +369,31 @@ cudaError_t launch_variant(const TcGemmPlan &p, void *C, int ldc, const float *b
   const int tiles = ((p.M + BM - 1) / BM) * ((p.N + BN - 1) / BN);
   const int grid = tiles < num_sms ? tiles : num_sms;
   gemm_tc_kernel<BN, EPI, OUT_F32, TMA_STORE><<<grid, NTHREADS, Cfg::SMEM_BYTES, st>>>(
-      p.map_a, p.map_b, p.map_c, C, ldc, p.M, p.N, p.K, bias, resid, status);
+      p.map_a, p.map_b, p.map_c, C, ldc, p.M, p.N, p.K, bias, resid, status, scale);
   return cudaGetLastError();
 }
 
 template <int BN, int EPI, int OUT_F32>
 cudaError_t launch_store(const TcGemmPlan &p, void *C, int ldc, const float *bias, const bf16 *resid, int *status,
-                         int num_sms, cudaStream_t st) {
+                         int num_sms, cudaStream_t st, const float *scale) {
   const bool tma = p.has_c && p.c_ptr == C && p.c_ld == ldc && p.c_f32 == OUT_F32;
-  if (tma) return launch_variant<BN, EPI, OUT_F32, 1>(p, C, ldc, bias, resid, status, num_sms, st);
-  return launch_variant<BN, EPI, OUT_F32, 0>(p, C, ldc, bias, resid, status, num_sms, st);
+  if (tma) return launch_variant<BN, EPI, OUT_F32, 1>(p, C, ldc, bias, resid, status, num_sms, st, scale);
+  return launch_variant<BN, EPI, OUT_F32, 0>(p, C, ldc, bias, resid, status, num_sms, st, scale);
 }
 
 template <int BN>
 cudaError_t dispatch_epi(const TcGemmPlan &p, void *C, int ldc, int out_f32, const float *bias, const bf16 *resid,
-                         int epi, int *status, int num_sms, cudaStream_t st) {
+                         int epi, int *status, int num_sms, cudaStream_t st, const float *scale) {
   if (out_f32) {
-    if (epi == EPI_NONE) return launch_store<BN, EPI_NONE, 1>(p, C, ldc, bias, resid, status, num_sms, st);
-    if (epi == EPI_BIAS) return launch_store<BN, EPI_BIAS, 1>(p, C, ldc, bias, resid, status, num_sms, st);
+    if (epi == EPI_NONE) return launch_store<BN, EPI_NONE, 1>(p, C, ldc, bias, resid, status, num_sms, st, scale);
+    if (epi == EPI_BIAS) return launch_store<BN, EPI_BIAS, 1>(p, C, ldc, bias, resid, status, num_sms, st, scale);
     return cudaErrorInvalidValue;
   }
   switch (epi) {
-    case EPI_NONE: return launch_store<BN, EPI_NONE, 0>(p, C, ldc, bias, resid, status, num_sms, st);
-    case EPI_BIAS: return launch_store<BN, EPI_BIAS, 0>(p, C, ldc, bias, resid, status, num_sms, st);
-    case EPI_BIAS_GELU: return launch_store<BN, EPI_BIAS_GELU, 0>(p, C, ldc, bias, resid, status, num_sms, st);
-    case EPI_BIAS_RESID: return launch_store<BN, EPI_BIAS_RESID, 0>(p, C, ldc, bias, resid, status, num_sms, st);
+    case EPI_NONE: return launch_store<BN, EPI_NONE, 0>(p, C, ldc, bias, resid, status, num_sms, st, scale);
+    case EPI_BIAS: return launch_store<BN, EPI_BIAS, 0>(p, C, ldc, bias, resid, status, num_sms, st, scale);
+    case EPI_BIAS_GELU: return launch_store<BN, EPI_BIAS_GELU, 0>(p, C, ldc, bias, resid, status, num_sms, st, scale);
+    case EPI_BIAS_RESID: return launch_store<BN, EPI_BIAS_RESID, 0>(p, C, ldc, bias, resid, status, num_sms, st, scale);
   }
   return cudaErrorInvalidValue;
 }
@@ -413,13 +421,14 @@ int tc_gemm_set_output(TcGemmPlan *plan, const void *C, int ldc, int out_f32) {
 }
 
 cudaError_t launch_gemm_tc(const TcGemmPlan &plan, void *C, int ldc, int out_f32, const float *bias,
-                           const bf16 *resid, int epi, int *status, int num_sms, cudaStream_t st) {
+                           const bf16 *resid, int epi, int *status, int num_sms, cudaStream_t st,
+                           const float *scale) {
   if (ldc < plan.N || num_sms <= 0) return cudaErrorInvalidValue;
   if (!out_f32 && ldc % 8) return cudaErrorInvalidValue;
   if (epi != EPI_NONE && !bias) return cudaErrorInvalidValue;
   if (epi == EPI_BIAS_RESID && !resid) return cudaErrorInvalidValue;
-  if (plan.bn == 256) return dispatch_epi<256>(plan, C, ldc, out_f32, bias, resid, epi, status, num_sms, st);
-  return dispatch_epi<128>(plan, C, ldc, out_f32, bias, resid, epi, status, num_sms, st);
+  if (plan.bn == 256) return dispatch_epi<256>(plan, C, ldc, out_f32, bias, resid, epi, status, num_sms, st, scale);
+  return dispatch_epi<128>(plan, C, ldc, out_f32, bias, resid, epi, status, num_sms, st, scale);
 }
 
 }  // namespace gpt2

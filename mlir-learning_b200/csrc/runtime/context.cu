@@ -122,8 +122,9 @@ void destroy_context() {
   if (c->wte_h) cudaFree(c->wte_h);
   if (c->wpe_h) cudaFree(c->wpe_h);
   for (auto &l : c->layers) {
-    bf16 *p[] = {l.qkv_wt, l.proj_wt, l.fc_wt, l.mproj_wt};
-    for (bf16 *q : p)
+    void *p[] = {l.qkv_wt, l.proj_wt, l.fc_wt, l.mproj_wt, l.qkv_q, l.proj_q, l.fc_q, l.mproj_q,
+                 l.qkv_s, l.proj_s, l.fc_s, l.mproj_s};
+    for (void *q : p)
       if (q) cudaFree(q);
   }
   if (c->d_status) cudaFree(c->d_status);
@@ -138,7 +139,7 @@ int create_context(const ModelDims &m, int dtype, int device) {
     set_error("unsupported GPT-2 configuration (need n_embd %% 64 == 0, head dim 64, n_inner %% 64 == 0)");
     return -1;
   }
-  if (dtype != 0 && dtype != 1) {
+  if (dtype < 0 || dtype > 2) {
     set_error("unsupported dtype %d", dtype);
     return -1;
   }
@@ -193,23 +194,53 @@ int load_blob(Context &c, const float *host_blob) {
     w.mproj_w = at(b + MPROJ_W);
     w.mproj_b = at(b + MPROJ_B);
   }
-  if (c.dtype == 1) {
+  if (c.dtype >= 1) {
     // BF16 copies: wte / wpe as stored ([V, d] is already the K-major B of the
     // lm_head), Conv1D weights transposed to [out, in] (K-major B operands).
     if (!c.wte_h) CK(cudaMalloc(&c.wte_h, sizeof(bf16) * (size_t)m.vocab * d));
     if (!c.wpe_h) CK(cudaMalloc(&c.wpe_h, sizeof(bf16) * (size_t)m.n_pos * d));
     CK(launch_pack_bf16(c.wte, c.wte_h, m.vocab, d, 0, c.stream));
     CK(launch_pack_bf16(c.wpe, c.wpe_h, m.n_pos, d, 0, c.stream));
+    std::vector<uint8_t> hq;
+    std::vector<float> hs;
     for (int l = 0; l < m.n_layer; ++l) {
       LayerWeights &w = c.layers[l];
       if (!w.qkv_wt) CK(cudaMalloc(&w.qkv_wt, sizeof(bf16) * (size_t)d * 3 * d));
       if (!w.proj_wt) CK(cudaMalloc(&w.proj_wt, sizeof(bf16) * (size_t)d * d));
       if (!w.fc_wt) CK(cudaMalloc(&w.fc_wt, sizeof(bf16) * (size_t)d * ff));
       if (!w.mproj_wt) CK(cudaMalloc(&w.mproj_wt, sizeof(bf16) * (size_t)ff * d));
-      CK(launch_pack_bf16(w.qkv_w, w.qkv_wt, d, 3 * d, 1, c.stream));
-      CK(launch_pack_bf16(w.proj_w, w.proj_wt, d, d, 1, c.stream));
-      CK(launch_pack_bf16(w.fc_w, w.fc_wt, d, ff, 1, c.stream));
-      CK(launch_pack_bf16(w.mproj_w, w.mproj_wt, ff, d, 1, c.stream));
+      if (c.dtype == 1) {
+        CK(launch_pack_bf16(w.qkv_w, w.qkv_wt, d, 3 * d, 1, c.stream));
+        CK(launch_pack_bf16(w.proj_w, w.proj_wt, d, d, 1, c.stream));
+        CK(launch_pack_bf16(w.fc_w, w.fc_wt, d, ff, 1, c.stream));
+        CK(launch_pack_bf16(w.mproj_w, w.mproj_wt, ff, d, 1, c.stream));
+        continue;
+      }
+      // Weight-only FP8: quantize on the host (per-output-channel scale), keep
+      // the E4M3 codes and scales resident, expand the codes exactly to the
+      // BF16 operands; the GEMM epilogue applies the scale.
+      const size_t b = 2 + PER_LAYER * l;
+      struct {
+        size_t idx;
+        int K, N;
+        uint8_t **q;
+        float **sc;
+        bf16 *wt;
+      } mats[4] = {{b + QKV_W, d, 3 * d, &w.qkv_q, &w.qkv_s, w.qkv_wt},
+                   {b + PROJ_W, d, d, &w.proj_q, &w.proj_s, w.proj_wt},
+                   {b + FC_W, d, ff, &w.fc_q, &w.fc_s, w.fc_wt},
+                   {b + MPROJ_W, ff, d, &w.mproj_q, &w.mproj_s, w.mproj_wt}};
+      for (auto &mt : mats) {
+        const size_t n = (size_t)mt.K * mt.N;
+        hq.resize(n);
+        hs.resize(mt.N);
+        fp8_quantize(host_blob + s[mt.idx].offset, mt.K, mt.N, hq.data(), hs.data());
+        if (!*mt.q) CK(cudaMalloc(mt.q, n));
+        if (!*mt.sc) CK(cudaMalloc(mt.sc, sizeof(float) * mt.N));
+        CK(cudaMemcpy(*mt.q, hq.data(), n, cudaMemcpyHostToDevice));
+        CK(cudaMemcpy(*mt.sc, hs.data(), sizeof(float) * mt.N, cudaMemcpyHostToDevice));
+        CK(launch_e4m3_to_bf16(*mt.q, mt.wt, (int64_t)n, c.stream));
+      }
     }
     CK(cudaStreamSynchronize(c.stream));
   }
@@ -232,7 +263,7 @@ int ensure_workspace(Context &c, int B, int S) {
   free_ws(w);
   w.logits = keep_logits.logits;
   w.logits_T = keep_logits.logits_T;
-  const size_t es = c.dtype == 1 ? 2 : 4;
+  const size_t es = c.dtype >= 1 ? 2 : 4;
   const int64_t d = c.dims.n_embd, ff = c.dims.n_inner;
   CK(cudaMalloc(&w.x, es * Tn * d));
   CK(cudaMalloc(&w.a, es * Tn * d));
@@ -390,13 +421,14 @@ int forward_device(Context &c, const int64_t *d_ids, const int64_t *d_mask, int 
     const LayerWeights &lw = c.layers[l];
     const TcGemmPlan *p = &c.plans[4 * l];
     CKP(K_LAYERNORM, launch_layernorm_bf16(x, lw.ln1_g, lw.ln1_b, a, (int)T, d, m.eps, st));
-    CKP(K_GEMM_QKV, launch_gemm_tc(p[0], qkv, 3 * d, 0, lw.qkv_b, nullptr, EPI_BIAS, c.d_status, ns, st));
+    CKP(K_GEMM_QKV, launch_gemm_tc(p[0], qkv, 3 * d, 0, lw.qkv_b, nullptr, EPI_BIAS, c.d_status, ns, st, lw.qkv_s));
     CKP(K_ATTENTION, launch_attention_tc(c.attn_plan, kv, o, c.d_status, st));
     if (d_mask) CKP(K_MASKED_ROWS, launch_attn_masked_rows_bf16(qkv, w.first_valid, o, B, S, H, st));
-    CKP(K_GEMM_PROJ, launch_gemm_tc(p[1], x, d, 0, lw.proj_b, x, EPI_BIAS_RESID, c.d_status, ns, st));
+    CKP(K_GEMM_PROJ, launch_gemm_tc(p[1], x, d, 0, lw.proj_b, x, EPI_BIAS_RESID, c.d_status, ns, st, lw.proj_s));
     CKP(K_LAYERNORM, launch_layernorm_bf16(x, lw.ln2_g, lw.ln2_b, a, (int)T, d, m.eps, st));
-    CKP(K_GEMM_FC, launch_gemm_tc(p[2], u, ff, 0, lw.fc_b, nullptr, EPI_BIAS_GELU, c.d_status, ns, st));
-    CKP(K_GEMM_MPROJ, launch_gemm_tc(p[3], x, d, 0, lw.mproj_b, x, EPI_BIAS_RESID, c.d_status, ns, st));
+    CKP(K_GEMM_FC, launch_gemm_tc(p[2], u, ff, 0, lw.fc_b, nullptr, EPI_BIAS_GELU, c.d_status, ns, st, lw.fc_s));
+    CKP(K_GEMM_MPROJ,
+        launch_gemm_tc(p[3], x, d, 0, lw.mproj_b, x, EPI_BIAS_RESID, c.d_status, ns, st, lw.mproj_s));
   }
   CKP(K_LAYERNORM, launch_layernorm_bf16(x, c.lnf_g, c.lnf_b, a, (int)T, d, m.eps, st));
   TcGemmPlan &head = c.plans[4 * m.n_layer];

@@ -36,11 +36,18 @@ void seeded_normal(float *out, int64_t n, uint64_t seed, uint32_t stream, double
 void seeded_ids(int64_t *ids, int64_t n, uint64_t seed, uint32_t stream, int64_t vocab);
 void seeded_blob(const ModelDims &m, uint64_t seed, int init_mode, float *blob);
 
+// Weight-only FP8: w [K, N] (Conv1D) -> q [N, K] E4M3 codes and scale [N].
+uint8_t e4m3_encode(float x);
+void fp8_quantize(const float *w, int K, int N, uint8_t *q, float *scale);
+
 // Device copies of the weights, in the layouts the kernels read.
 struct LayerWeights {
   const float *ln1_g, *ln1_b, *qkv_b, *proj_b, *ln2_g, *ln2_b, *fc_b, *mproj_b;  // FP32, in blob
   const float *qkv_w, *proj_w, *fc_w, *mproj_w;                                  // FP32 [in, out], in blob
   bf16 *qkv_wt, *proj_wt, *fc_wt, *mproj_wt;                                     // BF16 [out, in]
+  // weight-only FP8: E4M3 codes [out, in] and per-output-channel scales
+  uint8_t *qkv_q = nullptr, *proj_q = nullptr, *fc_q = nullptr, *mproj_q = nullptr;
+  float *qkv_s = nullptr, *proj_s = nullptr, *fc_s = nullptr, *mproj_s = nullptr;
 };
 
 // Activation buffers of one forward, grown on demand.

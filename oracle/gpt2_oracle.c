@@ -251,6 +251,80 @@ int oracle_seeded_blob(const OracleCfg *c, uint64_t seed, int init_mode, float *
 
 
 /* ------------------------------------------------------------------------- */
+/* FP8 E4M3 weight quantization (the weight-only FP8 configuration)           */
+/* ------------------------------------------------------------------------- */
+
+/* float -> E4M3 code (1 sign, 4 exponent bits with bias 7, 3 mantissa bits;
+ * largest finite 448, no infinities), round to nearest even on the float's
+ * bits, saturating at 448.  Subnormals are steps of 2^-9. */
+uint8_t oracle_e4m3_encode(float x) {
+  uint32_t b;
+  memcpy(&b, &x, 4);
+  const uint8_t sign = (uint8_t)((b >> 24) & 0x80);
+  const uint32_t ab = b & 0x7FFFFFFF;
+  float a;
+  memcpy(&a, &ab, 4);
+  if (!(a == a)) return (uint8_t)(sign | 0x7E); /* NaN input: saturate (not produced by the quantizer) */
+  if (a >= 448.0f) return (uint8_t)(sign | 0x7E);
+  int e = (int)((ab >> 23) & 0xFF) - 127;
+  if (e >= -6) {
+    uint32_t r = (ab & 0x7FFFFF) >> 20, rem = ab & 0xFFFFF;
+    if (rem > 0x80000 || (rem == 0x80000 && (r & 1))) ++r;
+    if (r == 8) { r = 0; ++e; }
+    if (e > 8 || (e == 8 && r == 7)) { e = 8; r = 6; }
+    return (uint8_t)(sign | ((uint32_t)(e + 7) << 3) | r);
+  }
+  /* subnormal range: a / 2^-9 rounded to nearest even (0..8; 8 is the smallest normal) */
+  const float u = a * 512.0f;
+  float n = rintf(u); /* the default rounding mode is round to nearest even */
+  return (uint8_t)(sign | (uint8_t)n);
+}
+
+float oracle_e4m3_decode(uint8_t q) {
+  const int e = (q >> 3) & 0xF, m = q & 7;
+  const float v = e == 0 ? ldexpf((float)m, -9) : ldexpf(1.0f + m / 8.0f, e - 7);
+  return (q & 0x80) ? -v : v;
+}
+
+/* Conv1D weight w [K in, N out]: per output channel n, scale[n] = max_k |w[k,n]| / 448
+ * and q[n*K + k] = e4m3(w[k,n] / scale[n]) (packed [N, K]).  A zero column gets scale 1. */
+void oracle_fp8_quantize(const float *w, int K, int N, uint8_t *q, float *scale) {
+  for (int n = 0; n < N; ++n) {
+    float mx = 0.f;
+    for (int k = 0; k < K; ++k) { const float a = fabsf(w[(int64_t)k * N + n]); if (a > mx) mx = a; }
+    const float sc = mx > 0.f ? mx / 448.0f : 1.0f;
+    scale[n] = sc;
+    for (int k = 0; k < K; ++k) q[(int64_t)n * K + k] = oracle_e4m3_encode(w[(int64_t)k * N + n] / sc);
+  }
+}
+
+/* Replaces the four Conv1D weights of every layer of a canonical blob by their
+ * FP8-dequantized values e4m3_decode(q) * scale, in place. */
+int oracle_fp8_dequantize_blob(const OracleCfg *c, float *blob) {
+  int64_t *off = (int64_t *)malloc(sizeof(int64_t) * (oracle_num_tensors(c) + 1));
+  if (!off) return -3;
+  oracle_blob_layout(c, off);
+  const int d = c->n_embd, ff = c->n_inner;
+  const int kinds[4] = {T_QKV_W, T_PROJ_W, T_FC_W, T_MPROJ_W};
+  for (int l = 0; l < c->n_layer; ++l)
+    for (int i = 0; i < 4; ++i) {
+      const int K = kinds[i] == T_MPROJ_W ? ff : d;
+      const int N = kinds[i] == T_QKV_W ? 3 * d : kinds[i] == T_FC_W ? ff : d;
+      float *w = blob + off[2 + T_PER_LAYER * l + kinds[i]];
+      uint8_t *q = (uint8_t *)malloc((size_t)K * N);
+      float *sc = (float *)malloc(sizeof(float) * N);
+      if (!q || !sc) { free(q); free(sc); free(off); return -3; }
+      oracle_fp8_quantize(w, K, N, q, sc);
+      for (int k = 0; k < K; ++k)
+        for (int n = 0; n < N; ++n) w[(int64_t)k * N + n] = oracle_e4m3_decode(q[(int64_t)n * K + k]) * sc[n];
+      free(q);
+      free(sc);
+    }
+  free(off);
+  return 0;
+}
+
+/* ------------------------------------------------------------------------- */
 /* sgemm: OpenBLAS through dlopen (as the reference's -lopenblas link), or a  */
 /* blocked fallback.  Row-major C[M,N] = A[M,K] * op(B).                      */
 /* ------------------------------------------------------------------------- */

@@ -114,6 +114,13 @@ def lib():
     L.oracle_gpt2_forward.argtypes = [P(OracleCfg), P(ctypes.c_float), P(ctypes.c_int64), P(ctypes.c_int64),
                                       ctypes.c_int, ctypes.c_int, P(ctypes.c_float)]
     L.oracle_gpt2_forward.restype = ctypes.c_int
+    L.oracle_e4m3_encode.argtypes = [ctypes.c_float]
+    L.oracle_e4m3_encode.restype = ctypes.c_uint8
+    L.oracle_e4m3_decode.argtypes = [ctypes.c_uint8]
+    L.oracle_e4m3_decode.restype = ctypes.c_float
+    L.oracle_fp8_quantize.argtypes = [P(ctypes.c_float), ctypes.c_int, ctypes.c_int, P(ctypes.c_uint8), P(ctypes.c_float)]
+    L.oracle_fp8_dequantize_blob.argtypes = [P(OracleCfg), P(ctypes.c_float)]
+    L.oracle_fp8_dequantize_blob.restype = ctypes.c_int
     blas = os.environ.get("ORACLE_BLAS", None)
     if blas is None:
         blas = find_openblas() or ""
@@ -181,6 +188,28 @@ def tensor_names(shape: ModelShape) -> list[str]:
         names += [f"transformer.h.{l}.{p}" for p in per]
     names += ["transformer.ln_f.weight", "transformer.ln_f.bias"]
     return names
+
+
+# GPT-2 XL-shaped model of the weight-only FP8 configuration.
+GPT2_XL = ModelShape(n_layer=48, n_embd=1600, n_head=25, n_inner=6400)
+
+
+def fp8_quantize(w: np.ndarray):
+    """Conv1D weight w [K, N] -> (q [N, K] uint8 E4M3 codes, scale [N])."""
+    w = np.ascontiguousarray(w, dtype=np.float32)
+    K, N = w.shape
+    q = np.empty((N, K), dtype=np.uint8)
+    sc = np.empty(N, dtype=np.float32)
+    lib().oracle_fp8_quantize(_ptr(w, ctypes.c_float), K, N, _ptr(q, ctypes.c_uint8), _ptr(sc, ctypes.c_float))
+    return q, sc
+
+
+def fp8_dequantized_blob(shape: ModelShape, blob: np.ndarray) -> np.ndarray:
+    """Copy of the blob whose Conv1D weights are replaced by their FP8-dequantized values."""
+    out = np.array(blob, dtype=np.float32, copy=True)
+    c = shape.c()
+    assert lib().oracle_fp8_dequantize_blob(ctypes.byref(c), _ptr(out, ctypes.c_float)) == 0
+    return out
 
 
 def forward(shape: ModelShape, blob: np.ndarray, ids: np.ndarray, mask: np.ndarray | None = None,

@@ -1,0 +1,72 @@
+"""Weight-only FP8 configuration (GPT-2 XL shape: d 1600, 25 heads of 64,
+MLP 6400; E4M3 Conv1D weights with per-output-channel scales, BF16
+activations, tied BF16 lm_head) on the GPU, through the C ABI.
+
+Two comparisons with the oracle on the same inputs:
+  * against the oracle run on the FP8-dequantized weights, which isolates the
+    kernels: the BF16 bound (BF16_RTOL of max |logit|) and top-5 identity;
+  * against the oracle on the original FP32 weights (the reference's own
+    computation): FP8_RTOL of max |logit|, and top-5 identity wherever the
+    oracle's top-5 is separated by more than twice that bound."""
+import numpy as np
+import pytest
+
+from helpers import load_oracle, load_pkg, shape_to_cfg, top5_agreement
+
+pytestmark = pytest.mark.gpu
+pkg = load_pkg()
+O = load_oracle()
+
+BF16_RTOL = 0.03
+FP8_RTOL = 0.10
+
+
+@pytest.fixture(scope="module")
+def torch():
+    import torch as t
+    assert t.cuda.is_available(), "GPU tests need a CUDA device"
+    t.cuda.set_device(0)
+    return t
+
+
+def _check(ref, got, rtol, label):
+    scale = float(np.abs(ref).max())
+    err = float(np.abs(got - ref).max())
+    bound = rtol * scale
+    checked, agree, total = top5_agreement(ref, got, bound)
+    print(f"{label}: max|diff| {err:.4g} (rel {err / scale:.4g}, bound {rtol}); top-5 checked {checked}/{total}, "
+          f"identical {agree}")
+    assert err <= bound, (err, bound)
+    assert agree == checked
+
+
+def _run(shape, seed, B, S, masked):
+    blob = O.seeded_blob(shape, seed, 1)
+    ids = O.token_ids(B, S, seed, shape.vocab_size)
+    mask = np.ones_like(ids)
+    if masked and B > 1:
+        mask[1, :9] = 0
+    O.set_loop_threads(8)
+    ref_q = O.forward(shape, O.fp8_dequantized_blob(shape, blob), ids, mask)
+    ref_f = O.forward(shape, blob, ids, mask)
+    O.set_loop_threads(1)
+    pkg.init(shape_to_cfg(pkg, shape, pkg.DTYPE_FP8W), 0)
+    pkg.load_weights(blob)
+    got = pkg.gpt2_decoder(ids, mask)
+    rows = np.cumsum(mask != 0, axis=1) > 0
+    return ref_q[rows], ref_f[rows], got[rows]
+
+
+def test_fp8w_xl_shape_two_layers(torch):
+    shape = O.ModelShape(n_layer=2, n_embd=1600, n_head=25, n_inner=6400)
+    ref_q, ref_f, got = _run(shape, 4321, 2, 200, True)
+    _check(ref_q, got, BF16_RTOL, "fp8w XL-shape L2 vs oracle on dequantized weights")
+    _check(ref_f, got, FP8_RTOL, "fp8w XL-shape L2 vs oracle on FP32 weights")
+
+
+def test_fp8w_gpt2_xl_48_layers(torch):
+    """Config 4's model (GPT-2 XL shape, 48 layers) on one short sequence."""
+    ref_q, ref_f, got = _run(O.GPT2_XL, 2024, 1, 128, False)
+    _check(ref_q, got, BF16_RTOL, "fp8w GPT-2 XL vs oracle on dequantized weights")
+    _check(ref_f, got, FP8_RTOL, "fp8w GPT-2 XL vs oracle on FP32 weights")
+    pkg.shutdown()
