@@ -33,8 +33,18 @@ import numpy as np
 
 ROOT = os.path.dirname(os.path.abspath(__file__))
 SEED = 1234
-D, FF, V, L, H, DH = 768, 3072, 50257, 12, 12, 64
+V, DH = 50257, 64
 LD_LOGITS = 50304  # row stride of the resident logits (16-byte aligned rows)
+
+# The workloads of the reference's configurations that run through this path:
+# (name, layers, d_model, heads, d_mlp, dtype code, dtype label, global batch, seq).
+CONFIGS = {
+    1: ("gpt2-small FP32 prefill B8xS1024 (config 1)", 12, 768, 12, 3072, 0, "f32", 8, 1024),
+    2: ("gpt2-small BF16 prefill B64xS1024 (config 2)", 12, 768, 12, 3072, 1, "bf16", 64, 1024),
+    4: ("gpt2-xl-shape FP8 weight-only prefill B32xS1024 (config 4)", 48, 1600, 25, 6400, 2, "fp8w-e4m3/bf16", 32,
+        1024),
+}
+L, D, H, FF = 12, 768, 12, 3072  # set from the chosen configuration in main()
 
 
 def _pkg():
@@ -154,15 +164,17 @@ class ClockSampler:
                 "samples": len(sm)}
 
 
-def cpu_reference_rate(S: int, n_seq: int = 1):
+def cpu_reference_rate(S: int, n_seq: int = 1, fp8: bool = False):
     """The oracle (the reference's CPU lowering restated in C: OpenBLAS sgemm for the 2-D
     matmuls on all cores, single-threaded loop nests for the rest) on n_seq sequences of S
     tokens of the workload; returns (tokens/s, seconds, cores)."""
     O = _oracle()
     O.build()
     O.set_loop_threads(1)
-    shape = O.GPT2_SMALL
+    shape = O.ModelShape(n_layer=L, n_embd=D, n_head=H, n_inner=FF)
     blob = O.seeded_blob(shape, SEED, 0)
+    if fp8:
+        blob = O.fp8_dequantized_blob(shape, blob)
     ids = O.token_ids(64, S, SEED, shape.vocab_size)[:n_seq]
     out = np.empty((n_seq, S, shape.vocab_size), dtype=np.float32)
     t0 = time.perf_counter()
@@ -177,7 +189,7 @@ def run_reference(args, rank, world):
     S = args.seq
     rates = []
     for i in range(args.warmup + args.steps):
-        r, dt, cores = cpu_reference_rate(S)
+        r, dt, cores = cpu_reference_rate(S, fp8=args.config == 4)
         if i >= args.warmup:
             rates.append((r, dt))
     total_tokens = S * len(rates)
@@ -190,7 +202,7 @@ def run_reference(args, rank, world):
         "value": value, "unit": "tokens/s", "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
         "ms_per_step": 1000.0 * total_s / len(rates), "higher_is_better": True, "scaling": "strong",
         "vs_baseline": None, "dtype": "f32", "data": "synthetic (seeded Philox weights N(0,0.02), uniform ids)",
-        "config": {"workload": "gpt2-small prefill B64xS1024 (config 2)", "global_batch": 64, "seq_len": S,
+        "config": {"workload": CONFIGS[args.config][0], "global_batch": args.batch, "seq_len": S,
                    "sample_per_step": f"1 sequence x {S} tokens"},
         "cpu_baseline": {"value": value, "unit": "tokens/s", "cores": cores, "kind": "port",
                          "sample": f"1 x {S} tokens per step; OpenBLAS sgemm ({O.blas_name().split('/')[-1]}) on "
@@ -206,13 +218,21 @@ def main():
     ap.add_argument("--steps", type=int, default=50)
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
-    ap.add_argument("--batch", type=int, default=64, help="global batch (sequences)")
-    ap.add_argument("--seq", type=int, default=1024)
+    ap.add_argument("--config", type=int, default=2, choices=sorted(CONFIGS),
+                    help="reference configuration (2 = the headline BF16 workload)")
+    ap.add_argument("--batch", type=int, default=None, help="global batch (sequences); default: the config's")
+    ap.add_argument("--seq", type=int, default=None, help="default: the config's")
     ap.add_argument("--e2e-steps", type=int, default=2)
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-gather", action="store_true", help="skip the NCCL logits gather (N > 1)")
     args = ap.parse_args()
 
+    global L, D, H, FF
+    wl_name, L, D, H, FF, dtype_code, dtype_label, gb, gs = CONFIGS[args.config]
+    if args.batch is None:
+        args.batch = gb
+    if args.seq is None:
+        args.seq = gs
     rank = int(os.environ.get("RANK", "0"))
     world = int(os.environ.get("WORLD_SIZE", "1"))
     local_rank = int(os.environ.get("LOCAL_RANK", "0"))
@@ -232,7 +252,7 @@ def main():
     B, S = row1 - row0, args.seq
     T = B * S
 
-    pkg.init(pkg.gpt2_small(pkg.DTYPE_BF16), local_rank)
+    pkg.init(pkg.Gpt2Config(L, D, H, FF, V, 1024, 1e-5, dtype_code), local_rank)
     pkg.init_seeded(SEED, 0)
     ids_all = pkg.seeded_ids(args.batch, S, SEED, V)
     ids_h = np.ascontiguousarray(ids_all[row0:row1])
@@ -365,7 +385,7 @@ def main():
 
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
-        r, dt, cores = cpu_reference_rate(S)
+        r, dt, cores = cpu_reference_rate(S, fp8=args.config == 4)
         O = _oracle()
         cpu = {"value": r, "unit": "tokens/s", "cores": cores, "kind": "port",
                "sample": f"1 sequence x {S} tokens ({dt:.1f} s); OpenBLAS sgemm "
@@ -376,12 +396,12 @@ def main():
         dist.barrier()
     if rank == 0:
         line = {
-            "metric": "GPT-2 prefill tokens/s (GPT-2 small, B64 x S1024)",
+            "metric": "GPT-2 prefill tokens/s" + (" (GPT-2 small, B64 x S1024)" if args.config == 2 else ""),
             "value": value, "unit": "tokens/s", "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
             "ms_per_step": 1000.0 * t_max / args.steps, "higher_is_better": True, "scaling": "strong",
-            "vs_baseline": None, "dtype": "bf16",
+            "vs_baseline": None, "dtype": dtype_label,
             "data": "synthetic (seeded Philox weights N(0,0.02), LN gain 1, biases 0; uniform token ids)",
-            "config": {"workload": "gpt2-small prefill B64xS1024 (config 2), logits FP32 resident per shard",
+            "config": {"workload": f"{wl_name} with global batch {args.batch} x {S}, logits FP32 resident per shard",
                        "global_batch": args.batch, "seq_len": S, "per_rank_batch": B,
                        "parallelism": f"batch-sharded dp{world}", "l2": "no flush: every step moves > 13 GB"},
             "forward_tflops": fwd_tflops,

@@ -55,16 +55,24 @@ def attendable_rows(mask: np.ndarray) -> np.ndarray:
     return np.cumsum(mask != 0, axis=1) > 0
 
 
-def top5_agreement(ref: np.ndarray, got: np.ndarray, bound: float):
-    """Top-5 identity over positions whose reference top-5 is separated by more than 2*bound
-    (between adjacent top-5 entries and between the 5th and 6th logit).  Returns
+def top5_agreement(ref: np.ndarray, got: np.ndarray, bound: float | None = None):
+    """Top-5 identity over the positions whose reference top-5 is separated (between adjacent
+    top-5 entries and between the 5th and 6th logit) by more than twice the error at that
+    position (the max |got - ref| over its row; or `bound` when given).  Returns
     (checked positions, agreeing positions, total positions)."""
     r = ref.reshape(-1, ref.shape[-1])
     g = got.reshape(-1, got.shape[-1])
     idx = np.argsort(-r, axis=1, kind="stable")[:, :6]
     vals = np.take_along_axis(r, idx, axis=1)
     gaps = vals[:, :5] - vals[:, 1:6]
-    separated = (gaps > 2 * bound).all(axis=1)
+    row_err = np.abs(g - r).max(axis=1) if bound is None else np.full(r.shape[0], bound)
+    separated = (gaps > 2 * row_err[:, None]).all(axis=1)
     gidx = np.argsort(-g, axis=1, kind="stable")[:, :5]
     same = (gidx == idx[:, :5]).all(axis=1)
     return int(separated.sum()), int((same & separated).sum()), r.shape[0]
+
+
+def top1_fraction(ref: np.ndarray, got: np.ndarray) -> float:
+    r = ref.reshape(-1, ref.shape[-1])
+    g = got.reshape(-1, got.shape[-1])
+    return float((r.argmax(axis=1) == g.argmax(axis=1)).mean())

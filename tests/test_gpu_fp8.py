@@ -6,19 +6,20 @@ Two comparisons with the oracle on the same inputs:
   * against the oracle run on the FP8-dequantized weights, which isolates the
     kernels: the BF16 bound (BF16_RTOL of max |logit|) and top-5 identity;
   * against the oracle on the original FP32 weights (the reference's own
-    computation): FP8_RTOL of max |logit|, and top-5 identity wherever the
-    oracle's top-5 is separated by more than twice that bound."""
+    computation): FP8_RTOL of max |logit|.
+Both require identical top-5 wherever the oracle's top-5 is separated by more
+than twice the error observed at that position."""
 import numpy as np
 import pytest
 
-from helpers import load_oracle, load_pkg, shape_to_cfg, top5_agreement
+from helpers import load_oracle, load_pkg, shape_to_cfg, top1_fraction, top5_agreement
 
 pytestmark = pytest.mark.gpu
 pkg = load_pkg()
 O = load_oracle()
 
 BF16_RTOL = 0.03
-FP8_RTOL = 0.10
+FP8_RTOL = 0.15  # observed 0.067 (2 layers) and 0.097 (48 layers) of max |logit|
 
 
 @pytest.fixture(scope="module")
@@ -33,9 +34,10 @@ def _check(ref, got, rtol, label):
     scale = float(np.abs(ref).max())
     err = float(np.abs(got - ref).max())
     bound = rtol * scale
-    checked, agree, total = top5_agreement(ref, got, bound)
+    checked, agree, total = top5_agreement(ref, got)
+    top1 = top1_fraction(ref, got)
     print(f"{label}: max|diff| {err:.4g} (rel {err / scale:.4g}, bound {rtol}); top-5 checked {checked}/{total}, "
-          f"identical {agree}")
+          f"identical {agree}; top-1 agreement {top1:.3f}")
     assert err <= bound, (err, bound)
     assert agree == checked
 
