@@ -440,7 +440,7 @@ static inline float gelu_new(float x) {
   return 0.5f * x * (1.0f + tanhf(k * (x + 0.044715f * x * x * x)));
 }
 
-typedef struct { const float *qkv; const int64_t *mask; float *o; int B, S, d, H; float *scratch; } attn_ctx;
+typedef struct { const float *qkv; const int64_t *mask; float *o; int B, S, d, H; float *scratch; int causal; } attn_ctx;
 
 static void attn_heads(void *vctx, int64_t i0, int64_t i1, int tid) {
   const attn_ctx *c = (const attn_ctx *)vctx;
@@ -454,8 +454,11 @@ static void attn_heads(void *vctx, int64_t i0, int64_t i1, int tid) {
     const int64_t *m = c->mask ? c->mask + (int64_t)b * S : NULL;
     int first_valid = 0;
     if (m) { first_valid = S; for (int k = 0; k < S; ++k) if (m[k]) { first_valid = k; break; } }
+    /* Without the causal mask a row lacks an attendable key only when the whole sequence is masked. */
+    if (!c->causal && first_valid < S) first_valid = 0;
     for (int q = 0; q < S; ++q) {
       float *out = c->o + ((int64_t)b * S + q) * d + h * dh;
+      const int klast = c->causal ? q : S - 1;
       if (q < first_valid) {
         for (int j = 0; j < dh; ++j) {
           double acc = 0.0;
@@ -466,7 +469,7 @@ static void attn_heads(void *vctx, int64_t i0, int64_t i1, int tid) {
       }
       const float *qv = base + (int64_t)q * ld + h * dh;
       float mx = -INFINITY;
-      for (int k = 0; k <= q; ++k) {
+      for (int k = 0; k <= klast; ++k) {
         if (m && !m[k]) { p[k] = -INFINITY; continue; }
         const float *kv = base + (int64_t)k * ld + d + h * dh;
         float s = 0.f;
@@ -476,14 +479,14 @@ static void attn_heads(void *vctx, int64_t i0, int64_t i1, int tid) {
         if (s > mx) mx = s;
       }
       float sum = 0.f;
-      for (int k = 0; k <= q; ++k) {
+      for (int k = 0; k <= klast; ++k) {
         const float e = p[k] == -INFINITY ? 0.f : expf(p[k] - mx);
         p[k] = e;
         sum += e;
       }
       const float inv = 1.0f / sum;
       for (int j = 0; j < dh; ++j) out[j] = 0.f;
-      for (int k = 0; k <= q; ++k) {
+      for (int k = 0; k <= klast; ++k) {
         if (p[k] == 0.f) continue;
         const float w = p[k] * inv;
         const float *vv = base + (int64_t)k * ld + 2 * d + h * dh;
@@ -502,7 +505,7 @@ static void attn_heads(void *vctx, int64_t i0, int64_t i1, int tid) {
  * every key and therefore averages V uniformly over all S keys. */
 static void attention(const float *qkv, const int64_t *mask, float *o, int B, int S, int d, int H,
                       float *scratch_all) {
-  attn_ctx c = {qkv, mask, o, B, S, d, H, scratch_all};
+  attn_ctx c = {qkv, mask, o, B, S, d, H, scratch_all, 1};
   parallel_for((int64_t)B * H, attn_heads, &c);
 }
 
@@ -572,5 +575,169 @@ int oracle_gpt2_forward(const OracleCfg *c, const float *blob, const int64_t *id
   sgemm((int)T, V, d, a, wte, 1, logits);
 
   free(off); free(x); free(a); free(o); free(tmp); free(big); free(scr);
+  return 0;
+}
+
+/* ------------------------------------------------------------------------- */
+/* BERT encoder (the reference's second exported model)                       */
+/* ------------------------------------------------------------------------- */
+/*
+ * Restates transformers' BertModel as wrapped by
+ * src/bert-base-uncased/lower_bert_model.py:7-18 (last_hidden_state and
+ * pooler_output) with eager attention: embeddings word + position + token
+ * type, LayerNorm; per layer (post-LN) ctx = softmax(q k^T / sqrt(dh) +
+ * key mask) v, h = LN(x + ctx Wo^T + bo), x = LN(h + gelu(h Wi^T + bi) Wo2^T
+ * + bo2) with the exact (erf) GELU; pooler tanh(x[:, 0] Wp^T + bp).  A
+ * sequence with no unmasked key averages V over all keys (the reference adds
+ * the same finfo.min to every score).  nn.Linear weights are [out, in].
+ *
+ * Canonical FP32 blob, HF order:
+ *   0 word_embeddings [V,d]  1 position_embeddings [P,d]  2 token_type_embeddings [TV,d]
+ *   3 embeddings.LayerNorm.weight [d]  4 .bias [d]
+ *   per layer l, index 5 + 16 l + j:
+ *     0 query.weight [d,d] 1 query.bias  2 key.weight 3 key.bias  4 value.weight 5 value.bias
+ *     6 attention.output.dense.weight [d,d] 7 .bias  8 attention.output.LayerNorm.weight 9 .bias
+ *    10 intermediate.dense.weight [ff,d] 11 .bias [ff]  12 output.dense.weight [d,ff] 13 .bias
+ *    14 output.LayerNorm.weight 15 .bias
+ *   5 + 16 L: pooler.dense.weight [d,d]   6 + 16 L: pooler.dense.bias [d]
+ */
+typedef struct OracleBertCfg {
+  int32_t n_layer, n_embd, n_head, n_inner, vocab_size, n_positions;
+  float layer_norm_eps;
+  int32_t type_vocab;
+} OracleBertCfg;
+
+enum { B_Q_W, B_Q_B, B_K_W, B_K_B, B_V_W, B_V_B, B_AO_W, B_AO_B, B_AOLN_G, B_AOLN_B, B_I_W, B_I_B, B_O_W, B_O_B,
+       B_OLN_G, B_OLN_B, B_PER_LAYER };
+
+int oracle_bert_num_tensors(const OracleBertCfg *c) { return 7 + B_PER_LAYER * c->n_layer; }
+
+static int64_t bert_numel(const OracleBertCfg *c, int t, int *kind) {
+  const int64_t d = c->n_embd, ff = c->n_inner;
+  const int L = c->n_layer;
+  if (t == 0) { *kind = 0; return (int64_t)c->vocab_size * d; }
+  if (t == 1) { *kind = 0; return (int64_t)c->n_positions * d; }
+  if (t == 2) { *kind = 0; return (int64_t)c->type_vocab * d; }
+  if (t == 3) { *kind = 1; return d; }
+  if (t == 4) { *kind = 2; return d; }
+  if (t == 5 + B_PER_LAYER * L) { *kind = 0; return d * d; }
+  if (t == 6 + B_PER_LAYER * L) { *kind = 2; return d; }
+  switch ((t - 5) % B_PER_LAYER) {
+    case B_Q_W: case B_K_W: case B_V_W: case B_AO_W: *kind = 0; return d * d;
+    case B_I_W: *kind = 0; return ff * d;
+    case B_O_W: *kind = 0; return d * ff;
+    case B_AOLN_G: case B_OLN_G: *kind = 1; return d;
+    case B_I_B: *kind = 2; return ff;
+    default: *kind = 2; return d;
+  }
+}
+
+int64_t oracle_bert_blob_layout(const OracleBertCfg *c, int64_t *offsets) {
+  int64_t off = 0;
+  const int n = oracle_bert_num_tensors(c);
+  for (int t = 0; t < n; ++t) {
+    int kind;
+    if (offsets) offsets[t] = off;
+    off += bert_numel(c, t, &kind);
+  }
+  if (offsets) offsets[n] = off;
+  return off;
+}
+
+/* Same generator and init modes as the GPT-2 blob; Philox streams 0x20000 + tensor index. */
+int oracle_bert_seeded_blob(const OracleBertCfg *c, uint64_t seed, int init_mode, float *blob) {
+  const int n = oracle_bert_num_tensors(c);
+  int64_t off = 0;
+  for (int t = 0; t < n; ++t) {
+    int kind;
+    const int64_t numel = bert_numel(c, t, &kind);
+    float *p = blob + off;
+    const uint32_t stream = 0x20000u + (uint32_t)t;
+    if (kind == 0) oracle_normal_fill(p, numel, seed, stream, 0.0, 0.02);
+    else if (init_mode == 0) { const float v = kind == 1 ? 1.0f : 0.0f; for (int64_t i = 0; i < numel; ++i) p[i] = v; }
+    else oracle_normal_fill(p, numel, seed, stream, kind == 1 ? 1.0 : 0.0, kind == 1 ? 0.1 : 0.02);
+    off += numel;
+  }
+  return 0;
+}
+
+static inline float gelu_erf(float x) { return 0.5f * x * (1.0f + erff(x * 0.7071067811865476f)); }
+
+/* hidden [B,S,d] and pooled [B,d] of BertModel(ids, token_type_ids, mask) with
+ * position ids pos[S] (NULL: 0..S-1); tt and mask may be NULL (zeros / ones).
+ * Returns 0, -1 bad shape, -2 an id out of range, -3 OOM. */
+int oracle_bert_forward(const OracleBertCfg *c, const float *blob, const int64_t *ids, const int64_t *tt,
+                        const int64_t *pos, const int64_t *mask, int B, int S, float *hidden, float *pooled) {
+  const int d = c->n_embd, H = c->n_head, ff = c->n_inner, L = c->n_layer;
+  if (B < 1 || S < 1 || S > c->n_positions || d % H) return -1;
+  const int64_t T = (int64_t)B * S;
+  for (int64_t i = 0; i < T; ++i) {
+    if (ids[i] < 0 || ids[i] >= c->vocab_size) return -2;
+    if (tt && (tt[i] < 0 || tt[i] >= c->type_vocab)) return -2;
+  }
+  for (int s = 0; s < S && pos; ++s)
+    if (pos[s] < 0 || pos[s] >= c->n_positions) return -2;
+  int64_t *off = (int64_t *)malloc(sizeof(int64_t) * (oracle_bert_num_tensors(c) + 1));
+  float *x = (float *)malloc(sizeof(float) * T * d);
+  float *h = (float *)malloc(sizeof(float) * T * d);
+  float *o = (float *)malloc(sizeof(float) * T * d);
+  float *tmp = (float *)malloc(sizeof(float) * T * d);
+  float *big = (float *)malloc(sizeof(float) * T * (ff > 3 * d ? ff : 3 * d));
+  float *wqkv = (float *)malloc(sizeof(float) * 3 * (int64_t)d * d);
+  float *bqkv = (float *)malloc(sizeof(float) * 3 * d);
+  float *scr = (float *)malloc(sizeof(float) * (int64_t)S * 257);
+  if (!off || !x || !h || !o || !tmp || !big || !wqkv || !bqkv || !scr) {
+    free(off); free(x); free(h); free(o); free(tmp); free(big); free(wqkv); free(bqkv); free(scr);
+    return -3;
+  }
+  oracle_bert_blob_layout(c, off);
+  const float *we = blob + off[0], *pe = blob + off[1], *te = blob + off[2];
+  for (int64_t t = 0; t < T; ++t) {
+    const int64_t p = pos ? pos[t % S] : t % S;
+    const int64_t ty = tt ? tt[t] : 0;
+    for (int i = 0; i < d; ++i) tmp[t * d + i] = (we[ids[t] * d + i] + pe[p * d + i]) + te[ty * d + i];
+  }
+  layer_norm(tmp, blob + off[3], blob + off[4], x, T, d, c->layer_norm_eps);
+  for (int l = 0; l < L; ++l) {
+    const int64_t *lo = off + 5 + B_PER_LAYER * l;
+    /* q, k, v as one [3d, d] weight: qkv [T, 3d] = x @ [Wq; Wk; Wv]^T + [bq; bk; bv] */
+    memcpy(wqkv, blob + lo[B_Q_W], sizeof(float) * d * d);
+    memcpy(wqkv + (int64_t)d * d, blob + lo[B_K_W], sizeof(float) * d * d);
+    memcpy(wqkv + 2 * (int64_t)d * d, blob + lo[B_V_W], sizeof(float) * d * d);
+    memcpy(bqkv, blob + lo[B_Q_B], sizeof(float) * d);
+    memcpy(bqkv + d, blob + lo[B_K_B], sizeof(float) * d);
+    memcpy(bqkv + 2 * d, blob + lo[B_V_B], sizeof(float) * d);
+    sgemm((int)T, 3 * d, d, x, wqkv, 1, big);
+    for (int64_t t = 0; t < T; ++t)
+      for (int j = 0; j < 3 * d; ++j) big[t * 3 * d + j] += bqkv[j];
+    attn_ctx ac = {big, mask, o, B, S, d, H, scr, 0};
+    parallel_for((int64_t)B * H, attn_heads, &ac);
+    sgemm((int)T, d, d, o, blob + lo[B_AO_W], 1, tmp);
+    const float *bao = blob + lo[B_AO_B];
+    for (int64_t t = 0; t < T; ++t)
+      for (int j = 0; j < d; ++j) tmp[t * d + j] = (tmp[t * d + j] + bao[j]) + x[t * d + j];
+    layer_norm(tmp, blob + lo[B_AOLN_G], blob + lo[B_AOLN_B], h, T, d, c->layer_norm_eps);
+    sgemm((int)T, ff, d, h, blob + lo[B_I_W], 1, big);
+    const float *bi = blob + lo[B_I_B];
+    for (int64_t t = 0; t < T; ++t)
+      for (int j = 0; j < ff; ++j) big[t * ff + j] = gelu_erf(big[t * ff + j] + bi[j]);
+    sgemm((int)T, d, ff, big, blob + lo[B_O_W], 1, tmp);
+    const float *bo = blob + lo[B_O_B];
+    for (int64_t t = 0; t < T; ++t)
+      for (int j = 0; j < d; ++j) tmp[t * d + j] = (tmp[t * d + j] + bo[j]) + h[t * d + j];
+    layer_norm(tmp, blob + lo[B_OLN_G], blob + lo[B_OLN_B], x, T, d, c->layer_norm_eps);
+  }
+  memcpy(hidden, x, sizeof(float) * T * d);
+  if (pooled) {
+    const float *wp = blob + off[5 + B_PER_LAYER * L], *bp = blob + off[6 + B_PER_LAYER * L];
+    for (int b = 0; b < B; ++b)
+      for (int n = 0; n < d; ++n) {
+        const float *r = x + (int64_t)b * S * d, *w = wp + (int64_t)n * d;
+        float acc = 0.f;
+        for (int k = 0; k < d; ++k) acc += r[k] * w[k];
+        pooled[(int64_t)b * d + n] = tanhf(acc + bp[n]);
+      }
+  }
+  free(off); free(x); free(h); free(o); free(tmp); free(big); free(wqkv); free(bqkv); free(scr);
   return 0;
 }

@@ -56,6 +56,37 @@ class ModelShape:
                          self.vocab_size, self.n_positions, self.layer_norm_eps, 0)
 
 
+class OracleBertCfg(ctypes.Structure):
+    _fields_ = [
+        ("n_layer", ctypes.c_int32),
+        ("n_embd", ctypes.c_int32),
+        ("n_head", ctypes.c_int32),
+        ("n_inner", ctypes.c_int32),
+        ("vocab_size", ctypes.c_int32),
+        ("n_positions", ctypes.c_int32),
+        ("layer_norm_eps", ctypes.c_float),
+        ("type_vocab", ctypes.c_int32),
+    ]
+
+
+@dataclass(frozen=True)
+class BertShape:
+    n_layer: int = 12
+    n_embd: int = 768
+    n_head: int = 12
+    n_inner: int = 3072
+    vocab_size: int = 30522
+    n_positions: int = 512
+    layer_norm_eps: float = 1e-12
+    type_vocab: int = 2
+
+    def c(self) -> OracleBertCfg:
+        return OracleBertCfg(self.n_layer, self.n_embd, self.n_head, self.n_inner, self.vocab_size,
+                             self.n_positions, self.layer_norm_eps, self.type_vocab)
+
+
+BERT_BASE = BertShape()
+BERT_TINY = BertShape(n_layer=2, n_embd=128, n_head=2, n_inner=512, vocab_size=1000, n_positions=64)
 GPT2_SMALL = ModelShape()
 # A small model of the same family for fast, mask-heavy parity cases.
 GPT2_TINY = ModelShape(n_layer=2, n_embd=128, n_head=2, n_inner=512, vocab_size=1000, n_positions=64)
@@ -121,6 +152,14 @@ def lib():
     L.oracle_fp8_quantize.argtypes = [P(ctypes.c_float), ctypes.c_int, ctypes.c_int, P(ctypes.c_uint8), P(ctypes.c_float)]
     L.oracle_fp8_dequantize_blob.argtypes = [P(OracleCfg), P(ctypes.c_float)]
     L.oracle_fp8_dequantize_blob.restype = ctypes.c_int
+    L.oracle_bert_num_tensors.argtypes = [P(OracleBertCfg)]
+    L.oracle_bert_blob_layout.argtypes = [P(OracleBertCfg), P(ctypes.c_int64)]
+    L.oracle_bert_blob_layout.restype = ctypes.c_int64
+    L.oracle_bert_seeded_blob.argtypes = [P(OracleBertCfg), ctypes.c_uint64, ctypes.c_int, P(ctypes.c_float)]
+    L.oracle_bert_forward.argtypes = [P(OracleBertCfg), P(ctypes.c_float), P(ctypes.c_int64), P(ctypes.c_int64),
+                                      P(ctypes.c_int64), P(ctypes.c_int64), ctypes.c_int, ctypes.c_int,
+                                      P(ctypes.c_float), P(ctypes.c_float)]
+    L.oracle_bert_forward.restype = ctypes.c_int
     blas = os.environ.get("ORACLE_BLAS", None)
     if blas is None:
         blas = find_openblas() or ""
@@ -229,3 +268,62 @@ def forward(shape: ModelShape, blob: np.ndarray, ids: np.ndarray, mask: np.ndarr
     if rc != 0:
         raise ValueError(f"oracle_gpt2_forward failed with code {rc}")
     return out
+
+
+# ---------------------------------------------------------------------------
+# BERT encoder
+# ---------------------------------------------------------------------------
+BERT_IDS_STREAM = 0x30000
+
+
+def bert_blob_layout(shape: BertShape) -> np.ndarray:
+    c = shape.c()
+    n = lib().oracle_bert_num_tensors(ctypes.byref(c))
+    off = np.zeros(n + 1, dtype=np.int64)
+    lib().oracle_bert_blob_layout(ctypes.byref(c), _ptr(off, ctypes.c_int64))
+    return off
+
+
+def bert_seeded_blob(shape: BertShape, seed: int, init_mode: int = 0) -> np.ndarray:
+    c = shape.c()
+    total = int(lib().oracle_bert_blob_layout(ctypes.byref(c), None))
+    blob = np.empty(total, dtype=np.float32)
+    lib().oracle_bert_seeded_blob(ctypes.byref(c), seed, init_mode, _ptr(blob, ctypes.c_float))
+    return blob
+
+
+def bert_tensor_names(shape: BertShape) -> list[str]:
+    names = ["embeddings.word_embeddings.weight", "embeddings.position_embeddings.weight",
+             "embeddings.token_type_embeddings.weight", "embeddings.LayerNorm.weight", "embeddings.LayerNorm.bias"]
+    per = ["attention.self.query.weight", "attention.self.query.bias", "attention.self.key.weight",
+           "attention.self.key.bias", "attention.self.value.weight", "attention.self.value.bias",
+           "attention.output.dense.weight", "attention.output.dense.bias", "attention.output.LayerNorm.weight",
+           "attention.output.LayerNorm.bias", "intermediate.dense.weight", "intermediate.dense.bias",
+           "output.dense.weight", "output.dense.bias", "output.LayerNorm.weight", "output.LayerNorm.bias"]
+    for l in range(shape.n_layer):
+        names += [f"encoder.layer.{l}.{p}" for p in per]
+    names += ["pooler.dense.weight", "pooler.dense.bias"]
+    return names
+
+
+def bert_forward(shape: BertShape, blob: np.ndarray, ids: np.ndarray, token_type_ids: np.ndarray | None = None,
+                 mask: np.ndarray | None = None, position_ids: np.ndarray | None = None):
+    """(last_hidden_state [B, S, d], pooler_output [B, d]) in FP32."""
+    ids = np.ascontiguousarray(ids, dtype=np.int64)
+    B, S = ids.shape
+    hidden = np.empty((B, S, shape.n_embd), dtype=np.float32)
+    pooled = np.empty((B, shape.n_embd), dtype=np.float32)
+    args = []
+    for a in (token_type_ids, position_ids, mask):
+        if a is None:
+            args.append(None)
+        else:
+            a = np.ascontiguousarray(a, dtype=np.int64)
+            args.append(a)
+    ptrs = [None if a is None else _ptr(a, ctypes.c_int64) for a in args]
+    c = shape.c()
+    rc = lib().oracle_bert_forward(ctypes.byref(c), _ptr(blob, ctypes.c_float), _ptr(ids, ctypes.c_int64), ptrs[0],
+                                   ptrs[1], ptrs[2], B, S, _ptr(hidden, ctypes.c_float), _ptr(pooled, ctypes.c_float))
+    if rc != 0:
+        raise ValueError(f"oracle_bert_forward failed with code {rc}")
+    return hidden, pooled

@@ -74,6 +74,63 @@ def run_case(name, shape, seed, init_mode, ids, mask, subset=False):
     print(f"wrote {path}: logits {rec['logits'].shape}")
 
 
+def hf_bert(shape: O.BertShape, blob: np.ndarray):
+    from transformers import BertConfig, BertModel
+    cfg = BertConfig(vocab_size=shape.vocab_size, hidden_size=shape.n_embd, num_hidden_layers=shape.n_layer,
+                     num_attention_heads=shape.n_head, intermediate_size=shape.n_inner,
+                     max_position_embeddings=shape.n_positions, type_vocab_size=shape.type_vocab,
+                     layer_norm_eps=shape.layer_norm_eps, hidden_act="gelu", hidden_dropout_prob=0.0,
+                     attention_probs_dropout_prob=0.0, attn_implementation="eager")
+    model = BertModel(cfg).eval()
+    off = O.bert_blob_layout(shape)
+    sd = model.state_dict()
+    new = {n: torch.from_numpy(blob[off[i]:off[i + 1]].copy()).reshape(sd[n].shape)
+           for i, n in enumerate(O.bert_tensor_names(shape))}
+    missing, unexpected = model.load_state_dict(new, strict=False)
+    assert not unexpected and not missing, (missing, unexpected)
+    return model
+
+
+def run_bert_case(name, shape, seed, init_mode, ids, tt, mask):
+    blob = O.bert_seeded_blob(shape, seed, init_mode)
+    model = hf_bert(shape, blob)
+    with torch.no_grad():
+        out = model(input_ids=torch.from_numpy(ids), token_type_ids=torch.from_numpy(tt),
+                    attention_mask=torch.from_numpy(mask))
+    rec = dict(
+        shape=np.array([shape.n_layer, shape.n_embd, shape.n_head, shape.n_inner, shape.vocab_size,
+                        shape.n_positions, shape.type_vocab], dtype=np.int64),
+        eps=np.float32(shape.layer_norm_eps), seed=np.uint64(seed), init_mode=np.int64(init_mode),
+        ids=ids, token_type_ids=tt, mask=mask, blob_sum=np.float64(blob.astype(np.float64).sum()),
+        blob_head=blob[:16].copy(), hidden=out.last_hidden_state.float().numpy(),
+        pooled=out.pooler_output.float().numpy())
+    path = os.path.join(HERE, f"{name}.npz")
+    np.savez_compressed(path, **rec)
+    print(f"wrote {path}: hidden {rec['hidden'].shape}")
+
+
+def main_bert():
+    tiny, base = O.BERT_TINY, O.BERT_BASE
+    # The reference BERT host program's call (src/bert-base-uncased/call_bert.cpp:61-64), seeded weights.
+    ids = np.array([[101, 2023, 2003, 1037, 7099, 7953, 2005, 14324, 2944, 9167, 1012, 102]], dtype=np.int64)
+    run_bert_case("bert_base_refcall", base, 1234, 0, ids, np.zeros_like(ids), np.ones_like(ids))
+    # BERT-base, right-padded batch (config 3's mask shape), token types 0 / 1 halves.
+    ids = O.token_ids(2, 64, 33, base.vocab_size, stream=O.BERT_IDS_STREAM)
+    tt = np.zeros_like(ids)
+    tt[:, 32:] = 1
+    mask = np.ones_like(ids)
+    mask[1, 40:] = 0
+    run_bert_case("bert_base_padded", base, 33, 1, ids, tt, mask)
+    # Tiny model of the same family: every kind of mask, random token types.
+    ids = O.token_ids(4, 23, 5, tiny.vocab_size, stream=O.BERT_IDS_STREAM)
+    tt = O.token_ids(4, 23, 6, 2, stream=O.BERT_IDS_STREAM + 1)
+    mask = np.ones_like(ids)
+    mask[1, 12:] = 0
+    mask[2, :] = 0
+    mask[3, ::3] = 0
+    run_bert_case("bert_tiny_masks", tiny, 5, 1, ids, tt, mask)
+
+
 def main():
     torch.manual_seed(0)
     small, tiny = O.GPT2_SMALL, O.GPT2_TINY
@@ -111,4 +168,8 @@ def main():
 
 
 if __name__ == "__main__":
-    main()
+    which = sys.argv[1:] or ["gpt2", "bert"]
+    if "gpt2" in which:
+        main()
+    if "bert" in which:
+        main_bert()

@@ -34,7 +34,20 @@ def load_oracle():
 
 
 def golden_files():
-    return sorted(glob.glob(os.path.join(GOLDEN, "*.npz")))
+    """GPT-2 fixtures."""
+    return sorted(f for f in glob.glob(os.path.join(GOLDEN, "*.npz")) if not os.path.basename(f).startswith("bert_"))
+
+
+def bert_golden_files():
+    return sorted(glob.glob(os.path.join(GOLDEN, "bert_*.npz")))
+
+
+def load_bert_golden(path):
+    O = load_oracle()
+    z = dict(np.load(path))
+    s = [int(x) for x in z["shape"]]
+    shape = O.BertShape(s[0], s[1], s[2], s[3], s[4], s[5], float(z["eps"]), s[6])
+    return shape, z
 
 
 def load_golden(path):

@@ -4,7 +4,7 @@ the published Philox4x32-10 known-answer vectors, and its own invariants."""
 import numpy as np
 import pytest
 
-from helpers import attendable_rows, golden_files, load_golden, load_oracle
+from helpers import attendable_rows, bert_golden_files, golden_files, load_bert_golden, load_golden, load_oracle
 
 O = load_oracle()
 
@@ -91,3 +91,15 @@ def test_oracle_rejects_bad_inputs():
         O.forward(shape, blob, np.array([[-1, 0]]))
     with pytest.raises(ValueError):
         O.forward(shape, blob, np.zeros((1, shape.n_positions + 1), dtype=np.int64))
+
+
+@pytest.mark.parametrize("path", bert_golden_files(), ids=lambda p: p.split("/")[-1])
+def test_bert_oracle_matches_transformers(path):
+    """BERT encoder (src/bert-base-uncased/lower_bert_model.py:7-18): last_hidden_state and
+    pooler_output of the oracle vs HF BertModel on the same seeded weights, within 1e-4."""
+    shape, z = load_bert_golden(path)
+    blob = O.bert_seeded_blob(shape, int(z["seed"]), int(z["init_mode"]))
+    assert np.array_equal(blob[:16], z["blob_head"]), "seeded generator drifted"
+    hidden, pooled = O.bert_forward(shape, blob, z["ids"], z["token_type_ids"], z["mask"])
+    assert np.abs(hidden - z["hidden"]).max() <= 1e-4
+    assert np.abs(pooled - z["pooled"]).max() <= 1e-4
