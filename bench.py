@@ -5,6 +5,12 @@ on each shard.
   python bench.py [--gpus N --steps K --warmup W]        # this library
   python bench.py --impl reference [...]                  # the CPU reference path
   torchrun --nproc-per-node N bench.py --gpus N ...       # one process per GPU
+  python bench.py --config 3                              # BERT-base encoder, B128 x S512
+
+--config selects another of the reference's workloads (1: GPT-2 small FP32
+B8xS1024, 3: the BERT-base BF16 encoder B128xS512 with right-padded
+sequences of seeded lengths in [64, 512], 4: the GPT-2-XL shape with FP8
+weight-only GEMMs B32xS1024); the default is the headline workload.
 
 One step = one forward over this rank's B/N sequences (ids resident in HBM,
 FP32 logits written to HBM).  value = all ranks' tokens / max-over-ranks
@@ -41,9 +47,14 @@ LD_LOGITS = 50304  # row stride of the resident logits (16-byte aligned rows)
 CONFIGS = {
     1: ("gpt2-small FP32 prefill B8xS1024 (config 1)", 12, 768, 12, 3072, 0, "f32", 8, 1024),
     2: ("gpt2-small BF16 prefill B64xS1024 (config 2)", 12, 768, 12, 3072, 1, "bf16", 64, 1024),
+    3: ("bert-base BF16 encoder B128xS512, valid lengths uniform in [64, 512] (config 3)", 12, 768, 12, 3072, 1,
+        "bf16", 128, 512),
     4: ("gpt2-xl-shape FP8 weight-only prefill B32xS1024 (config 4)", 48, 1600, 25, 6400, 2, "fp8w-e4m3/bf16", 32,
         1024),
 }
+BERT_V, BERT_P, BERT_TV = 30522, 512, 2
+METRICS = {2: "GPT-2 prefill tokens/s (GPT-2 small, B64 x S1024)",
+           3: "BERT-base encoder tokens/s (B128 x S512 positions, padding included)"}
 L, D, H, FF = 12, 768, 12, 3072  # set from the chosen configuration in main()
 
 
@@ -164,6 +175,92 @@ class ClockSampler:
                 "samples": len(sm)}
 
 
+def traffic_per_launch(config: int, kernel: str, tokens: int):
+    """DRAM bytes (read + write) per launch of `kernel` at `tokens` tokens per rank, scaled by
+    tokens from the ncu capture recorded in profiles/traffic.json (None if not captured)."""
+    try:
+        with open(os.path.join(ROOT, "profiles", "traffic.json")) as f:
+            ent = json.load(f).get(str(config), {}).get(kernel)
+        return int(ent["bytes_per_launch_captured"] * tokens / ent["captured_tokens"])
+    except Exception:
+        return None
+
+
+def kernel_breakdown(prof: dict, work: dict, nprof: int, peaks: dict, config: int, tokens: int):
+    """Per-kernel ms / share / rate of `nprof` profiled steps and the roofline of the dominant
+    kernel (achieved = algorithmic work per launch / average event-timed launch duration)."""
+    kernels = {}
+    for k, (ms, n) in prof.items():
+        if n == 0:
+            continue
+        ent = {"ms_per_step": ms / nprof, "launches_per_step": n // nprof, "avg_launch_ms": ms / n}
+        if k in work:
+            kind, amount = work[k]
+            per_launch_s = ms / n / 1000.0
+            if kind == "flop":
+                ent["tflops"] = amount / per_launch_s / 1e12
+            else:
+                ent["gbs"] = amount / per_launch_s / 1e9
+        kernels[k] = ent
+    step_ms = sum(e["ms_per_step"] for e in kernels.values())
+    for e in kernels.values():
+        e["share"] = e["ms_per_step"] / step_ms if step_ms else None
+    dom = max(kernels, key=lambda k: kernels[k]["ms_per_step"])
+    traffic = traffic_per_launch(config, dom, tokens)
+    kind, amount = work.get(dom, ("flop", 0.0))
+    per_launch_s = kernels[dom]["avg_launch_ms"] / 1000.0
+    if kind == "flop":
+        achieved = amount / per_launch_s / 1e12
+        roof = {"bound": "tensor", "achieved": achieved, "peak": peaks["bf16_sus"], "unit": "TFLOP/s",
+                "frac": achieved / peaks["bf16_sus"], "traffic": traffic, "kernel": dom,
+                "peak_kind": f"bf16 sustained ({peaks['src']})", "algorithmic_per_launch": amount}
+    else:
+        achieved = amount / per_launch_s / 1e9
+        roof = {"bound": "hbm", "achieved": achieved, "peak": peaks["hbm_gbs"], "unit": "GB/s",
+                "frac": achieved / peaks["hbm_gbs"], "traffic": traffic, "kernel": dom,
+                "peak_kind": f"hbm copy ({peaks['src']})", "algorithmic_per_launch": amount}
+    return kernels, roof
+
+
+def bert_lengths(global_batch: int, S: int) -> np.ndarray:
+    """Seeded valid lengths of the BERT workload, uniform in [64, S] (Philox stream 0x30002)."""
+    O = _oracle()
+    lo = min(64, S)
+    return lo + O.token_ids(1, global_batch, SEED, S - lo + 1, stream=O.BERT_IDS_STREAM + 2)[0]
+
+
+def bert_kernel_work(B, S, lens):
+    """Algorithmic work per launch of each BERT kernel kind for B sequences of S positions with
+    valid lengths `lens`: attention counts every query row against the valid keys only."""
+    T = B * S
+    return {
+        "gemm_qkv": ("flop", 2.0 * T * D * 3 * D),
+        "gemm_attn_out": ("flop", 2.0 * T * D * D),
+        "gemm_intermediate": ("flop", 2.0 * T * D * FF),
+        "gemm_output": ("flop", 2.0 * T * FF * D),
+        "attention": ("flop", 4.0 * H * DH * S * float(np.sum(lens))),
+        "layernorm": ("bytes", T * D * (2 + 2) + 2 * D * 4),
+        "embed_ln": ("bytes", T * (16 + 4 * D + 2 * D) + (S + BERT_TV) * 4 * D),
+        "pooler": ("flop", 2.0 * B * D * D),
+    }
+
+
+def cpu_bert_rate(S: int, length: int):
+    """The oracle's BERT encoder on one sequence of S positions (first `length` valid); returns
+    (positions/s, seconds, cores)."""
+    O = _oracle()
+    O.build()
+    O.set_loop_threads(1)
+    shape = O.BERT_BASE
+    blob = O.bert_seeded_blob(shape, SEED, 0)
+    ids = O.token_ids(1, S, SEED, shape.vocab_size, stream=O.BERT_IDS_STREAM)
+    mask = (np.arange(S)[None, :] < length).astype(np.int64)
+    t0 = time.perf_counter()
+    O.bert_forward(shape, blob, ids, None, mask)
+    dt = time.perf_counter() - t0
+    return S / dt, dt, os.cpu_count() or 1
+
+
 def cpu_reference_rate(S: int, n_seq: int = 1, fp8: bool = False):
     """The oracle (the reference's CPU lowering restated in C: OpenBLAS sgemm for the 2-D
     matmuls on all cores, single-threaded loop nests for the rest) on n_seq sequences of S
@@ -188,8 +285,12 @@ def run_reference(args, rank, world):
         return
     S = args.seq
     rates = []
+    med = int(np.median(bert_lengths(args.batch, S))) if args.config == 3 else S
     for i in range(args.warmup + args.steps):
-        r, dt, cores = cpu_reference_rate(S, fp8=args.config == 4)
+        if args.config == 3:
+            r, dt, cores = cpu_bert_rate(S, med)
+        else:
+            r, dt, cores = cpu_reference_rate(S, fp8=args.config == 4)
         if i >= args.warmup:
             rates.append((r, dt))
     total_tokens = S * len(rates)
@@ -198,18 +299,136 @@ def run_reference(args, rank, world):
     O = _oracle()
     line = {
         "impl": "reference",
-        "metric": "GPT-2 prefill tokens/s (GPT-2 small, B64 x S1024)",
+        "metric": METRICS.get(args.config, "GPT-2 prefill tokens/s"),
         "value": value, "unit": "tokens/s", "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
         "ms_per_step": 1000.0 * total_s / len(rates), "higher_is_better": True, "scaling": "strong",
         "vs_baseline": None, "dtype": "f32", "data": "synthetic (seeded Philox weights N(0,0.02), uniform ids)",
         "config": {"workload": CONFIGS[args.config][0], "global_batch": args.batch, "seq_len": S,
-                   "sample_per_step": f"1 sequence x {S} tokens"},
+                   "sample_per_step": f"1 sequence x {S} tokens"
+                   + (f" ({med} valid, the median length)" if args.config == 3 else "")},
         "cpu_baseline": {"value": value, "unit": "tokens/s", "cores": cores, "kind": "port",
                          "sample": f"1 x {S} tokens per step; OpenBLAS sgemm ({O.blas_name().split('/')[-1]}) on "
-                                   f"all {cores} cores, loop nests single-threaded as the reference's CPU lowering"},
+                                   f"all {cores} cores, loop nests single-threaded as the reference's CPU lowering"
+                                   + (" (BERT-base encoder)" if args.config == 3 else "")},
         "e2e": {"value": value, "unit": "tokens/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
     }
     print(json.dumps(line), flush=True)
+
+
+def run_bert(args, rank, world, local_rank, pkg, torch, dist):
+    """Config 3: the BERT-base BF16 encoder over this rank's shard of B128 x S512 right-padded
+    sequences (device-resident ids, token types and mask; FP32 hidden states and pooled output
+    written to HBM each step)."""
+    Bm = pkg.bert
+    row0, row1 = shard_rows(args.batch, world, rank)
+    B, S = row1 - row0, args.seq
+    T = B * S
+    O = _oracle()
+    lens_all = bert_lengths(args.batch, S)
+    lens = lens_all[row0:row1]
+    ids_h = np.ascontiguousarray(O.token_ids(args.batch, S, SEED, BERT_V, stream=O.BERT_IDS_STREAM)[row0:row1])
+    mask_h = (np.arange(S)[None, :] < lens[:, None]).astype(np.int64)
+    tt_h = np.zeros_like(ids_h)
+    for b, n in enumerate(lens):  # second segment: the back half of the valid positions
+        tt_h[b, n // 2:n] = 1
+    Bm.init(Bm.BertConfig(L, D, H, FF, BERT_V, BERT_P, 1e-12, BERT_TV, 1), local_rank)
+    Bm.init_seeded(SEED, 0)
+    ids, tt, mask = (torch.from_numpy(a).cuda() for a in (ids_h, tt_h, mask_h))
+    hidden = torch.empty(T, D, device="cuda", dtype=torch.float32)
+    pooled = torch.empty(B, D, device="cuda", dtype=torch.float32)
+    stream = torch.cuda.Stream()
+    torch.cuda.set_stream(stream)
+    sp = stream.cuda_stream
+
+    def step():
+        Bm.forward_device(ids.data_ptr(), tt.data_ptr(), None, mask.data_ptr(), B, S, hidden.data_ptr(),
+                          pooled.data_ptr(), sp)
+
+    def barrier():
+        if world > 1:
+            dist.barrier()
+
+    for _ in range(max(args.warmup, 3)):
+        step()
+    torch.cuda.synchronize()
+    if Bm.status() != 0:
+        raise SystemExit("device status word set during warm-up")
+    barrier()
+    torch.cuda.synchronize()
+    ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    with ClockSampler(local_rank) as clk:
+        ev0.record(stream)
+        for _ in range(args.steps):
+            step()
+        ev1.record(stream)
+        torch.cuda.synchronize()
+    barrier()
+    t_max = max_over_ranks(ev0.elapsed_time(ev1) / 1000.0, dist, "cuda")
+    value = args.batch * S * args.steps / t_max
+
+    Bm.profile_begin()
+    nprof = 2
+    for _ in range(nprof):
+        step()
+    prof = Bm.profile_end()
+    torch.cuda.synchronize()
+    work = bert_kernel_work(B, S, lens)
+    kernels, roof = kernel_breakdown(prof, work, nprof, _peaks(), 3, T)
+    ws = bert_kernel_work(args.batch, S, lens_all)
+    total_flop = (ws["gemm_qkv"][1] + ws["gemm_attn_out"][1] + ws["gemm_intermediate"][1] + ws["gemm_output"][1]
+                  + ws["attention"][1]) * L + ws["pooler"][1]
+
+    e2e = None
+    if args.e2e_steps > 0:
+        pins = [torch.from_numpy(a).pin_memory() for a in (ids_h, tt_h, mask_h)]
+        h_out = torch.empty((B, S, D), dtype=torch.float32).pin_memory()
+        p_out = torch.empty((B, D), dtype=torch.float32).pin_memory()
+        lib = Bm.lib()
+        ptrs = [t.data_ptr() for t in pins]
+        rc = lib.bert_forward_host(ptrs[0], ptrs[1], None, ptrs[2], B, S, h_out.data_ptr(), p_out.data_ptr())
+        if rc != 0:
+            raise SystemExit("bert_forward_host failed: " + Bm.last_error())
+        barrier()
+        t0 = time.perf_counter()
+        for _ in range(args.e2e_steps):
+            lib.bert_forward_host(ptrs[0], ptrs[1], None, ptrs[2], B, S, h_out.data_ptr(), p_out.data_ptr())
+        et = time.perf_counter() - t0
+        e2e = {"value": args.batch * S * args.e2e_steps / max_over_ranks(et, dist, "cuda"), "unit": "tokens/s",
+               "h2d_bytes_per_step": int(sum(t.numel() * 8 for t in pins) * world),
+               "d2h_bytes_per_step": int((h_out.numel() + p_out.numel()) * 4 * world), "steps": args.e2e_steps,
+               "api": "bert_forward_host (C ABI, host buffers, synchronous)"}
+
+    cpu = None
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+        med = int(np.median(lens_all))
+        r, dt, cores = cpu_bert_rate(S, med)
+        cpu = {"value": r, "unit": "tokens/s", "cores": cores, "kind": "port",
+               "sample": f"1 sequence x {S} positions, {med} valid (the median length) ({dt:.1f} s); OpenBLAS "
+                         f"sgemm ({O.blas_name().split('/')[-1]}) on all {cores} cores, loop nests single-threaded"}
+
+    clocks = clk.summary()
+    if world > 1:
+        dist.barrier()
+    if rank == 0:
+        line = {
+            "metric": METRICS[3], "value": value, "unit": "tokens/s", "n_gpus": world, "steps": args.steps,
+            "warmup": args.warmup, "ms_per_step": 1000.0 * t_max / args.steps, "higher_is_better": True,
+            "scaling": "strong", "vs_baseline": None, "dtype": "bf16",
+            "data": "synthetic (seeded Philox weights N(0,0.02), LN gain 1, biases 0; uniform ids; seeded lengths)",
+            "config": {"workload": f"{CONFIGS[3][0]}; FP32 hidden + pooled resident per shard",
+                       "global_batch": args.batch, "seq_len": S, "per_rank_batch": B,
+                       "valid_tokens": int(np.sum(lens_all)), "mean_length": float(np.mean(lens_all)),
+                       "parallelism": f"batch-sharded dp{world}",
+                       "l2": "no flush: every step moves > 2 GB of activations"},
+            "valid_tokens_per_s": float(np.sum(lens_all)) * args.steps / t_max,
+            "forward_tflops": total_flop / (t_max / args.steps) / 1e12,
+            "roofline": roof, "kernels": kernels, "cpu_baseline": cpu, "e2e": e2e, "clocks": clocks,
+            "gpu_launches": Bm.forward_launches(True, True) * args.steps,
+        }
+        print(json.dumps(line), flush=True)
+    Bm.shutdown()
+    if world > 1:
+        dist.destroy_process_group()
 
 
 def main():
@@ -248,6 +467,9 @@ def main():
     if world > 1:
         dist.init_process_group("nccl", timeout=timedelta(seconds=120), device_id=torch.device("cuda", local_rank))
     pkg = _pkg()
+    if args.config == 3:
+        run_bert(args, rank, world, local_rank, pkg, torch, dist)
+        return
     row0, row1 = shard_rows(args.batch, world, rank)
     B, S = row1 - row0, args.seq
     T = B * S
@@ -316,44 +538,7 @@ def main():
     prof = pkg.profile_end()
     torch.cuda.synchronize()
     work = kernel_work(B, S)
-    peaks = _peaks()
-    kernels = {}
-    for k, (ms, n) in prof.items():
-        if n == 0:
-            continue
-        ent = {"ms_per_step": ms / nprof, "launches_per_step": n // nprof, "avg_launch_ms": ms / n}
-        if k in work:
-            kind, amount = work[k]
-            per_launch_s = ms / n / 1000.0
-            if kind == "flop":
-                ent["tflops"] = amount / per_launch_s / 1e12
-            else:
-                ent["gbs"] = amount / per_launch_s / 1e9
-        kernels[k] = ent
-    step_ms = sum(e["ms_per_step"] for e in kernels.values())
-    for e in kernels.values():
-        e["share"] = e["ms_per_step"] / step_ms if step_ms else None
-    dom = max(kernels, key=lambda k: kernels[k]["ms_per_step"])
-    traffic = None
-    try:
-        with open(os.path.join(ROOT, "profiles", "traffic.json")) as f:
-            tr = json.load(f)
-        traffic = tr.get(dom, {}).get("bytes_per_launch_full")
-    except Exception:
-        pass
-    kind, amount = work.get(dom, ("flop", 0.0))
-    per_launch_s = kernels[dom]["avg_launch_ms"] / 1000.0
-    if kind == "flop":
-        achieved = amount / per_launch_s / 1e12
-        roof = {"bound": "tensor", "achieved": achieved, "peak": peaks["bf16_sus"], "unit": "TFLOP/s",
-                "frac": achieved / peaks["bf16_sus"], "traffic": traffic, "kernel": dom,
-                "peak_kind": f"bf16 sustained ({peaks['src']})",
-                "algorithmic_per_launch": amount}
-    else:
-        achieved = amount / per_launch_s / 1e9
-        roof = {"bound": "hbm", "achieved": achieved, "peak": peaks["hbm_gbs"], "unit": "GB/s",
-                "frac": achieved / peaks["hbm_gbs"], "traffic": traffic, "kernel": dom,
-                "peak_kind": f"hbm copy ({peaks['src']})", "algorithmic_per_launch": amount}
+    kernels, roof = kernel_breakdown(prof, work, nprof, _peaks(), args.config, T)
     total_flop = (work["gemm_qkv"][1] + work["gemm_proj"][1] + work["gemm_fc"][1] + work["gemm_mproj"][1]) * L \
         + work["lm_head"][1] + work["attention"][1] * L
     fwd_tflops = total_flop / (t_max / args.steps) / 1e12

@@ -192,7 +192,8 @@ int gpt2_profile_end(double *ms_per_kind, int64_t *launches_per_kind, int n_kind
 /* ------------------------------------------------------------------------ */
 
 /* Epilogues fused into the GEMMs. */
-enum { GPT2_EPI_NONE = 0, GPT2_EPI_BIAS = 1, GPT2_EPI_BIAS_GELU = 2, GPT2_EPI_BIAS_RESID = 3 };
+enum { GPT2_EPI_NONE = 0, GPT2_EPI_BIAS = 1, GPT2_EPI_BIAS_GELU = 2, GPT2_EPI_BIAS_RESID = 3,
+       GPT2_EPI_BIAS_GELU_ERF = 4 /* exact erf GELU of the BERT intermediate layer */ };
 
 /* Exact-FP32 SIMT GEMM: C[M,N] (row stride ldc) = epi(A[M,K] @ op(B)),
  * op(B) = B[K,N] (b_nk = 0) or B[N,K]^T (b_nk = 1); resid row stride ldc. */

@@ -27,9 +27,10 @@ import numpy as np
 HERE = os.path.dirname(os.path.abspath(__file__))
 LIB_PATH = os.path.join(HERE, "libgpt2_b200.so")
 HEADER = os.path.join(os.path.dirname(HERE), "include", "gpt2_b200.h")
+BERT_HEADER = os.path.join(os.path.dirname(HERE), "include", "bert_b200.h")
 
 DTYPE_F32, DTYPE_BF16, DTYPE_FP8W = 0, 1, 2
-EPI_NONE, EPI_BIAS, EPI_BIAS_GELU, EPI_BIAS_RESID = 0, 1, 2, 3
+EPI_NONE, EPI_BIAS, EPI_BIAS_GELU, EPI_BIAS_RESID, EPI_BIAS_GELU_ERF = 0, 1, 2, 3, 4
 STATUS_NAMES = {0: "ok", 1: "token id out of range", 2: "barrier wait timed out", 3: "bad launch"}
 
 
@@ -140,13 +141,16 @@ def _check(rc: int, what: str) -> int:
     return rc
 
 
-def declared_functions() -> list[str]:
-    """Names of the functions include/gpt2_b200.h declares."""
+def declared_functions(headers: tuple[str, ...] = (HEADER, BERT_HEADER)) -> list[str]:
+    """Names of the functions include/gpt2_b200.h and include/bert_b200.h declare."""
     import re
-    text = open(HEADER).read()
-    text = re.sub(r"/\*.*?\*/", "", text, flags=re.S)
-    text = "\n".join(line for line in text.splitlines() if not line.lstrip().startswith("#"))
-    return sorted(set(re.findall(r"\b([A-Za-z_][A-Za-z0-9_]*)\s*\(", text)))
+    names = set()
+    for h in headers:
+        text = open(h).read()
+        text = re.sub(r"/\*.*?\*/", "", text, flags=re.S)
+        text = "\n".join(line for line in text.splitlines() if not line.lstrip().startswith("#"))
+        names |= set(re.findall(r"\b([A-Za-z_][A-Za-z0-9_]*)\s*\(", text))
+    return sorted(names)
 
 
 # ---------------------------------------------------------------------------
@@ -353,3 +357,6 @@ def k_attention_noalloc(qkv, mask, o, B, S, H, dtype, stream=None):
 
 def k_embed(ids, wte, wpe, x, T, S, d, V, dtype, status_ptr=None, stream=None):
     _check(lib().gpt2k_embed(ids, wte, wpe, x, T, S, d, V, dtype, status_ptr, stream), "gpt2k_embed")
+
+
+from . import bert  # noqa: E402  (the BERT encoder entry points, include/bert_b200.h)

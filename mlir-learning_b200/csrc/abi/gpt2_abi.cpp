@@ -368,7 +368,7 @@ int gpt2_profile_begin(void) {
   std::lock_guard<std::mutex> lk(g_api_mu);
   Context *c = context();
   if (!c) return GPT2_ENOMODEL;
-  return profile_begin(*c);
+  return profile_begin(c->prof);
 }
 
 int gpt2_profile_end(double *ms_per_kind, int64_t *launches_per_kind, int n_kinds) {
@@ -377,7 +377,7 @@ int gpt2_profile_end(double *ms_per_kind, int64_t *launches_per_kind, int n_kind
   if (!c) return GPT2_ENOMODEL;
   if (!ms_per_kind || !launches_per_kind || n_kinds < 0) return GPT2_EINVAL;
   cudaSetDevice(c->device);
-  return profile_end(*c, ms_per_kind, launches_per_kind, n_kinds < K_NUM_KINDS ? n_kinds : K_NUM_KINDS);
+  return profile_end(c->prof, ms_per_kind, launches_per_kind, n_kinds < K_NUM_KINDS ? n_kinds : K_NUM_KINDS);
 }
 
 // ---------------------------------------------------------------------------

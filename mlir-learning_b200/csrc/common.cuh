@@ -309,6 +309,9 @@ __device__ __forceinline__ float gelu_new_exact(float x) {
   const float k = 0.7978845608028654f;
   return 0.5f * x * (1.0f + tanhf(k * (x + 0.044715f * x * x * x)));
 }
+// The exact GELU of BERT ("gelu"): 0.5 x (1 + erf(x / sqrt(2))), CUDA's erff.
+__device__ __forceinline__ float gelu_erf(float x) { return 0.5f * x * (1.0f + erff(x * 0.7071067811865476f)); }
+
 __device__ __forceinline__ float gelu_new_fast(float x) {
   const float k = 0.7978845608028654f;
   return 0.5f * x * (1.0f + tanh_approx(k * (x + 0.044715f * x * x * x)));

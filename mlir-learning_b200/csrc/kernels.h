@@ -32,13 +32,15 @@ inline cudaError_t set_smem_once(Kernel kernel, int bytes, std::atomic<uint64_t>
 //   EPI_BIAS       C = acc + bias[col]
 //   EPI_BIAS_GELU  C = gelu_new(acc + bias[col])
 //   EPI_BIAS_RESID C = resid[row, col] + (acc + bias[col])   (resid may alias C)
-enum Epilogue : int { EPI_NONE = 0, EPI_BIAS = 1, EPI_BIAS_GELU = 2, EPI_BIAS_RESID = 3 };
+//   EPI_BIAS_GELU_ERF C = gelu(acc + bias[col]), the exact (erf) GELU of BERT
+enum Epilogue : int { EPI_NONE = 0, EPI_BIAS = 1, EPI_BIAS_GELU = 2, EPI_BIAS_RESID = 3, EPI_BIAS_GELU_ERF = 4 };
 
 // ---- sequence / mask preparation -------------------------------------------
 // first_valid[b] = smallest k with mask[b, k] != 0 (S if none);
-// key_valid[b*S + k] = mask[b, k] != 0.  mask is contiguous [B, S] int64.
+// key_valid[b*S + k] = mask[b, k] != 0; kv_end[b] (optional) = 1 + the
+// largest such k (0 if none).  mask is contiguous [B, S] int64.
 cudaError_t launch_seq_info(const int64_t *mask, int B, int S, int *first_valid, uint8_t *key_valid,
-                            cudaStream_t st);
+                            cudaStream_t st, int *kv_end = nullptr);
 
 // ---- embedding: x[t] = wte[ids[t]] + wpe[t % S] -------------------------------
 cudaError_t launch_embed_f32(const int64_t *ids, const float *wte, const float *wpe, float *x, int T, int S, int d,
@@ -51,6 +53,25 @@ cudaError_t launch_layernorm_f32(const float *x, const float *g, const float *b,
                                  cudaStream_t st);
 cudaError_t launch_layernorm_bf16(const bf16 *x, const float *g, const float *b, bf16 *y, int T, int d, float eps,
                                   cudaStream_t st);
+cudaError_t launch_layernorm_bf16_f32out(const bf16 *x, const float *g, const float *b, float *y, int T, int d,
+                                         float eps, cudaStream_t st);
+
+// ---- BERT encoder ------------------------------------------------------------
+// x[t] = LayerNorm(word[ids[t]] + pos[p(t)] + type[tt[t]]) with p(t) =
+// pos_ids[t % S] (t % S when pos_ids is null) and tt null meaning type 0;
+// FP32 tables, FP32 statistics; ids / types / positions out of range record
+// status 1 and read row 0.  d % 4 == 0, d <= 2048.
+cudaError_t launch_bert_embed_ln_f32(const int64_t *ids, const int64_t *tt, const int64_t *pos_ids, const float *word,
+                                     const float *pos, const float *type, const float *g, const float *b, float *x,
+                                     int T, int S, int d, int V, int P, int TV, float eps, int *status,
+                                     cudaStream_t st);
+cudaError_t launch_bert_embed_ln_bf16(const int64_t *ids, const int64_t *tt, const int64_t *pos_ids,
+                                      const float *word, const float *pos, const float *type, const float *g,
+                                      const float *b, bf16 *x, int T, int S, int d, int V, int P, int TV, float eps,
+                                      int *status, cudaStream_t st);
+// pooled[b, n] = tanh(hidden[b, 0, :] . w[n, :] + bias[n]) (nn.Linear [out, in]).
+cudaError_t launch_bert_pooler(const float *hidden, const float *w, const float *bias, float *pooled, int B, int S,
+                               int d, cudaStream_t st);
 
 // ---- exact-FP32 SIMT GEMM ----------------------------------------------------
 // C[M, N] (row stride ldc) = epilogue(A[M, K] @ op(B)), op(B) = B[K, N] when
@@ -87,10 +108,11 @@ cudaError_t launch_gemm_tc(const TcGemmPlan &plan, void *C, int ldc, int out_f32
 // qkv [B*S, 3*H*64] (q | k | v, head h at columns h*64), o [B*S, H*64].
 // key_valid may be null (all keys valid); a query row with no attendable key
 // is written by launch_attn_masked_rows afterwards.
+// causal = 0: every key of the sequence is attendable (the BERT encoder).
 cudaError_t launch_attention_f32(const float *qkv, const uint8_t *key_valid, float *o, int B, int S, int H,
-                                 cudaStream_t st);
+                                 cudaStream_t st, int causal = 1);
 cudaError_t launch_attention_bf16(const bf16 *qkv, const uint8_t *key_valid, bf16 *o, int B, int S, int H,
-                                  cudaStream_t st);
+                                  cudaStream_t st, int causal = 1);
 // tcgen05 attention: TMA descriptor over qkv viewed as [B][S][3*H*64].
 struct AttnTcPlan {
   CUtensorMap map_qkv;
@@ -98,13 +120,17 @@ struct AttnTcPlan {
   int B = 0, S = 0, H = 0;
 };
 int attention_tc_plan(AttnTcPlan *plan, const bf16 *qkv, int B, int S, int H);
+// kv_end (optional, [B]): keys at or past kv_end[b] are all masked, so their
+// tiles are skipped (right padding costs no attention work).
 cudaError_t launch_attention_tc(const AttnTcPlan &plan, const uint8_t *key_valid, bf16 *o, int *status,
-                                cudaStream_t st);
-// Rows q < first_valid[b] (no attendable key) get the mean of V over all S keys.
+                                cudaStream_t st, int causal = 1, const int *kv_end = nullptr);
+// Rows without an attendable key get the mean of V over all S keys: with the
+// causal mask the rows q < first_valid[b]; without it, every row of a
+// sequence whose mask is all zero.
 cudaError_t launch_attn_masked_rows_f32(const float *qkv, const int *first_valid, float *o, int B, int S, int H,
-                                        cudaStream_t st);
+                                        cudaStream_t st, int causal = 1);
 cudaError_t launch_attn_masked_rows_bf16(const bf16 *qkv, const int *first_valid, bf16 *o, int B, int S, int H,
-                                         cudaStream_t st);
+                                         cudaStream_t st, int causal = 1);
 
 // ---- weight packing --------------------------------------------------------
 // dst[i] = bf16(decode_e4m3(src[i])), exact (every E4M3 value is a BF16 value).

@@ -65,7 +65,7 @@ __device__ __forceinline__ float fast_exp2(float x) {
 
 __global__ void __launch_bounds__(NT) attention_bf16_kernel(const bf16 *__restrict__ qkv,
                                                             const uint8_t *__restrict__ key_valid,
-                                                            bf16 *__restrict__ o, int S, int H) {
+                                                            bf16 *__restrict__ o, int S, int H, int causal) {
   __shared__ __align__(128) unsigned char sq[BQ * DH * 2];
   __shared__ __align__(128) unsigned char sk[2][BKV * DH * 2];
   __shared__ __align__(128) unsigned char sv[2][BKV * DH * 2];
@@ -97,7 +97,7 @@ __global__ void __launch_bounds__(NT) attention_bf16_kernel(const bf16 *__restri
   load_tile(sv[0], 0, 2 * D + h * DH);
   cp_async_commit();
 
-  const int n_tiles = qb + 1;  // key tiles 0..qb (causal)
+  const int n_tiles = causal ? qb + 1 : (S + BKV - 1) / BKV;  // causal: key tiles 0..qb
   uint32_t qf[4][4];
   float oacc[8][4];
 #pragma unroll
@@ -143,15 +143,15 @@ __global__ void __launch_bounds__(NT) attention_bf16_kernel(const bf16 *__restri
     }
 
     // Masking: causal only on the diagonal tile; key validity everywhere.
-    const bool diag = it == qb;
+    const bool diag = causal && it == qb;
 #pragma unroll
     for (int j = 0; j < 8; ++j)
 #pragma unroll
       for (int e = 0; e < 4; ++e) {
         const int key = kv0 + j * 8 + 2 * t + (e & 1);
         const int row = q0 + warp * 16 + g + (e >> 1) * 8;
-        bool ok = !kv_ok || (key < S && kv_ok[key]);
-        if (diag) ok = ok && key <= row && key < S;
+        bool ok = key < S && (!kv_ok || kv_ok[key]);
+        if (diag) ok = ok && key <= row;
         s[j][e] = ok ? s[j][e] * sl2 : -INFINITY;
       }
 
@@ -219,10 +219,10 @@ __global__ void __launch_bounds__(NT) attention_bf16_kernel(const bf16 *__restri
 }  // namespace
 
 cudaError_t launch_attention_bf16(const bf16 *qkv, const uint8_t *key_valid, bf16 *o, int B, int S, int H,
-                                  cudaStream_t st) {
+                                  cudaStream_t st, int causal) {
   if (B <= 0 || S <= 0 || H <= 0 || H > 65535 || B > 65535) return cudaErrorInvalidValue;
   dim3 grid((S + BQ - 1) / BQ, H, B);
-  attention_bf16_kernel<<<grid, NT, 0, st>>>(qkv, key_valid, o, S, H);
+  attention_bf16_kernel<<<grid, NT, 0, st>>>(qkv, key_valid, o, S, H, causal);
   return cudaGetLastError();
 }
 

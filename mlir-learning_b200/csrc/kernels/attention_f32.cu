@@ -7,9 +7,13 @@
 // softmax chain (src/gpt/README.md:6, lib/DeadArgmaxElimination.cpp:4-6):
 // the S x S scores never leave shared memory and no argmax is computed.
 //
+// With causal = 0 it is the BERT encoder's self-attention
+// (src/bert-base-uncased/lower_bert_model.py:12-18: every key of the
+// sequence, padding mask only).
+//
 // Semantics (identical to the reference on every row that has at least one
-// attendable key): key k is attendable from query q iff k <= q and
-// mask[b, k] != 0; masked keys weigh exactly 0 (exp(finfo.min - max) == 0 in
+// attendable key): key k is attendable from query q iff mask[b, k] != 0 and,
+// when causal, k <= q; masked keys weigh exactly 0 (exp(finfo.min - max) == 0 in
 // FP32).  Rows without an attendable key are finished by
 // attn_masked_rows_*_kernel (mean of V over all S keys, which is what the
 // reference's uniform finfo.min row produces).
@@ -52,7 +56,7 @@ __device__ __forceinline__ float hmax16(float v) {
 
 __global__ void __launch_bounds__(NT) attention_f32_kernel(const float *__restrict__ qkv,
                                                            const uint8_t *__restrict__ key_valid,
-                                                           float *__restrict__ o, int S, int H) {
+                                                           float *__restrict__ o, int S, int H, int causal) {
   extern __shared__ __align__(16) unsigned char smem_raw[];
   AttnSmem &sm = *reinterpret_cast<AttnSmem *>(smem_raw);
   const int nqb = (S + BQ - 1) / BQ;
@@ -86,7 +90,7 @@ __global__ void __launch_bounds__(NT) attention_f32_kernel(const float *__restri
     for (int c = 0; c < 4; ++c) acc[r][c] = 0.f;
   }
 
-  const int kv_end = min(S, q0 + BQ);  // causal: keys beyond the last query are never needed
+  const int kv_end = causal ? min(S, q0 + BQ) : S;  // causal: keys beyond the last query are never needed
   for (int kv0 = 0; kv0 < kv_end; kv0 += BKV) {
     __syncthreads();
     for (int idx = tid; idx < BKV * DH / 4; idx += NT) {
@@ -129,7 +133,7 @@ __global__ void __launch_bounds__(NT) attention_f32_kernel(const float *__restri
 #pragma unroll
       for (int c = 0; c < 4; ++c) {
         const int kj = kv0 + tx * 4 + c;
-        const bool ok = kj <= qi && kj < S && (!kv_ok || kv_ok[kj]);
+        const bool ok = (!causal || kj <= qi) && kj < S && (!kv_ok || kv_ok[kj]);
         s[r][c] = ok ? s[r][c] * scale : -INFINITY;
         mt = fmaxf(mt, s[r][c]);
       }
@@ -196,9 +200,9 @@ __device__ __forceinline__ bf16 from_f<bf16>(float v) { return __float2bfloat16_
 // One block per (head, batch), one thread per head column.
 template <typename T>
 __global__ void attn_masked_rows_kernel(const T *__restrict__ qkv, const int *__restrict__ first_valid,
-                                        T *__restrict__ o, int S, int H) {
+                                        T *__restrict__ o, int S, int H, int causal) {
   const int h = blockIdx.x, b = blockIdx.y, d = threadIdx.x;
-  const int nrows = min(first_valid[b], S);
+  const int nrows = causal ? min(first_valid[b], S) : (first_valid[b] >= S ? S : 0);
   if (nrows == 0) return;
   const int D = H * DH;
   const int64_t ld = 3 * (int64_t)D;
@@ -211,26 +215,26 @@ __global__ void attn_masked_rows_kernel(const T *__restrict__ qkv, const int *__
 }  // namespace
 
 cudaError_t launch_attention_f32(const float *qkv, const uint8_t *key_valid, float *o, int B, int S, int H,
-                                 cudaStream_t st) {
+                                 cudaStream_t st, int causal) {
   if (B <= 0 || S <= 0 || H <= 0 || H > 65535 || B > 65535) return cudaErrorInvalidValue;
   static std::atomic<uint64_t> attr_done{0};
   const int smem = (int)sizeof(AttnSmem);
   cudaError_t e = set_smem_once(attention_f32_kernel, smem, attr_done);
   if (e != cudaSuccess) return e;
   dim3 grid((S + BQ - 1) / BQ, H, B);
-  attention_f32_kernel<<<grid, NT, smem, st>>>(qkv, key_valid, o, S, H);
+  attention_f32_kernel<<<grid, NT, smem, st>>>(qkv, key_valid, o, S, H, causal);
   return cudaGetLastError();
 }
 
 cudaError_t launch_attn_masked_rows_f32(const float *qkv, const int *first_valid, float *o, int B, int S, int H,
-                                        cudaStream_t st) {
-  attn_masked_rows_kernel<float><<<dim3(H, B), DH, 0, st>>>(qkv, first_valid, o, S, H);
+                                        cudaStream_t st, int causal) {
+  attn_masked_rows_kernel<float><<<dim3(H, B), DH, 0, st>>>(qkv, first_valid, o, S, H, causal);
   return cudaGetLastError();
 }
 
 cudaError_t launch_attn_masked_rows_bf16(const bf16 *qkv, const int *first_valid, bf16 *o, int B, int S, int H,
-                                         cudaStream_t st) {
-  attn_masked_rows_kernel<bf16><<<dim3(H, B), DH, 0, st>>>(qkv, first_valid, o, S, H);
+                                         cudaStream_t st, int causal) {
+  attn_masked_rows_kernel<bf16><<<dim3(H, B), DH, 0, st>>>(qkv, first_valid, o, S, H, causal);
   return cudaGetLastError();
 }
 

@@ -1,13 +1,15 @@
-// attention_tc.cu -- BF16 causal attention on the 5th-generation tensor cores
+// attention_tc.cu -- BF16 attention on the 5th-generation tensor cores
 // (tcgen05, S and O accumulators in TMEM, Q / K / V staged by TMA), head
 // dim 64.
 //
 // Replaces, per layer, the reference's q k^T and p v linalg.batch_matmul
 // launches and the scale / causal where / additive mask / softmax generics
 // between them (src/gpt/README.md:6, lib/DeadArgmaxElimination.cpp:4-6) in the
-// BF16 configuration.  Semantics are those of attention_f32.cu: key k is
-// attendable from query q iff k <= q and mask[b, k] != 0; masked keys weigh 0;
-// rows without an attendable key are finished by attn_masked_rows_kernel.
+// BF16 configuration, and the BERT encoder's self-attention
+// (src/bert-base-uncased/lower_bert_model.py:12-18) with causal = 0.
+// Semantics are those of attention_f32.cu: key k is attendable from query q
+// iff mask[b, k] != 0 and, when causal, k <= q; masked keys weigh 0; rows
+// without an attendable key are finished by attn_masked_rows_kernel.
 //
 // Persistent: one CTA per SM walks work items (batch, head, two 128-query
 // tiles q0 .. q0+255), heaviest first; Q is double-buffered so the next
@@ -96,7 +98,7 @@ __device__ __forceinline__ float max3(float a, float b, float c) {
 struct AttnItem {
   int b, h, q0, n_kv[2], n_kv_max;
 };
-__device__ __forceinline__ AttnItem attn_item(int w, int S, int B, int H) {
+__device__ __forceinline__ AttnItem attn_item(int w, int S, int B, int H, int causal, const int *kv_end) {
   AttnItem it;
   const int n_pairs = (S + 2 * BQ - 1) / (2 * BQ);
   const int pair = n_pairs - 1 - w / (B * H);
@@ -104,11 +106,16 @@ __device__ __forceinline__ AttnItem attn_item(int w, int S, int B, int H) {
   it.b = bh / H;
   it.h = bh % H;
   it.q0 = pair * 2 * BQ;
-  const int n_kv_total = (S + BKV - 1) / BKV;
+  // Key tiles past the last unmasked key carry no weight; at least one tile
+  // is kept so every role sees the same non-empty schedule (a sequence
+  // without unmasked keys gets zeros here and is finished by the
+  // masked-rows pass).
+  int n_kv_total = (S + BKV - 1) / BKV;
+  if (kv_end) n_kv_total = min(n_kv_total, max(1, (kv_end[it.b] + BKV - 1) / BKV));
 #pragma unroll
   for (int t = 0; t < 2; ++t) {
     const int qs = it.q0 + t * BQ;
-    it.n_kv[t] = qs < S ? min(qs / BKV + 1, n_kv_total) : 0;
+    it.n_kv[t] = qs < S ? (causal ? min(qs / BKV + 1, n_kv_total) : n_kv_total) : 0;
   }
   it.n_kv_max = max(it.n_kv[0], it.n_kv[1]);
   return it;
@@ -116,7 +123,8 @@ __device__ __forceinline__ AttnItem attn_item(int w, int S, int B, int H) {
 
 __global__ void __launch_bounds__(NTHREADS, 1)
     attention_tc_kernel(const __grid_constant__ CUtensorMap map_qkv, const uint8_t *__restrict__ key_valid,
-                        bf16 *__restrict__ out, int B, int S, int H, int *status) {
+                        bf16 *__restrict__ out, int B, int S, int H, int *status, int causal,
+                        const int *__restrict__ kv_end) {
   extern __shared__ unsigned char smem_raw[];
   unsigned char *sm =
       reinterpret_cast<unsigned char *>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
@@ -169,7 +177,7 @@ __global__ void __launch_bounds__(NTHREADS, 1)
     int qi = 0, kvi = 0;
     bool ok = true;
     for (int w = blockIdx.x; w < n_items && ok; w += gridDim.x, ++qi) {
-      const AttnItem it = attn_item(w, S, B, H);
+      const AttnItem it = attn_item(w, S, B, H, causal, kv_end);
       const int qb = qi & 1;
       if (!mbar_wait_warp(&q_empty[qb], ((qi >> 1) & 1) ^ 1, abort_flag, status)) { ok = false; break; }
       if (leader) {
@@ -228,7 +236,7 @@ __global__ void __launch_bounds__(NTHREADS, 1)
     int qi = 0, kv_base = 0;
     bool ok = true;
     for (int w = blockIdx.x; w < n_items && ok; w += gridDim.x, ++qi) {
-      const AttnItem it = attn_item(w, S, B, H);
+      const AttnItem it = attn_item(w, S, B, H, causal, kv_end);
       const int qb = qi & 1;
       const uint64_t dq = dq0 + qb * 2 * kTile16;
       if (!mbar_wait_warp(&q_full[qb], (qi >> 1) & 1, abort_flag, status)) { ok = false; break; }
@@ -340,7 +348,7 @@ __global__ void __launch_bounds__(NTHREADS, 1)
     };
     int g_base = 0;
     for (int w = blockIdx.x; w < n_items; w += gridDim.x) {
-      const AttnItem it = attn_item(w, S, B, H);
+      const AttnItem it = attn_item(w, S, B, H, causal, kv_end);
       const int n = it.n_kv[t];
       if (n == 0) continue;
       const int qrow = it.q0 + t * BQ + r;  // query index within the sequence
@@ -351,7 +359,7 @@ __global__ void __launch_bounds__(NTHREADS, 1)
         wait(&s_full[t], g & 1);
         tc_fence_after();
         const int kv0 = j * BKV + half * 64;  // first key of this thread's 64 columns
-        const bool diag = j * BKV + BKV > it.q0 + t * BQ;  // tile touches the causal diagonal
+        const bool diag = causal && j * BKV + BKV > it.q0 + t * BQ;  // tile touches the causal diagonal
         const bool tail = j * BKV + BKV > S;                // tile runs past the sequence end
         uint32_t sv[64];
         tmem_ld_32x32b_x32(s_tmem, *reinterpret_cast<uint32_t(*)[32]>(&sv[0]));
@@ -391,7 +399,7 @@ __global__ void __launch_bounds__(NTHREADS, 1)
 #pragma unroll
             for (int e = 0; e < 16; ++e) {
               const int key = kv0 + c + e;
-              const bool okk = ((fw[e >> 2] >> (8 * (e & 3))) & 0xffu) != 0 && key <= qrow && key < S;
+              const bool okk = ((fw[e >> 2] >> (8 * (e & 3))) & 0xffu) != 0 && (!causal || key <= qrow) && key < S;
               const float x = okk ? __uint_as_float(sv[c + e]) : -INFINITY;
               sv[c + e] = __float_as_uint(x);
               mx[e & 7] = fmaxf(mx[e & 7], x);
@@ -536,7 +544,7 @@ int attention_tc_plan(AttnTcPlan *plan, const bf16 *qkv, int B, int S, int H) {
 }
 
 cudaError_t launch_attention_tc(const AttnTcPlan &plan, const uint8_t *key_valid, bf16 *o, int *status,
-                                cudaStream_t st) {
+                                cudaStream_t st, int causal, const int *kv_end) {
   if (plan.B <= 0 || plan.S <= 0 || plan.H <= 0 || plan.H > 65535 || plan.B > 65535) return cudaErrorInvalidValue;
   static std::atomic<uint64_t> attr_done{0};
   cudaError_t e = set_smem_once(attention_tc_kernel, AttnTcSmem::ALLOC, attr_done);
@@ -547,7 +555,7 @@ cudaError_t launch_attention_tc(const AttnTcPlan &plan, const uint8_t *key_valid
   const int items = ((plan.S + 2 * BQ - 1) / (2 * BQ)) * plan.B * plan.H;
   const int grid = items < sms ? items : sms;
   attention_tc_kernel<<<grid, NTHREADS, AttnTcSmem::ALLOC, st>>>(plan.map_qkv, key_valid, o, plan.B, plan.S, plan.H,
-                                                                  status);
+                                                                  status, causal, kv_end);
   return cudaGetLastError();
 }
 

@@ -14,25 +14,35 @@ namespace gpt2 {
 // Mask preparation: one block per sequence.
 // ---------------------------------------------------------------------------
 __global__ void seq_info_kernel(const int64_t *__restrict__ mask, int S, int *__restrict__ first_valid,
-                                uint8_t *__restrict__ key_valid) {
+                                uint8_t *__restrict__ key_valid, int *__restrict__ kv_end) {
   const int b = blockIdx.x;
-  __shared__ int first;
-  if (threadIdx.x == 0) first = S;
+  __shared__ int first, last;
+  if (threadIdx.x == 0) {
+    first = S;
+    last = -1;
+  }
   __syncthreads();
-  int local = S;
+  int lo = S, hi = -1;
   for (int k = threadIdx.x; k < S; k += blockDim.x) {
     const bool v = mask[(int64_t)b * S + k] != 0;
     key_valid[(int64_t)b * S + k] = v ? 1 : 0;
-    if (v && k < local) local = k;
+    if (v) {
+      lo = min(lo, k);
+      hi = max(hi, k);
+    }
   }
-  if (local < S) atomicMin(&first, local);
+  if (lo < S) atomicMin(&first, lo);
+  if (hi >= 0) atomicMax(&last, hi);
   __syncthreads();
-  if (threadIdx.x == 0) first_valid[b] = first;
+  if (threadIdx.x == 0) {
+    first_valid[b] = first;
+    if (kv_end) kv_end[b] = last + 1;
+  }
 }
 
 cudaError_t launch_seq_info(const int64_t *mask, int B, int S, int *first_valid, uint8_t *key_valid,
-                            cudaStream_t st) {
-  seq_info_kernel<<<B, 256, 0, st>>>(mask, S, first_valid, key_valid);
+                            cudaStream_t st, int *kv_end) {
+  seq_info_kernel<<<B, 256, 0, st>>>(mask, S, first_valid, key_valid, kv_end);
   return cudaGetLastError();
 }
 
@@ -146,9 +156,9 @@ __global__ void layernorm_f32_kernel(const float *__restrict__ x, const float *_
   }
 }
 
-template <int VPT>
+template <int VPT, typename OutT>
 __global__ void layernorm_bf16_kernel(const bf16 *__restrict__ x, const float *__restrict__ g,
-                                      const float *__restrict__ b, bf16 *__restrict__ y, int T, int d, float eps) {
+                                      const float *__restrict__ b, OutT *__restrict__ y, int T, int d, float eps) {
   const int row = (blockIdx.x * blockDim.x + threadIdx.x) >> 5;
   const int lane = threadIdx.x & 31;
   if (row >= T) return;
@@ -183,7 +193,6 @@ __global__ void layernorm_bf16_kernel(const bf16 *__restrict__ x, const float *_
     }
   }
   const float rstd = rsqrtf(warp_sum(q) / d + eps);
-  uint4 *yr = reinterpret_cast<uint4 *>(y + (int64_t)row * d);
 #pragma unroll
   for (int i = 0; i < VPT; ++i) {
     const int c = lane + 32 * i;
@@ -192,13 +201,18 @@ __global__ void layernorm_bf16_kernel(const bf16 *__restrict__ x, const float *_
       const float4 b0 = reinterpret_cast<const float4 *>(b)[2 * c], b1 = reinterpret_cast<const float4 *>(b)[2 * c + 1];
       const float gg[8] = {g0.x, g0.y, g0.z, g0.w, g1.x, g1.y, g1.z, g1.w};
       const float bb[8] = {b0.x, b0.y, b0.z, b0.w, b1.x, b1.y, b1.z, b1.w};
-      uint4 r;
-      uint32_t *r2 = reinterpret_cast<uint32_t *>(&r);
+      float o[8];
 #pragma unroll
-      for (int j = 0; j < 4; ++j)
-        r2[j] = pack_bf16x2((v[i][2 * j] - mean) * rstd * gg[2 * j] + bb[2 * j],
-                            (v[i][2 * j + 1] - mean) * rstd * gg[2 * j + 1] + bb[2 * j + 1]);
-      yr[c] = r;
+      for (int j = 0; j < 8; ++j) o[j] = (v[i][j] - mean) * rstd * gg[j] + bb[j];
+      if constexpr (sizeof(OutT) == 4) {  // FP32 output (the encoder's last LayerNorm)
+        float4 *yr = reinterpret_cast<float4 *>(y + (int64_t)row * d);
+        yr[2 * c] = make_float4(o[0], o[1], o[2], o[3]);
+        yr[2 * c + 1] = make_float4(o[4], o[5], o[6], o[7]);
+      } else {
+        uint4 *yr = reinterpret_cast<uint4 *>(y + (int64_t)row * d);
+        yr[c] = make_uint4(pack_bf16x2(o[0], o[1]), pack_bf16x2(o[2], o[3]), pack_bf16x2(o[4], o[5]),
+                           pack_bf16x2(o[6], o[7]));
+      }
     }
   }
 }
@@ -232,23 +246,35 @@ cudaError_t launch_layernorm_f32(const float *x, const float *g, const float *b,
   return cudaGetLastError();
 }
 
-cudaError_t launch_layernorm_bf16(const bf16 *x, const float *g, const float *b, bf16 *y, int T, int d, float eps,
-                                  cudaStream_t st) {
+namespace {
+template <typename OutT>
+cudaError_t layernorm_bf16_any(const bf16 *x, const float *g, const float *b, OutT *y, int T, int d, float eps,
+                               cudaStream_t st) {
   if (d % 8 || d > 256 * 8) return cudaErrorInvalidValue;
-  const int threads = 256, rows = threads / 32;
+  const int threads = 256, blocks = (T + threads / 32 - 1) / (threads / 32);
   switch ((d + 255) / 256) {
-    LN_CASE(1, layernorm_bf16_kernel, x, g, b, y, T, d, eps)
-    LN_CASE(2, layernorm_bf16_kernel, x, g, b, y, T, d, eps)
-    LN_CASE(3, layernorm_bf16_kernel, x, g, b, y, T, d, eps)
-    LN_CASE(4, layernorm_bf16_kernel, x, g, b, y, T, d, eps)
-    LN_CASE(5, layernorm_bf16_kernel, x, g, b, y, T, d, eps)
-    LN_CASE(6, layernorm_bf16_kernel, x, g, b, y, T, d, eps)
-    LN_CASE(7, layernorm_bf16_kernel, x, g, b, y, T, d, eps)
-    LN_CASE(8, layernorm_bf16_kernel, x, g, b, y, T, d, eps)
-    default:
-      return cudaErrorInvalidValue;
+    case 1: layernorm_bf16_kernel<1, OutT><<<blocks, threads, 0, st>>>(x, g, b, y, T, d, eps); break;
+    case 2: layernorm_bf16_kernel<2, OutT><<<blocks, threads, 0, st>>>(x, g, b, y, T, d, eps); break;
+    case 3: layernorm_bf16_kernel<3, OutT><<<blocks, threads, 0, st>>>(x, g, b, y, T, d, eps); break;
+    case 4: layernorm_bf16_kernel<4, OutT><<<blocks, threads, 0, st>>>(x, g, b, y, T, d, eps); break;
+    case 5: layernorm_bf16_kernel<5, OutT><<<blocks, threads, 0, st>>>(x, g, b, y, T, d, eps); break;
+    case 6: layernorm_bf16_kernel<6, OutT><<<blocks, threads, 0, st>>>(x, g, b, y, T, d, eps); break;
+    case 7: layernorm_bf16_kernel<7, OutT><<<blocks, threads, 0, st>>>(x, g, b, y, T, d, eps); break;
+    case 8: layernorm_bf16_kernel<8, OutT><<<blocks, threads, 0, st>>>(x, g, b, y, T, d, eps); break;
+    default: return cudaErrorInvalidValue;
   }
   return cudaGetLastError();
+}
+}  // namespace
+
+cudaError_t launch_layernorm_bf16(const bf16 *x, const float *g, const float *b, bf16 *y, int T, int d, float eps,
+                                  cudaStream_t st) {
+  return layernorm_bf16_any(x, g, b, y, T, d, eps, st);
+}
+
+cudaError_t launch_layernorm_bf16_f32out(const bf16 *x, const float *g, const float *b, float *y, int T, int d,
+                                         float eps, cudaStream_t st) {
+  return layernorm_bf16_any(x, g, b, y, T, d, eps, st);
 }
 
 // ---------------------------------------------------------------------------

@@ -25,6 +25,7 @@ __device__ __forceinline__ float apply_epi(float acc, const float *bias, const f
   if (EPI == EPI_NONE) return acc;
   float v = acc + bias[col];
   if (EPI == EPI_BIAS_GELU) v = gelu_new_exact(v);
+  if (EPI == EPI_BIAS_GELU_ERF) v = gelu_erf(v);
   if (EPI == EPI_BIAS_RESID) v = resid[ridx] + v;
   return v;
 }
@@ -157,6 +158,7 @@ cudaError_t launch_gemm_f32(const float *A, const float *B, int b_nk, float *C, 
     case EPI_BIAS: return launch_epi<EPI_BIAS>(A, B, b_nk, C, M, N, K, ldc, bias, resid, st);
     case EPI_BIAS_GELU: return launch_epi<EPI_BIAS_GELU>(A, B, b_nk, C, M, N, K, ldc, bias, resid, st);
     case EPI_BIAS_RESID: return launch_epi<EPI_BIAS_RESID>(A, B, b_nk, C, M, N, K, ldc, bias, resid, st);
+    case EPI_BIAS_GELU_ERF: return launch_epi<EPI_BIAS_GELU_ERF>(A, B, b_nk, C, M, N, K, ldc, bias, resid, st);
   }
   return cudaErrorInvalidValue;
 }

@@ -233,6 +233,7 @@ __global__ void __launch_bounds__(NTHREADS, 1)
           float x = __uint_as_float(r[j]);
           if (EPI != EPI_NONE) x += __shfl_sync(0xffffffffu, j < 32 ? bias_lo : bias_hi, j & 31);
           if (EPI == EPI_BIAS_GELU) x = gelu_new_fast(x);
+          if (EPI == EPI_BIAS_GELU_ERF) x = gelu_erf(x);
           v[j] = x;
         }
         const bool full_chunk = col0 + CH <= N;
@@ -394,6 +395,8 @@ cudaError_t dispatch_epi(const TcGemmPlan &p, void *C, int ldc, int out_f32, con
     case EPI_BIAS: return launch_store<BN, EPI_BIAS, 0>(p, C, ldc, bias, resid, status, num_sms, st, scale);
     case EPI_BIAS_GELU: return launch_store<BN, EPI_BIAS_GELU, 0>(p, C, ldc, bias, resid, status, num_sms, st, scale);
     case EPI_BIAS_RESID: return launch_store<BN, EPI_BIAS_RESID, 0>(p, C, ldc, bias, resid, status, num_sms, st, scale);
+    case EPI_BIAS_GELU_ERF:
+      return launch_store<BN, EPI_BIAS_GELU_ERF, 0>(p, C, ldc, bias, resid, status, num_sms, st, scale);
   }
   return cudaErrorInvalidValue;
 }

@@ -24,34 +24,6 @@ namespace {
 thread_local std::string g_err;
 Context *g_ctx = nullptr;
 
-int cuda_fail(cudaError_t e, const char *what) {
-  set_error("%s: %s", what, cudaGetErrorString(e));
-  return -2;
-}
-#define CK(call)                                   \
-  do {                                             \
-    cudaError_t e_ = (call);                       \
-    if (e_ != cudaSuccess) return cuda_fail(e_, #call); \
-  } while (0)
-
-// A kernel launch of kind K on stream `st`, bracketed by profiler events when
-// profiling is on.
-#define CKP(K, call)                                                          \
-  do {                                                                        \
-    cudaEvent_t pa_ = nullptr, pb_ = nullptr;                                 \
-    if (c.prof.on) {                                                          \
-      pa_ = prof_event(c.prof);                                               \
-      pb_ = prof_event(c.prof);                                               \
-      if (pa_ && pb_) cudaEventRecord(pa_, st);                               \
-    }                                                                         \
-    cudaError_t e_ = (call);                                                  \
-    if (e_ != cudaSuccess) return cuda_fail(e_, #call);                       \
-    if (pa_ && pb_) {                                                         \
-      cudaEventRecord(pb_, st);                                               \
-      c.prof.kinds.push_back(K);                                              \
-    }                                                                         \
-  } while (0)
-
 void free_ws(Workspace &w) {
   void *ptrs[] = {w.x, w.a, w.qkv, w.o, w.u, w.first_valid, w.key_valid, w.ids, w.mask};
   for (void *p : ptrs)
@@ -319,7 +291,11 @@ int ensure_plans(Context &c, int64_t T) {
 }
 }  // namespace
 
-namespace {
+int cuda_fail(cudaError_t e, const char *what) {
+  set_error("%s: %s", what, cudaGetErrorString(e));
+  return -2;
+}
+
 cudaEvent_t prof_event(Profiler &p) {
   if (p.used == p.pool.size()) {
     cudaEvent_t e;
@@ -328,17 +304,15 @@ cudaEvent_t prof_event(Profiler &p) {
   }
   return p.pool[p.used++];
 }
-}  // namespace
 
-int profile_begin(Context &c) {
-  c.prof.on = true;
-  c.prof.used = 0;
-  c.prof.kinds.clear();
+int profile_begin(Profiler &p) {
+  p.on = true;
+  p.used = 0;
+  p.kinds.clear();
   return 0;
 }
 
-int profile_end(Context &c, double *ms, int64_t *count, int n) {
-  Profiler &p = c.prof;
+int profile_end(Profiler &p, double *ms, int64_t *count, int n) {
   p.on = false;
   for (int k = 0; k < n; ++k) {
     ms[k] = 0.0;

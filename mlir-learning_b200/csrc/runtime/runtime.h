@@ -113,9 +113,36 @@ int ensure_workspace(Context &c, int B, int S);
 int forward_device(Context &c, const int64_t *d_ids, const int64_t *d_mask, int B, int S, float *d_logits,
                    int64_t ld_logits, cudaStream_t st);
 int forward_launch_count(const Context &c, int has_mask);
-int profile_begin(Context &c);
-int profile_end(Context &c, double *ms, int64_t *count, int n);
+int profile_begin(Profiler &p);
+int profile_end(Profiler &p, double *ms, int64_t *count, int n);
+cudaEvent_t prof_event(Profiler &p);  // the next event of the pool (null if none can be created)
 
 void set_error(const char *fmt, ...);
+int cuda_fail(cudaError_t e, const char *what);  // records the error text, returns -2
+
+// Status-checked CUDA call inside a function returning int.
+#define CK(call)                                          \
+  do {                                                    \
+    cudaError_t e_ = (call);                              \
+    if (e_ != cudaSuccess) return cuda_fail(e_, #call);   \
+  } while (0)
+
+// A kernel launch of kind K on stream `st` of context `c`, bracketed by
+// profiler events when profiling is on.
+#define CKP(K, call)                                      \
+  do {                                                    \
+    cudaEvent_t pa_ = nullptr, pb_ = nullptr;             \
+    if (c.prof.on) {                                      \
+      pa_ = prof_event(c.prof);                           \
+      pb_ = prof_event(c.prof);                           \
+      if (pa_ && pb_) cudaEventRecord(pa_, st);           \
+    }                                                     \
+    cudaError_t e_ = (call);                              \
+    if (e_ != cudaSuccess) return cuda_fail(e_, #call);   \
+    if (pa_ && pb_) {                                     \
+      cudaEventRecord(pb_, st);                           \
+      c.prof.kinds.push_back(K);                          \
+    }                                                     \
+  } while (0)
 
 }  // namespace gpt2
