@@ -222,6 +222,17 @@ size_t gpt2k_attention_workspace_bytes(int B, int S);
 int gpt2k_attention(const void *qkv, const int64_t *d_mask, void *o, int B, int S, int H, int dtype,
                     void *workspace, void *stream);
 
+/* Attention with the causal mask selectable: causal = 1 is gpt2k_attention;
+ * causal = 0 lets every query attend to every unmasked key of its sequence
+ * (the BERT encoder's self-attention), and a sequence whose mask is all
+ * zero gets the mean of V in every row.  With a mask, key tiles past a
+ * sequence's last unmasked key are skipped.  workspace: device memory of
+ * gpt2k_attention_ex_workspace_bytes(B, S) bytes (may be NULL without a
+ * mask). */
+size_t gpt2k_attention_ex_workspace_bytes(int B, int S);
+int gpt2k_attention_ex(const void *qkv, const int64_t *d_mask, void *o, int B, int S, int H, int dtype, int causal,
+                       void *workspace, void *stream);
+
 /* Attention without a workspace argument, for callers that cannot allocate
  * device memory at call time: hosts whose device memory is reserved up front
  * by another allocator, generated code with no allocation hook at this call,

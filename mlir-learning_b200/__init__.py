@@ -126,6 +126,9 @@ def lib() -> ctypes.CDLL:
     L.gpt2k_attention_workspace_bytes.restype = ctypes.c_size_t
     L.gpt2k_attention.argtypes = [vp, vp, vp, i32, i32, i32, i32, vp, vp]
     L.gpt2k_attention_noalloc.argtypes = [vp, vp, vp, i32, i32, i32, i32, vp]
+    L.gpt2k_attention_ex_workspace_bytes.argtypes = [i32, i32]
+    L.gpt2k_attention_ex_workspace_bytes.restype = ctypes.c_size_t
+    L.gpt2k_attention_ex.argtypes = [vp, vp, vp, i32, i32, i32, i32, i32, vp, vp]
     L.gpt2k_embed.argtypes = [vp, vp, vp, vp, i32, i32, i32, i32, i32, vp, vp]
     _lib = L
     return L
@@ -349,6 +352,14 @@ def k_attention_workspace_bytes(B, S) -> int:
 
 def k_attention(qkv, mask, o, B, S, H, dtype, workspace=None, stream=None):
     _check(lib().gpt2k_attention(qkv, mask, o, B, S, H, dtype, workspace, stream), "gpt2k_attention")
+
+
+def k_attention_ex_workspace_bytes(B, S) -> int:
+    return int(lib().gpt2k_attention_ex_workspace_bytes(B, S))
+
+
+def k_attention_ex(qkv, mask, o, B, S, H, dtype, causal, workspace=None, stream=None):
+    _check(lib().gpt2k_attention_ex(qkv, mask, o, B, S, H, dtype, causal, workspace, stream), "gpt2k_attention_ex")
 
 
 def k_attention_noalloc(qkv, mask, o, B, S, H, dtype, stream=None):

@@ -475,6 +475,59 @@ int gpt2k_attention(const void *qkv, const int64_t *d_mask, void *o, int B, int 
   return r;
 }
 
+size_t gpt2k_attention_ex_workspace_bytes(int B, int S) {
+  return 256 + 2 * sizeof(int) * (size_t)B + (size_t)B * S;
+}
+
+int gpt2k_attention_ex(const void *qkv, const int64_t *d_mask, void *o, int B, int S, int H, int dtype, int causal,
+                       void *workspace, void *stream) {
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  const int c = causal ? 1 : 0;
+  int *first_valid = nullptr, *kv_end = nullptr;
+  uint8_t *key_valid = nullptr;
+  if (d_mask) {
+    if (!workspace) {
+      set_error("gpt2k_attention_ex: a mask needs a workspace");
+      return GPT2_EINVAL;
+    }
+    first_valid = static_cast<int *>(workspace);
+    kv_end = first_valid + B;
+    key_valid = static_cast<uint8_t *>(workspace) + 256 + 2 * sizeof(int) * (size_t)B;
+    int r = ck(launch_seq_info(d_mask, B, S, first_valid, key_valid, st, kv_end), "gpt2k_attention_ex");
+    if (r) return r;
+  }
+  int r;
+  if (dtype == GPT2_DTYPE_F32) {
+    r = ck(launch_attention_f32(static_cast<const float *>(qkv), key_valid, static_cast<float *>(o), B, S, H, st, c),
+           "gpt2k_attention_ex");
+    if (!r && d_mask)
+      r = ck(launch_attn_masked_rows_f32(static_cast<const float *>(qkv), first_valid, static_cast<float *>(o), B, S,
+                                         H, st, c),
+             "gpt2k_attention_ex");
+    return r;
+  }
+  if (dtype == GPT2_DTYPE_BF16) {
+    AttnTcPlan plan;
+    if (attention_tc_plan(&plan, static_cast<const bf16 *>(qkv), B, S, H)) {
+      set_error("gpt2k_attention_ex: TMA descriptor creation failed");
+      return GPT2_EINVAL;
+    }
+    r = ck(launch_attention_tc(plan, key_valid, static_cast<bf16 *>(o), nullptr, st, c, kv_end),
+           "gpt2k_attention_ex");
+  } else if (dtype == GPT2K_ATTN_BF16_MMA_SYNC) {
+    r = ck(launch_attention_bf16(static_cast<const bf16 *>(qkv), key_valid, static_cast<bf16 *>(o), B, S, H, st, c),
+           "gpt2k_attention_ex");
+  } else {
+    set_error("gpt2k_attention_ex: bad dtype");
+    return GPT2_EINVAL;
+  }
+  if (!r && d_mask)
+    r = ck(launch_attn_masked_rows_bf16(static_cast<const bf16 *>(qkv), first_valid, static_cast<bf16 *>(o), B, S, H,
+                                        st, c),
+           "gpt2k_attention_ex");
+  return r;
+}
+
 int gpt2k_embed(const int64_t *d_ids, const void *wte, const void *wpe, void *x, int T, int S, int d, int V, int dtype,
                 int *d_status, void *stream) {
   cudaStream_t st = static_cast<cudaStream_t>(stream);

@@ -312,6 +312,26 @@ __device__ __forceinline__ float gelu_new_exact(float x) {
 // The exact GELU of BERT ("gelu"): 0.5 x (1 + erf(x / sqrt(2))), CUDA's erff.
 __device__ __forceinline__ float gelu_erf(float x) { return 0.5f * x * (1.0f + erff(x * 0.7071067811865476f)); }
 
+// The same GELU for the BF16 epilogues, with erf from Abramowitz & Stegun,
+// Handbook of Mathematical Functions, formula 7.1.26 (|error| <= 1.5e-7 for
+// z >= 0): 1 - erf(z) = (a1 t + a2 t^2 + a3 t^3 + a4 t^4 + a5 t^5) e^(-z^2),
+// t = 1 / (1 + p z).  For x < 0 the factor 1 + erf(z) is that product itself,
+// so no cancellation occurs in the negative tail.  Two MUFU operations
+// (reciprocal, exp2) instead of erff's longer sequence; the error is far
+// below the bf16 rounding of the result.
+__device__ __forceinline__ float gelu_erf_fast(float x) {
+  const float z = fabsf(x) * 0.7071067811865476f;
+  float t, e;
+  asm("rcp.approx.ftz.f32 %0, %1;" : "=f"(t) : "f"(fmaf(0.3275911f, z, 1.0f)));
+  asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(e) : "f"(-z * z * 1.4426950408889634f));
+  float poly = fmaf(1.061405429f, t, -1.453152027f);
+  poly = fmaf(poly, t, 1.421413741f);
+  poly = fmaf(poly, t, -0.284496736f);
+  poly = fmaf(poly, t, 0.254829592f);
+  const float q = poly * t * e;  // 1 - erf(|x| / sqrt 2)
+  return 0.5f * x * (x >= 0.f ? 2.0f - q : q);
+}
+
 __device__ __forceinline__ float gelu_new_fast(float x) {
   const float k = 0.7978845608028654f;
   return 0.5f * x * (1.0f + tanh_approx(k * (x + 0.044715f * x * x * x)));

@@ -371,7 +371,27 @@ __global__ void __launch_bounds__(NTHREADS, 1)
         float mx[8];
 #pragma unroll
         for (int e = 0; e < 8; ++e) mx[e] = -INFINITY;
-        if (diag || tail || kv_ok) {
+        // Key flags are checked element by element only when this half-tile
+        // has a masked key (one 64-byte AND test, warp-uniform: every lane
+        // of the warp reads the same 64 flags); right-padded batches take
+        // the plain path on every tile but the last.
+        bool need_mask = diag || tail;
+        if (!need_mask && kv_ok) {
+          const uint8_t *fp = kv_ok + kv0;
+          if ((reinterpret_cast<uintptr_t>(fp) & 15) == 0) {
+            const uint4 *f4 = reinterpret_cast<const uint4 *>(fp);
+            uint32_t all = 0x01010101u;
+#pragma unroll
+            for (int c4 = 0; c4 < 4; ++c4) {
+              const uint4 v4 = f4[c4];
+              all &= v4.x & v4.y & v4.z & v4.w;
+            }
+            need_mask = all != 0x01010101u;  // flags are 0 / 1 bytes
+          } else {
+            need_mask = true;
+          }
+        }
+        if (need_mask) {
 #pragma unroll
           for (int c = 0; c < 64; c += 16) {
             uint32_t fw[4] = {0x01010101u, 0x01010101u, 0x01010101u, 0x01010101u};

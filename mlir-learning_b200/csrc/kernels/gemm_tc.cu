@@ -233,7 +233,7 @@ __global__ void __launch_bounds__(NTHREADS, 1)
           float x = __uint_as_float(r[j]);
           if (EPI != EPI_NONE) x += __shfl_sync(0xffffffffu, j < 32 ? bias_lo : bias_hi, j & 31);
           if (EPI == EPI_BIAS_GELU) x = gelu_new_fast(x);
-          if (EPI == EPI_BIAS_GELU_ERF) x = gelu_erf(x);
+          if (EPI == EPI_BIAS_GELU_ERF) x = gelu_erf_fast(x);
           v[j] = x;
         }
         const bool full_chunk = col0 + CH <= N;

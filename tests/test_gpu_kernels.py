@@ -30,6 +30,8 @@ def _epi_ref(torch, acc, bias, resid, epi):
     v = acc + bias.double()
     if epi == pkg.EPI_BIAS_GELU:
         v = 0.5 * v * (1.0 + torch.tanh(0.7978845608028654 * (v + 0.044715 * v ** 3)))
+    if epi == pkg.EPI_BIAS_GELU_ERF:
+        v = 0.5 * v * (1.0 + torch.erf(v * 0.7071067811865476))
     if epi == pkg.EPI_BIAS_RESID:
         v = resid.double() + v
     return v
@@ -39,6 +41,7 @@ def _epi_ref(torch, acc, bias, resid, epi):
     (5, 2304, 768, 0, pkg.EPI_BIAS, 2304),
     (130, 768, 3072, 0, pkg.EPI_BIAS_RESID, 768),
     (257, 3072, 768, 0, pkg.EPI_BIAS_GELU, 3072),
+    (129, 3072, 768, 1, pkg.EPI_BIAS_GELU_ERF, 3072),
     (77, 50257, 768, 1, pkg.EPI_NONE, 50257),
     (64, 1000, 128, 1, pkg.EPI_NONE, 1008),
 ])
@@ -63,6 +66,8 @@ def test_gemm_f32(torch, M, N, K, b_nk, epi, ldc):
     (1000, 2304, 768, pkg.EPI_BIAS, 0, 256, 2304),
     (300, 768, 3072, pkg.EPI_BIAS_RESID, 0, 128, 768),
     (513, 3072, 768, pkg.EPI_BIAS_GELU, 0, 256, 3072),
+    (513, 3072, 768, pkg.EPI_BIAS_GELU_ERF, 0, 256, 3072),
+    (300, 3072, 768, pkg.EPI_BIAS_GELU_ERF, 0, 128, 3072),
     (200, 50257, 768, pkg.EPI_NONE, 1, 256, 50304),
     (200, 50257, 768, pkg.EPI_NONE, 1, 128, 50257),
     (64, 1000, 128, pkg.EPI_BIAS, 1, 128, 1000),
@@ -113,14 +118,16 @@ def test_layernorm(torch, T, d, dtype):
     assert err <= (1e-5 if dtype == 0 else 2e-2 * ref.abs().max().item()), err
 
 
-def attention_ref(torch, qkv, mask, B, S, H):
+def attention_ref(torch, qkv, mask, B, S, H, causal=True):
     """float64 restatement of the oracle's attention semantics."""
     D = H * 64
     x = qkv.double().view(B, S, 3, H, 64)
     q, k, v = x[:, :, 0].transpose(1, 2), x[:, :, 1].transpose(1, 2), x[:, :, 2].transpose(1, 2)
     s = q @ k.transpose(-1, -2) * 0.125
-    causal = torch.ones(S, S, dtype=torch.bool, device=qkv.device).tril()
-    ok = causal[None, None]
+    ok = torch.ones(S, S, dtype=torch.bool, device=qkv.device)
+    if causal:
+        ok = ok.tril()
+    ok = ok[None, None]
     if mask is not None:
         ok = ok & (mask != 0)[:, None, None, :]
     s = s.masked_fill(~ok, float("-inf"))
@@ -160,6 +167,48 @@ def test_attention(torch, dtype, B, S, H, masked):
     err = (o.double() - ref).abs().max().item()
     assert err <= (2e-5 if dtype == 0 else 3e-2), err
     assert torch.isfinite(o.float()).all()
+
+
+@pytest.mark.parametrize("dtype", [0, 1, 2])
+@pytest.mark.parametrize("B,S,H,mask_kind", [(2, 1, 12, None), (3, 77, 2, "mixed"), (1, 512, 12, None),
+                                             (4, 512, 2, "right"), (3, 300, 12, "mixed"), (2, 129, 3, "right"),
+                                             (5, 384, 2, "right")])
+def test_attention_non_causal(torch, dtype, B, S, H, mask_kind):
+    """The encoder (BERT) form: every unmasked key of the sequence; right padding (lengths ending
+    inside, on and past 128-key tiles, so key tiles past the last valid key are skipped), holes,
+    left padding and a sequence with no unmasked key."""
+    g = torch.Generator(device="cuda").manual_seed(B * 7919 + S)
+    qkv = torch.randn(B * S, 3 * H * 64, device="cuda", generator=g)
+    mask = None
+    if mask_kind == "right":
+        lens = [S, max(1, S // 2), 64, 128, 129, 1][:B]
+        mask = torch.zeros(B, S, dtype=torch.int64, device="cuda")
+        for b, n in enumerate(lens):
+            mask[b, :min(n, S)] = 1
+    elif mask_kind == "mixed":
+        mask = torch.ones(B, S, dtype=torch.int64, device="cuda")
+        mask[0, : min(5, S)] = 0
+        if B > 1:
+            mask[1, S // 3: S // 2] = 0
+        if B > 2:
+            mask[2, :] = 0
+    if dtype >= 1:
+        qkv = qkv.bfloat16()
+    o = torch.full((B * S, H * 64), 3.0, device="cuda", dtype=qkv.dtype)
+    ws = torch.empty(pkg.k_attention_ex_workspace_bytes(B, S), dtype=torch.uint8, device="cuda")
+    pkg.k_attention_ex(qkv.data_ptr(), mask.data_ptr() if mask is not None else None, o.data_ptr(), B, S, H, dtype, 0,
+                       ws.data_ptr(), _stream(torch))
+    torch.cuda.synchronize()
+    ref = attention_ref(torch, qkv, mask, B, S, H, causal=False)
+    err = (o.double() - ref).abs().max().item()
+    assert err <= (2e-5 if dtype == 0 else 3e-2), err
+    # causal = 1 through the same entry point equals gpt2k_attention
+    o2 = torch.full_like(o, 3.0)
+    pkg.k_attention_ex(qkv.data_ptr(), mask.data_ptr() if mask is not None else None, o2.data_ptr(), B, S, H, dtype,
+                       1, ws.data_ptr(), _stream(torch))
+    torch.cuda.synchronize()
+    ref_c = attention_ref(torch, qkv, mask, B, S, H, causal=True)
+    assert (o2.double() - ref_c).abs().max().item() <= (2e-5 if dtype == 0 else 3e-2)
 
 
 @pytest.mark.parametrize("dtype", [0, 1])
