@@ -116,14 +116,22 @@ cudaError_t launch_attention_bf16(const bf16 *qkv, const uint8_t *key_valid, bf1
 // tcgen05 attention: TMA descriptor over qkv viewed as [B][S][3*H*64].
 struct AttnTcPlan {
   CUtensorMap map_qkv;
+  CUtensorMap map_out;  // o viewed as [B][S][H*64], for the TMA-stored epilogue
   const bf16 *qkv = nullptr;
+  const bf16 *out = nullptr;
   int B = 0, S = 0, H = 0;
 };
-int attention_tc_plan(AttnTcPlan *plan, const bf16 *qkv, int B, int S, int H);
+// Builds the qkv descriptor and, when o is given, the output descriptor.
+int attention_tc_plan(AttnTcPlan *plan, const bf16 *qkv, int B, int S, int H, const bf16 *o = nullptr);
 // kv_end (optional, [B]): keys at or past kv_end[b] are all masked, so their
 // tiles are skipped (right padding costs no attention work).
 cudaError_t launch_attention_tc(const AttnTcPlan &plan, const uint8_t *key_valid, bf16 *o, int *status,
                                 cudaStream_t st, int causal = 1, const int *kv_end = nullptr);
+// The same attention with one softmax thread per query row and P kept in
+// tensor memory (the P.V MMA reads its A operand from TMEM); o must be the
+// output the plan was built with.
+cudaError_t launch_attention_tc2(const AttnTcPlan &plan, const uint8_t *key_valid, bf16 *o, int *status,
+                                 cudaStream_t st, int causal = 1, const int *kv_end = nullptr);
 // Rows without an attendable key get the mean of V over all S keys: with the
 // causal mask the rows q < first_valid[b]; without it, every row of a
 // sequence whose mask is all zero.

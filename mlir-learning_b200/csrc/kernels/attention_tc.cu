@@ -1,6 +1,9 @@
-// attention_tc.cu -- BF16 attention on the 5th-generation tensor cores
-// (tcgen05, S and O accumulators in TMEM, Q / K / V staged by TMA), head
-// dim 64.
+// attention_tc.cu -- an earlier BF16 attention on the 5th-generation tensor
+// cores (tcgen05, S and O accumulators in TMEM, Q / K / V staged by TMA,
+// two softmax threads per query row, P through shared memory), head dim 64.
+// The forward runs attention_tc2.cu; this kernel stays as an independent
+// cross-check (gpt2k_attention_ex with GPT2K_ATTN_BF16_TC_SMEM_P) and owns
+// the tensor-map plan both kernels use.
 //
 // Replaces, per layer, the reference's q k^T and p v linalg.batch_matmul
 // launches and the scale / causal where / additive mask / softmax generics
@@ -543,7 +546,7 @@ EncodeTiledFn encode_fn_attn() {
 }
 }  // namespace
 
-int attention_tc_plan(AttnTcPlan *plan, const bf16 *qkv, int B, int S, int H) {
+int attention_tc_plan(AttnTcPlan *plan, const bf16 *qkv, int B, int S, int H, const bf16 *o) {
   EncodeTiledFn f = encode_fn_attn();
   if (!f) return -1;
   if (reinterpret_cast<uintptr_t>(qkv) & 15) return -2;
@@ -556,6 +559,19 @@ int attention_tc_plan(AttnTcPlan *plan, const bf16 *qkv, int B, int S, int H) {
                  estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
                  CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
   if (r != CUDA_SUCCESS) return -3;
+  plan->out = nullptr;
+  if (o) {
+    if (reinterpret_cast<uintptr_t>(o) & 15) return -2;
+    const int64_t D = (int64_t)H * DH;
+    const cuuint64_t odims[3] = {static_cast<cuuint64_t>(D), static_cast<cuuint64_t>(S), static_cast<cuuint64_t>(B)};
+    const cuuint64_t ostrides[2] = {static_cast<cuuint64_t>(D * 2), static_cast<cuuint64_t>(D * 2 * S)};
+    const cuuint32_t obox[3] = {64, 32, 1};
+    r = f(&plan->map_out, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 3, const_cast<bf16 *>(o), odims, ostrides, obox, estr,
+          CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_NONE,
+          CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    if (r != CUDA_SUCCESS) return -3;
+    plan->out = o;
+  }
   plan->qkv = qkv;
   plan->B = B;
   plan->S = S;

@@ -310,8 +310,9 @@ int bert_forward_device(BertContext &c, const int64_t *d_ids, const int64_t *d_t
   } else {
     r = bert_ensure_plans(c, T);
     if (r) return r;
-    if (c.attn_plan.qkv != w.qkv || c.attn_plan.B != B || c.attn_plan.S != S || c.attn_plan.H != H) {
-      if (attention_tc_plan(&c.attn_plan, static_cast<const bf16 *>(w.qkv), B, S, H)) {
+    if (c.attn_plan.qkv != w.qkv || c.attn_plan.out != w.o || c.attn_plan.B != B || c.attn_plan.S != S ||
+        c.attn_plan.H != H) {
+      if (attention_tc_plan(&c.attn_plan, static_cast<const bf16 *>(w.qkv), B, S, H, static_cast<const bf16 *>(w.o))) {
         set_error("TMA descriptor creation failed (attention)");
         return -2;
       }
@@ -325,7 +326,7 @@ int bert_forward_device(BertContext &c, const int64_t *d_ids, const int64_t *d_t
       const BertLayer &lw = c.layers[l];
       const TcGemmPlan *p = &c.plans[4 * l];
       CKP(K_GEMM_QKV, launch_gemm_tc(p[0], qkv, 3 * d, 0, lw.qkv_b, nullptr, EPI_BIAS, c.d_status, ns, st));
-      CKP(K_ATTENTION, launch_attention_tc(c.attn_plan, kv, o, c.d_status, st, 0, kv_end));
+      CKP(K_ATTENTION, launch_attention_tc2(c.attn_plan, kv, o, c.d_status, st, 0, kv_end));
       if (d_mask) CKP(K_MASKED_ROWS, launch_attn_masked_rows_bf16(qkv, w.first_valid, o, B, S, H, st, 0));
       CKP(K_GEMM_PROJ, launch_gemm_tc(p[1], y, d, 0, lw.ao_b, x, EPI_BIAS_RESID, c.d_status, ns, st));
       CKP(K_LAYERNORM, launch_layernorm_bf16(y, lw.aoln_g, lw.aoln_b, h, (int)T, d, m.eps, st));

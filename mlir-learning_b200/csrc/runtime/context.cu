@@ -381,8 +381,10 @@ int forward_device(Context &c, const int64_t *d_ids, const int64_t *d_mask, int 
   }
   r = ensure_plans(c, T);
   if (r) return r;
-  if (c.attn_plan.qkv != w.qkv || c.attn_plan.B != B || c.attn_plan.S != S || c.attn_plan.H != m.n_head) {
-    if (attention_tc_plan(&c.attn_plan, static_cast<const bf16 *>(w.qkv), B, S, m.n_head)) {
+  if (c.attn_plan.qkv != w.qkv || c.attn_plan.out != w.o || c.attn_plan.B != B || c.attn_plan.S != S ||
+      c.attn_plan.H != m.n_head) {
+    if (attention_tc_plan(&c.attn_plan, static_cast<const bf16 *>(w.qkv), B, S, m.n_head,
+                          static_cast<const bf16 *>(w.o))) {
       set_error("TMA descriptor creation failed (attention)");
       return -2;
     }
@@ -396,7 +398,7 @@ int forward_device(Context &c, const int64_t *d_ids, const int64_t *d_mask, int 
     const TcGemmPlan *p = &c.plans[4 * l];
     CKP(K_LAYERNORM, launch_layernorm_bf16(x, lw.ln1_g, lw.ln1_b, a, (int)T, d, m.eps, st));
     CKP(K_GEMM_QKV, launch_gemm_tc(p[0], qkv, 3 * d, 0, lw.qkv_b, nullptr, EPI_BIAS, c.d_status, ns, st, lw.qkv_s));
-    CKP(K_ATTENTION, launch_attention_tc(c.attn_plan, kv, o, c.d_status, st));
+    CKP(K_ATTENTION, launch_attention_tc2(c.attn_plan, kv, o, c.d_status, st));
     if (d_mask) CKP(K_MASKED_ROWS, launch_attn_masked_rows_bf16(qkv, w.first_valid, o, B, S, H, st));
     CKP(K_GEMM_PROJ, launch_gemm_tc(p[1], x, d, 0, lw.proj_b, x, EPI_BIAS_RESID, c.d_status, ns, st, lw.proj_s));
     CKP(K_LAYERNORM, launch_layernorm_bf16(x, lw.ln2_g, lw.ln2_b, a, (int)T, d, m.eps, st));
