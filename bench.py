@@ -533,10 +533,14 @@ def main():
     # Per-kernel breakdown (separate, profiled steps of the same workload).
     pkg.profile_begin()
     nprof = 2
+    p0, p1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    p0.record(stream)
     for _ in range(nprof):
         step()
+    p1.record(stream)
     prof = pkg.profile_end()
     torch.cuda.synchronize()
+    profiled_step_ms = p0.elapsed_time(p1) / nprof
     work = kernel_work(B, S)
     kernels, roof = kernel_breakdown(prof, work, nprof, _peaks(), args.config, T)
     total_flop = (work["gemm_qkv"][1] + work["gemm_proj"][1] + work["gemm_fc"][1] + work["gemm_mproj"][1]) * L \
@@ -590,6 +594,7 @@ def main():
                        "global_batch": args.batch, "seq_len": S, "per_rank_batch": B,
                        "parallelism": f"batch-sharded dp{world}", "l2": "no flush: every step moves > 13 GB"},
             "forward_tflops": fwd_tflops,
+            "profiled_step_ms": profiled_step_ms,
             "roofline": roof,
             "kernels": kernels,
             "cpu_baseline": cpu,

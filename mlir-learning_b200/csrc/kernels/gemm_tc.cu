@@ -184,6 +184,18 @@ __global__ void __launch_bounds__(NTHREADS, 1)
       tile_coords(t, num_m, num_n, mb, nb);
       const int acc = local & 1;
       const uint32_t aph = (local >> 1) & 1;
+      if (EPI == EPI_BIAS_RESID && !OUT_F32) {
+        // Pull this row's residual into L2 while the tile's main loop runs,
+        // so the chunked loads below do not wait on HBM (short-K GEMMs
+        // would otherwise be bound by the epilogue).
+        const int prow = mb * BM + row_in_tile;
+        if (prow < M) {
+          const bf16 *rp = resid + (int64_t)prow * ldc + nb * BN;
+#pragma unroll
+          for (int i = 0; i < BN / 64; ++i)
+            if (nb * BN + i * 64 < N) asm volatile("prefetch.global.L2 [%0];" ::"l"(rp + i * 64));
+        }
+      }
       if (!mbar_wait(&tfull[acc], aph, abort_flag, status)) {
         set_status(status, GPT2_ERR_WAIT_TIMEOUT);
         *abort_flag = 1;

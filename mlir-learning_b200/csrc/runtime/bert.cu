@@ -10,6 +10,7 @@
 //   hidden = x (FP32); pooled = tanh(hidden[:, 0] @ Wp^T + b)
 // as 2 + 7 L launches (+ 1 + L with a mask).  Linear weights are [out, in],
 // which is already the K-major B operand of the tcgen05 GEMM.
+#include <stdlib.h>
 #include <string.h>
 
 #include <algorithm>
@@ -94,6 +95,7 @@ void bert_destroy_context() {
   cudaGetDevice(&prev);
   cudaSetDevice(c->device);
   cudaDeviceSynchronize();
+  drop_graph(c->graph);
   free_bert_ws(c->ws);
   if (c->d_blob) cudaFree(c->d_blob);
   for (auto &l : c->layers) {
@@ -136,6 +138,7 @@ int bert_create_context(const BertDims &m, int dtype, int device) {
     return cuda_fail(e, "BERT context setup");
   }
   c->specs = bert_blob_specs(m);
+  if (const char *e = getenv("GPT2_GRAPHS")) c->use_graphs = strcmp(e, "0") != 0;
   g_bert = c;
   return 0;
 }
@@ -194,6 +197,7 @@ int bert_load_blob(BertContext &c, const float *host_blob) {
   CK(cudaStreamSynchronize(c.stream));
   c.loaded = true;
   c.plans_T = -1;
+  drop_graph(c.graph);
   return 0;
 }
 
@@ -204,6 +208,7 @@ int bert_ensure_workspace(BertContext &c, int B, int S) {
   const int64_t Tn = std::max(T, w.T);
   const int Bn = std::max(B, w.B);
   CK(cudaDeviceSynchronize());  // earlier forwards may still read the buffers
+  drop_graph(c.graph);           // it captured the old buffers
   free_bert_ws(w);
   const size_t es = c.dtype == 1 ? 2 : 4;
   const int64_t d = c.dims.n_embd, ff = c.dims.n_inner;
@@ -265,6 +270,12 @@ int bert_forward_launch_count(const BertContext &c, int has_mask, int has_pooler
   return 1 + 7 * c.dims.n_layer + (has_pooler ? 1 : 0) + (has_mask ? 1 + c.dims.n_layer : 0);
 }
 
+namespace {
+int bert_prepare(BertContext &c, int B, int S);
+int bert_launch(BertContext &c, const int64_t *d_ids, const int64_t *d_tt, const int64_t *d_pos,
+                const int64_t *d_mask, int B, int S, float *d_hidden, float *d_pooled, cudaStream_t st);
+}  // namespace
+
 int bert_forward_device(BertContext &c, const int64_t *d_ids, const int64_t *d_tt, const int64_t *d_pos,
                         const int64_t *d_mask, int B, int S, float *d_hidden, float *d_pooled, cudaStream_t st) {
   const BertDims &m = c.dims;
@@ -278,8 +289,40 @@ int bert_forward_device(BertContext &c, const int64_t *d_ids, const int64_t *d_t
               m.n_pos);
     return -1;
   }
-  int r = bert_ensure_workspace(c, B, S);
+  int r = bert_prepare(c, B, S);
   if (r) return r;
+  auto launch = [&](cudaStream_t s) { return bert_launch(c, d_ids, d_tt, d_pos, d_mask, B, S, d_hidden, d_pooled, s); };
+  if (c.prof.on) return launch(st);  // per-launch events need plain launches
+  const uintptr_t key[8] = {reinterpret_cast<uintptr_t>(d_ids),    reinterpret_cast<uintptr_t>(d_tt),
+                            reinterpret_cast<uintptr_t>(d_pos),    reinterpret_cast<uintptr_t>(d_mask),
+                            reinterpret_cast<uintptr_t>(d_hidden), reinterpret_cast<uintptr_t>(d_pooled),
+                            static_cast<uintptr_t>(B),             static_cast<uintptr_t>(S)};
+  return run_with_graph(c.graph, &c.use_graphs, key, 8, c.stream, st, launch);
+}
+
+namespace {
+// Buffers and descriptors of a forward of (B, S), before any launch (and
+// outside any graph capture).
+int bert_prepare(BertContext &c, int B, int S) {
+  int r = bert_ensure_workspace(c, B, S);
+  if (r || c.dtype == 0) return r;
+  BertWorkspace &w = c.ws;
+  r = bert_ensure_plans(c, (int64_t)B * S);
+  if (r) return r;
+  if (c.attn_plan.qkv != w.qkv || c.attn_plan.out != w.o || c.attn_plan.B != B || c.attn_plan.S != S ||
+      c.attn_plan.H != c.dims.n_head) {
+    if (attention_tc_plan(&c.attn_plan, static_cast<const bf16 *>(w.qkv), B, S, c.dims.n_head,
+                          static_cast<const bf16 *>(w.o))) {
+      set_error("TMA descriptor creation failed (attention)");
+      return -2;
+    }
+  }
+  return 0;
+}
+
+int bert_launch(BertContext &c, const int64_t *d_ids, const int64_t *d_tt, const int64_t *d_pos,
+                const int64_t *d_mask, int B, int S, float *d_hidden, float *d_pooled, cudaStream_t st) {
+  const BertDims &m = c.dims;
   const int64_t T = (int64_t)B * S;
   const int d = m.n_embd, ff = m.n_inner, H = m.n_head;
   BertWorkspace &w = c.ws;
@@ -308,15 +351,6 @@ int bert_forward_device(BertContext &c, const int64_t *d_ids, const int64_t *d_t
       CKP(K_LAYERNORM, launch_layernorm_f32(y, lw.oln_g, lw.oln_b, l == L - 1 ? d_hidden : x, (int)T, d, m.eps, st));
     }
   } else {
-    r = bert_ensure_plans(c, T);
-    if (r) return r;
-    if (c.attn_plan.qkv != w.qkv || c.attn_plan.out != w.o || c.attn_plan.B != B || c.attn_plan.S != S ||
-        c.attn_plan.H != H) {
-      if (attention_tc_plan(&c.attn_plan, static_cast<const bf16 *>(w.qkv), B, S, H, static_cast<const bf16 *>(w.o))) {
-        set_error("TMA descriptor creation failed (attention)");
-        return -2;
-      }
-    }
     bf16 *x = static_cast<bf16 *>(w.x), *qkv = static_cast<bf16 *>(w.qkv), *o = static_cast<bf16 *>(w.o),
          *y = static_cast<bf16 *>(w.y), *h = static_cast<bf16 *>(w.h), *u = static_cast<bf16 *>(w.u);
     const int ns = c.num_sms;
@@ -341,5 +375,6 @@ int bert_forward_device(BertContext &c, const int64_t *d_ids, const int64_t *d_t
   if (d_pooled) CKP(K_LM_HEAD, launch_bert_pooler(d_hidden, c.pool_w, c.pool_b, d_pooled, B, S, d, st));
   return 0;
 }
+}  // namespace
 
 }  // namespace gpt2

@@ -60,6 +60,8 @@ struct BertContext {
   AttnTcPlan attn_plan;
 
   Profiler prof;
+  GraphCache graph;
+  bool use_graphs = true;  // env GPT2_GRAPHS=0 turns graph replay off
 };
 
 BertContext *bert_context();

@@ -12,6 +12,7 @@
 // the reference's ~797 (README.md:96).
 #include <stdarg.h>
 #include <stdio.h>
+#include <stdlib.h>
 #include <string.h>
 
 #include <algorithm>
@@ -81,6 +82,11 @@ int64_t blob_floats(const ModelDims &m) {
 
 Context *context() { return g_ctx; }
 
+void drop_graph(GraphCache &g) {
+  if (g.exec) cudaGraphExecDestroy(g.exec);
+  g = GraphCache();
+}
+
 void destroy_context() {
   if (!g_ctx) return;
   Context *c = g_ctx;
@@ -89,6 +95,8 @@ void destroy_context() {
   cudaGetDevice(&prev);
   cudaSetDevice(c->device);
   cudaDeviceSynchronize();
+  drop_graph(c->graph);
+  for (cudaEvent_t e : c->prof.pool) cudaEventDestroy(e);
   free_ws(c->ws);
   if (c->d_blob) cudaFree(c->d_blob);
   if (c->wte_h) cudaFree(c->wte_h);
@@ -132,6 +140,7 @@ int create_context(const ModelDims &m, int dtype, int device) {
     return cuda_fail(e, "context setup");
   }
   c->specs = blob_specs(m);
+  if (const char *e = getenv("GPT2_GRAPHS")) c->use_graphs = strcmp(e, "0") != 0;
   g_ctx = c;
   return 0;
 }
@@ -218,6 +227,7 @@ int load_blob(Context &c, const float *host_blob) {
   }
   c.loaded = true;
   c.plans_T = -1;  // weights moved: rebuild TMA descriptors
+  drop_graph(c.graph);
   return 0;
 }
 
@@ -228,6 +238,7 @@ int ensure_workspace(Context &c, int B, int S) {
   const int64_t Tn = std::max(T, w.T);
   const int Bn = std::max(B, w.B);
   CK(cudaDeviceSynchronize());  // earlier forwards may still read the buffers on any stream
+  drop_graph(c.graph);           // it captured the old buffers
   Workspace keep_logits;
   keep_logits.logits = w.logits;
   keep_logits.logits_T = w.logits_T;
@@ -339,19 +350,35 @@ int forward_launch_count(const Context &c, int has_mask) {
   return 3 + 7 * c.dims.n_layer + (has_mask ? 1 + c.dims.n_layer : 0);
 }
 
-int forward_device(Context &c, const int64_t *d_ids, const int64_t *d_mask, int B, int S, float *d_logits,
+namespace {
+// Buffers, TMA descriptors and output descriptor of a forward of (B, S) into
+// d_logits: everything that allocates or encodes on the host, done before
+// any launch (and outside any graph capture).
+int prepare_forward(Context &c, int B, int S, float *d_logits, int64_t ld_logits) {
+  const ModelDims &m = c.dims;
+  int r = ensure_workspace(c, B, S);
+  if (r || c.dtype == 0) return r;
+  Workspace &w = c.ws;
+  r = ensure_plans(c, (int64_t)B * S);
+  if (r) return r;
+  if (c.attn_plan.qkv != w.qkv || c.attn_plan.out != w.o || c.attn_plan.B != B || c.attn_plan.S != S ||
+      c.attn_plan.H != m.n_head) {
+    if (attention_tc_plan(&c.attn_plan, static_cast<const bf16 *>(w.qkv), B, S, m.n_head,
+                          static_cast<const bf16 *>(w.o))) {
+      set_error("TMA descriptor creation failed (attention)");
+      return -2;
+    }
+  }
+  TcGemmPlan &head = c.plans[4 * m.n_layer];
+  if (head.c_ptr != d_logits || head.c_ld != (int)ld_logits || !head.c_f32)
+    tc_gemm_set_output(&head, d_logits, (int)ld_logits, 1);
+  return 0;
+}
+
+// Enqueues the forward's kernels on st (prepare_forward has run).
+int launch_forward(Context &c, const int64_t *d_ids, const int64_t *d_mask, int B, int S, float *d_logits,
                    int64_t ld_logits, cudaStream_t st) {
   const ModelDims &m = c.dims;
-  if (!c.loaded) {
-    set_error("no weights loaded");
-    return -3;
-  }
-  if (B < 1 || S < 1 || S > m.n_pos || (int64_t)B * S > (int64_t)1 << 30 || ld_logits < m.vocab) {
-    set_error("bad forward shape B=%d S=%d (n_positions %d) ld_logits=%lld", B, S, m.n_pos, (long long)ld_logits);
-    return -1;
-  }
-  int r = ensure_workspace(c, B, S);
-  if (r) return r;
   const int64_t T = (int64_t)B * S;
   const int d = m.n_embd, ff = m.n_inner, H = m.n_head, V = m.vocab;
   Workspace &w = c.ws;
@@ -379,16 +406,6 @@ int forward_device(Context &c, const int64_t *d_ids, const int64_t *d_mask, int 
     CKP(K_LM_HEAD, launch_gemm_f32(a, c.wte, 1, d_logits, (int)T, V, d, (int)ld_logits, nullptr, nullptr, EPI_NONE, st));
     return 0;
   }
-  r = ensure_plans(c, T);
-  if (r) return r;
-  if (c.attn_plan.qkv != w.qkv || c.attn_plan.out != w.o || c.attn_plan.B != B || c.attn_plan.S != S ||
-      c.attn_plan.H != m.n_head) {
-    if (attention_tc_plan(&c.attn_plan, static_cast<const bf16 *>(w.qkv), B, S, m.n_head,
-                          static_cast<const bf16 *>(w.o))) {
-      set_error("TMA descriptor creation failed (attention)");
-      return -2;
-    }
-  }
   bf16 *x = static_cast<bf16 *>(w.x), *a = static_cast<bf16 *>(w.a), *qkv = static_cast<bf16 *>(w.qkv),
        *o = static_cast<bf16 *>(w.o), *u = static_cast<bf16 *>(w.u);
   const int ns = c.num_sms;
@@ -407,12 +424,32 @@ int forward_device(Context &c, const int64_t *d_ids, const int64_t *d_mask, int 
         launch_gemm_tc(p[3], x, d, 0, lw.mproj_b, x, EPI_BIAS_RESID, c.d_status, ns, st, lw.mproj_s));
   }
   CKP(K_LAYERNORM, launch_layernorm_bf16(x, c.lnf_g, c.lnf_b, a, (int)T, d, m.eps, st));
-  TcGemmPlan &head = c.plans[4 * m.n_layer];
-  if (head.c_ptr != d_logits || head.c_ld != (int)ld_logits || !head.c_f32)
-    tc_gemm_set_output(&head, d_logits, (int)ld_logits, 1);
+  const TcGemmPlan &head = c.plans[4 * m.n_layer];
   CKP(K_LM_HEAD, launch_gemm_tc(head, d_logits, (int)ld_logits, 1, nullptr, nullptr, EPI_NONE, c.d_status, ns,
                     st));
   return 0;
+}
+}  // namespace
+
+int forward_device(Context &c, const int64_t *d_ids, const int64_t *d_mask, int B, int S, float *d_logits,
+                   int64_t ld_logits, cudaStream_t st) {
+  const ModelDims &m = c.dims;
+  if (!c.loaded) {
+    set_error("no weights loaded");
+    return -3;
+  }
+  if (B < 1 || S < 1 || S > m.n_pos || (int64_t)B * S > (int64_t)1 << 30 || ld_logits < m.vocab) {
+    set_error("bad forward shape B=%d S=%d (n_positions %d) ld_logits=%lld", B, S, m.n_pos, (long long)ld_logits);
+    return -1;
+  }
+  int r = prepare_forward(c, B, S, d_logits, ld_logits);
+  if (r) return r;
+  auto launch = [&](cudaStream_t s) { return launch_forward(c, d_ids, d_mask, B, S, d_logits, ld_logits, s); };
+  if (c.prof.on) return launch(st);  // per-launch events need plain launches
+  const uintptr_t key[6] = {reinterpret_cast<uintptr_t>(d_ids), reinterpret_cast<uintptr_t>(d_mask),
+                            reinterpret_cast<uintptr_t>(d_logits), static_cast<uintptr_t>(ld_logits),
+                            static_cast<uintptr_t>(B), static_cast<uintptr_t>(S)};
+  return run_with_graph(c.graph, &c.use_graphs, key, 6, c.stream, st, launch);
 }
 
 }  // namespace gpt2

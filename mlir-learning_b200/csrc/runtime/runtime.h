@@ -77,6 +77,55 @@ struct Profiler {
   std::vector<int> kinds;  // kind of record i; events 2i, 2i+1
 };
 
+// The forward captured as one CUDA graph for a fixed set of arguments and
+// buffers: replayed when a call repeats them (one graph launch instead of
+// ~85 kernel launches).  Dropped whenever the workspace is reallocated.
+struct GraphCache {
+  cudaGraphExec_t exec = nullptr;
+  uintptr_t key[12] = {};  // the call's pointers and sizes
+  int nkey = 0;
+  bool seen = false;  // the key has run once uncaptured (buffers, plans and kernel attributes set up)
+};
+
+void drop_graph(GraphCache &g);
+int cuda_fail(cudaError_t e, const char *what);  // records the error text, returns -2
+
+// Runs launch(stream) -- the enqueue of one forward whose buffers and
+// descriptors are already prepared -- through the graph cache: the first
+// call with a key runs uncaptured, the second captures on cap_stream and
+// launches the graph on st, later ones replay it.  If capture or
+// instantiation fails, *enabled is cleared and plain launches continue.
+template <typename F>
+int run_with_graph(GraphCache &g, bool *enabled, const uintptr_t *key, int nkey, cudaStream_t cap_stream,
+                   cudaStream_t st, F launch) {
+  if (!*enabled) return launch(st);
+  bool same = g.nkey == nkey;
+  for (int i = 0; same && i < nkey; ++i) same = g.key[i] == key[i];
+  if (same && g.exec) return cudaGraphLaunch(g.exec, st) == cudaSuccess ? 0 : cuda_fail(cudaGetLastError(), "graph launch");
+  if (!same || !g.seen) {
+    drop_graph(g);
+    for (int i = 0; i < nkey; ++i) g.key[i] = key[i];
+    g.nkey = nkey;
+    g.seen = true;
+    return launch(st);
+  }
+  cudaGraph_t graph = nullptr;
+  cudaError_t e = cudaStreamBeginCapture(cap_stream, cudaStreamCaptureModeThreadLocal);
+  int r = e == cudaSuccess ? launch(cap_stream) : 0;
+  if (e == cudaSuccess) e = cudaStreamEndCapture(cap_stream, &graph);
+  if (r == 0 && e == cudaSuccess) e = cudaGraphInstantiate(&g.exec, graph, 0);
+  if (graph) cudaGraphDestroy(graph);
+  if (r || e != cudaSuccess) {
+    cudaGetLastError();
+    g.exec = nullptr;
+    drop_graph(g);
+    *enabled = false;
+    if (r) return r;
+    return launch(st);
+  }
+  return cudaGraphLaunch(g.exec, st) == cudaSuccess ? 0 : cuda_fail(cudaGetLastError(), "graph launch");
+}
+
 struct Context {
   ModelDims dims;
   int dtype = 0;
@@ -99,6 +148,8 @@ struct Context {
   AttnTcPlan attn_plan;  // tcgen05 attention descriptor for (ws.qkv, B, S)
 
   Profiler prof;
+  GraphCache graph;
+  bool use_graphs = true;  // env GPT2_GRAPHS=0 turns graph replay off
   std::mutex mu;
 };
 
@@ -118,7 +169,6 @@ int profile_end(Profiler &p, double *ms, int64_t *count, int n);
 cudaEvent_t prof_event(Profiler &p);  // the next event of the pool (null if none can be created)
 
 void set_error(const char *fmt, ...);
-int cuda_fail(cudaError_t e, const char *what);  // records the error text, returns -2
 
 // Status-checked CUDA call inside a function returning int.
 #define CK(call)                                          \

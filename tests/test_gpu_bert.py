@@ -182,3 +182,33 @@ def test_errors_are_reported_not_fatal(torch):
     h, p = B.bert_model(np.array([[1, 2, 3]]))
     assert np.isfinite(h).all() and np.isfinite(p).all()
     B.shutdown()
+
+
+def test_graph_replay_matches_plain_launches(torch):
+    """BERT device entry point: plain, captured and replayed forwards agree bit for bit; new ids in
+    the same buffer are picked up by the replay."""
+    shape = O.BERT_TINY
+    blob = O.bert_seeded_blob(shape, 21, 1)
+    _model(shape, blob, B.DTYPE_BF16)
+    Bn, S, d = 3, 50, shape.n_embd
+    st = torch.cuda.current_stream().cuda_stream
+    ids = torch.from_numpy(O.token_ids(Bn, S, 21, shape.vocab_size, stream=O.BERT_IDS_STREAM)).cuda()
+    mask = torch.ones(Bn, S, dtype=torch.int64, device="cuda")
+    mask[1, 30:] = 0
+    hidden = torch.empty(Bn, S, d, device="cuda")
+    pooled = torch.empty(Bn, d, device="cuda")
+    got = []
+    for _ in range(3):
+        B.forward_device(ids.data_ptr(), None, None, mask.data_ptr(), Bn, S, hidden.data_ptr(), pooled.data_ptr(), st)
+        torch.cuda.synchronize()
+        got.append((hidden.clone(), pooled.clone()))
+    assert all(torch.equal(got[0][0], g[0]) and torch.equal(got[0][1], g[1]) for g in got)
+    ids.copy_(torch.from_numpy(O.token_ids(Bn, S, 22, shape.vocab_size, stream=O.BERT_IDS_STREAM)).cuda())
+    B.forward_device(ids.data_ptr(), None, None, mask.data_ptr(), Bn, S, hidden.data_ptr(), pooled.data_ptr(), st)
+    h2 = torch.empty_like(hidden)
+    B.forward_device(ids.data_ptr(), None, None, mask.data_ptr(), Bn, S, h2.data_ptr(), None, st)
+    torch.cuda.synchronize()
+    assert torch.equal(hidden, h2) and not torch.equal(hidden, got[0][0])
+    rh, rp = O.bert_forward(shape, blob, ids.cpu().numpy(), None, mask.cpu().numpy())
+    _bf16_check(rh, hidden.cpu().numpy(), rp, pooled.cpu().numpy(), "bert tiny graph replay")
+    assert B.status() == 0

@@ -189,3 +189,38 @@ def test_errors_are_reported_not_fatal(torch):
     assert pkg.status() == 0
     good = pkg.gpt2_decoder(np.array([[1, 2, 3]]))
     assert np.isfinite(good).all()
+
+
+@pytest.mark.parametrize("dtype", [0, 1])
+def test_graph_replay_matches_plain_launches(torch, dtype):
+    """The device entry point runs a new argument set plainly, captures the forward as one CUDA graph
+    on the second identical call and replays it afterwards: every call gives the same logits, ids
+    changed in place change the replayed result exactly as a plain launch does, and profiling
+    falls back to plain launches (one event pair per kernel)."""
+    shape = O.GPT2_TINY
+    blob = O.seeded_blob(shape, 12, 1)
+    _model(shape, blob, dtype)
+    B, S, V = 3, 40, shape.vocab_size
+    st = torch.cuda.current_stream().cuda_stream
+    ids = torch.from_numpy(O.token_ids(B, S, 12, V)).cuda()
+    out = torch.empty(B * S, V, device="cuda")
+    got = []
+    for _ in range(3):  # plain, capture + launch, replay
+        pkg.forward_device(ids.data_ptr(), None, B, S, out.data_ptr(), V, st)
+        torch.cuda.synchronize()
+        got.append(out.clone())
+    assert torch.equal(got[0], got[1]) and torch.equal(got[0], got[2])
+    ids.copy_(torch.from_numpy(O.token_ids(B, S, 13, V)).cuda())
+    pkg.forward_device(ids.data_ptr(), None, B, S, out.data_ptr(), V, st)  # replay with new ids
+    other = torch.empty(B * S, V, device="cuda")
+    pkg.forward_device(ids.data_ptr(), None, B, S, other.data_ptr(), V, st)  # new key: plain launch
+    torch.cuda.synchronize()
+    assert torch.equal(out, other) and not torch.equal(out, got[0])
+    ref = O.forward(shape, blob, ids.cpu().numpy())
+    if dtype == 0:
+        assert np.abs(out.view(B, S, V).cpu().numpy() - ref).max() <= FP32_ATOL
+    pkg.profile_begin()
+    pkg.forward_device(ids.data_ptr(), None, B, S, out.data_ptr(), V, st)
+    prof = pkg.profile_end()
+    assert sum(n for _, n in prof.values()) == pkg.forward_launches(B, S, False)
+    assert pkg.status() == 0
