@@ -186,9 +186,16 @@ def traffic_per_launch(config: int, kernel: str, tokens: int):
         return None
 
 
+# FP32 SIMT (FFMA) peak of a B200: 148 SMs x 128 FP32 lanes x 2 FLOP at the 1965 MHz maximum SM
+# clock.  There is no measured FP32 figure; the exact-FP32 configuration is rated against this.
+FP32_SIMT_NOMINAL_TFLOPS = 148 * 128 * 2 * 1.965e9 / 1e12
+
+
 def kernel_breakdown(prof: dict, work: dict, nprof: int, peaks: dict, config: int, tokens: int):
     """Per-kernel ms / share / rate of `nprof` profiled steps and the roofline of the dominant
-    kernel (achieved = algorithmic work per launch / average event-timed launch duration)."""
+    kernel (achieved = algorithmic work per launch / average event-timed launch duration).  The
+    exact-FP32 configuration (config 1) runs on FFMA, not the tensor cores: its FLOP-bound
+    kernels are rated against the FP32 SIMT peak."""
     kernels = {}
     for k, (ms, n) in prof.items():
         if n == 0:
@@ -209,7 +216,13 @@ def kernel_breakdown(prof: dict, work: dict, nprof: int, peaks: dict, config: in
     traffic = traffic_per_launch(config, dom, tokens)
     kind, amount = work.get(dom, ("flop", 0.0))
     per_launch_s = kernels[dom]["avg_launch_ms"] / 1000.0
-    if kind == "flop":
+    if kind == "flop" and config == 1:
+        achieved = amount / per_launch_s / 1e12
+        roof = {"bound": "fp32-simt", "achieved": achieved, "peak": FP32_SIMT_NOMINAL_TFLOPS, "unit": "TFLOP/s",
+                "frac": achieved / FP32_SIMT_NOMINAL_TFLOPS, "traffic": traffic, "kernel": dom,
+                "peak_kind": "FFMA nominal (148 SMs x 128 lanes x 2 x 1965 MHz; no measured FP32 peak)",
+                "algorithmic_per_launch": amount}
+    elif kind == "flop":
         achieved = amount / per_launch_s / 1e12
         roof = {"bound": "tensor", "achieved": achieved, "peak": peaks["bf16_sus"], "unit": "TFLOP/s",
                 "frac": achieved / peaks["bf16_sus"], "traffic": traffic, "kernel": dom,
