@@ -85,6 +85,13 @@ int64_t bert_blob_floats(const BertConfig *cfg);
  * be NULL or name the layout "bert-canonical-f32-v1". */
 int bert_load_weights(const void *packed, size_t bytes, const char *manifest_json);
 
+/* HF safetensors checkpoint of a BERT model (transformers names with or
+ * without "bert.", LayerNorm gamma / beta accepted; F32, F16 or BF16) into
+ * the canonical blob (no GPU needed), or loaded into the current model.
+ * Extra tensors (a pre-training head, position_ids buffers) are ignored. */
+int bert_safetensors_to_blob(const char *path, const BertConfig *cfg, float *out);
+int bert_load_safetensors(const char *path);
+
 /* Seeded synthetic weights (Philox4x32-10 stream 0x20000 + tensor index;
  * init modes as gpt2_init_seeded), generated and loaded / written out. */
 int bert_init_seeded(uint64_t seed, int init_mode);

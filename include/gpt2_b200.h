@@ -125,6 +125,17 @@ int64_t gpt2_blob_floats(const Gpt2Config *cfg);
  * may be NULL, or a JSON object whose "layout" is "gpt2-canonical-f32-v1". */
 int gpt2_load_weights(const void *packed, size_t bytes, const char *manifest_json);
 
+/* Reads an HF safetensors checkpoint of a GPT-2 model (transformers names,
+ * with or without the "transformer." prefix; F32, F16 or BF16 tensors,
+ * widened exactly to FP32) whose shapes match cfg, into out[0 ..
+ * gpt2_blob_floats(cfg)) in the canonical order.  Needs no GPU.  Extra
+ * tensors (attn.bias buffers, a tied lm_head.weight) are ignored; a missing
+ * or mis-shaped tensor is an error naming it. */
+int gpt2_safetensors_to_blob(const char *path, const Gpt2Config *cfg, float *out);
+
+/* The same checkpoint loaded into the current model (gpt2_init first). */
+int gpt2_load_safetensors(const char *path);
+
 /* Generates the seeded synthetic weights (Philox4x32-10 + Box-Muller) and
  * loads them.  init_mode 0: matrices N(0, 0.02), LayerNorm gain 1, every
  * bias 0.  init_mode 1: also gains 1 + N(0, 0.1) and biases N(0, 0.02). */
@@ -194,6 +205,20 @@ int gpt2_profile_end(double *ms_per_kind, int64_t *launches_per_kind, int n_kind
 /* Epilogues fused into the GEMMs. */
 enum { GPT2_EPI_NONE = 0, GPT2_EPI_BIAS = 1, GPT2_EPI_BIAS_GELU = 2, GPT2_EPI_BIAS_RESID = 3,
        GPT2_EPI_BIAS_GELU_ERF = 4 /* exact erf GELU of the BERT intermediate layer */ };
+
+/* The call a BLAS lowering of linalg.matmul emits, on the GPU: the argument
+ * list of cblas_sgemm exactly as lib/ConvertMatMulToBlas.cpp:84-160 builds it
+ * (CblasRowMajor = 101, CblasNoTrans = 111, alpha 1, beta 0, lda = K,
+ * ldb = N, ldc = N), so a lowering retargets by changing only the callee's
+ * name.  A, B, C may be host or device memory (host operands are staged
+ * through device buffers); the product runs on the exact-FP32 SIMT GEMM and
+ * C is complete when the call returns.  Also accepted: transB = 112
+ * (CblasTrans, B given as [N, K] with ldb = K) and any ldc >= N.  Other
+ * orders, transposed A, alpha != 1 or beta != 0 return GPT2_EINVAL (the
+ * lowering never emits them).  Returns 0 on success; a lowering that
+ * declares the callee void may ignore the result. */
+int gpt2_blas_sgemm(int order, int transA, int transB, int M, int N, int K, float alpha, const float *A, int lda,
+                    const float *B, int ldb, float beta, float *C, int ldc);
 
 /* Exact-FP32 SIMT GEMM: C[M,N] (row stride ldc) = epi(A[M,K] @ op(B)),
  * op(B) = B[K,N] (b_nk = 0) or B[N,K]^T (b_nk = 1); resid row stride ldc. */

@@ -119,6 +119,10 @@ def lib() -> ctypes.CDLL:
     L.gpt2_forward_host.argtypes = [P(i64), P(i64), i32, i32, P(ctypes.c_float)]
     L.gpt2_forward_launches.argtypes = [i32, i32, i32]
     L.gpt2_profile_end.argtypes = [P(ctypes.c_double), P(i64), i32]
+    L.gpt2_safetensors_to_blob.argtypes = [ctypes.c_char_p, P(Gpt2Config), P(ctypes.c_float)]
+    L.gpt2_load_safetensors.argtypes = [ctypes.c_char_p]
+    L.gpt2_blas_sgemm.argtypes = [i32, i32, i32, i32, i32, i32, ctypes.c_float, vp, i32, vp, i32, ctypes.c_float,
+                                  vp, i32]
     L.gpt2k_gemm_f32.argtypes = [vp, vp, i32, vp, i32, i32, i32, i32, vp, vp, i32, vp]
     L.gpt2k_gemm_bf16.argtypes = [vp, vp, vp, i32, i32, i32, i32, i32, vp, vp, i32, i32, vp]
     L.gpt2k_layernorm.argtypes = [vp, vp, vp, vp, i32, i32, ctypes.c_float, i32, vp]
@@ -208,6 +212,18 @@ def load_weights(blob: np.ndarray, manifest: str | None = None) -> None:
     blob = np.ascontiguousarray(blob, dtype=np.float32)
     _check(lib().gpt2_load_weights(blob.ctypes.data, blob.nbytes, manifest.encode() if manifest else None),
            "gpt2_load_weights")
+
+
+def safetensors_to_blob(path: str, cfg: Gpt2Config) -> np.ndarray:
+    """The canonical FP32 blob of an HF GPT-2 safetensors checkpoint (no GPU needed)."""
+    out = np.empty(blob_floats(cfg), dtype=np.float32)
+    _check(lib().gpt2_safetensors_to_blob(os.fsencode(path), ctypes.byref(cfg),
+                                          out.ctypes.data_as(ctypes.POINTER(ctypes.c_float))), "gpt2_safetensors_to_blob")
+    return out
+
+
+def load_safetensors(path: str) -> None:
+    _check(lib().gpt2_load_safetensors(os.fsencode(path)), "gpt2_load_safetensors")
 
 
 def init_seeded(seed: int, init_mode: int = 0) -> None:

@@ -19,6 +19,7 @@ No CPU fallback: every call goes to the CUDA library.
 from __future__ import annotations
 
 import ctypes
+import os
 
 import numpy as np
 
@@ -81,6 +82,8 @@ def lib() -> ctypes.CDLL:
     L.bert_get_config.argtypes = [P(BertConfig)]
     L.bert_shutdown.restype = None
     L.bert_last_error.restype = ctypes.c_char_p
+    L.bert_safetensors_to_blob.argtypes = [ctypes.c_char_p, P(BertConfig), P(ctypes.c_float)]
+    L.bert_load_safetensors.argtypes = [ctypes.c_char_p]
     L.bert_forward_device.argtypes = [vp, vp, vp, vp, i32, i32, vp, vp, vp]
     L.bert_forward_host.argtypes = [vp, vp, vp, vp, i32, i32, vp, vp]
     L.bert_forward_launches.argtypes = [i32, i32]
@@ -124,6 +127,18 @@ def load_weights(blob: np.ndarray, manifest: str | None = None) -> None:
     blob = np.ascontiguousarray(blob, dtype=np.float32)
     _check(lib().bert_load_weights(blob.ctypes.data, blob.nbytes, manifest.encode() if manifest else None),
            "bert_load_weights")
+
+
+def safetensors_to_blob(path: str, cfg: BertConfig) -> np.ndarray:
+    """The canonical FP32 blob of an HF BERT safetensors checkpoint (no GPU needed)."""
+    out = np.empty(blob_floats(cfg), dtype=np.float32)
+    _check(lib().bert_safetensors_to_blob(os.fsencode(path), ctypes.byref(cfg),
+                                          out.ctypes.data_as(ctypes.POINTER(ctypes.c_float))), "bert_safetensors_to_blob")
+    return out
+
+
+def load_safetensors(path: str) -> None:
+    _check(lib().bert_load_safetensors(os.fsencode(path)), "bert_load_safetensors")
 
 
 def init_seeded(seed: int, init_mode: int = 0) -> None:

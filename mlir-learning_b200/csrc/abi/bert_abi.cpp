@@ -295,6 +295,29 @@ int bert_load_weights(const void *packed, size_t bytes, const char *manifest_jso
   return bert_load_blob(*c, static_cast<const float *>(packed));
 }
 
+int bert_safetensors_to_blob(const char *path, const BertConfig *cfg, float *out) {
+  clear_error();
+  if (!path || !valid_dims(cfg) || !out) {
+    set_error("bert_safetensors_to_blob: need a path, a valid configuration and an output buffer");
+    return GPT2_EINVAL;
+  }
+  return bert_safetensors_blob(path, dims_of(cfg), out) ? GPT2_EINVAL : 0;
+}
+
+int bert_load_safetensors(const char *path) {
+  std::lock_guard<std::mutex> lk(g_bert_mu);
+  clear_error();
+  BertContext *c = bert_context();
+  if (!c) {
+    set_error("bert_load_safetensors: no model, call bert_init first");
+    return GPT2_ENOMODEL;
+  }
+  if (!path) return GPT2_EINVAL;
+  std::vector<float> blob(static_cast<size_t>(bert_blob_floats(c->dims)));
+  if (bert_safetensors_blob(path, c->dims, blob.data())) return GPT2_EINVAL;
+  return bert_load_blob(*c, blob.data());
+}
+
 int bert_init_seeded(uint64_t seed, int init_mode) {
   std::lock_guard<std::mutex> lk(g_bert_mu);
   clear_error();

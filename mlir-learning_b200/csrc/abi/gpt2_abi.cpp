@@ -266,6 +266,29 @@ int gpt2_load_weights(const void *packed, size_t bytes, const char *manifest_jso
   return load_blob(*c, static_cast<const float *>(packed));
 }
 
+int gpt2_safetensors_to_blob(const char *path, const Gpt2Config *cfg, float *out) {
+  clear_error();
+  if (!path || !valid_dims(cfg) || !out) {
+    set_error("gpt2_safetensors_to_blob: need a path, a valid configuration and an output buffer");
+    return GPT2_EINVAL;
+  }
+  return gpt2_safetensors_blob(path, dims_of(cfg), out) ? GPT2_EINVAL : 0;
+}
+
+int gpt2_load_safetensors(const char *path) {
+  std::lock_guard<std::mutex> lk(g_api_mu);
+  clear_error();
+  Context *c = context();
+  if (!c) {
+    set_error("gpt2_load_safetensors: no model, call gpt2_init first");
+    return GPT2_ENOMODEL;
+  }
+  if (!path) return GPT2_EINVAL;
+  std::vector<float> blob(static_cast<size_t>(blob_floats(c->dims)));
+  if (gpt2_safetensors_blob(path, c->dims, blob.data())) return GPT2_EINVAL;
+  return load_blob(*c, blob.data());
+}
+
 int gpt2_init_seeded(uint64_t seed, int init_mode) {
   std::lock_guard<std::mutex> lk(g_api_mu);
   clear_error();
@@ -423,6 +446,80 @@ int gpt2k_layernorm(const void *x, const float *gain, const float *shift, void *
               "gpt2k_layernorm");
   set_error("gpt2k_layernorm: bad dtype");
   return GPT2_EINVAL;
+}
+
+namespace {
+std::mutex g_blas_mu;
+struct BlasStage {
+  float *a = nullptr, *b = nullptr, *c = nullptr;
+  size_t na = 0, nb = 0, nc = 0;
+} g_blas;
+
+bool is_device_ptr(const void *p) {
+  cudaPointerAttributes at;
+  if (cudaPointerGetAttributes(&at, p) != cudaSuccess) {
+    cudaGetLastError();
+    return false;
+  }
+  return at.type == cudaMemoryTypeDevice || at.type == cudaMemoryTypeManaged;
+}
+
+int grow(float **p, size_t *cap, size_t n) {
+  if (*cap >= n) return 0;
+  if (*p) cudaFree(*p);
+  *p = nullptr;
+  *cap = 0;
+  if (cudaMalloc(p, n * sizeof(float)) != cudaSuccess) return -1;
+  *cap = n;
+  return 0;
+}
+}  // namespace
+
+int gpt2_blas_sgemm(int order, int transA, int transB, int M, int N, int K, float alpha, const float *A, int lda,
+                    const float *B, int ldb, float beta, float *C, int ldc) {
+  clear_error();
+  const bool b_nk = transB == 112;
+  if (order != 101 || transA != 111 || (transB != 111 && transB != 112) || alpha != 1.0f || beta != 0.0f) {
+    set_error("gpt2_blas_sgemm: only RowMajor, NoTrans A, NoTrans/Trans B, alpha 1, beta 0 (the lowering's call)");
+    return GPT2_EINVAL;
+  }
+  if (M < 1 || N < 1 || K < 1 || !A || !B || !C || lda != K || ldb != (b_nk ? K : N) || ldc < N) {
+    set_error("gpt2_blas_sgemm: bad sizes M=%d N=%d K=%d lda=%d ldb=%d ldc=%d", M, N, K, lda, ldb, ldc);
+    return GPT2_EINVAL;
+  }
+  std::lock_guard<std::mutex> lk(g_blas_mu);
+  // The SIMT kernel wants K % 8 == 0 and, for [K, N] B, N % 4 == 0; other
+  // shapes (and host operands) go through zero-padded device copies.
+  const int Kp = (K + 7) / 8 * 8, Np = b_nk ? N : (N + 3) / 4 * 4;
+  const bool dev = is_device_ptr(A) && is_device_ptr(B) && is_device_ptr(C);
+  cudaStream_t st = nullptr;
+  cudaError_t e;
+  if (dev && Kp == K && Np == N) {
+    e = launch_gemm_f32(A, B, b_nk, C, M, N, K, ldc, nullptr, nullptr, EPI_NONE, st);
+    if (e == cudaSuccess) e = cudaStreamSynchronize(st);
+    return ck(e, "gpt2_blas_sgemm");
+  }
+  const size_t brows = b_nk ? (size_t)N : (size_t)Kp, bcols = b_nk ? (size_t)Kp : (size_t)Np;
+  if (grow(&g_blas.a, &g_blas.na, (size_t)M * Kp) || grow(&g_blas.b, &g_blas.nb, brows * bcols) ||
+      grow(&g_blas.c, &g_blas.nc, (size_t)M * Np)) {
+    set_error("gpt2_blas_sgemm: cannot allocate staging buffers");
+    return GPT2_ENOMEM;
+  }
+  const cudaMemcpyKind in = dev ? cudaMemcpyDeviceToDevice : cudaMemcpyDefault;
+  e = cudaMemsetAsync(g_blas.a, 0, sizeof(float) * (size_t)M * Kp, st);
+  if (e == cudaSuccess) e = cudaMemsetAsync(g_blas.b, 0, sizeof(float) * brows * bcols, st);
+  if (e == cudaSuccess)
+    e = cudaMemcpy2DAsync(g_blas.a, sizeof(float) * Kp, A, sizeof(float) * K, sizeof(float) * K, M, in, st);
+  if (e == cudaSuccess)
+    e = b_nk ? cudaMemcpy2DAsync(g_blas.b, sizeof(float) * Kp, B, sizeof(float) * K, sizeof(float) * K, N, in, st)
+             : cudaMemcpy2DAsync(g_blas.b, sizeof(float) * Np, B, sizeof(float) * N, sizeof(float) * N, K, in, st);
+  if (e == cudaSuccess)
+    e = launch_gemm_f32(g_blas.a, g_blas.b, b_nk, g_blas.c, M, b_nk ? N : Np, Kp, Np, nullptr, nullptr, EPI_NONE, st);
+  if (e == cudaSuccess)
+    e = cudaMemcpy2DAsync(C, sizeof(float) * ldc, g_blas.c, sizeof(float) * Np, sizeof(float) * N, M,
+                          dev ? cudaMemcpyDeviceToDevice : cudaMemcpyDefault, st);
+  if (e == cudaSuccess) e = cudaStreamSynchronize(st);
+  return ck(e, "gpt2_blas_sgemm");
 }
 
 size_t gpt2k_attention_workspace_bytes(int B, int S) {

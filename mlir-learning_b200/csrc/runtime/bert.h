@@ -72,5 +72,6 @@ int bert_ensure_workspace(BertContext &c, int B, int S);
 int bert_forward_device(BertContext &c, const int64_t *d_ids, const int64_t *d_tt, const int64_t *d_pos,
                         const int64_t *d_mask, int B, int S, float *d_hidden, float *d_pooled, cudaStream_t st);
 int bert_forward_launch_count(const BertContext &c, int has_mask, int has_pooler);
+int bert_safetensors_blob(const char *path, const BertDims &m, float *blob);
 
 }  // namespace gpt2

@@ -164,6 +164,8 @@ int ensure_workspace(Context &c, int B, int S);
 int forward_device(Context &c, const int64_t *d_ids, const int64_t *d_mask, int B, int S, float *d_logits,
                    int64_t ld_logits, cudaStream_t st);
 int forward_launch_count(const Context &c, int has_mask);
+// Fills the canonical blob of m from an HF safetensors checkpoint (F32 / F16 / BF16).
+int gpt2_safetensors_blob(const char *path, const ModelDims &m, float *blob);
 int profile_begin(Profiler &p);
 int profile_end(Profiler &p, double *ms, int64_t *count, int n);
 cudaEvent_t prof_event(Profiler &p);  // the next event of the pool (null if none can be created)

@@ -6,6 +6,8 @@ and of the oracle, the reference's own tolerance (src/compare_outputs.py:17).
 BF16 path: relative error bound BF16_RTOL on the logits (max |diff| over
 max |logit|) and top-5 identity wherever the oracle's top-5 is separated by
 more than twice the error observed at that position."""
+import os
+
 import numpy as np
 import pytest
 
@@ -224,3 +226,56 @@ def test_graph_replay_matches_plain_launches(torch, dtype):
     prof = pkg.profile_end()
     assert sum(n for _, n in prof.values()) == pkg.forward_launches(B, S, False)
     assert pkg.status() == 0
+
+
+def test_safetensors_checkpoint_loads_and_matches_blob(torch, tmp_path):
+    """An HF-named safetensors checkpoint (hub layout, BF16 tensors) loaded with
+    gpt2_load_safetensors gives the same logits as the blob it was written from, widened."""
+    st = pytest.importorskip("safetensors.torch")
+    shape = O.GPT2_TINY
+    blob = O.seeded_blob(shape, 41, 1)
+    names = O.tensor_names(shape)
+    off = O.blob_layout(shape)
+    cfg = shape_to_cfg(pkg, shape, pkg.DTYPE_F32)
+    sizes = {"wte.weight": (shape.vocab_size, shape.n_embd), "wpe.weight": (shape.n_positions, shape.n_embd)}
+    tensors = {}
+    for i, n in enumerate(names):
+        k = n.removeprefix("transformer.")
+        v = torch.from_numpy(blob[off[i]:off[i + 1]].copy()).to(torch.bfloat16)
+        if k in sizes:
+            v = v.view(*sizes[k])
+        elif k.endswith("c_attn.weight"):
+            v = v.view(shape.n_embd, 3 * shape.n_embd)
+        elif k.endswith("attn.c_proj.weight"):
+            v = v.view(shape.n_embd, shape.n_embd)
+        elif k.endswith("c_fc.weight"):
+            v = v.view(shape.n_embd, shape.n_inner)
+        elif k.endswith("mlp.c_proj.weight"):
+            v = v.view(shape.n_inner, shape.n_embd)
+        tensors[k] = v.contiguous()
+    path = str(tmp_path / "model.safetensors")
+    st.save_file(tensors, path)
+    widened = torch.from_numpy(blob).to(torch.bfloat16).float().numpy()
+    ids = O.token_ids(2, 30, 41, shape.vocab_size)
+    pkg.init(cfg, 0)
+    pkg.load_safetensors(path)
+    a = pkg.forward_host(ids)
+    pkg.load_weights(widened)
+    b = pkg.forward_host(ids)
+    assert np.array_equal(a, b)
+    assert np.abs(a - O.forward(shape, widened, ids)).max() <= FP32_ATOL
+
+
+@pytest.mark.skipif(not os.environ.get("GPT2_HF_CHECKPOINT"),
+                    reason="needs the pretrained HF gpt2 model.safetensors (env GPT2_HF_CHECKPOINT)")
+def test_reference_readme_top5_with_pretrained_weights(torch):
+    """The reference's published check (src/gpt/README.md, Verification): pretrained gpt2, ids
+    [464, 3139, 286, 4881, 318] ("The capital of France is"), top-5 of the last position
+    262, 783, 257, 4881, 6342 with logits -100.2498 .. -101.2143 (printed to 4 decimals)."""
+    pkg.init(pkg.gpt2_small(pkg.DTYPE_F32), 0)
+    pkg.load_safetensors(os.environ["GPT2_HF_CHECKPOINT"])
+    logits = pkg.gpt2_decoder(np.array([[464, 3139, 286, 4881, 318]]))[0, -1]
+    top = np.argsort(-logits, kind="stable")[:5]
+    assert list(top) == [262, 783, 257, 4881, 6342]
+    want = np.array([-100.2498, -100.8175, -100.8555, -101.2102, -101.2143])
+    assert np.abs(logits[top] - want).max() <= 1.5e-4

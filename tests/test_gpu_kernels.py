@@ -239,3 +239,39 @@ def test_embed_and_bad_ids(torch, dtype):
     err = (x.double()[good] - ref[good]).abs().max().item()
     assert err <= (1e-6 if dtype == 0 else 3e-2), err
     assert torch.all(x[S + 3].double() == wpe.double()[3])
+
+
+@pytest.mark.parametrize("M,N,K,transB,where", [(77, 50, 33, 111, "host"), (128, 256, 64, 111, "device"),
+                                                (5, 2304, 768, 111, "host"), (40, 100, 17, 112, "device"),
+                                                (64, 1000, 128, 112, "host")])
+def test_blas_sgemm_lowering_call(torch, M, N, K, transB, where):
+    """gpt2_blas_sgemm with the argument list a BLAS lowering of linalg.matmul emits
+    (lib/ConvertMatMulToBlas.cpp:84-160: RowMajor, NoTrans, alpha 1, beta 0, lda K, ldb N, ldc N),
+    on host or device operands, shapes the SIMT kernel needs padded for included."""
+    import ctypes
+    rng = np.random.default_rng(M * 131 + N)
+    A = rng.standard_normal((M, K), dtype=np.float32)
+    Bm = rng.standard_normal((N, K) if transB == 112 else (K, N), dtype=np.float32)
+    ref = A.astype(np.float64) @ (Bm.T if transB == 112 else Bm).astype(np.float64)
+    lib = pkg.lib()
+    ldb = K if transB == 112 else N
+    if where == "host":
+        C = np.full((M, N), 7.0, dtype=np.float32)
+        rc = lib.gpt2_blas_sgemm(101, 111, transB, M, N, K, 1.0, A.ctypes.data, K, Bm.ctypes.data, ldb, 0.0,
+                                 C.ctypes.data, N)
+        got = C
+    else:
+        dA, dB = torch.from_numpy(A).cuda(), torch.from_numpy(Bm).cuda()
+        dC = torch.full((M, N), 7.0, device="cuda")
+        rc = lib.gpt2_blas_sgemm(101, 111, transB, M, N, K, 1.0, dA.data_ptr(), K, dB.data_ptr(), ldb, 0.0,
+                                 dC.data_ptr(), N)
+        got = dC.cpu().numpy()
+    assert rc == 0, pkg.last_error()
+    assert np.abs(got - ref).max() <= 2e-5 * np.abs(ref).max() + 1e-5
+    # calls the lowering never emits are refused, not computed
+    assert lib.gpt2_blas_sgemm(101, 111, 111, M, N, K, 2.0, A.ctypes.data, K, A.ctypes.data, N, 0.0,
+                               A.ctypes.data, N) == pkg_einval()
+
+
+def pkg_einval():
+    return -1
