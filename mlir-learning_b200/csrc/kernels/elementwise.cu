@@ -156,64 +156,86 @@ __global__ void layernorm_f32_kernel(const float *__restrict__ x, const float *_
   }
 }
 
+// BF16 rows: a grid-stride loop of warps over rows, the next row's loads
+// issued before the current row is reduced (two rows in flight per warp), the
+// gain and shift staged once per block in shared memory.
 template <int VPT, typename OutT>
-__global__ void layernorm_bf16_kernel(const bf16 *__restrict__ x, const float *__restrict__ g,
-                                      const float *__restrict__ b, OutT *__restrict__ y, int T, int d, float eps) {
-  const int row = (blockIdx.x * blockDim.x + threadIdx.x) >> 5;
+__global__ void __launch_bounds__(256) layernorm_bf16_kernel(const bf16 *__restrict__ x, const float *__restrict__ g,
+                                                             const float *__restrict__ b, OutT *__restrict__ y, int T,
+                                                             int d, float eps) {
   const int lane = threadIdx.x & 31;
-  if (row >= T) return;
+  const int nwarps = (gridDim.x * blockDim.x) >> 5;
   const int nv = d / 8;
-  const uint4 *xr = reinterpret_cast<const uint4 *>(x + (int64_t)row * d);
-  float v[VPT][8];
-  float s = 0.f;
-#pragma unroll
-  for (int i = 0; i < VPT; ++i) {
-    const int c = lane + 32 * i;
-    uint4 raw = c < nv ? xr[c] : make_uint4(0, 0, 0, 0);
-    const __nv_bfloat162 *h = reinterpret_cast<const __nv_bfloat162 *>(&raw);
-#pragma unroll
-    for (int j = 0; j < 4; ++j) {
-      const float2 f = __bfloat1622float2(h[j]);
-      v[i][2 * j] = f.x;
-      v[i][2 * j + 1] = f.y;
-      s += f.x + f.y;
-    }
+  extern __shared__ float4 gb_sm[];  // gain then shift, d floats each
+  for (int i = threadIdx.x; i < d / 4; i += blockDim.x) {
+    gb_sm[i] = reinterpret_cast<const float4 *>(g)[i];
+    gb_sm[d / 4 + i] = reinterpret_cast<const float4 *>(b)[i];
   }
-  const float mean = warp_sum(s) / d;
-  float q = 0.f;
+  __syncthreads();
+  auto load = [&](int row, uint4 (&dst)[VPT]) {
+    const uint4 *xr = reinterpret_cast<const uint4 *>(x + (int64_t)row * d);
 #pragma unroll
-  for (int i = 0; i < VPT; ++i) {
-    const int c = lane + 32 * i;
-    if (c < nv) {
+    for (int i = 0; i < VPT; ++i) {
+      const int c = lane + 32 * i;
+      dst[i] = c < nv ? xr[c] : make_uint4(0, 0, 0, 0);
+    }
+  };
+  int row = (blockIdx.x * blockDim.x + threadIdx.x) >> 5;
+  uint4 cur[VPT], nxt[VPT];
+  if (row < T) load(row, cur);
+  for (; row < T; row += nwarps) {
+    if (row + nwarps < T) load(row + nwarps, nxt);
+    float v[VPT][8];
+    float s = 0.f;
 #pragma unroll
-      for (int j = 0; j < 8; ++j) {
-        const float e = v[i][j] - mean;
-        q += e * e;
+    for (int i = 0; i < VPT; ++i) {
+      const __nv_bfloat162 *h = reinterpret_cast<const __nv_bfloat162 *>(&cur[i]);
+#pragma unroll
+      for (int j = 0; j < 4; ++j) {
+        const float2 f = __bfloat1622float2(h[j]);
+        v[i][2 * j] = f.x;
+        v[i][2 * j + 1] = f.y;
+        s += f.x + f.y;
       }
     }
-  }
-  const float rstd = rsqrtf(warp_sum(q) / d + eps);
+    const float mean = warp_sum(s) / d;
+    float q = 0.f;
 #pragma unroll
-  for (int i = 0; i < VPT; ++i) {
-    const int c = lane + 32 * i;
-    if (c < nv) {
-      const float4 g0 = reinterpret_cast<const float4 *>(g)[2 * c], g1 = reinterpret_cast<const float4 *>(g)[2 * c + 1];
-      const float4 b0 = reinterpret_cast<const float4 *>(b)[2 * c], b1 = reinterpret_cast<const float4 *>(b)[2 * c + 1];
-      const float gg[8] = {g0.x, g0.y, g0.z, g0.w, g1.x, g1.y, g1.z, g1.w};
-      const float bb[8] = {b0.x, b0.y, b0.z, b0.w, b1.x, b1.y, b1.z, b1.w};
-      float o[8];
+    for (int i = 0; i < VPT; ++i) {
+      const int c = lane + 32 * i;
+      if (c < nv) {
 #pragma unroll
-      for (int j = 0; j < 8; ++j) o[j] = (v[i][j] - mean) * rstd * gg[j] + bb[j];
-      if constexpr (sizeof(OutT) == 4) {  // FP32 output (the encoder's last LayerNorm)
-        float4 *yr = reinterpret_cast<float4 *>(y + (int64_t)row * d);
-        yr[2 * c] = make_float4(o[0], o[1], o[2], o[3]);
-        yr[2 * c + 1] = make_float4(o[4], o[5], o[6], o[7]);
-      } else {
-        uint4 *yr = reinterpret_cast<uint4 *>(y + (int64_t)row * d);
-        yr[c] = make_uint4(pack_bf16x2(o[0], o[1]), pack_bf16x2(o[2], o[3]), pack_bf16x2(o[4], o[5]),
-                           pack_bf16x2(o[6], o[7]));
+        for (int j = 0; j < 8; ++j) {
+          const float e = v[i][j] - mean;
+          q += e * e;
+        }
       }
     }
+    const float rstd = rsqrtf(warp_sum(q) / d + eps);
+#pragma unroll
+    for (int i = 0; i < VPT; ++i) {
+      const int c = lane + 32 * i;
+      if (c < nv) {
+        const float4 g0 = gb_sm[2 * c], g1 = gb_sm[2 * c + 1];
+        const float4 b0 = gb_sm[d / 4 + 2 * c], b1 = gb_sm[d / 4 + 2 * c + 1];
+        const float gg[8] = {g0.x, g0.y, g0.z, g0.w, g1.x, g1.y, g1.z, g1.w};
+        const float bb[8] = {b0.x, b0.y, b0.z, b0.w, b1.x, b1.y, b1.z, b1.w};
+        float o[8];
+#pragma unroll
+        for (int j = 0; j < 8; ++j) o[j] = (v[i][j] - mean) * rstd * gg[j] + bb[j];
+        if constexpr (sizeof(OutT) == 4) {  // FP32 output (the encoder's last LayerNorm)
+          float4 *yr = reinterpret_cast<float4 *>(y + (int64_t)row * d);
+          yr[2 * c] = make_float4(o[0], o[1], o[2], o[3]);
+          yr[2 * c + 1] = make_float4(o[4], o[5], o[6], o[7]);
+        } else {
+          uint4 *yr = reinterpret_cast<uint4 *>(y + (int64_t)row * d);
+          yr[c] = make_uint4(pack_bf16x2(o[0], o[1]), pack_bf16x2(o[2], o[3]), pack_bf16x2(o[4], o[5]),
+                             pack_bf16x2(o[6], o[7]));
+        }
+      }
+    }
+#pragma unroll
+    for (int i = 0; i < VPT; ++i) cur[i] = nxt[i];
   }
 }
 
@@ -251,16 +273,30 @@ template <typename OutT>
 cudaError_t layernorm_bf16_any(const bf16 *x, const float *g, const float *b, OutT *y, int T, int d, float eps,
                                cudaStream_t st) {
   if (d % 8 || d > 256 * 8) return cudaErrorInvalidValue;
-  const int threads = 256, blocks = (T + threads / 32 - 1) / (threads / 32);
+  int dev = 0, sms = 148;
+  cudaGetDevice(&dev);
+  cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+  // Enough warps to keep two rows in flight each on every SM, no more than there are rows.
+  const int threads = 256, rows_per_block = threads / 32;
+  const size_t smem = 2 * sizeof(float) * d;
+  const int want = (T + rows_per_block - 1) / rows_per_block;
+  // One resident wave: as many blocks as the SMs hold at once.
+  auto grid_for = [&](auto kernel) {
+    int per_sm = 0;
+    if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, kernel, threads, smem) != cudaSuccess || per_sm < 1)
+      per_sm = 1;
+    const int cap = sms * per_sm;
+    return want < cap ? want : cap;
+  };
   switch ((d + 255) / 256) {
-    case 1: layernorm_bf16_kernel<1, OutT><<<blocks, threads, 0, st>>>(x, g, b, y, T, d, eps); break;
-    case 2: layernorm_bf16_kernel<2, OutT><<<blocks, threads, 0, st>>>(x, g, b, y, T, d, eps); break;
-    case 3: layernorm_bf16_kernel<3, OutT><<<blocks, threads, 0, st>>>(x, g, b, y, T, d, eps); break;
-    case 4: layernorm_bf16_kernel<4, OutT><<<blocks, threads, 0, st>>>(x, g, b, y, T, d, eps); break;
-    case 5: layernorm_bf16_kernel<5, OutT><<<blocks, threads, 0, st>>>(x, g, b, y, T, d, eps); break;
-    case 6: layernorm_bf16_kernel<6, OutT><<<blocks, threads, 0, st>>>(x, g, b, y, T, d, eps); break;
-    case 7: layernorm_bf16_kernel<7, OutT><<<blocks, threads, 0, st>>>(x, g, b, y, T, d, eps); break;
-    case 8: layernorm_bf16_kernel<8, OutT><<<blocks, threads, 0, st>>>(x, g, b, y, T, d, eps); break;
+    case 1: layernorm_bf16_kernel<1, OutT><<<grid_for(layernorm_bf16_kernel<1, OutT>), threads, smem, st>>>(x, g, b, y, T, d, eps); break;
+    case 2: layernorm_bf16_kernel<2, OutT><<<grid_for(layernorm_bf16_kernel<2, OutT>), threads, smem, st>>>(x, g, b, y, T, d, eps); break;
+    case 3: layernorm_bf16_kernel<3, OutT><<<grid_for(layernorm_bf16_kernel<3, OutT>), threads, smem, st>>>(x, g, b, y, T, d, eps); break;
+    case 4: layernorm_bf16_kernel<4, OutT><<<grid_for(layernorm_bf16_kernel<4, OutT>), threads, smem, st>>>(x, g, b, y, T, d, eps); break;
+    case 5: layernorm_bf16_kernel<5, OutT><<<grid_for(layernorm_bf16_kernel<5, OutT>), threads, smem, st>>>(x, g, b, y, T, d, eps); break;
+    case 6: layernorm_bf16_kernel<6, OutT><<<grid_for(layernorm_bf16_kernel<6, OutT>), threads, smem, st>>>(x, g, b, y, T, d, eps); break;
+    case 7: layernorm_bf16_kernel<7, OutT><<<grid_for(layernorm_bf16_kernel<7, OutT>), threads, smem, st>>>(x, g, b, y, T, d, eps); break;
+    case 8: layernorm_bf16_kernel<8, OutT><<<grid_for(layernorm_bf16_kernel<8, OutT>), threads, smem, st>>>(x, g, b, y, T, d, eps); break;
     default: return cudaErrorInvalidValue;
   }
   return cudaGetLastError();
