@@ -188,6 +188,36 @@ int gpt2_forward_host(const int64_t *ids, const int64_t *mask, int B, int S, flo
 /* Number of kernel launches one forward of (B, S) enqueues. */
 int gpt2_forward_launches(int B, int S, int has_mask);
 
+/* ------------------------------------------------------------------------ */
+/* Incremental decoding with a key / value cache                            */
+/* ------------------------------------------------------------------------ */
+/* The reference generates by re-running the whole forward on the grown
+ * sequence (src/gpt/lower_gpt_model.py:190-198, HF generate in
+ * src/gpt/run_gpt.py:20-24); these entry points keep every layer's keys and
+ * values in HBM so that each new token costs one token's work.  Sequences
+ * advance together (all-ones mask).  Logits of a step equal those of the
+ * full forward at that position, up to accumulation order. */
+
+/* Reserves the cache for B (1..16) sequences of up to max_len tokens and
+ * empties it. */
+int gpt2_kv_reserve(int B, int max_len);
+
+/* The forward over d_ids [B, S] (device) that also fills cache positions
+ * 0 .. S-1; writes only the last position's logits, d_logits [B, ld_logits]. */
+int gpt2_prefill(const int64_t *d_ids, int B, int S, float *d_logits, int64_t ld_logits, void *stream);
+
+/* One token per sequence (d_tokens [B], device) at the next position;
+ * d_logits [B, ld_logits].  Fails when the cache is full. */
+int gpt2_decode_step(const int64_t *d_tokens, int B, float *d_logits, int64_t ld_logits, void *stream);
+
+/* Positions currently cached. */
+int gpt2_kv_length(void);
+
+/* Greedy generation (argmax, first maximum on ties): prompt ids [B, S]
+ * (host), n_new tokens per sequence into out_tokens [B, n_new] (host).
+ * Synchronous. */
+int gpt2_generate(const int64_t *ids, int B, int S, int n_new, int64_t *out_tokens);
+
 /* Per-kernel timing: between gpt2_profile_begin() and gpt2_profile_end(),
  * every launch of the forward is bracketed by CUDA events on its stream.
  * gpt2_profile_end waits for them and writes, per kernel kind, the summed

@@ -123,6 +123,10 @@ def lib() -> ctypes.CDLL:
     L.gpt2_load_safetensors.argtypes = [ctypes.c_char_p]
     L.gpt2_blas_sgemm.argtypes = [i32, i32, i32, i32, i32, i32, ctypes.c_float, vp, i32, vp, i32, ctypes.c_float,
                                   vp, i32]
+    L.gpt2_kv_reserve.argtypes = [i32, i32]
+    L.gpt2_prefill.argtypes = [vp, i32, i32, vp, i64, vp]
+    L.gpt2_decode_step.argtypes = [vp, i32, vp, i64, vp]
+    L.gpt2_generate.argtypes = [P(i64), i32, i32, i32, P(i64)]
     L.gpt2k_gemm_f32.argtypes = [vp, vp, i32, vp, i32, i32, i32, i32, vp, vp, i32, vp]
     L.gpt2k_gemm_bf16.argtypes = [vp, vp, vp, i32, i32, i32, i32, i32, vp, vp, i32, i32, vp]
     L.gpt2k_layernorm.argtypes = [vp, vp, vp, vp, i32, i32, ctypes.c_float, i32, vp]
@@ -309,6 +313,33 @@ def forward_device(ids_ptr: int, mask_ptr: int | None, B: int, S: int, logits_pt
                    stream_ptr: int | None = None) -> None:
     _check(lib().gpt2_forward_device(ids_ptr, mask_ptr, B, S, logits_ptr, ld_logits, DTYPE_F32, stream_ptr),
            "gpt2_forward_device")
+
+
+def kv_reserve(B: int, max_len: int) -> None:
+    _check(lib().gpt2_kv_reserve(B, max_len), "gpt2_kv_reserve")
+
+
+def prefill(ids_ptr: int, B: int, S: int, logits_ptr: int, ld: int, stream_ptr: int | None = None) -> None:
+    _check(lib().gpt2_prefill(ids_ptr, B, S, logits_ptr, ld, stream_ptr), "gpt2_prefill")
+
+
+def decode_step(tokens_ptr: int, B: int, logits_ptr: int, ld: int, stream_ptr: int | None = None) -> None:
+    _check(lib().gpt2_decode_step(tokens_ptr, B, logits_ptr, ld, stream_ptr), "gpt2_decode_step")
+
+
+def kv_length() -> int:
+    return lib().gpt2_kv_length()
+
+
+def generate(input_ids, n_new: int) -> np.ndarray:
+    """Greedy continuation of each prompt row: int64 [B, n_new] (the argmax chain HF generate's greedy
+    search produces, src/gpt/run_gpt.py:20-24), with a KV cache on the GPU."""
+    ids = np.ascontiguousarray(_as_i64(input_ids))
+    B, S = ids.shape
+    out = np.empty((B, n_new), dtype=np.int64)
+    P = ctypes.POINTER(ctypes.c_int64)
+    _check(lib().gpt2_generate(ids.ctypes.data_as(P), B, S, n_new, out.ctypes.data_as(P)), "gpt2_generate")
+    return out
 
 
 KERNEL_KINDS = ["seq_info", "embed", "layernorm", "gemm_qkv", "attention", "masked_rows", "gemm_proj", "gemm_fc",

@@ -379,6 +379,70 @@ int gpt2_forward_host(const int64_t *ids, const int64_t *mask, int B, int S, flo
   return forward_host_locked(ids, mask, B, S, logits);
 }
 
+int gpt2_kv_reserve(int B, int max_len) {
+  std::lock_guard<std::mutex> lk(g_api_mu);
+  clear_error();
+  Context *c = context();
+  if (!c || !c->loaded) {
+    set_error("gpt2_kv_reserve: no model loaded");
+    return GPT2_ENOMODEL;
+  }
+  return kv_reserve(*c, B, max_len);
+}
+
+int gpt2_prefill(const int64_t *d_ids, int B, int S, float *d_logits, int64_t ld_logits, void *stream) {
+  std::lock_guard<std::mutex> lk(g_api_mu);
+  clear_error();
+  Context *c = context();
+  if (!c || !c->loaded) {
+    set_error("gpt2_prefill: no model loaded");
+    return GPT2_ENOMODEL;
+  }
+  if (!d_ids || !d_logits) return GPT2_EINVAL;
+  cudaSetDevice(c->device);
+  return prefill(*c, d_ids, B, S, d_logits, ld_logits, static_cast<cudaStream_t>(stream));
+}
+
+int gpt2_decode_step(const int64_t *d_tokens, int B, float *d_logits, int64_t ld_logits, void *stream) {
+  std::lock_guard<std::mutex> lk(g_api_mu);
+  clear_error();
+  Context *c = context();
+  if (!c || !c->loaded) {
+    set_error("gpt2_decode_step: no model loaded");
+    return GPT2_ENOMODEL;
+  }
+  if (!d_tokens || !d_logits) return GPT2_EINVAL;
+  cudaSetDevice(c->device);
+  return decode_step(*c, d_tokens, B, d_logits, ld_logits, static_cast<cudaStream_t>(stream));
+}
+
+int gpt2_kv_length(void) {
+  std::lock_guard<std::mutex> lk(g_api_mu);
+  Context *c = context();
+  return c ? c->dec.len : GPT2_ENOMODEL;
+}
+
+int gpt2_generate(const int64_t *ids, int B, int S, int n_new, int64_t *out_tokens) {
+  std::lock_guard<std::mutex> lk(g_api_mu);
+  clear_error();
+  if (!ids || !out_tokens) {
+    set_error("gpt2_generate: null ids or output");
+    return GPT2_EINVAL;
+  }
+  int r = ensure_default_model_locked();
+  if (r) return r;
+  Context &c = *context();
+  cudaSetDevice(c.device);
+  r = generate(c, ids, B, S, n_new, out_tokens);
+  if (r) return r;
+  const int s = read_status_locked(c);
+  if (s) {
+    set_error("device status %d after generation", s);
+    return GPT2_EDEVICE;
+  }
+  return 0;
+}
+
 int gpt2_forward_launches(int B, int S, int has_mask) {
   (void)B;
   (void)S;

@@ -140,6 +140,35 @@ cudaError_t launch_attn_masked_rows_f32(const float *qkv, const int *first_valid
 cudaError_t launch_attn_masked_rows_bf16(const bf16 *qkv, const int *first_valid, bf16 *o, int B, int S, int H,
                                          cudaStream_t st, int causal = 1);
 
+// ---- incremental decoding (KV cache; M = B <= 16 rows per product) -----------
+cudaError_t launch_decode_embed_f32(const int64_t *tok, const float *wte, const float *wpe, float *x, int B, int d,
+                                    int V, int pos, int *status, cudaStream_t st);
+cudaError_t launch_decode_embed_bf16(const int64_t *tok, const bf16 *wte, const bf16 *wpe, bf16 *x, int B, int d,
+                                     int V, int pos, int *status, cudaStream_t st);
+// y[M, N] (row stride ldy) = epi(x[M, K] @ W[N, K]^T); resid has stride ldy;
+// scale (optional) multiplies the product per column before the epilogue.
+cudaError_t launch_gemv_f32(const float *x, const float *W, float *y, int M, int N, int K, int ldy, const float *bias,
+                            const float *resid, int epi, cudaStream_t st);
+cudaError_t launch_gemv_bf16(const bf16 *x, const bf16 *W, bf16 *y, int M, int N, int K, int ldy, const float *bias,
+                             const bf16 *resid, const float *scale, int epi, cudaStream_t st);
+cudaError_t launch_gemv_bf16_f32out(const bf16 *x, const bf16 *W, float *y, int M, int N, int K, int ldy,
+                                    cudaStream_t st);
+// cache [B][max_len][2D] (keys | values of every head) <- qkv rows of positions pos0 ..
+cudaError_t launch_kv_store_f32(const float *qkv, float *cache, int B, int S, int D, int max_len, int pos0,
+                                cudaStream_t st);
+cudaError_t launch_kv_store_bf16(const bf16 *qkv, bf16 *cache, int B, int S, int D, int max_len, int pos0,
+                                 cudaStream_t st);
+// One query per sequence at position pos (qkv [B, 3D]) against cache
+// positions 0 .. pos - 1 plus its own key / value, which it appends.
+cudaError_t launch_attn_decode_f32(const float *qkv, float *cache, float *out, int B, int H, int pos, int max_len,
+                                   cudaStream_t st);
+cudaError_t launch_attn_decode_bf16(const bf16 *qkv, bf16 *cache, bf16 *out, int B, int H, int pos, int max_len,
+                                    cudaStream_t st);
+// tokens[b] = first argmax of logits[b, :V]
+cudaError_t launch_argmax_rows(const float *logits, int64_t ld, int B, int V, int64_t *tokens, cudaStream_t st);
+// dst[cols, rows] = src[rows, cols]^T (FP32)
+cudaError_t launch_transpose_f32(const float *src, float *dst, int rows, int cols, cudaStream_t st);
+
 // ---- weight packing --------------------------------------------------------
 // dst[i] = bf16(decode_e4m3(src[i])), exact (every E4M3 value is a BF16 value).
 cudaError_t launch_e4m3_to_bf16(const uint8_t *src, bf16 *dst, int64_t n, cudaStream_t st);

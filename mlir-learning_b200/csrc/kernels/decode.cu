@@ -1,0 +1,347 @@
+// decode.cu -- the kernels of incremental (KV-cache) decoding: one new token
+// per sequence per step, so every matrix product has M = B <= 16 rows and is
+// bound by streaming the weights once.
+//
+// Replaces the reference's generation pattern -- re-running the whole
+// forward on the grown sequence each step and taking logits[:, -1]
+// (src/gpt/lower_gpt_model.py:190-198; HF generate's greedy search in
+// src/gpt/run_gpt.py:20-24) -- with per-token work against cached keys and
+// values.  Results equal the last position of the full forward on the same
+// sequence (up to accumulation order).
+#include <math.h>
+
+#include "../common.cuh"
+#include "../kernels.h"
+
+namespace gpt2 {
+
+namespace {
+template <typename T>
+__device__ __forceinline__ float to_f(T v);
+template <>
+__device__ __forceinline__ float to_f<float>(float v) {
+  return v;
+}
+template <>
+__device__ __forceinline__ float to_f<bf16>(bf16 v) {
+  return __bfloat162float(v);
+}
+template <typename T>
+__device__ __forceinline__ T from_f(float v);
+template <>
+__device__ __forceinline__ float from_f<float>(float v) {
+  return v;
+}
+template <>
+__device__ __forceinline__ bf16 from_f<bf16>(float v) {
+  return __float2bfloat16_rn(v);
+}
+
+// 16-byte chunk of a row as floats: 4 (f32) or 8 (bf16) values.
+template <typename T>
+struct Chunk {
+  static constexpr int N = 16 / sizeof(T);
+};
+template <typename T>
+__device__ __forceinline__ void load_chunk(const T *p, float (&v)[Chunk<T>::N]) {
+  const uint4 u = *reinterpret_cast<const uint4 *>(p);
+  if constexpr (sizeof(T) == 4) {
+    v[0] = __uint_as_float(u.x), v[1] = __uint_as_float(u.y), v[2] = __uint_as_float(u.z), v[3] = __uint_as_float(u.w);
+  } else {
+    const __nv_bfloat162 *h = reinterpret_cast<const __nv_bfloat162 *>(&u);
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      const float2 f = __bfloat1622float2(h[j]);
+      v[2 * j] = f.x;
+      v[2 * j + 1] = f.y;
+    }
+  }
+}
+
+// x[b] = wte[tok[b]] + wpe[pos]: one warp per sequence.
+template <typename T>
+__global__ void decode_embed_kernel(const int64_t *__restrict__ tok, const T *__restrict__ wte,
+                                    const T *__restrict__ wpe, T *__restrict__ x, int B, int d, int V, int pos,
+                                    int *status) {
+  const int b = (blockIdx.x * blockDim.x + threadIdx.x) >> 5, lane = threadIdx.x & 31;
+  if (b >= B) return;
+  const int64_t id = tok[b];
+  const bool ok = id >= 0 && id < V;
+  if (!ok && lane == 0) set_status(status, GPT2_ERR_TOKEN_RANGE);
+  const T *e = wte + (ok ? id : 0) * (int64_t)d;
+  const T *p = wpe + (int64_t)pos * d;
+  for (int i = lane; i < d; i += 32) x[(int64_t)b * d + i] = from_f<T>((ok ? to_f(e[i]) : 0.f) + to_f(p[i]));
+}
+
+// y[m, n] = epi(sum_k x[m, k] W[n, k]) for m < M <= 16: one warp per output
+// column n streams W's row n (16-byte loads along k) once for all M rows; x
+// comes from L1 (it is tiny and shared by every warp).  FP32 accumulation,
+// warp-shuffle reduction, the epilogue on lane m for row m.
+template <typename WT, typename AT, typename OT, int EPI, bool EXACT>
+__global__ void __launch_bounds__(256) gemv_nk_kernel(const AT *__restrict__ x, const WT *__restrict__ W,
+                                                      OT *__restrict__ y, int M, int N, int K, int ldy,
+                                                      const float *__restrict__ bias, const OT *resid,
+                                                      const float *__restrict__ scale) {
+  constexpr int MMAX = 16;
+  const int n = (blockIdx.x * blockDim.x + threadIdx.x) >> 5, lane = threadIdx.x & 31;
+  if (n >= N) return;
+  constexpr int WC = Chunk<WT>::N;  // weights per 16-byte chunk
+  float acc[MMAX];
+#pragma unroll
+  for (int m = 0; m < MMAX; ++m) acc[m] = 0.f;
+  const WT *wr = W + (int64_t)n * K;
+  for (int k0 = lane * WC; k0 < K; k0 += 32 * WC) {
+    float w[WC];
+    load_chunk<WT>(wr + k0, w);
+#pragma unroll
+    for (int m = 0; m < MMAX; ++m) {
+      if (m < M) {
+        const AT *xr = x + (int64_t)m * K + k0;
+#pragma unroll
+        for (int j = 0; j < WC; j += Chunk<AT>::N) {
+          float xv[Chunk<AT>::N];
+          load_chunk<AT>(xr + j, xv);
+#pragma unroll
+          for (int e = 0; e < Chunk<AT>::N; ++e) acc[m] = fmaf(xv[e], w[j + e], acc[m]);
+        }
+      }
+    }
+  }
+#pragma unroll
+  for (int m = 0; m < MMAX; ++m) acc[m] = warp_sum(acc[m]);
+  if (lane < M) {
+    float v = 0.f;
+#pragma unroll
+    for (int m = 0; m < MMAX; ++m)
+      if (m == lane) v = acc[m];
+    if (scale) v *= scale[n];
+    if (EPI != EPI_NONE) v += bias[n];
+    if (EPI == EPI_BIAS_GELU) v = EXACT ? gelu_new_exact(v) : gelu_new_fast(v);
+    if (EPI == EPI_BIAS_GELU_ERF) v = EXACT ? gelu_erf(v) : gelu_erf_fast(v);
+    const int64_t idx = (int64_t)lane * ldy + n;
+    if (EPI == EPI_BIAS_RESID) v += to_f(resid[idx]);
+    y[idx] = from_f<OT>(v);
+  }
+}
+
+// Copies the keys and values of S tokens per sequence (positions pos0 ..
+// pos0 + S - 1) from qkv [B*S, 3D] into the cache [B][max_len][2D].
+template <typename T>
+__global__ void kv_store_kernel(const T *__restrict__ qkv, T *__restrict__ cache, int B, int S, int D, int max_len,
+                                int pos0) {
+  const int64_t total = (int64_t)B * S * 2 * D;
+  for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < total; i += (int64_t)gridDim.x * blockDim.x) {
+    const int64_t t = i / (2 * D);
+    const int c = static_cast<int>(i % (2 * D));
+    const int b = static_cast<int>(t / S), s = static_cast<int>(t % S);
+    cache[((int64_t)b * max_len + pos0 + s) * 2 * D + c] = qkv[t * 3 * D + D + c];
+  }
+}
+
+// Attention of one new query per sequence at position pos against cached
+// keys / values 0 .. pos - 1 and its own (taken from qkv, and appended to the
+// cache).  One 128-thread block per (sequence, head): scores in shared memory,
+// block max and sum, then O = P V with two key groups of 64 threads.
+template <typename T, bool EXACT>
+__global__ void __launch_bounds__(128) attn_decode_kernel(const T *__restrict__ qkv, T *__restrict__ cache,
+                                                          T *__restrict__ out, int H, int pos, int max_len) {
+  constexpr int DH = 64;
+  extern __shared__ float sc[];  // pos + 1 scores, then reduction scratch
+  const int h = blockIdx.x, b = blockIdx.y, tid = threadIdx.x;
+  const int D = H * DH, n = pos + 1;
+  const T *q = qkv + (int64_t)b * 3 * D + h * DH;
+  const T *knew = q + D, *vnew = q + 2 * D;
+  T *cb = cache + (int64_t)b * max_len * 2 * D;
+  __shared__ float qs[DH], red[2 * DH];
+  __shared__ float stat[4];
+  if (tid < DH) qs[tid] = to_f(q[tid]);
+  // append this token's key and value
+  if (tid < DH) {
+    cb[(int64_t)pos * 2 * D + h * DH + tid] = knew[tid];
+    cb[(int64_t)pos * 2 * D + D + h * DH + tid] = vnew[tid];
+  }
+  __syncthreads();
+  float mx = -INFINITY;
+  for (int j = tid; j < n; j += blockDim.x) {
+    const T *kr = j == pos ? knew : cb + (int64_t)j * 2 * D + h * DH;
+    float s = 0.f;
+#pragma unroll
+    for (int c = 0; c < DH; c += Chunk<T>::N) {
+      float kv[Chunk<T>::N];
+      load_chunk<T>(kr + c, kv);
+#pragma unroll
+      for (int e = 0; e < Chunk<T>::N; ++e) s = fmaf(qs[c + e], kv[e], s);
+    }
+    s *= 0.125f;
+    sc[j] = s;
+    mx = fmaxf(mx, s);
+  }
+  mx = warp_max(mx);
+  if ((tid & 31) == 0) red[tid >> 5] = mx;
+  __syncthreads();
+  if (tid == 0) stat[0] = fmaxf(fmaxf(red[0], red[1]), fmaxf(red[2], red[3]));
+  __syncthreads();
+  const float m = stat[0];
+  float sum = 0.f;
+  for (int j = tid; j < n; j += blockDim.x) {
+    const float p = EXACT ? expf(sc[j] - m) : __expf(sc[j] - m);
+    sc[j] = p;
+    sum += p;
+  }
+  sum = warp_sum(sum);
+  __syncthreads();
+  if ((tid & 31) == 0) red[tid >> 5] = sum;
+  __syncthreads();
+  if (tid == 0) stat[1] = (red[0] + red[1]) + (red[2] + red[3]);
+  __syncthreads();
+  const float inv = 1.0f / stat[1];
+  const int dim = tid & 63, grp = tid >> 6;
+  float o = 0.f;
+  for (int j = grp; j < n; j += 2) {
+    const T *vr = j == pos ? vnew : cb + (int64_t)j * 2 * D + D + h * DH;
+    o = fmaf(sc[j], to_f(vr[dim]), o);
+  }
+  red[grp * DH + dim] = o;
+  __syncthreads();
+  if (tid < DH) out[(int64_t)b * D + h * DH + tid] = from_f<T>((red[tid] + red[DH + tid]) * inv);
+}
+
+// tokens[b] = argmax_n logits[b, n] (the first maximum, as torch.argmax).
+__global__ void argmax_rows_kernel(const float *__restrict__ logits, int64_t ld, int V, int64_t *__restrict__ tokens) {
+  const int b = blockIdx.x, tid = threadIdx.x;
+  const float *r = logits + (int64_t)b * ld;
+  float best = -INFINITY;
+  int bi = 0x7fffffff;
+  for (int i = tid; i < V; i += blockDim.x) {
+    const float v = r[i];
+    if (v > best || (v == best && i < bi)) {
+      best = v;
+      bi = i;
+    }
+  }
+  for (int o = 16; o; o >>= 1) {
+    const float ov = __shfl_xor_sync(0xffffffffu, best, o);
+    const int oi = __shfl_xor_sync(0xffffffffu, bi, o);
+    if (ov > best || (ov == best && oi < bi)) {
+      best = ov;
+      bi = oi;
+    }
+  }
+  __shared__ float sv[32];
+  __shared__ int si[32];
+  if ((tid & 31) == 0) {
+    sv[tid >> 5] = best;
+    si[tid >> 5] = bi;
+  }
+  __syncthreads();
+  if (tid == 0) {
+    for (int w = 1; w < (int)(blockDim.x >> 5); ++w)
+      if (sv[w] > best || (sv[w] == best && si[w] < bi)) {
+        best = sv[w];
+        bi = si[w];
+      }
+    tokens[b] = bi == 0x7fffffff ? 0 : bi;
+  }
+}
+
+__global__ void transpose_f32_kernel(const float *__restrict__ src, float *__restrict__ dst, int rows, int cols) {
+  __shared__ float tile[32][33];
+  const int bx = blockIdx.x * 32, by = blockIdx.y * 32;
+  for (int i = threadIdx.y; i < 32; i += blockDim.y) {
+    const int r = by + i, c = bx + threadIdx.x;
+    tile[i][threadIdx.x] = (r < rows && c < cols) ? src[(int64_t)r * cols + c] : 0.f;
+  }
+  __syncthreads();
+  for (int i = threadIdx.y; i < 32; i += blockDim.y) {
+    const int c = bx + i, r = by + threadIdx.x;
+    if (c < cols && r < rows) dst[(int64_t)c * rows + r] = tile[threadIdx.x][i];
+  }
+}
+
+template <typename WT, typename AT, typename OT, bool EXACT>
+cudaError_t gemv_dispatch(const AT *x, const WT *W, OT *y, int M, int N, int K, int ldy, const float *bias,
+                          const OT *resid, const float *scale, int epi, cudaStream_t st) {
+  const int blocks = (N + 7) / 8;
+#define GEMV_CASE(E)                                                                                               \
+  case E:                                                                                                          \
+    gemv_nk_kernel<WT, AT, OT, E, EXACT><<<blocks, 256, 0, st>>>(x, W, y, M, N, K, ldy, bias, resid, scale);     \
+    break;
+  switch (epi) {
+    GEMV_CASE(EPI_NONE)
+    GEMV_CASE(EPI_BIAS)
+    GEMV_CASE(EPI_BIAS_GELU)
+    GEMV_CASE(EPI_BIAS_RESID)
+    GEMV_CASE(EPI_BIAS_GELU_ERF)
+    default:
+      return cudaErrorInvalidValue;
+  }
+#undef GEMV_CASE
+  return cudaGetLastError();
+}
+}  // namespace
+
+cudaError_t launch_decode_embed_f32(const int64_t *tok, const float *wte, const float *wpe, float *x, int B, int d,
+                                    int V, int pos, int *status, cudaStream_t st) {
+  decode_embed_kernel<float><<<(B * 32 + 127) / 128, 128, 0, st>>>(tok, wte, wpe, x, B, d, V, pos, status);
+  return cudaGetLastError();
+}
+cudaError_t launch_decode_embed_bf16(const int64_t *tok, const bf16 *wte, const bf16 *wpe, bf16 *x, int B, int d,
+                                     int V, int pos, int *status, cudaStream_t st) {
+  decode_embed_kernel<bf16><<<(B * 32 + 127) / 128, 128, 0, st>>>(tok, wte, wpe, x, B, d, V, pos, status);
+  return cudaGetLastError();
+}
+
+cudaError_t launch_gemv_f32(const float *x, const float *W, float *y, int M, int N, int K, int ldy, const float *bias,
+                            const float *resid, int epi, cudaStream_t st) {
+  if (M < 1 || M > 16 || K % 4 || ldy < N) return cudaErrorInvalidValue;
+  return gemv_dispatch<float, float, float, true>(x, W, y, M, N, K, ldy, bias, resid, nullptr, epi, st);
+}
+cudaError_t launch_gemv_bf16(const bf16 *x, const bf16 *W, bf16 *y, int M, int N, int K, int ldy, const float *bias,
+                             const bf16 *resid, const float *scale, int epi, cudaStream_t st) {
+  if (M < 1 || M > 16 || K % 8 || ldy < N) return cudaErrorInvalidValue;
+  return gemv_dispatch<bf16, bf16, bf16, false>(x, W, y, M, N, K, ldy, bias, resid, scale, epi, st);
+}
+cudaError_t launch_gemv_bf16_f32out(const bf16 *x, const bf16 *W, float *y, int M, int N, int K, int ldy,
+                                    cudaStream_t st) {
+  if (M < 1 || M > 16 || K % 8 || ldy < N) return cudaErrorInvalidValue;
+  return gemv_dispatch<bf16, bf16, float, false>(x, W, y, M, N, K, ldy, nullptr, nullptr, nullptr, EPI_NONE, st);
+}
+
+cudaError_t launch_kv_store_f32(const float *qkv, float *cache, int B, int S, int D, int max_len, int pos0,
+                                cudaStream_t st) {
+  kv_store_kernel<float><<<592, 256, 0, st>>>(qkv, cache, B, S, D, max_len, pos0);
+  return cudaGetLastError();
+}
+cudaError_t launch_kv_store_bf16(const bf16 *qkv, bf16 *cache, int B, int S, int D, int max_len, int pos0,
+                                 cudaStream_t st) {
+  kv_store_kernel<bf16><<<592, 256, 0, st>>>(qkv, cache, B, S, D, max_len, pos0);
+  return cudaGetLastError();
+}
+
+cudaError_t launch_attn_decode_f32(const float *qkv, float *cache, float *out, int B, int H, int pos, int max_len,
+                                   cudaStream_t st) {
+  if (pos < 0 || pos >= max_len) return cudaErrorInvalidValue;
+  attn_decode_kernel<float, true><<<dim3(H, B), 128, sizeof(float) * (pos + 1), st>>>(qkv, cache, out, H, pos,
+                                                                                       max_len);
+  return cudaGetLastError();
+}
+cudaError_t launch_attn_decode_bf16(const bf16 *qkv, bf16 *cache, bf16 *out, int B, int H, int pos, int max_len,
+                                    cudaStream_t st) {
+  if (pos < 0 || pos >= max_len) return cudaErrorInvalidValue;
+  attn_decode_kernel<bf16, false><<<dim3(H, B), 128, sizeof(float) * (pos + 1), st>>>(qkv, cache, out, H, pos,
+                                                                                      max_len);
+  return cudaGetLastError();
+}
+
+cudaError_t launch_argmax_rows(const float *logits, int64_t ld, int B, int V, int64_t *tokens, cudaStream_t st) {
+  argmax_rows_kernel<<<B, 1024, 0, st>>>(logits, ld, V, tokens);
+  return cudaGetLastError();
+}
+
+cudaError_t launch_transpose_f32(const float *src, float *dst, int rows, int cols, cudaStream_t st) {
+  dim3 grid((cols + 31) / 32, (rows + 31) / 32), block(32, 8);
+  transpose_f32_kernel<<<grid, block, 0, st>>>(src, dst, rows, cols);
+  return cudaGetLastError();
+}
+
+}  // namespace gpt2

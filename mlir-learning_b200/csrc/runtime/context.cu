@@ -96,6 +96,7 @@ void destroy_context() {
   cudaSetDevice(c->device);
   cudaDeviceSynchronize();
   drop_graph(c->graph);
+  free_decode(c->dec);
   for (cudaEvent_t e : c->prof.pool) cudaEventDestroy(e);
   free_ws(c->ws);
   if (c->d_blob) cudaFree(c->d_blob);
@@ -350,7 +351,6 @@ int forward_launch_count(const Context &c, int has_mask) {
   return 3 + 7 * c.dims.n_layer + (has_mask ? 1 + c.dims.n_layer : 0);
 }
 
-namespace {
 // Buffers, TMA descriptors and output descriptor of a forward of (B, S) into
 // d_logits: everything that allocates or encodes on the host, done before
 // any launch (and outside any graph capture).
@@ -370,14 +370,16 @@ int prepare_forward(Context &c, int B, int S, float *d_logits, int64_t ld_logits
     }
   }
   TcGemmPlan &head = c.plans[4 * m.n_layer];
-  if (head.c_ptr != d_logits || head.c_ld != (int)ld_logits || !head.c_f32)
+  if (d_logits && (head.c_ptr != d_logits || head.c_ld != (int)ld_logits || !head.c_f32))
     tc_gemm_set_output(&head, d_logits, (int)ld_logits, 1);
   return 0;
 }
 
-// Enqueues the forward's kernels on st (prepare_forward has run).
+// Enqueues the forward's kernels on st (prepare_forward has run).  With
+// kv_fill, every layer's keys and values also go to the decode cache, and
+// only the last position's logits are computed, into d_logits [B, ld_logits].
 int launch_forward(Context &c, const int64_t *d_ids, const int64_t *d_mask, int B, int S, float *d_logits,
-                   int64_t ld_logits, cudaStream_t st) {
+                   int64_t ld_logits, cudaStream_t st, bool kv_fill) {
   const ModelDims &m = c.dims;
   const int64_t T = (int64_t)B * S;
   const int d = m.n_embd, ff = m.n_inner, H = m.n_head, V = m.vocab;
@@ -395,6 +397,8 @@ int launch_forward(Context &c, const int64_t *d_ids, const int64_t *d_mask, int 
       const LayerWeights &lw = c.layers[l];
       CKP(K_LAYERNORM, launch_layernorm_f32(x, lw.ln1_g, lw.ln1_b, a, (int)T, d, m.eps, st));
       CKP(K_GEMM_QKV, launch_gemm_f32(a, lw.qkv_w, 0, qkv, (int)T, 3 * d, d, 3 * d, lw.qkv_b, nullptr, EPI_BIAS, st));
+      if (kv_fill)
+        CK(launch_kv_store_f32(qkv, static_cast<float *>(c.dec.cache[l]), B, S, d, c.dec.max_len, 0, st));
       CKP(K_ATTENTION, launch_attention_f32(qkv, kv, o, B, S, H, st));
       if (d_mask) CKP(K_MASKED_ROWS, launch_attn_masked_rows_f32(qkv, w.first_valid, o, B, S, H, st));
       CKP(K_GEMM_PROJ, launch_gemm_f32(o, lw.proj_w, 0, x, (int)T, d, d, d, lw.proj_b, x, EPI_BIAS_RESID, st));
@@ -403,6 +407,13 @@ int launch_forward(Context &c, const int64_t *d_ids, const int64_t *d_mask, int 
       CKP(K_GEMM_MPROJ, launch_gemm_f32(u, lw.mproj_w, 0, x, (int)T, d, ff, d, lw.mproj_b, x, EPI_BIAS_RESID, st));
     }
     CKP(K_LAYERNORM, launch_layernorm_f32(x, c.lnf_g, c.lnf_b, a, (int)T, d, m.eps, st));
+    if (kv_fill) {
+      float *al = static_cast<float *>(c.dec.a_last);
+      CK(cudaMemcpy2DAsync(al, sizeof(float) * d, a + (int64_t)(S - 1) * d, sizeof(float) * S * d,
+                           sizeof(float) * d, B, cudaMemcpyDeviceToDevice, st));
+      CKP(K_LM_HEAD, launch_gemv_f32(al, c.wte, d_logits, B, V, d, (int)ld_logits, nullptr, nullptr, EPI_NONE, st));
+      return 0;
+    }
     CKP(K_LM_HEAD, launch_gemm_f32(a, c.wte, 1, d_logits, (int)T, V, d, (int)ld_logits, nullptr, nullptr, EPI_NONE, st));
     return 0;
   }
@@ -415,6 +426,7 @@ int launch_forward(Context &c, const int64_t *d_ids, const int64_t *d_mask, int 
     const TcGemmPlan *p = &c.plans[4 * l];
     CKP(K_LAYERNORM, launch_layernorm_bf16(x, lw.ln1_g, lw.ln1_b, a, (int)T, d, m.eps, st));
     CKP(K_GEMM_QKV, launch_gemm_tc(p[0], qkv, 3 * d, 0, lw.qkv_b, nullptr, EPI_BIAS, c.d_status, ns, st, lw.qkv_s));
+    if (kv_fill) CK(launch_kv_store_bf16(qkv, static_cast<bf16 *>(c.dec.cache[l]), B, S, d, c.dec.max_len, 0, st));
     CKP(K_ATTENTION, launch_attention_tc2(c.attn_plan, kv, o, c.d_status, st));
     if (d_mask) CKP(K_MASKED_ROWS, launch_attn_masked_rows_bf16(qkv, w.first_valid, o, B, S, H, st));
     CKP(K_GEMM_PROJ, launch_gemm_tc(p[1], x, d, 0, lw.proj_b, x, EPI_BIAS_RESID, c.d_status, ns, st, lw.proj_s));
@@ -424,12 +436,18 @@ int launch_forward(Context &c, const int64_t *d_ids, const int64_t *d_mask, int 
         launch_gemm_tc(p[3], x, d, 0, lw.mproj_b, x, EPI_BIAS_RESID, c.d_status, ns, st, lw.mproj_s));
   }
   CKP(K_LAYERNORM, launch_layernorm_bf16(x, c.lnf_g, c.lnf_b, a, (int)T, d, m.eps, st));
+  if (kv_fill) {
+    bf16 *al = static_cast<bf16 *>(c.dec.a_last);
+    CK(cudaMemcpy2DAsync(al, sizeof(bf16) * d, a + (int64_t)(S - 1) * d, sizeof(bf16) * S * d, sizeof(bf16) * d, B,
+                         cudaMemcpyDeviceToDevice, st));
+    CKP(K_LM_HEAD, launch_gemv_bf16_f32out(al, c.wte_h, d_logits, B, V, d, (int)ld_logits, st));
+    return 0;
+  }
   const TcGemmPlan &head = c.plans[4 * m.n_layer];
   CKP(K_LM_HEAD, launch_gemm_tc(head, d_logits, (int)ld_logits, 1, nullptr, nullptr, EPI_NONE, c.d_status, ns,
                     st));
   return 0;
 }
-}  // namespace
 
 int forward_device(Context &c, const int64_t *d_ids, const int64_t *d_mask, int B, int S, float *d_logits,
                    int64_t ld_logits, cudaStream_t st) {
@@ -444,7 +462,7 @@ int forward_device(Context &c, const int64_t *d_ids, const int64_t *d_mask, int 
   }
   int r = prepare_forward(c, B, S, d_logits, ld_logits);
   if (r) return r;
-  auto launch = [&](cudaStream_t s) { return launch_forward(c, d_ids, d_mask, B, S, d_logits, ld_logits, s); };
+  auto launch = [&](cudaStream_t s) { return launch_forward(c, d_ids, d_mask, B, S, d_logits, ld_logits, s, false); };
   if (c.prof.on) return launch(st);  // per-launch events need plain launches
   const uintptr_t key[6] = {reinterpret_cast<uintptr_t>(d_ids), reinterpret_cast<uintptr_t>(d_mask),
                             reinterpret_cast<uintptr_t>(d_logits), static_cast<uintptr_t>(ld_logits),

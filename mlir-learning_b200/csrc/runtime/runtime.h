@@ -77,6 +77,18 @@ struct Profiler {
   std::vector<int> kinds;  // kind of record i; events 2i, 2i+1
 };
 
+// Incremental decoding: the key / value cache and the buffers of one step.
+struct DecodeState {
+  int B = 0, max_len = 0, len = 0;  // len = positions cached so far
+  std::vector<void *> cache;        // per layer [B][max_len][2D], activation dtype
+  void *x = nullptr, *a = nullptr, *qkv = nullptr, *o = nullptr, *u = nullptr, *a_last = nullptr;
+  float *logits = nullptr;          // [B, ld_logits] for gpt2_generate
+  int64_t ld_logits = 0;
+  int64_t *tokens = nullptr;        // generated tokens [n_new][B] for gpt2_generate
+  int64_t tokens_cap = 0;
+  std::vector<float *> wt;          // FP32 path: [out, in] copies of the Conv1D weights, 4 per layer
+};
+
 // The forward captured as one CUDA graph for a fixed set of arguments and
 // buffers: replayed when a call repeats them (one graph launch instead of
 // ~85 kernel launches).  Dropped whenever the workspace is reallocated.
@@ -150,6 +162,7 @@ struct Context {
   Profiler prof;
   GraphCache graph;
   bool use_graphs = true;  // env GPT2_GRAPHS=0 turns graph replay off
+  DecodeState dec;
   std::mutex mu;
 };
 
@@ -164,6 +177,19 @@ int ensure_workspace(Context &c, int B, int S);
 int forward_device(Context &c, const int64_t *d_ids, const int64_t *d_mask, int B, int S, float *d_logits,
                    int64_t ld_logits, cudaStream_t st);
 int forward_launch_count(const Context &c, int has_mask);
+int prepare_forward(Context &c, int B, int S, float *d_logits, int64_t ld_logits);
+int launch_forward(Context &c, const int64_t *d_ids, const int64_t *d_mask, int B, int S, float *d_logits,
+                   int64_t ld_logits, cudaStream_t st, bool kv_fill);
+// Incremental decoding (B <= 16 sequences of up to max_len tokens).
+int kv_reserve(Context &c, int B, int max_len);
+// The forward over B x S ids that also fills the cache (positions 0 .. S-1)
+// and writes only the last position's logits [B, ld].
+int prefill(Context &c, const int64_t *d_ids, int B, int S, float *d_logits, int64_t ld, cudaStream_t st);
+// One token per sequence at position c.dec.len; logits [B, ld].
+int decode_step(Context &c, const int64_t *d_tokens, int B, float *d_logits, int64_t ld, cudaStream_t st);
+int generate(Context &c, const int64_t *ids, int B, int S, int n_new, int64_t *out_tokens);
+void free_decode(DecodeState &d);
+
 // Fills the canonical blob of m from an HF safetensors checkpoint (F32 / F16 / BF16).
 int gpt2_safetensors_blob(const char *path, const ModelDims &m, float *blob);
 int profile_begin(Profiler &p);
