@@ -91,6 +91,33 @@ __device__ __forceinline__ uint64_t add2(uint64_t a, uint64_t b) {
   asm("add.rn.f32x2 %0, %1, %2;" : "=l"(d) : "l"(a), "l"(b));
   return d;
 }
+// 2^x for a pair on the FMA pipe, to take load off the MUFU unit: Cody-Waite
+// split x = n + f with the round-to-nearest magic constant 1.5 * 2^23
+// (f in [-0.5, 0.5]), 2^f by a degree-3 polynomial fitted here for minimum
+// relative error on that interval (|rel err| < 1e-4, below the bf16 rounding
+// of P), 2^n added to the exponent field.  x <= -125 (masked or negligible
+// terms) gives exactly 0.
+constexpr int kPolyPairs = 4;  // of every 16 score pairs, this many take the polynomial path
+__device__ __forceinline__ uint64_t exp2_poly2(uint64_t x2) {
+  float x0, x1;
+  up2(x2, x0, x1);
+  const float c0 = fmaxf(x0, -126.f), c1 = fmaxf(x1, -126.f);
+  const uint64_t xc = pk2(c0, c1);
+  const uint64_t t = add2(xc, pk2(12582912.f, 12582912.f));
+  const uint64_t r = add2(t, pk2(-12582912.f, -12582912.f));
+  const uint64_t f = fma2(r, pk2(-1.f, -1.f), xc);
+  uint64_t p = fma2(pk2(0.0551716610789299f, 0.0551716610789299f), f, pk2(0.24261115491390228f, 0.24261115491390228f));
+  p = fma2(p, f, pk2(0.6932609677314758f, 0.6932609677314758f));
+  p = fma2(p, f, pk2(0.9999280571937561f, 0.9999280571937561f));
+  float t0, t1, p0, p1;
+  up2(t, t0, t1);
+  up2(p, p0, p1);
+  // (bits(t) - bits(1.5 * 2^23)) << 23 == bits(t) << 23 modulo 2^32
+  const float e0 = __uint_as_float(__float_as_uint(p0) + (__float_as_uint(t0) << 23));
+  const float e1 = __uint_as_float(__float_as_uint(p1) + (__float_as_uint(t1) << 23));
+  return pk2(x0 <= -125.f ? 0.f : e0, x1 <= -125.f ? 0.f : e1);
+}
+
 __device__ __forceinline__ float max3(float a, float b, float c) {
   float d;
   asm("max.f32 %0, %1, %2, %3;" : "=f"(d) : "f"(a), "f"(b), "f"(c));
@@ -467,9 +494,15 @@ __global__ void __launch_bounds__(NTHREADS, 1)
           for (int e2 = 0; e2 < 16; ++e2) {
             const int c = q4 * 32 + 2 * e2;
             const uint64_t x2 = fma2(pk2(__uint_as_float(sv[c]), __uint_as_float(sv[c + 1])), sl2x2, negm2);
-            float x0, x1;
-            up2(x2, x0, x1);
-            const float p0 = ex2(x0), p1 = ex2(x1);
+            float p0, p1;
+            if ((e2 & 3) * 4 >= 16 - kPolyPairs) {  // the last kPolyPairs / 4 of every 4 pairs
+              up2(exp2_poly2(x2), p0, p1);
+            } else {
+              float x0, x1;
+              up2(x2, x0, x1);
+              p0 = ex2(x0);
+              p1 = ex2(x1);
+            }
             rs2[e2 & 3] = add2(rs2[e2 & 3], pk2(p0, p1));
             pw[e2] = pack_bf16x2(p0, p1);
           }
