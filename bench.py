@@ -45,11 +45,11 @@ LD_LOGITS = 50304  # row stride of the resident logits (16-byte aligned rows)
 # The workloads of the reference's configurations that run through this path:
 # (name, layers, d_model, heads, d_mlp, dtype code, dtype label, global batch, seq).
 CONFIGS = {
-    1: ("gpt2-small FP32 prefill B8xS1024 (config 1)", 12, 768, 12, 3072, 0, "f32", 8, 1024),
-    2: ("gpt2-small BF16 prefill B64xS1024 (config 2)", 12, 768, 12, 3072, 1, "bf16", 64, 1024),
-    3: ("bert-base BF16 encoder B128xS512, valid lengths uniform in [64, 512] (config 3)", 12, 768, 12, 3072, 1,
+    1: ("gpt2-small FP32 prefill B8xS1024", 12, 768, 12, 3072, 0, "f32", 8, 1024),
+    2: ("gpt2-small BF16 prefill B64xS1024", 12, 768, 12, 3072, 1, "bf16", 64, 1024),
+    3: ("bert-base BF16 encoder B128xS512, valid lengths uniform in [64, 512]", 12, 768, 12, 3072, 1,
         "bf16", 128, 512),
-    4: ("gpt2-xl-shape FP8 weight-only prefill B32xS1024 (config 4)", 48, 1600, 25, 6400, 2, "fp8w-e4m3/bf16", 32,
+    4: ("gpt2-xl-shape FP8 weight-only prefill B32xS1024", 48, 1600, 25, 6400, 2, "fp8w-e4m3/bf16", 32,
         1024),
 }
 BERT_V, BERT_P, BERT_TV = 30522, 512, 2
@@ -194,7 +194,7 @@ FP32_SIMT_NOMINAL_TFLOPS = 148 * 128 * 2 * 1.965e9 / 1e12
 def kernel_breakdown(prof: dict, work: dict, nprof: int, peaks: dict, config: int, tokens: int):
     """Per-kernel ms / share / rate of `nprof` profiled steps and the roofline of the dominant
     kernel (achieved = algorithmic work per launch / average event-timed launch duration).  The
-    exact-FP32 configuration (config 1) runs on FFMA, not the tensor cores: its FLOP-bound
+    exact-FP32 workload (--config 1) runs on FFMA, not the tensor cores: its FLOP-bound
     kernels are rated against the FP32 SIMT peak."""
     kernels = {}
     for k, (ms, n) in prof.items():
@@ -329,7 +329,7 @@ def run_reference(args, rank, world):
 
 
 def run_bert(args, rank, world, local_rank, pkg, torch, dist):
-    """Config 3: the BERT-base BF16 encoder over this rank's shard of B128 x S512 right-padded
+    """--config 3: the BERT-base BF16 encoder over this rank's shard of B128 x S512 right-padded
     sequences (device-resident ids, token types and mask; FP32 hidden states and pooled output
     written to HBM each step)."""
     Bm = pkg.bert

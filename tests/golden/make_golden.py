@@ -114,7 +114,7 @@ def main_bert():
     # The reference BERT host program's call (src/bert-base-uncased/call_bert.cpp:61-64), seeded weights.
     ids = np.array([[101, 2023, 2003, 1037, 7099, 7953, 2005, 14324, 2944, 9167, 1012, 102]], dtype=np.int64)
     run_bert_case("bert_base_refcall", base, 1234, 0, ids, np.zeros_like(ids), np.ones_like(ids))
-    # BERT-base, right-padded batch (config 3's mask shape), token types 0 / 1 halves.
+    # BERT-base, right-padded batch (the benchmark's mask shape), token types 0 / 1 halves.
     ids = O.token_ids(2, 64, 33, base.vocab_size, stream=O.BERT_IDS_STREAM)
     tt = np.zeros_like(ids)
     tt[:, 32:] = 1
@@ -141,7 +141,7 @@ def main():
     ref_ids = np.array([[464, 3139, 286, 4881, 318]], dtype=np.int64)
     run_case("gpt2_small_refcall", small, 1234, 0, ref_ids, ones(1, 5))
 
-    # Config 0: GPT-2 small, B=1, S=5, seeded ids.
+    # GPT-2 small, B=1, S=5, seeded ids (the CPU-runnable case).
     run_case("gpt2_small_cfg0", small, 1234, 0, O.token_ids(1, 5, 1234, small.vocab_size), ones(1, 5))
 
     # Every tensor random (biases, gains, shifts), B=2, S=9, a left-padded row.

@@ -4,7 +4,7 @@ device entry point.
 
 FP32 path: last_hidden_state and pooler_output within 1e-4 absolute of the
 golden fixtures (HF BertModel on the same seeded weights) and of the oracle.
-BF16 path (the config-3 arithmetic): max |diff| of the hidden states at most
+BF16 path (the arithmetic of the B128 x S512 BF16 workload): max |diff| of the hidden states at most
 BERT_BF16_RTOL times max |hidden| of the reference, every token's hidden
 vector at cosine similarity >= BERT_BF16_MIN_COS, pooled outputs (tanh, in
 [-1, 1]) within BERT_BF16_POOLED_ATOL."""
@@ -128,7 +128,7 @@ def test_bf16_right_padding_lengths_s512_vs_oracle(torch):
 
 
 def test_bf16_config3_batch_invariance(torch):
-    """Config 3 (B=128 x S=512, BF16, lengths uniform in [64, 512]) on the device entry point:
+    """The BERT workload (B=128 x S=512, BF16, lengths uniform in [64, 512]) on the device entry point:
     every sequence equals the same sequence run alone, bit for bit; two are checked against
     the oracle."""
     shape = O.BERT_BASE
@@ -155,7 +155,7 @@ def test_bf16_config3_batch_invariance(torch):
         assert torch.equal(hidden[b:b + 1], h1) and torch.equal(pooled[b:b + 1], p1)
         if b != 0:
             rh, rp = O.bert_forward(shape, blob, ids_h[b:b + 1], None, mask_h[b:b + 1])
-            _bf16_check(rh, h1.cpu().numpy(), rp, p1.cpu().numpy(), f"bf16 config-3 seq {b} (len {lens[b]})")
+            _bf16_check(rh, h1.cpu().numpy(), rp, p1.cpu().numpy(), f"bf16 B128xS512 seq {b} (len {lens[b]})")
     O.set_loop_threads(1)
     assert torch.isfinite(hidden).all() and torch.isfinite(pooled).all()
 

@@ -94,7 +94,7 @@ def test_refcall_through_both_symbols_and_strides(torch):
 
 
 def test_fp32_full_context_vs_oracle(torch):
-    """GPT-2 small, B=2 x S=1024 (the config-1 sequence length) against the oracle."""
+    """GPT-2 small, B=2 x S=1024 (the FP32 workload's sequence length) against the oracle."""
     shape = O.GPT2_SMALL
     blob = O.seeded_blob(shape, 1234, 0)
     ids = O.token_ids(2, 1024, 1234, shape.vocab_size)
@@ -109,7 +109,7 @@ def test_fp32_full_context_vs_oracle(torch):
 
 
 def test_fp32_batch_invariance_config1(torch):
-    """Config 1 (B=8 x S=1024, FP32): each sequence's logits equal those of the same sequence run
+    """The FP32 workload (B=8 x S=1024): each sequence's logits equal those of the same sequence run
     alone, bit for bit (rows never mix), so the B=2 oracle check covers all 8."""
     shape = O.GPT2_SMALL
     blob = O.seeded_blob(shape, 1234, 0)
@@ -123,7 +123,7 @@ def test_fp32_batch_invariance_config1(torch):
 
 
 def test_bf16_vs_oracle_and_batch_invariance_config2(torch):
-    """Config 2 (B=64 x S=1024, BF16) on the device entry point: sequences are independent and
+    """The headline BF16 workload (B=64 x S=1024) on the device entry point: sequences are independent and
     bit-identical to single-sequence runs; two of them are checked against the oracle."""
     shape = O.GPT2_SMALL
     blob = O.seeded_blob(shape, 1234, 0)
@@ -144,7 +144,7 @@ def test_bf16_vs_oracle_and_batch_invariance_config2(torch):
         torch.cuda.synchronize()
         assert torch.equal(logits[b * S:(b + 1) * S, :V], one[:, :V])
         ref = O.forward(shape, blob, ids_h[b:b + 1])
-        _bf16_check(ref[0], one[:, :V].cpu().numpy(), f"bf16 config-2 seq {b}")
+        _bf16_check(ref[0], one[:, :V].cpu().numpy(), f"bf16 B64xS1024 seq {b}")
     O.set_loop_threads(1)
     assert torch.isfinite(logits[:, :V]).all()
 

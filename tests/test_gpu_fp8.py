@@ -67,7 +67,7 @@ def test_fp8w_xl_shape_two_layers(torch):
 
 
 def test_fp8w_gpt2_xl_48_layers(torch):
-    """Config 4's model (GPT-2 XL shape, 48 layers) on one short sequence."""
+    """The FP8-weight workload's model (GPT-2 XL shape, 48 layers) on one short sequence."""
     ref_q, ref_f, got = _run(O.GPT2_XL, 2024, 1, 128, False)
     _check(ref_q, got, BF16_RTOL, "fp8w GPT-2 XL vs oracle on dequantized weights")
     _check(ref_f, got, FP8_RTOL, "fp8w GPT-2 XL vs oracle on FP32 weights")

@@ -1,4 +1,4 @@
-"""Multi-GPU batch sharding with the NCCL logits gather (SURVEY row e), on
+"""Multi-GPU batch sharding with the NCCL logits gather, on
 every GPU of the box: launches tests/multirank_worker.py with torchrun; the
 gathered logits must equal a single-GPU forward of the whole batch bit for
 bit.  Skipped on boxes with fewer than two GPUs."""
