@@ -141,10 +141,12 @@ cudaError_t launch_attn_masked_rows_bf16(const bf16 *qkv, const int *first_valid
                                          cudaStream_t st, int causal = 1);
 
 // ---- incremental decoding (KV cache; M = B <= 16 rows per product) -----------
+// The step's position is read from device memory (*d_pos), so one captured
+// step serves every position.
 cudaError_t launch_decode_embed_f32(const int64_t *tok, const float *wte, const float *wpe, float *x, int B, int d,
-                                    int V, int pos, int *status, cudaStream_t st);
+                                    int V, const int *d_pos, int P, int *status, cudaStream_t st);
 cudaError_t launch_decode_embed_bf16(const int64_t *tok, const bf16 *wte, const bf16 *wpe, bf16 *x, int B, int d,
-                                     int V, int pos, int *status, cudaStream_t st);
+                                     int V, const int *d_pos, int P, int *status, cudaStream_t st);
 // y[M, N] (row stride ldy) = epi(x[M, K] @ W[N, K]^T); resid has stride ldy;
 // scale (optional) multiplies the product per column before the epilogue.
 cudaError_t launch_gemv_f32(const float *x, const float *W, float *y, int M, int N, int K, int ldy, const float *bias,
@@ -158,12 +160,18 @@ cudaError_t launch_kv_store_f32(const float *qkv, float *cache, int B, int S, in
                                 cudaStream_t st);
 cudaError_t launch_kv_store_bf16(const bf16 *qkv, bf16 *cache, int B, int S, int D, int max_len, int pos0,
                                  cudaStream_t st);
-// One query per sequence at position pos (qkv [B, 3D]) against cache
-// positions 0 .. pos - 1 plus its own key / value, which it appends.
-cudaError_t launch_attn_decode_f32(const float *qkv, float *cache, float *out, int B, int H, int pos, int max_len,
-                                   cudaStream_t st);
-cudaError_t launch_attn_decode_bf16(const bf16 *qkv, bf16 *cache, bf16 *out, int B, int H, int pos, int max_len,
-                                    cudaStream_t st);
+// One query per sequence at position *d_pos (qkv [B, 3D]) against cache
+// positions 0 .. pos - 1 plus its own key / value, which it appends; a
+// position at or past max_len records status 3 and changes nothing.
+cudaError_t launch_attn_decode_f32(const float *qkv, float *cache, float *out, int B, int H, const int *d_pos,
+                                   int max_len, int *status, cudaStream_t st);
+cudaError_t launch_attn_decode_bf16(const bf16 *qkv, bf16 *cache, bf16 *out, int B, int H, const int *d_pos,
+                                    int max_len, int *status, cudaStream_t st);
+cudaError_t launch_set_int(int *p, int v, cudaStream_t st);
+cudaError_t launch_add_int(int *p, int v, cudaStream_t st);
+// hist[(*d_pos - base) * B + b] = cur[b] for b < B (bounded by cap entries)
+cudaError_t launch_append_tokens(const int64_t *cur, int64_t *hist, const int *d_pos, int base, int B, int cap,
+                                 cudaStream_t st);
 // tokens[b] = first argmax of logits[b, :V]
 cudaError_t launch_argmax_rows(const float *logits, int64_t ld, int B, int V, int64_t *tokens, cudaStream_t st);
 // dst[cols, rows] = src[rows, cols]^T (FP32)

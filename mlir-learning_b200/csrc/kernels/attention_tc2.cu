@@ -258,18 +258,19 @@ __global__ void __launch_bounds__(NTHREADS, 1)
     int g_base[2] = {0, 0};  // running per-tile iteration count (barrier phases)
     int qi = 0, kv_base = 0;
     bool ok = true;
+    bool pre_s0 = false;  // S_0(0) of this item was issued while the previous item finished
     for (int w = blockIdx.x; w < n_items && ok; w += gridDim.x, ++qi) {
       const AttnItem it = attn_item(w, S, B, H, causal, kv_end);
       const int qb = qi & 1;
       const uint64_t dq = dq0 + qb * 2 * kTile16;
+      bool pre_next = false;
       if (!mbar_wait_warp(&q_full[qb], (qi >> 1) & 1, abort_flag, status)) { ok = false; break; }
-      // S_t(j) = Q_t K_j^T into TMEM columns [t*128, t*128+128)
-      auto issue_s = [&](int t, int j) -> bool {
-        const int g = g_base[t] + j;
-        const int s = (kv_base + j) % ST;
+      // S_t = Q_t K^T into TMEM columns [t*128, t*128+128): global step g of
+      // tile t, K from ring slot `slot`, Q tiles at descriptor dqx.
+      auto issue_s_at = [&](int t, int g, int slot, uint64_t dqx) -> bool {
         if (g > 0 && !mbar_wait_warp(&s_free[t], (g - 1) & 1, abort_flag, status)) return false;
         tc_fence_after();
-        const uint64_t a = dq + t * kTile16, b = dk0 + s * kTile16;
+        const uint64_t a = dqx + t * kTile16, b = dk0 + slot * kTile16;
         if (leader) {
 #pragma unroll
           for (int k = 0; k < DH / 16; ++k)
@@ -277,6 +278,20 @@ __global__ void __launch_bounds__(NTHREADS, 1)
           tc_commit(&s_full[t]);
         }
         __syncwarp();
+        return true;
+      };
+      auto issue_s = [&](int t, int j) -> bool { return issue_s_at(t, g_base[t] + j, (kv_base + j) % ST, dq); };
+      // Once tile 0 has its last P.V of this item, the next item's first
+      // S_0 goes out (its Q and first K tile are loaded independently of the
+      // rest of this item), so tile 0's softmax starts the next item while
+      // tile 1 finishes this one.
+      auto prefetch_next_s0 = [&]() -> bool {
+        if (w + (int)gridDim.x >= n_items) return true;
+        const int qn = qi + 1, qbn = qn & 1, kvn = kv_base + it.n_kv_max;
+        if (!mbar_wait_warp(&q_full[qbn], (qn >> 1) & 1, abort_flag, status)) return false;
+        if (!mbar_wait_warp(&k_full[kvn % ST], (kvn / ST) & 1, abort_flag, status)) return false;
+        if (!issue_s_at(0, g_base[0] + it.n_kv[0], kvn % ST, dq0 + qbn * 2 * kTile16)) return false;
+        pre_next = true;
         return true;
       };
       // O_t (+)= P_t V_j: P_t from TMEM columns [384 + t*64, +64), 8 columns per K=16 step
@@ -299,7 +314,7 @@ __global__ void __launch_bounds__(NTHREADS, 1)
       };
       ok = mbar_wait_warp(&k_full[kv_base % ST], (kv_base / ST) & 1, abort_flag, status);
       for (int t = 0; t < 2 && ok; ++t)
-        if (it.n_kv[t] > 0) ok = issue_s(t, 0);
+        if (it.n_kv[t] > 0 && !(t == 0 && pre_s0)) ok = issue_s(t, 0);
       if (ok && leader) tc_commit(&k_empty[kv_base % ST]);
       for (int j = 0; j < it.n_kv_max && ok; ++j) {
         const int kv = kv_base + j;
@@ -316,8 +331,10 @@ __global__ void __launch_bounds__(NTHREADS, 1)
         if (!ok) break;
         if (k_ready && leader) tc_commit(&k_empty[(kv + 1) % ST]);
         if (!mbar_wait_warp(&v_full[kv % ST], (kv / ST) & 1, abort_flag, status)) { ok = false; break; }
-        for (int t = 0; t < 2 && ok; ++t)
+        for (int t = 0; t < 2 && ok; ++t) {
           if (j < it.n_kv[t]) ok = issue_pv(t, j);
+          if (ok && t == 0 && j == it.n_kv[0] - 1) ok = prefetch_next_s0();
+        }
         if (leader) tc_commit(&v_empty[kv % ST]);
       }
       if (!ok) break;
@@ -325,6 +342,7 @@ __global__ void __launch_bounds__(NTHREADS, 1)
       g_base[0] += it.n_kv[0];
       g_base[1] += it.n_kv[1];
       kv_base += it.n_kv_max;
+      pre_s0 = pre_next;
     }
     if (!ok) {
       set_status(status, GPT2_ERR_WAIT_TIMEOUT);

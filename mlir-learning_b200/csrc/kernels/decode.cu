@@ -58,14 +58,19 @@ __device__ __forceinline__ void load_chunk(const T *p, float (&v)[Chunk<T>::N]) 
   }
 }
 
-// x[b] = wte[tok[b]] + wpe[pos]: one warp per sequence.
+// x[b] = wte[tok[b]] + wpe[*d_pos]: one warp per sequence.  The position is
+// read from device memory so that one captured step serves every position.
 template <typename T>
 __global__ void decode_embed_kernel(const int64_t *__restrict__ tok, const T *__restrict__ wte,
-                                    const T *__restrict__ wpe, T *__restrict__ x, int B, int d, int V, int pos,
-                                    int *status) {
+                                    const T *__restrict__ wpe, T *__restrict__ x, int B, int d, int V,
+                                    const int *__restrict__ d_pos, int P, int *status) {
   const int b = (blockIdx.x * blockDim.x + threadIdx.x) >> 5, lane = threadIdx.x & 31;
   if (b >= B) return;
   const int64_t id = tok[b];
+  const int pos0 = *d_pos;
+  const bool pos_ok = pos0 >= 0 && pos0 < P;
+  const int pos = pos_ok ? pos0 : 0;
+  if (!pos_ok && lane == 0) set_status(status, GPT2_ERR_TOKEN_RANGE);
   const bool ok = id >= 0 && id < V;
   if (!ok && lane == 0) set_status(status, GPT2_ERR_TOKEN_RANGE);
   const T *e = wte + (ok ? id : 0) * (int64_t)d;
@@ -144,10 +149,16 @@ __global__ void kv_store_kernel(const T *__restrict__ qkv, T *__restrict__ cache
 // block max and sum, then O = P V with two key groups of 64 threads.
 template <typename T, bool EXACT>
 __global__ void __launch_bounds__(128) attn_decode_kernel(const T *__restrict__ qkv, T *__restrict__ cache,
-                                                          T *__restrict__ out, int H, int pos, int max_len) {
+                                                          T *__restrict__ out, int H, const int *__restrict__ d_pos,
+                                                          int max_len, int *status) {
   constexpr int DH = 64;
-  extern __shared__ float sc[];  // pos + 1 scores, then reduction scratch
+  extern __shared__ float sc[];  // up to max_len scores
   const int h = blockIdx.x, b = blockIdx.y, tid = threadIdx.x;
+  const int pos = *d_pos;
+  if (pos < 0 || pos >= max_len) {  // the cache is full: report, touch nothing
+    if (tid == 0) set_status(status, GPT2_ERR_BAD_LAUNCH);
+    return;
+  }
   const int D = H * DH, n = pos + 1;
   const T *q = qkv + (int64_t)b * 3 * D + h * DH;
   const T *knew = q + D, *vnew = q + 2 * D;
@@ -281,13 +292,13 @@ cudaError_t gemv_dispatch(const AT *x, const WT *W, OT *y, int M, int N, int K, 
 }  // namespace
 
 cudaError_t launch_decode_embed_f32(const int64_t *tok, const float *wte, const float *wpe, float *x, int B, int d,
-                                    int V, int pos, int *status, cudaStream_t st) {
-  decode_embed_kernel<float><<<(B * 32 + 127) / 128, 128, 0, st>>>(tok, wte, wpe, x, B, d, V, pos, status);
+                                    int V, const int *d_pos, int P, int *status, cudaStream_t st) {
+  decode_embed_kernel<float><<<(B * 32 + 127) / 128, 128, 0, st>>>(tok, wte, wpe, x, B, d, V, d_pos, P, status);
   return cudaGetLastError();
 }
 cudaError_t launch_decode_embed_bf16(const int64_t *tok, const bf16 *wte, const bf16 *wpe, bf16 *x, int B, int d,
-                                     int V, int pos, int *status, cudaStream_t st) {
-  decode_embed_kernel<bf16><<<(B * 32 + 127) / 128, 128, 0, st>>>(tok, wte, wpe, x, B, d, V, pos, status);
+                                     int V, const int *d_pos, int P, int *status, cudaStream_t st) {
+  decode_embed_kernel<bf16><<<(B * 32 + 127) / 128, 128, 0, st>>>(tok, wte, wpe, x, B, d, V, d_pos, P, status);
   return cudaGetLastError();
 }
 
@@ -318,18 +329,44 @@ cudaError_t launch_kv_store_bf16(const bf16 *qkv, bf16 *cache, int B, int S, int
   return cudaGetLastError();
 }
 
-cudaError_t launch_attn_decode_f32(const float *qkv, float *cache, float *out, int B, int H, int pos, int max_len,
-                                   cudaStream_t st) {
-  if (pos < 0 || pos >= max_len) return cudaErrorInvalidValue;
-  attn_decode_kernel<float, true><<<dim3(H, B), 128, sizeof(float) * (pos + 1), st>>>(qkv, cache, out, H, pos,
-                                                                                       max_len);
+cudaError_t launch_attn_decode_f32(const float *qkv, float *cache, float *out, int B, int H, const int *d_pos,
+                                   int max_len, int *status, cudaStream_t st) {
+  if (max_len < 1 || max_len > 8192) return cudaErrorInvalidValue;
+  attn_decode_kernel<float, true><<<dim3(H, B), 128, sizeof(float) * max_len, st>>>(qkv, cache, out, H, d_pos,
+                                                                                     max_len, status);
   return cudaGetLastError();
 }
-cudaError_t launch_attn_decode_bf16(const bf16 *qkv, bf16 *cache, bf16 *out, int B, int H, int pos, int max_len,
-                                    cudaStream_t st) {
-  if (pos < 0 || pos >= max_len) return cudaErrorInvalidValue;
-  attn_decode_kernel<bf16, false><<<dim3(H, B), 128, sizeof(float) * (pos + 1), st>>>(qkv, cache, out, H, pos,
-                                                                                      max_len);
+cudaError_t launch_attn_decode_bf16(const bf16 *qkv, bf16 *cache, bf16 *out, int B, int H, const int *d_pos,
+                                    int max_len, int *status, cudaStream_t st) {
+  if (max_len < 1 || max_len > 8192) return cudaErrorInvalidValue;
+  attn_decode_kernel<bf16, false><<<dim3(H, B), 128, sizeof(float) * max_len, st>>>(qkv, cache, out, H, d_pos,
+                                                                                    max_len, status);
+  return cudaGetLastError();
+}
+
+namespace {
+__global__ void set_int_kernel(int *p, int v) { *p = v; }
+__global__ void add_int_kernel(int *p, int v) { *p += v; }
+// hist[(*d_pos - base) * B + b] = cur[b] (the generated-token history).
+__global__ void append_tokens_kernel(const int64_t *__restrict__ cur, int64_t *__restrict__ hist,
+                                     const int *__restrict__ d_pos, int base, int B, int cap) {
+  const int b = threadIdx.x;
+  const int i = *d_pos - base;
+  if (b < B && i >= 0 && (int64_t)i * B + b < cap) hist[(int64_t)i * B + b] = cur[b];
+}
+}  // namespace
+
+cudaError_t launch_set_int(int *p, int v, cudaStream_t st) {
+  set_int_kernel<<<1, 1, 0, st>>>(p, v);
+  return cudaGetLastError();
+}
+cudaError_t launch_add_int(int *p, int v, cudaStream_t st) {
+  add_int_kernel<<<1, 1, 0, st>>>(p, v);
+  return cudaGetLastError();
+}
+cudaError_t launch_append_tokens(const int64_t *cur, int64_t *hist, const int *d_pos, int base, int B, int cap,
+                                 cudaStream_t st) {
+  append_tokens_kernel<<<1, 32, 0, st>>>(cur, hist, d_pos, base, B, cap);
   return cudaGetLastError();
 }
 

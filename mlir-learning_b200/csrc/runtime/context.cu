@@ -96,6 +96,7 @@ void destroy_context() {
   cudaSetDevice(c->device);
   cudaDeviceSynchronize();
   drop_graph(c->graph);
+  drop_graph(c->dec_graph);
   free_decode(c->dec);
   for (cudaEvent_t e : c->prof.pool) cudaEventDestroy(e);
   free_ws(c->ws);
@@ -229,6 +230,10 @@ int load_blob(Context &c, const float *host_blob) {
   c.loaded = true;
   c.plans_T = -1;  // weights moved: rebuild TMA descriptors
   drop_graph(c.graph);
+  // A decode cache (and the FP32 transposed weights) belongs to the old weights.
+  CK(cudaDeviceSynchronize());
+  drop_graph(c.dec_graph);
+  free_decode(c.dec);
   return 0;
 }
 

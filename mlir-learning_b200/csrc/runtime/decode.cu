@@ -22,7 +22,7 @@ namespace gpt2 {
 void free_decode(DecodeState &d) {
   for (void *p : d.cache)
     if (p) cudaFree(p);
-  void *ptrs[] = {d.x, d.a, d.qkv, d.o, d.u, d.a_last, d.logits, d.tokens};
+  void *ptrs[] = {d.x, d.a, d.qkv, d.o, d.u, d.a_last, d.logits, d.tokens, d.cur, d.d_pos};
   for (void *p : ptrs)
     if (p) cudaFree(p);
   for (float *p : d.wt)
@@ -46,6 +46,7 @@ int kv_reserve(Context &c, int B, int max_len) {
   const size_t es = c.dtype >= 1 ? 2 : 4;
   if (d.B != B || d.max_len != max_len || d.cache.empty()) {
     CK(cudaDeviceSynchronize());
+    drop_graph(c.dec_graph);  // it captured the old buffers
     std::vector<float *> keep_wt;
     keep_wt.swap(d.wt);
     free_decode(d);
@@ -60,10 +61,14 @@ int kv_reserve(Context &c, int B, int max_len) {
     CK(cudaMalloc(&d.a_last, es * B * D));
     d.ld_logits = (m.vocab + 3) / 4 * 4;
     CK(cudaMalloc(&d.logits, sizeof(float) * B * d.ld_logits));
+    CK(cudaMalloc(&d.cur, sizeof(int64_t) * B));
+    CK(cudaMalloc(&d.d_pos, sizeof(int)));
     d.B = B;
     d.max_len = max_len;
   }
   d.len = 0;
+  CK(launch_set_int(d.d_pos, 0, c.stream));
+  CK(cudaStreamSynchronize(c.stream));
   if (c.dtype == 0 && d.wt.empty()) {
     // The GEMV kernels read weights as [out, in]; the FP32 blob holds the
     // Conv1D weights as [in, out].
@@ -93,30 +98,31 @@ int prefill(Context &c, const int64_t *d_ids, int B, int S, float *d_logits, int
   if (r) return r;
   r = launch_forward(c, d_ids, nullptr, B, S, d_logits, ld, st, true);
   if (r) return r;
+  CK(launch_set_int(d.d_pos, S, st));
   d.len = S;
   return 0;
 }
 
-int decode_step(Context &c, const int64_t *d_tokens, int B, float *d_logits, int64_t ld, cudaStream_t st) {
+namespace {
+// The kernels of one decode step at position *d.d_pos, then the position
+// advance; everything reads its position from the device.
+int launch_step(Context &c, const int64_t *d_tokens, int B, float *d_logits, int64_t ld, cudaStream_t st) {
   const ModelDims &m = c.dims;
   DecodeState &d = c.dec;
-  if (d.cache.empty() || B != d.B || d.len < 1 || d.len >= d.max_len || ld < m.vocab) {
-    set_error("decode step: cache for B=%d holds %d of %d positions (prefill first; B must match; ld >= V)", d.B,
-              d.len, d.max_len);
-    return -1;
-  }
-  const int pos = d.len, D = m.n_embd, ff = m.n_inner, H = m.n_head, V = m.vocab;
+  const int D = m.n_embd, ff = m.n_inner, H = m.n_head, V = m.vocab;
+  const int *dp = d.d_pos;
+
   if (c.dtype == 0) {
     float *x = static_cast<float *>(d.x), *a = static_cast<float *>(d.a), *qkv = static_cast<float *>(d.qkv),
           *o = static_cast<float *>(d.o), *u = static_cast<float *>(d.u);
-    CKP(K_EMBED, launch_decode_embed_f32(d_tokens, c.wte, c.wpe, x, B, D, V, pos, c.d_status, st));
+    CKP(K_EMBED, launch_decode_embed_f32(d_tokens, c.wte, c.wpe, x, B, D, V, dp, m.n_pos, c.d_status, st));
     for (int l = 0; l < m.n_layer; ++l) {
       const LayerWeights &lw = c.layers[l];
       float *const *wt = &d.wt[4 * l];
       CKP(K_LAYERNORM, launch_layernorm_f32(x, lw.ln1_g, lw.ln1_b, a, B, D, m.eps, st));
       CKP(K_GEMM_QKV, launch_gemv_f32(a, wt[0], qkv, B, 3 * D, D, 3 * D, lw.qkv_b, nullptr, EPI_BIAS, st));
       CKP(K_ATTENTION,
-          launch_attn_decode_f32(qkv, static_cast<float *>(d.cache[l]), o, B, H, pos, d.max_len, st));
+          launch_attn_decode_f32(qkv, static_cast<float *>(d.cache[l]), o, B, H, dp, d.max_len, c.d_status, st));
       CKP(K_GEMM_PROJ, launch_gemv_f32(o, wt[1], x, B, D, D, D, lw.proj_b, x, EPI_BIAS_RESID, st));
       CKP(K_LAYERNORM, launch_layernorm_f32(x, lw.ln2_g, lw.ln2_b, a, B, D, m.eps, st));
       CKP(K_GEMM_FC, launch_gemv_f32(a, wt[2], u, B, ff, D, ff, lw.fc_b, nullptr, EPI_BIAS_GELU, st));
@@ -127,13 +133,13 @@ int decode_step(Context &c, const int64_t *d_tokens, int B, float *d_logits, int
   } else {
     bf16 *x = static_cast<bf16 *>(d.x), *a = static_cast<bf16 *>(d.a), *qkv = static_cast<bf16 *>(d.qkv),
          *o = static_cast<bf16 *>(d.o), *u = static_cast<bf16 *>(d.u);
-    CKP(K_EMBED, launch_decode_embed_bf16(d_tokens, c.wte_h, c.wpe_h, x, B, D, V, pos, c.d_status, st));
+    CKP(K_EMBED, launch_decode_embed_bf16(d_tokens, c.wte_h, c.wpe_h, x, B, D, V, dp, m.n_pos, c.d_status, st));
     for (int l = 0; l < m.n_layer; ++l) {
       const LayerWeights &lw = c.layers[l];
       CKP(K_LAYERNORM, launch_layernorm_bf16(x, lw.ln1_g, lw.ln1_b, a, B, D, m.eps, st));
       CKP(K_GEMM_QKV,
           launch_gemv_bf16(a, lw.qkv_wt, qkv, B, 3 * D, D, 3 * D, lw.qkv_b, nullptr, lw.qkv_s, EPI_BIAS, st));
-      CKP(K_ATTENTION, launch_attn_decode_bf16(qkv, static_cast<bf16 *>(d.cache[l]), o, B, H, pos, d.max_len, st));
+      CKP(K_ATTENTION, launch_attn_decode_bf16(qkv, static_cast<bf16 *>(d.cache[l]), o, B, H, dp, d.max_len, c.d_status, st));
       CKP(K_GEMM_PROJ, launch_gemv_bf16(o, lw.proj_wt, x, B, D, D, D, lw.proj_b, x, lw.proj_s, EPI_BIAS_RESID, st));
       CKP(K_LAYERNORM, launch_layernorm_bf16(x, lw.ln2_g, lw.ln2_b, a, B, D, m.eps, st));
       CKP(K_GEMM_FC, launch_gemv_bf16(a, lw.fc_wt, u, B, ff, D, ff, lw.fc_b, nullptr, lw.fc_s, EPI_BIAS_GELU, st));
@@ -143,7 +149,30 @@ int decode_step(Context &c, const int64_t *d_tokens, int B, float *d_logits, int
     CKP(K_LAYERNORM, launch_layernorm_bf16(x, c.lnf_g, c.lnf_b, a, B, D, m.eps, st));
     CKP(K_LM_HEAD, launch_gemv_bf16_f32out(a, c.wte_h, d_logits, B, V, D, (int)ld, st));
   }
-  d.len = pos + 1;
+  CK(launch_add_int(d.d_pos, 1, st));
+  return 0;
+}
+}  // namespace
+
+int decode_step(Context &c, const int64_t *d_tokens, int B, float *d_logits, int64_t ld, cudaStream_t st) {
+  const ModelDims &m = c.dims;
+  DecodeState &d = c.dec;
+  if (d.cache.empty() || B != d.B || d.len < 1 || d.len >= d.max_len || ld < m.vocab) {
+    set_error("decode step: cache for B=%d holds %d of %d positions (prefill first; B must match; ld >= V)", d.B,
+              d.len, d.max_len);
+    return -1;
+  }
+  auto launch = [&](cudaStream_t s) { return launch_step(c, d_tokens, B, d_logits, ld, s); };
+  int r;
+  if (c.prof.on) {
+    r = launch(st);
+  } else {
+    const uintptr_t key[5] = {1, reinterpret_cast<uintptr_t>(d_tokens), static_cast<uintptr_t>(B),
+                              reinterpret_cast<uintptr_t>(d_logits), static_cast<uintptr_t>(ld)};
+    r = run_with_graph(c.dec_graph, &c.use_graphs, key, 5, c.stream, st, launch);
+  }
+  if (r) return r;
+  d.len += 1;
   return 0;
 }
 
@@ -175,11 +204,23 @@ int generate(Context &c, const int64_t *ids, int B, int S, int n_new, int64_t *o
   CK(cudaMemcpyAsync(c.ws.ids, ids, sizeof(int64_t) * B * S, cudaMemcpyHostToDevice, st));
   r = prefill(c, c.ws.ids, B, S, d.logits, d.ld_logits, st);
   if (r) return r;
-  CK(launch_argmax_rows(d.logits, d.ld_logits, B, m.vocab, d.tokens, st));
+  CK(launch_argmax_rows(d.logits, d.ld_logits, B, m.vocab, d.cur, st));
+  CK(launch_append_tokens(d.cur, d.tokens, d.d_pos, S, B, (int)d.tokens_cap, st));  // token 0 at *d_pos == S
+  // One greedy step: decode the latest tokens, argmax, record them at index
+  // (position - S + 1), advance; captured once and replayed per token.
+  auto greedy = [&](cudaStream_t s) -> int {
+    int rr = launch_step(c, d.cur, B, d.logits, d.ld_logits, s);
+    if (rr) return rr;
+    CK(launch_argmax_rows(d.logits, d.ld_logits, B, m.vocab, d.cur, s));
+    CK(launch_append_tokens(d.cur, d.tokens, d.d_pos, S, B, (int)d.tokens_cap, s));
+    return 0;
+  };
+  const uintptr_t key[4] = {2, static_cast<uintptr_t>(B), static_cast<uintptr_t>(S),
+                            reinterpret_cast<uintptr_t>(d.tokens)};
   for (int i = 1; i < n_new; ++i) {
-    r = decode_step(c, d.tokens + (int64_t)(i - 1) * B, B, d.logits, d.ld_logits, st);
+    r = run_with_graph(c.dec_graph, &c.use_graphs, key, 4, c.stream, st, greedy);
     if (r) return r;
-    CK(launch_argmax_rows(d.logits, d.ld_logits, B, m.vocab, d.tokens + (int64_t)i * B, st));
+    d.len += 1;
   }
   std::vector<int64_t> t((size_t)n_new * B);
   CK(cudaMemcpyAsync(t.data(), d.tokens, sizeof(int64_t) * n_new * B, cudaMemcpyDeviceToHost, st));

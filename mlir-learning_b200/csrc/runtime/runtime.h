@@ -86,6 +86,8 @@ struct DecodeState {
   int64_t ld_logits = 0;
   int64_t *tokens = nullptr;        // generated tokens [n_new][B] for gpt2_generate
   int64_t tokens_cap = 0;
+  int64_t *cur = nullptr;           // the latest greedy tokens [B] (gpt2_generate)
+  int *d_pos = nullptr;             // the next position, on the device (read by the step's kernels)
   std::vector<float *> wt;          // FP32 path: [out, in] copies of the Conv1D weights, 4 per layer
 };
 
@@ -139,6 +141,7 @@ int run_with_graph(GraphCache &g, bool *enabled, const uintptr_t *key, int nkey,
 }
 
 struct Context {
+  GraphCache dec_graph;  // the decode step (position read from the device, so one graph serves all)
   ModelDims dims;
   int dtype = 0;
   int device = 0;

@@ -5,6 +5,7 @@ and small, single-kernel ncu captures.
   python mlir-learning_b200/kernel_bench.py attention --batch 64 --seq 1024 [--causal 0 --lengths uniform]
   python mlir-learning_b200/kernel_bench.py gemm --m 65536 --n 3072 --k 768 --epi 2
   python mlir-learning_b200/kernel_bench.py layernorm --rows 65536 --d 768
+  python mlir-learning_b200/kernel_bench.py decode --batch 1 --seq 128 --new 64 --dtype 1
 
 Inputs are seeded random device tensors; each run does --warmup untimed and
 --iters timed launches between CUDA events on one stream and prints one JSON
@@ -51,7 +52,8 @@ def _time(torch, fn, warmup, iters):
 
 def main():
     ap = argparse.ArgumentParser()
-    ap.add_argument("kernel", choices=["attention", "gemm", "layernorm"])
+    ap.add_argument("kernel", choices=["attention", "gemm", "layernorm", "decode"])
+    ap.add_argument("--new", type=int, default=64, help="decode: tokens generated per sequence")
     ap.add_argument("--batch", type=int, default=64)
     ap.add_argument("--seq", type=int, default=1024)
     ap.add_argument("--heads", type=int, default=12)
@@ -109,6 +111,26 @@ def main():
         ms = _time(torch, fn, args.warmup, args.iters)
         out.update(M=M, N=N, K=K, epi=args.epi, bn=args.bn, out_f32=args.out_f32, ms=ms,
                    tflops=2.0 * M * N * K / ms / 1e9)
+    elif args.kernel == "decode":
+        # Greedy generation with the KV cache on GPT-2 small (seeded weights): the time per
+        # generated token is the difference between n_new and 1 new tokens, per step of B tokens.
+        import time
+        B, S, n = args.batch, args.seq, args.new
+        pkg.init(pkg.gpt2_small(args.dtype), 0)
+        pkg.init_seeded(1234, 0)
+        prompt = pkg.seeded_ids(B, S, 1234, 50257)
+
+        def run(k):
+            t0 = time.perf_counter()
+            pkg.generate(prompt, k)
+            return time.perf_counter() - t0
+        for _ in range(args.warmup):
+            run(n)
+        t1 = min(run(1) for _ in range(3))
+        tn = min(run(n) for _ in range(3))
+        step = (tn - t1) / (n - 1)
+        out.update(B=B, S=S, new=n, dtype=args.dtype, prefill_plus_first_ms=1e3 * t1, ms_per_step=1e3 * step,
+                   tokens_per_s=B / step)
     else:
         T, d = args.rows, args.d
         x = torch.randn(T, d, device="cuda", generator=g).bfloat16()
