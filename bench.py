@@ -457,6 +457,7 @@ def main():
     ap.add_argument("--e2e-steps", type=int, default=2)
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-gather", action="store_true", help="skip the NCCL logits gather (N > 1)")
+    ap.add_argument("--no-decode", action="store_true", help="skip the KV-cache decode measurement")
     args = ap.parse_args()
 
     global L, D, H, FF
@@ -585,6 +586,28 @@ def main():
                "steps": args.e2e_steps, "api": "gpt2_forward_host (C ABI, host buffers, synchronous)"}
         del host_logits
 
+    # Incremental decoding on the same model (reported beside the prefill number): greedy
+    # generation with the KV cache, 64 new tokens after a 128-token prompt, per-token time from the
+    # difference between 64 and 1 generated tokens.
+    decode = None
+    if args.config in (1, 2) and world == 1 and not args.no_decode:
+        decode = {}
+        for db in (1, 16):
+            prompt = pkg.seeded_ids(db, 128, SEED, V)
+
+            def gen(k):
+                torch.cuda.synchronize()
+                t0 = time.perf_counter()
+                pkg.generate(prompt, k)
+                return time.perf_counter() - t0
+            gen(64)
+            t1 = min(gen(1) for _ in range(3))
+            tn = min(gen(64) for _ in range(3))
+            step = (tn - t1) / 63
+            decode[f"B{db}"] = {"ms_per_token_step": 1e3 * step, "tokens_per_s": db / step, "prompt": 128,
+                                "new_tokens": 64}
+        decode["api"] = "gpt2_generate (KV cache, one CUDA graph per step)"
+
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
         r, dt, cores = cpu_reference_rate(S, fp8=args.config == 4)
@@ -613,6 +636,7 @@ def main():
             "cpu_baseline": cpu,
             "e2e": e2e,
             "logits_gather": gather,
+            "decode": decode,
             "clocks": clocks,
             "gpu_launches": pkg.forward_launches(B, S, False) * args.steps,
         }

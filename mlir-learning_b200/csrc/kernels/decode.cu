@@ -78,43 +78,64 @@ __global__ void decode_embed_kernel(const int64_t *__restrict__ tok, const T *__
   for (int i = lane; i < d; i += 32) x[(int64_t)b * d + i] = from_f<T>((ok ? to_f(e[i]) : 0.f) + to_f(p[i]));
 }
 
-// y[m, n] = epi(sum_k x[m, k] W[n, k]) for m < M <= 16: one warp per output
-// column n streams W's row n (16-byte loads along k) once for all M rows; x
-// comes from L1 (it is tiny and shared by every warp).  FP32 accumulation,
-// warp-shuffle reduction, the epilogue on lane m for row m.
-template <typename WT, typename AT, typename OT, int EPI, bool EXACT>
+// y[m, n] = epi(sum_k x[m, k] W[n, k]) for m < M <= 16: KS warps per output
+// column n stream W's row n (16-byte loads along k, each warp a 1/KS slice
+// of k) once for all M rows; x comes from L1 (it is tiny and shared by every
+// warp).  FP32 accumulation, warp-shuffle reduction, the KS partial sums
+// added through shared memory, the epilogue on lane m for row m.  KS > 1 puts
+// more warps (and loads in flight) on the narrow products.
+template <typename WT, typename AT, typename OT, int EPI, bool EXACT, int KS>
 __global__ void __launch_bounds__(256) gemv_nk_kernel(const AT *__restrict__ x, const WT *__restrict__ W,
                                                       OT *__restrict__ y, int M, int N, int K, int ldy,
                                                       const float *__restrict__ bias, const OT *resid,
                                                       const float *__restrict__ scale) {
   constexpr int MMAX = 16;
-  const int n = (blockIdx.x * blockDim.x + threadIdx.x) >> 5, lane = threadIdx.x & 31;
-  if (n >= N) return;
+  __shared__ float part[8][MMAX];
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int n = blockIdx.x * (8 / KS) + warp / KS, ks = warp % KS;
   constexpr int WC = Chunk<WT>::N;  // weights per 16-byte chunk
   float acc[MMAX];
 #pragma unroll
   for (int m = 0; m < MMAX; ++m) acc[m] = 0.f;
-  const WT *wr = W + (int64_t)n * K;
-  for (int k0 = lane * WC; k0 < K; k0 += 32 * WC) {
-    float w[WC];
-    load_chunk<WT>(wr + k0, w);
+  if (n < N) {
+    const WT *wr = W + (int64_t)n * K;
+#pragma unroll 4
+    for (int k0 = (ks * 32 + lane) * WC; k0 < K; k0 += 32 * KS * WC) {
+      float w[WC];
+      load_chunk<WT>(wr + k0, w);
 #pragma unroll
-    for (int m = 0; m < MMAX; ++m) {
-      if (m < M) {
-        const AT *xr = x + (int64_t)m * K + k0;
+      for (int m = 0; m < MMAX; ++m) {
+        if (m < M) {
+          const AT *xr = x + (int64_t)m * K + k0;
 #pragma unroll
-        for (int j = 0; j < WC; j += Chunk<AT>::N) {
-          float xv[Chunk<AT>::N];
-          load_chunk<AT>(xr + j, xv);
+          for (int j = 0; j < WC; j += Chunk<AT>::N) {
+            float xv[Chunk<AT>::N];
+            load_chunk<AT>(xr + j, xv);
 #pragma unroll
-          for (int e = 0; e < Chunk<AT>::N; ++e) acc[m] = fmaf(xv[e], w[j + e], acc[m]);
+            for (int e = 0; e < Chunk<AT>::N; ++e) acc[m] = fmaf(xv[e], w[j + e], acc[m]);
+          }
         }
       }
     }
   }
 #pragma unroll
   for (int m = 0; m < MMAX; ++m) acc[m] = warp_sum(acc[m]);
-  if (lane < M) {
+  if (KS > 1) {
+    if (lane == 0) {
+#pragma unroll
+      for (int m = 0; m < MMAX; ++m) part[warp][m] = acc[m];
+    }
+    __syncthreads();
+    if (ks != 0) return;
+#pragma unroll
+    for (int m = 0; m < MMAX; ++m) {
+      float t = part[warp][m];
+#pragma unroll
+      for (int i = 1; i < KS; ++i) t += part[warp + i][m];
+      acc[m] = t;
+    }
+  }
+  if (n < N && lane < M) {
     float v = 0.f;
 #pragma unroll
     for (int m = 0; m < MMAX; ++m)
@@ -152,7 +173,7 @@ __global__ void __launch_bounds__(128) attn_decode_kernel(const T *__restrict__ 
                                                           T *__restrict__ out, int H, const int *__restrict__ d_pos,
                                                           int max_len, int *status) {
   constexpr int DH = 64;
-  extern __shared__ float sc[];  // up to max_len scores
+  extern __shared__ float sc[];  // max(max_len, 1024) floats: the scores, then partial output rows
   const int h = blockIdx.x, b = blockIdx.y, tid = threadIdx.x;
   const int pos = *d_pos;
   if (pos < 0 || pos >= max_len) {  // the cache is full: report, touch nothing
@@ -206,15 +227,33 @@ __global__ void __launch_bounds__(128) attn_decode_kernel(const T *__restrict__ 
   if (tid == 0) stat[1] = (red[0] + red[1]) + (red[2] + red[3]);
   __syncthreads();
   const float inv = 1.0f / stat[1];
-  const int dim = tid & 63, grp = tid >> 6;
-  float o = 0.f;
-  for (int j = grp; j < n; j += 2) {
+  // O = P V: thread = (key group kg of 128 / CPR, 16-byte column chunk cc);
+  // each key row is read with one 16-byte load per chunk, the key groups'
+  // partial rows are added through shared memory.
+  constexpr int CW = Chunk<T>::N, CPR = DH / CW;  // values per chunk, chunks per row
+  constexpr int KG = 128 / CPR;                     // key groups
+  const int cc = tid % CPR, kg = tid / CPR;
+  float acc[CW];
+#pragma unroll
+  for (int e = 0; e < CW; ++e) acc[e] = 0.f;
+#pragma unroll 4
+  for (int j = kg; j < n; j += KG) {
     const T *vr = j == pos ? vnew : cb + (int64_t)j * 2 * D + D + h * DH;
-    o = fmaf(sc[j], to_f(vr[dim]), o);
+    float v[CW];
+    load_chunk<T>(vr + cc * CW, v);
+    const float p = sc[j];
+#pragma unroll
+    for (int e = 0; e < CW; ++e) acc[e] = fmaf(p, v[e], acc[e]);
   }
-  red[grp * DH + dim] = o;
+  __syncthreads();  // every thread is done with sc before it is reused
+#pragma unroll
+  for (int e = 0; e < CW; ++e) sc[kg * DH + cc * CW + e] = acc[e];
   __syncthreads();
-  if (tid < DH) out[(int64_t)b * D + h * DH + tid] = from_f<T>((red[tid] + red[DH + tid]) * inv);
+  if (tid < DH) {
+    float o = 0.f;
+    for (int g = 0; g < KG; ++g) o += sc[g * DH + tid];
+    out[(int64_t)b * D + h * DH + tid] = from_f<T>(o * inv);
+  }
 }
 
 // tokens[b] = argmax_n logits[b, n] (the first maximum, as torch.argmax).
@@ -269,13 +308,13 @@ __global__ void transpose_f32_kernel(const float *__restrict__ src, float *__res
   }
 }
 
-template <typename WT, typename AT, typename OT, bool EXACT>
-cudaError_t gemv_dispatch(const AT *x, const WT *W, OT *y, int M, int N, int K, int ldy, const float *bias,
-                          const OT *resid, const float *scale, int epi, cudaStream_t st) {
-  const int blocks = (N + 7) / 8;
-#define GEMV_CASE(E)                                                                                               \
-  case E:                                                                                                          \
-    gemv_nk_kernel<WT, AT, OT, E, EXACT><<<blocks, 256, 0, st>>>(x, W, y, M, N, K, ldy, bias, resid, scale);     \
+template <typename WT, typename AT, typename OT, bool EXACT, int KS>
+cudaError_t gemv_launch(const AT *x, const WT *W, OT *y, int M, int N, int K, int ldy, const float *bias,
+                        const OT *resid, const float *scale, int epi, cudaStream_t st) {
+  const int blocks = (N + 8 / KS - 1) / (8 / KS);
+#define GEMV_CASE(E)                                                                                              \
+  case E:                                                                                                         \
+    gemv_nk_kernel<WT, AT, OT, E, EXACT, KS><<<blocks, 256, 0, st>>>(x, W, y, M, N, K, ldy, bias, resid, scale); \
     break;
   switch (epi) {
     GEMV_CASE(EPI_NONE)
@@ -288,6 +327,16 @@ cudaError_t gemv_dispatch(const AT *x, const WT *W, OT *y, int M, int N, int K, 
   }
 #undef GEMV_CASE
   return cudaGetLastError();
+}
+
+// Split k over up to 4 warps per column while the columns alone would not
+// give every SM several blocks.
+template <typename WT, typename AT, typename OT, bool EXACT>
+cudaError_t gemv_dispatch(const AT *x, const WT *W, OT *y, int M, int N, int K, int ldy, const float *bias,
+                          const OT *resid, const float *scale, int epi, cudaStream_t st) {
+  if (N <= 1024) return gemv_launch<WT, AT, OT, EXACT, 4>(x, W, y, M, N, K, ldy, bias, resid, scale, epi, st);
+  if (N <= 4096) return gemv_launch<WT, AT, OT, EXACT, 2>(x, W, y, M, N, K, ldy, bias, resid, scale, epi, st);
+  return gemv_launch<WT, AT, OT, EXACT, 1>(x, W, y, M, N, K, ldy, bias, resid, scale, epi, st);
 }
 }  // namespace
 
@@ -332,15 +381,17 @@ cudaError_t launch_kv_store_bf16(const bf16 *qkv, bf16 *cache, int B, int S, int
 cudaError_t launch_attn_decode_f32(const float *qkv, float *cache, float *out, int B, int H, const int *d_pos,
                                    int max_len, int *status, cudaStream_t st) {
   if (max_len < 1 || max_len > 8192) return cudaErrorInvalidValue;
-  attn_decode_kernel<float, true><<<dim3(H, B), 128, sizeof(float) * max_len, st>>>(qkv, cache, out, H, d_pos,
-                                                                                     max_len, status);
+  const int sm = max_len > 1024 ? max_len : 1024;  // scores, then the key groups' partial rows
+  attn_decode_kernel<float, true><<<dim3(H, B), 128, sizeof(float) * sm, st>>>(qkv, cache, out, H, d_pos, max_len,
+                                                                                status);
   return cudaGetLastError();
 }
 cudaError_t launch_attn_decode_bf16(const bf16 *qkv, bf16 *cache, bf16 *out, int B, int H, const int *d_pos,
                                     int max_len, int *status, cudaStream_t st) {
   if (max_len < 1 || max_len > 8192) return cudaErrorInvalidValue;
-  attn_decode_kernel<bf16, false><<<dim3(H, B), 128, sizeof(float) * max_len, st>>>(qkv, cache, out, H, d_pos,
-                                                                                    max_len, status);
+  const int sm = max_len > 1024 ? max_len : 1024;  // scores, then the key groups' partial rows
+  attn_decode_kernel<bf16, false><<<dim3(H, B), 128, sizeof(float) * sm, st>>>(qkv, cache, out, H, d_pos, max_len,
+                                                                               status);
   return cudaGetLastError();
 }
 
