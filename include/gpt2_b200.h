@@ -257,7 +257,8 @@ int gpt2k_gemm_f32(const float *A, const float *B, int b_nk, float *C, int M, in
 
 /* tcgen05 BF16 GEMM: C[M,N] = epi(A[M,K] @ B[N,K]^T), A and B bf16
  * row-major; C bf16 (out_f32 = 0) or f32 (out_f32 = 1, EPI_NONE / EPI_BIAS);
- * resid bf16 with row stride ldc; bn = 128 or 256 (output tile width). */
+ * resid bf16 with row stride ldc; bn = 128 or 256: one SM per 128 x bn
+ * output tile; bn = 2: two SMs (a CTA pair) per 256 x 256 tile. */
 int gpt2k_gemm_bf16(const void *A, const void *B, void *C, int M, int N, int K, int ldc, int out_f32,
                     const float *bias, const void *resid, int epi, int bn, void *stream);
 

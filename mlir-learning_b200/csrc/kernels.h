@@ -88,11 +88,16 @@ struct TcGemmPlan {
   CUtensorMap map_b;
   CUtensorMap map_c;  // output, when the output can be stored by TMA
   int M, N, K;
-  int bn;  // 128 or 256
+  int bn;  // width of the B box: 128 or 256
+  int two_sm = 0;  // 256 x 256 tiles on CTA pairs (gemm_tc2sm.cu); B boxes of 128 rows
   const void *c_ptr = nullptr;
   int c_ld = 0, c_f32 = 0, has_c = 0;
 };
 // Builds the TMA descriptors of A and B; returns 0 or a negative error.
+// bn = 128 or 256: one SM per 128 x bn output tile (gemm_tc.cu);
+// bn = TC_TILE_PAIR: two SMs per 256 x 256 tile (gemm_tc2sm.cu), used when
+// C can be stored by TMA (else the 128 x 128 single-SM kernel runs).
+constexpr int TC_TILE_PAIR = 2;
 int tc_gemm_plan(TcGemmPlan *plan, const bf16 *A, const bf16 *B, int M, int N, int K, int bn);
 // Builds the output descriptor for C (row stride ldc elements, f32 or bf16)
 // when C is 16-byte aligned and ldc * element size is a multiple of 16;
@@ -103,6 +108,11 @@ int tc_gemm_set_output(TcGemmPlan *plan, const void *C, int ldc, int out_f32);
 cudaError_t launch_gemm_tc(const TcGemmPlan &plan, void *C, int ldc, int out_f32, const float *bias,
                            const bf16 *resid, int epi, int *status, int num_sms, cudaStream_t st,
                            const float *scale = nullptr);
+// The CTA-pair kernel (called by launch_gemm_tc for TC_TILE_PAIR plans).
+bool gemm_tc2sm_usable(const TcGemmPlan &plan, const void *C, int ldc, int out_f32);
+cudaError_t launch_gemm_tc2sm(const TcGemmPlan &plan, void *C, int ldc, int out_f32, const float *bias,
+                              const bf16 *resid, int epi, int *status, int num_sms, cudaStream_t st,
+                              const float *scale);
 
 // ---- attention ----------------------------------------------------------------
 // qkv [B*S, 3*H*64] (q | k | v, head h at columns h*64), o [B*S, H*64].

@@ -415,7 +415,9 @@ cudaError_t dispatch_epi(const TcGemmPlan &p, void *C, int ldc, int out_f32, con
 }  // namespace
 
 int tc_gemm_plan(TcGemmPlan *plan, const bf16 *A, const bf16 *B, int M, int N, int K, int bn) {
-  if (!plan || M <= 0 || N <= 0 || K <= 0 || K % 8 || (bn != 128 && bn != 256)) return -10;
+  if (!plan || M <= 0 || N <= 0 || K <= 0 || K % 8 || (bn != 128 && bn != 256 && bn != TC_TILE_PAIR)) return -10;
+  plan->two_sm = bn == TC_TILE_PAIR;
+  if (plan->two_sm) bn = 128;
   plan->has_c = 0;
   plan->c_ptr = nullptr;
   plan->M = M;
@@ -442,6 +444,8 @@ cudaError_t launch_gemm_tc(const TcGemmPlan &plan, void *C, int ldc, int out_f32
   if (!out_f32 && ldc % 8) return cudaErrorInvalidValue;
   if (epi != EPI_NONE && !bias) return cudaErrorInvalidValue;
   if (epi == EPI_BIAS_RESID && !resid) return cudaErrorInvalidValue;
+  if (plan.two_sm && gemm_tc2sm_usable(plan, C, ldc, out_f32) && num_sms >= 2)
+    return launch_gemm_tc2sm(plan, C, ldc, out_f32, bias, resid, epi, status, num_sms, st, scale);
   if (plan.bn == 256) return dispatch_epi<256>(plan, C, ldc, out_f32, bias, resid, epi, status, num_sms, st, scale);
   return dispatch_epi<128>(plan, C, ldc, out_f32, bias, resid, epi, status, num_sms, st, scale);
 }

@@ -244,13 +244,21 @@ int bert_ensure_plans(BertContext &c, int64_t T) {
     const int64_t tiles256 = ((T + 127) / 128) * ((N + 255) / 256);
     return tiles256 >= 2 * c.num_sms ? 256 : 128;
   };
+  // 256 x 256 tiles on CTA pairs where there are enough of them to fill the
+  // GPU twice over; measured faster for the QKV, fc, MLP-proj and lm_head
+  // shapes and slower for the narrow short-K attention out-proj (N = K = d),
+  // which keeps the single-SM tiles.
+  auto pick_tile = [&](int N) {
+    const int64_t pair_tiles = ((T + 255) / 256) * ((N + 255) / 256);
+    return pair_tiles >= 2 * (c.num_sms / 2) ? TC_TILE_PAIR : pick_bn(N);
+  };
   for (int l = 0; l < m.n_layer; ++l) {
     const BertLayer &w = c.layers[l];
     TcGemmPlan *p = &c.plans[4 * l];
-    int r = tc_gemm_plan(&p[0], static_cast<const bf16 *>(ws.x), w.qkv_h, (int)T, 3 * d, d, pick_bn(3 * d));
+    int r = tc_gemm_plan(&p[0], static_cast<const bf16 *>(ws.x), w.qkv_h, (int)T, 3 * d, d, pick_tile(3 * d));
     if (!r) r = tc_gemm_plan(&p[1], static_cast<const bf16 *>(ws.o), w.ao_h, (int)T, d, d, pick_bn(d));
-    if (!r) r = tc_gemm_plan(&p[2], static_cast<const bf16 *>(ws.h), w.i_h, (int)T, ff, d, pick_bn(ff));
-    if (!r) r = tc_gemm_plan(&p[3], static_cast<const bf16 *>(ws.u), w.o_h, (int)T, d, ff, pick_bn(d));
+    if (!r) r = tc_gemm_plan(&p[2], static_cast<const bf16 *>(ws.h), w.i_h, (int)T, ff, d, pick_tile(ff));
+    if (!r) r = tc_gemm_plan(&p[3], static_cast<const bf16 *>(ws.u), w.o_h, (int)T, d, ff, pick_tile(d));
     if (r) {
       set_error("TMA descriptor creation failed (%d)", r);
       return -2;

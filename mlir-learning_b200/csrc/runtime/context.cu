@@ -283,13 +283,21 @@ int ensure_plans(Context &c, int64_t T) {
     const int64_t tiles256 = ((T + 127) / 128) * ((N + 255) / 256);
     return tiles256 >= 2 * c.num_sms ? 256 : 128;
   };
+  // 256 x 256 tiles on CTA pairs where there are enough of them to fill the
+  // GPU twice over; measured faster for the QKV, fc, MLP-proj and lm_head
+  // shapes and slower for the narrow short-K attention out-proj (N = K = d),
+  // which keeps the single-SM tiles.
+  auto pick_tile = [&](int N) {
+    const int64_t pair_tiles = ((T + 255) / 256) * ((N + 255) / 256);
+    return pair_tiles >= 2 * (c.num_sms / 2) ? TC_TILE_PAIR : pick_bn(N);
+  };
   for (int l = 0; l < m.n_layer; ++l) {
     const LayerWeights &w = c.layers[l];
     TcGemmPlan *p = &c.plans[4 * l];
-    int r = tc_gemm_plan(&p[0], a, w.qkv_wt, (int)T, 3 * d, d, pick_bn(3 * d));
+    int r = tc_gemm_plan(&p[0], a, w.qkv_wt, (int)T, 3 * d, d, pick_tile(3 * d));
     if (!r) r = tc_gemm_plan(&p[1], o, w.proj_wt, (int)T, d, d, pick_bn(d));
-    if (!r) r = tc_gemm_plan(&p[2], a, w.fc_wt, (int)T, ff, d, pick_bn(ff));
-    if (!r) r = tc_gemm_plan(&p[3], u, w.mproj_wt, (int)T, d, ff, pick_bn(d));
+    if (!r) r = tc_gemm_plan(&p[2], a, w.fc_wt, (int)T, ff, d, pick_tile(ff));
+    if (!r) r = tc_gemm_plan(&p[3], u, w.mproj_wt, (int)T, d, ff, pick_tile(d));
     if (r) {
       set_error("TMA descriptor creation failed (%d)", r);
       return -2;
@@ -299,7 +307,9 @@ int ensure_plans(Context &c, int64_t T) {
     tc_gemm_set_output(&p[2], c.ws.u, ff, 0);
     tc_gemm_set_output(&p[3], c.ws.x, d, 0);
   }
-  if (tc_gemm_plan(&c.plans[4 * m.n_layer], a, c.wte_h, (int)T, m.vocab, d, pick_bn(m.vocab))) {
+  c.head_tile = pick_tile(m.vocab);
+  c.head_bn = pick_bn(m.vocab);
+  if (tc_gemm_plan(&c.plans[4 * m.n_layer], a, c.wte_h, (int)T, m.vocab, d, c.head_tile)) {
     set_error("TMA descriptor creation failed (lm_head)");
     return -2;
   }
@@ -375,8 +385,19 @@ int prepare_forward(Context &c, int B, int S, float *d_logits, int64_t ld_logits
     }
   }
   TcGemmPlan &head = c.plans[4 * m.n_layer];
-  if (d_logits && (head.c_ptr != d_logits || head.c_ld != (int)ld_logits || !head.c_f32))
+  if (d_logits && (head.c_ptr != d_logits || head.c_ld != (int)ld_logits || !head.c_f32)) {
+    // Logits rows that TMA cannot store (unaligned base or row stride) go
+    // through the single-SM kernel's direct stores, with its own tile width.
+    const bool storable = !(reinterpret_cast<uintptr_t>(d_logits) & 15) && (ld_logits * 4) % 16 == 0;
+    const int tile = storable ? c.head_tile : c.head_bn;
+    if (head.two_sm != (tile == TC_TILE_PAIR) || (!head.two_sm && head.bn != tile)) {
+      if (tc_gemm_plan(&head, static_cast<const bf16 *>(w.a), c.wte_h, B * S, m.vocab, m.n_embd, tile)) {
+        set_error("TMA descriptor creation failed (lm_head)");
+        return -2;
+      }
+    }
     tc_gemm_set_output(&head, d_logits, (int)ld_logits, 1);
+  }
   return 0;
 }
 

@@ -160,6 +160,7 @@ struct Context {
   // tcgen05 GEMM plans for the current workspace: 4 per layer + lm_head.
   std::vector<TcGemmPlan> plans;
   int64_t plans_T = -1;
+  int head_tile = 0, head_bn = 0;  // lm_head tile choice, and the single-SM one for unaligned logits
   AttnTcPlan attn_plan;  // tcgen05 attention descriptor for (ws.qkv, B, S)
 
   Profiler prof;

@@ -72,6 +72,18 @@ def test_gemm_f32(torch, M, N, K, b_nk, epi, ldc):
     (200, 50257, 768, pkg.EPI_NONE, 1, 128, 50257),
     (64, 1000, 128, pkg.EPI_BIAS, 1, 128, 1000),
     (4096, 768, 768, pkg.EPI_BIAS_RESID, 0, 256, 768),
+    # bn = 2: 256 x 256 tiles on CTA pairs (tcgen05.mma.cta_group::2)
+    (256, 256, 64, pkg.EPI_NONE, 0, 2, 256),
+    (100, 2304, 768, pkg.EPI_BIAS, 0, 2, 2304),       # the second CTA's rows all past M
+    (1000, 2304, 768, pkg.EPI_BIAS, 0, 2, 2304),
+    (300, 768, 3072, pkg.EPI_BIAS_RESID, 0, 2, 768),
+    (513, 3072, 768, pkg.EPI_BIAS_GELU, 0, 2, 3072),
+    (513, 3072, 768, pkg.EPI_BIAS_GELU_ERF, 0, 2, 3072),
+    (8192, 3072, 768, pkg.EPI_BIAS_GELU, 0, 2, 3072),  # more tiles than pairs: both accumulators
+    (8192, 768, 3072, pkg.EPI_BIAS_RESID, 0, 2, 768),
+    (200, 50257, 768, pkg.EPI_NONE, 1, 2, 50304),
+    (1000, 1000, 136, pkg.EPI_BIAS, 1, 2, 1000),        # ragged K (zero-filled) and N
+    (200, 50257, 768, pkg.EPI_NONE, 1, 2, 50257),       # C not TMA-storable: single-SM kernel
 ])
 def test_gemm_bf16_tcgen05(torch, M, N, K, epi, out_f32, bn, ldc):
     g = torch.Generator(device="cuda").manual_seed(M + N + K)
