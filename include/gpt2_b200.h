@@ -234,7 +234,10 @@ int gpt2_profile_end(double *ms_per_kind, int64_t *launches_per_kind, int n_kind
 
 /* Epilogues fused into the GEMMs. */
 enum { GPT2_EPI_NONE = 0, GPT2_EPI_BIAS = 1, GPT2_EPI_BIAS_GELU = 2, GPT2_EPI_BIAS_RESID = 3,
-       GPT2_EPI_BIAS_GELU_ERF = 4 /* exact erf GELU of the BERT intermediate layer */ };
+       GPT2_EPI_BIAS_GELU_ERF = 4 /* exact erf GELU of the BERT intermediate layer */,
+       GPT2_EPI_LN_BIAS = 5 /* a LayerNorm of A folded in (gpt2k_gemm_bf16_ln) */,
+       GPT2_EPI_LN_BIAS_GELU = 6 /* the same, then gelu_new */,
+       GPT2_EPI_BIAS_RESID_STATS = 7 /* EPI_BIAS_RESID and the row statistics of C */ };
 
 /* The call a BLAS lowering of linalg.matmul emits, on the GPU: the argument
  * list of cblas_sgemm exactly as lib/ConvertMatMulToBlas.cpp:84-160 builds it
@@ -261,6 +264,27 @@ int gpt2k_gemm_f32(const float *A, const float *B, int b_nk, float *C, int M, in
  * output tile; bn = 2: two SMs (a CTA pair) per 256 x 256 tile. */
 int gpt2k_gemm_bf16(const void *A, const void *B, void *C, int M, int N, int K, int ldc, int out_f32,
                     const float *bias, const void *resid, int epi, int bn, void *stream);
+
+/* The GEMM epilogues of the BF16 forward's folded LayerNorms (C bf16, or f32
+ * for GPT2_EPI_LN_BIAS).  A LayerNorm LN(a) = (a - mean) * rstd * gain + shift
+ * of A's rows followed by a linear layer with weight W [N, K] and bias is
+ * computed as C = rstd * (A @ B^T) - rstd * mean * c1 + c2 with
+ * B = bf16(W * gain) (gpt2k_ln_fold_pack), c1[n] = sum_k B[n, k] and
+ * c2 = W @ shift + bias ([N rounded up to 256] floats, 16-byte aligned,
+ * zero past N).  mean and rstd (1/sqrt(var + eps), biased variance over K)
+ * come from stats_in [M][ceil(K / 128)]: per row and 128-column segment the
+ * sum and the sum of squares (float pairs) of A's bf16 values.
+ * GPT2_EPI_BIAS_RESID_STATS: C = resid + A @ B^T + bias and stats_out
+ * [M][ceil(N / 128)] of the bf16 C, in the stats_in format.  Other epi values
+ * behave as in gpt2k_gemm_bf16. */
+int gpt2k_gemm_bf16_ln(const void *A, const void *B, void *C, int M, int N, int K, int ldc, int out_f32,
+                       const float *bias, const void *resid, int epi, int bn, const float *c1, const float *c2,
+                       const float *stats_in, float *stats_out, float eps, void *stream);
+/* B [N, K] = bf16(W * gain) and the c1 / c2 vectors of a folded LayerNorm,
+ * from an FP32 weight W stored [K, N] (w_kn = 1, the GPT-2 Conv1D layout) or
+ * [N, K] (w_kn = 0); bias may be null. */
+int gpt2k_ln_fold_pack(const float *W, int w_kn, const float *gain, const float *shift, const float *bias, void *B,
+                       float *c1, float *c2, int N, int K, void *stream);
 
 /* LayerNorm over rows of width d (FP32 statistics): dtype GPT2_DTYPE_F32
  * (x, y float) or GPT2_DTYPE_BF16 (x, y bf16); gain and shift are float. */

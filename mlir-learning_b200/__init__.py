@@ -31,6 +31,8 @@ BERT_HEADER = os.path.join(os.path.dirname(HERE), "include", "bert_b200.h")
 
 DTYPE_F32, DTYPE_BF16, DTYPE_FP8W = 0, 1, 2
 EPI_NONE, EPI_BIAS, EPI_BIAS_GELU, EPI_BIAS_RESID, EPI_BIAS_GELU_ERF = 0, 1, 2, 3, 4
+EPI_LN_BIAS, EPI_LN_BIAS_GELU, EPI_BIAS_RESID_STATS = 5, 6, 7
+LN_SEG = 128  # columns per row-statistics segment of the folded LayerNorm
 STATUS_NAMES = {0: "ok", 1: "token id out of range", 2: "barrier wait timed out", 3: "bad launch"}
 
 
@@ -129,6 +131,9 @@ def lib() -> ctypes.CDLL:
     L.gpt2_generate.argtypes = [P(i64), i32, i32, i32, P(i64)]
     L.gpt2k_gemm_f32.argtypes = [vp, vp, i32, vp, i32, i32, i32, i32, vp, vp, i32, vp]
     L.gpt2k_gemm_bf16.argtypes = [vp, vp, vp, i32, i32, i32, i32, i32, vp, vp, i32, i32, vp]
+    L.gpt2k_gemm_bf16_ln.argtypes = [vp, vp, vp, i32, i32, i32, i32, i32, vp, vp, i32, i32, vp, vp, vp, vp,
+                                     ctypes.c_float, vp]
+    L.gpt2k_ln_fold_pack.argtypes = [vp, i32, vp, vp, vp, vp, vp, vp, i32, i32, vp]
     L.gpt2k_layernorm.argtypes = [vp, vp, vp, vp, i32, i32, ctypes.c_float, i32, vp]
     L.gpt2k_attention_workspace_bytes.argtypes = [i32, i32]
     L.gpt2k_attention_workspace_bytes.restype = ctypes.c_size_t
@@ -387,6 +392,16 @@ def k_gemm_f32(A, B, b_nk, C, M, N, K, ldc, bias=None, resid=None, epi=EPI_NONE,
 
 def k_gemm_bf16(A, B, C, M, N, K, ldc, out_f32=0, bias=None, resid=None, epi=EPI_NONE, bn=256, stream=None):
     _check(lib().gpt2k_gemm_bf16(A, B, C, M, N, K, ldc, out_f32, bias, resid, epi, bn, stream), "gpt2k_gemm_bf16")
+
+
+def k_gemm_bf16_ln(A, B, C, M, N, K, ldc, out_f32=0, bias=None, resid=None, epi=EPI_LN_BIAS, bn=256, c1=None,
+                   c2=None, stats_in=None, stats_out=None, eps=1e-5, stream=None):
+    _check(lib().gpt2k_gemm_bf16_ln(A, B, C, M, N, K, ldc, out_f32, bias, resid, epi, bn, c1, c2, stats_in,
+                                    stats_out, eps, stream), "gpt2k_gemm_bf16_ln")
+
+
+def k_ln_fold_pack(W, w_kn, gain, shift, bias, B, c1, c2, N, K, stream=None):
+    _check(lib().gpt2k_ln_fold_pack(W, w_kn, gain, shift, bias, B, c1, c2, N, K, stream), "gpt2k_ln_fold_pack")
 
 
 def k_layernorm(x, gain, shift, y, T, d, eps, dtype, stream=None):

@@ -499,6 +499,40 @@ int gpt2k_gemm_bf16(const void *A, const void *B, void *C, int M, int N, int K, 
             "gpt2k_gemm_bf16");
 }
 
+int gpt2k_gemm_bf16_ln(const void *A, const void *B, void *C, int M, int N, int K, int ldc, int out_f32,
+                       const float *bias, const void *resid, int epi, int bn, const float *c1, const float *c2,
+                       const float *stats_in, float *stats_out, float eps, void *stream) {
+  TcGemmPlan plan;
+  const int r = tc_gemm_plan(&plan, static_cast<const bf16 *>(A), static_cast<const bf16 *>(B), M, N, K, bn);
+  if (r) {
+    set_error("gpt2k_gemm_bf16_ln: TMA descriptor creation failed (%d)", r);
+    return GPT2_EINVAL;
+  }
+  tc_gemm_set_output(&plan, C, ldc, out_f32);
+  LnFold ln;
+  ln.c1 = c1;
+  ln.c2 = c2;
+  ln.stats_in = reinterpret_cast<const float2 *>(stats_in);
+  ln.nseg_in = ln_segments(K);
+  ln.k = K;
+  ln.eps = eps;
+  ln.stats_out = reinterpret_cast<float2 *>(stats_out);
+  ln.nseg_out = ln_segments(N);
+  int dev = 0, sms = 148;
+  cudaGetDevice(&dev);
+  cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+  return ck(launch_gemm_tc(plan, C, ldc, out_f32, bias, static_cast<const bf16 *>(resid), epi, nullptr, sms,
+                           static_cast<cudaStream_t>(stream), nullptr, &ln),
+            "gpt2k_gemm_bf16_ln");
+}
+
+int gpt2k_ln_fold_pack(const float *W, int w_kn, const float *gain, const float *shift, const float *bias, void *B,
+                       float *c1, float *c2, int N, int K, void *stream) {
+  return ck(launch_ln_fold_pack(W, w_kn, gain, shift, bias, static_cast<bf16 *>(B), c1, c2, N, K,
+                                static_cast<cudaStream_t>(stream)),
+            "gpt2k_ln_fold_pack");
+}
+
 int gpt2k_layernorm(const void *x, const float *gain, const float *shift, void *y, int T, int d, float eps,
                     int dtype, void *stream) {
   cudaStream_t st = static_cast<cudaStream_t>(stream);

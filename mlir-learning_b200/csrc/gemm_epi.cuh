@@ -1,0 +1,88 @@
+// gemm_epi.cuh -- pieces of the tcgen05 GEMM epilogues shared by gemm_tc.cu
+// and gemm_tc2sm.cu: the folded LayerNorm (EPI_LN_*) and the row statistics
+// of a residual GEMM's output (EPI_BIAS_RESID_STATS).  In both kernels one
+// epilogue thread owns one output row of the tile and walks it in chunks of
+// columns, so every quantity here is per thread, with no shuffles.
+#pragma once
+
+#include "common.cuh"
+#include "kernels.h"
+
+namespace gpt2 {
+
+template <int EPI>
+struct EpiKind {
+  static constexpr bool ln = EPI == EPI_LN_BIAS || EPI == EPI_LN_BIAS_GELU;
+  static constexpr bool resid = EPI == EPI_BIAS_RESID || EPI == EPI_BIAS_RESID_STATS;
+  static constexpr bool stats = EPI == EPI_BIAS_RESID_STATS;
+  static constexpr bool bias = EPI != EPI_NONE && !ln;
+  static constexpr bool gelu_new = EPI == EPI_BIAS_GELU || EPI == EPI_LN_BIAS_GELU;
+  static constexpr bool gelu_erf = EPI == EPI_BIAS_GELU_ERF;
+};
+
+// Mean and 1/sqrt(var + eps) of A's row from its segment statistics; the
+// epilogue then computes rstd * acc + (c2 - rstd * mean * c1) per column
+// (returned as rstd and -rstd * mean).
+__device__ __forceinline__ void ln_row_stats(const LnFold &ln, int row, float &rstd, float &neg_mean_rstd) {
+  const float2 *s = ln.stats_in + (int64_t)row * ln.nseg_in;
+  float sum = 0.f, sq = 0.f;
+  for (int i = 0; i < ln.nseg_in; ++i) {
+    const float2 v = s[i];
+    sum += v.x;
+    sq += v.y;
+  }
+  const float inv_k = 1.f / static_cast<float>(ln.k);
+  const float mean = sum * inv_k;
+  const float var = fmaxf(fmaf(sq, inv_k, -mean * mean), 0.f);
+  rstd = rsqrtf(var + ln.eps);
+  neg_mean_rstd = -mean * rstd;
+}
+
+// v[0..CH) = rstd * acc + (c2 - rstd * mean * c1) for columns col0.. (the
+// vectors are padded, so no column check), then gelu_new when GELU.  The
+// vectors are read with 16-byte loads that every lane of the warp issues for
+// the same address (one broadcast transaction each).
+template <int CH, bool GELU>
+__device__ __forceinline__ void ln_affine(float *v, const LnFold &ln, int col0, float rstd, float nmr) {
+  const float4 *c1 = reinterpret_cast<const float4 *>(ln.c1 + col0);
+  const float4 *c2 = reinterpret_cast<const float4 *>(ln.c2 + col0);
+#pragma unroll
+  for (int g = 0; g < CH / 4; ++g) {
+    const float4 a = __ldg(c1 + g), b = __ldg(c2 + g);
+    v[4 * g + 0] = fmaf(rstd, v[4 * g + 0], fmaf(nmr, a.x, b.x));
+    v[4 * g + 1] = fmaf(rstd, v[4 * g + 1], fmaf(nmr, a.y, b.y));
+    v[4 * g + 2] = fmaf(rstd, v[4 * g + 2], fmaf(nmr, a.z, b.z));
+    v[4 * g + 3] = fmaf(rstd, v[4 * g + 3], fmaf(nmr, a.w, b.w));
+    if (GELU) {
+#pragma unroll
+      for (int i = 0; i < 4; ++i) v[4 * g + i] = gelu_new_fast(v[4 * g + i]);
+    }
+  }
+}
+
+// Running (sum, sum of squares) of the bf16-rounded values a thread stores,
+// as packed f32 pairs; flushed once per LN_SEG columns.
+struct RowStats {
+  uint64_t s = 0, q = 0;  // bit patterns of (+0.0f, +0.0f)
+  template <int CH>
+  __device__ __forceinline__ void add_bf16(const float *v) {
+#pragma unroll
+    for (int j = 0; j < CH; j += 2) {
+      const uint32_t w = pack_bf16x2(v[j], v[j + 1]);
+      const uint64_t x2 = pk2(__uint_as_float(w << 16), __uint_as_float(w & 0xffff0000u));
+      s = add2(s, x2);
+      q = fma2(x2, x2, q);
+    }
+  }
+  __device__ __forceinline__ void flush(const LnFold &ln, int row, int seg, bool row_ok) {
+    float s0, s1, q0, q1;
+    up2(s, s0, s1);
+    up2(q, q0, q1);
+    if (row_ok && seg < ln.nseg_out)
+      ln.stats_out[(int64_t)row * ln.nseg_out + seg] = make_float2(s0 + s1, q0 + q1);
+    s = 0;
+    q = 0;
+  }
+};
+
+}  // namespace gpt2

@@ -33,7 +33,44 @@ inline cudaError_t set_smem_once(Kernel kernel, int bytes, std::atomic<uint64_t>
 //   EPI_BIAS_GELU  C = gelu_new(acc + bias[col])
 //   EPI_BIAS_RESID C = resid[row, col] + (acc + bias[col])   (resid may alias C)
 //   EPI_BIAS_GELU_ERF C = gelu(acc + bias[col]), the exact (erf) GELU of BERT
-enum Epilogue : int { EPI_NONE = 0, EPI_BIAS = 1, EPI_BIAS_GELU = 2, EPI_BIAS_RESID = 3, EPI_BIAS_GELU_ERF = 4 };
+//   EPI_LN_BIAS    C = rstd[row] * acc - rstd[row] * mean[row] * c1[col] + c2[col]
+//   EPI_LN_BIAS_GELU  gelu_new of the same: a LayerNorm of A folded into the
+//                  GEMM (LnFold below)
+//   EPI_BIAS_RESID_STATS  EPI_BIAS_RESID, and the row statistics of the bf16
+//                  C it stores for the LayerNorm folded into the next GEMM
+enum Epilogue : int {
+  EPI_NONE = 0,
+  EPI_BIAS = 1,
+  EPI_BIAS_GELU = 2,
+  EPI_BIAS_RESID = 3,
+  EPI_BIAS_GELU_ERF = 4,
+  EPI_LN_BIAS = 5,
+  EPI_LN_BIAS_GELU = 6,
+  EPI_BIAS_RESID_STATS = 7,
+};
+
+// A pre-LayerNorm folded into the GEMM that consumes it:
+//   LN(x) @ W^T + bias = rstd * (x @ W'^T) - rstd * mean * c1 + c2,
+//   W'[n, k] = bf16(W[n, k] * gain[k]),  c1[n] = sum_k W'[n, k],
+//   c2[n] = sum_k W[n, k] * shift[k] + bias[n],
+// so the GEMM reads x itself and the LayerNorm kernel and its output go
+// away.  mean and rstd come from row statistics that the producer of x (the
+// embedding or a residual GEMM) writes while it stores x: per row and per
+// LN_SEG-column segment, the sum and the sum of squares of the bf16 values.
+constexpr int LN_SEG = 128;
+struct LnFold {
+  const float *c1 = nullptr, *c2 = nullptr;  // [N rounded up to 256], 16-byte aligned, zero past N
+  const float2 *stats_in = nullptr;          // [M][nseg_in] statistics of A's rows
+  int nseg_in = 0, k = 0;                    // ceil(k / LN_SEG); the row width (K)
+  float eps = 1e-5f;
+  float2 *stats_out = nullptr;               // [M][nseg_out] of C's rows (EPI_BIAS_RESID_STATS)
+  int nseg_out = 0;                          // ceil(N / LN_SEG)
+};
+inline int ln_segments(int width) { return (width + LN_SEG - 1) / LN_SEG; }
+inline int64_t ln_vector_len(int n) { return ((int64_t)n + 255) / 256 * 256; }
+// W' (bf16 [N, K], transposed from a [K, N] master when w_kn) and c1 / c2.
+cudaError_t launch_ln_fold_pack(const float *W, int w_kn, const float *gain, const float *shift, const float *bias,
+                                bf16 *Wp, float *c1, float *c2, int N, int K, cudaStream_t st);
 
 // ---- sequence / mask preparation -------------------------------------------
 // first_valid[b] = smallest k with mask[b, k] != 0 (S if none);
@@ -45,8 +82,10 @@ cudaError_t launch_seq_info(const int64_t *mask, int B, int S, int *first_valid,
 // ---- embedding: x[t] = wte[ids[t]] + wpe[t % S] -------------------------------
 cudaError_t launch_embed_f32(const int64_t *ids, const float *wte, const float *wpe, float *x, int T, int S, int d,
                              int V, int *status, cudaStream_t st);
+// stats (optional, [T][ceil(d / LN_SEG)]): the row statistics of the bf16 x
+// for a LayerNorm folded into the next GEMM (LnFold).
 cudaError_t launch_embed_bf16(const int64_t *ids, const bf16 *wte, const bf16 *wpe, bf16 *x, int T, int S, int d,
-                              int V, int *status, cudaStream_t st);
+                              int V, int *status, cudaStream_t st, float2 *stats = nullptr);
 
 // ---- LayerNorm (biased variance, FP32 statistics) ----------------------------
 cudaError_t launch_layernorm_f32(const float *x, const float *g, const float *b, float *y, int T, int d, float eps,
@@ -105,14 +144,17 @@ int tc_gemm_plan(TcGemmPlan *plan, const bf16 *A, const bf16 *B, int M, int N, i
 int tc_gemm_set_output(TcGemmPlan *plan, const void *C, int ldc, int out_f32);
 // scale (optional, [N]): per-output-column factor applied to the accumulator
 // before the epilogue (weight-only FP8 dequantization).
+// ln: the folded LayerNorm of EPI_LN_* and the statistics output of
+// EPI_BIAS_RESID_STATS (checked by ln_fold_valid).
 cudaError_t launch_gemm_tc(const TcGemmPlan &plan, void *C, int ldc, int out_f32, const float *bias,
                            const bf16 *resid, int epi, int *status, int num_sms, cudaStream_t st,
-                           const float *scale = nullptr);
+                           const float *scale = nullptr, const LnFold *ln = nullptr);
+bool ln_fold_valid(const TcGemmPlan &plan, int epi, int out_f32, const LnFold *ln);
 // The CTA-pair kernel (called by launch_gemm_tc for TC_TILE_PAIR plans).
 bool gemm_tc2sm_usable(const TcGemmPlan &plan, const void *C, int ldc, int out_f32);
 cudaError_t launch_gemm_tc2sm(const TcGemmPlan &plan, void *C, int ldc, int out_f32, const float *bias,
                               const bf16 *resid, int epi, int *status, int num_sms, cudaStream_t st,
-                              const float *scale);
+                              const float *scale, const LnFold &ln);
 
 // ---- attention ----------------------------------------------------------------
 // qkv [B*S, 3*H*64] (q | k | v, head h at columns h*64), o [B*S, H*64].

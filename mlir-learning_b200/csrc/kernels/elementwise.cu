@@ -69,7 +69,7 @@ __global__ void embed_f32_kernel(const int64_t *__restrict__ ids, const float *_
 
 __global__ void embed_bf16_kernel(const int64_t *__restrict__ ids, const bf16 *__restrict__ wte,
                                   const bf16 *__restrict__ wpe, bf16 *__restrict__ x, int T, int S, int d, int V,
-                                  int *status) {
+                                  int *status, float2 *__restrict__ stats) {
   const int warp = (blockIdx.x * blockDim.x + threadIdx.x) >> 5;
   const int lane = threadIdx.x & 31;
   if (warp >= T) return;
@@ -79,19 +79,38 @@ __global__ void embed_bf16_kernel(const int64_t *__restrict__ ids, const bf16 *_
   const uint4 *e = reinterpret_cast<const uint4 *>(wte + (ok ? id : 0) * (int64_t)d);
   const uint4 *p = reinterpret_cast<const uint4 *>(wpe + (int64_t)(warp % S) * d);
   uint4 *o = reinterpret_cast<uint4 *>(x + (int64_t)warp * d);
-  for (int i = lane; i < d / 8; i += 32) {
-    uint4 a = ok ? e[i] : make_uint4(0, 0, 0, 0);
-    const uint4 b = p[i];
-    const __nv_bfloat162 *a2 = reinterpret_cast<const __nv_bfloat162 *>(&a);
-    const __nv_bfloat162 *b2 = reinterpret_cast<const __nv_bfloat162 *>(&b);
-    uint4 r;
-    uint32_t *r2 = reinterpret_cast<uint32_t *>(&r);
+  const int nv = d / 8, nseg = (d + LN_SEG - 1) / LN_SEG;
+  // 32 vectors of 8 per pass = two LN_SEG-column segments: lanes 0-15 hold
+  // segment 2 * pass, lanes 16-31 segment 2 * pass + 1.
+  for (int i0 = 0; i0 < nv; i0 += 32) {
+    const int i = i0 + lane;
+    float sum = 0.f, sq = 0.f;
+    if (i < nv) {
+      uint4 a = ok ? e[i] : make_uint4(0, 0, 0, 0);
+      const uint4 b = p[i];
+      const __nv_bfloat162 *a2 = reinterpret_cast<const __nv_bfloat162 *>(&a);
+      const __nv_bfloat162 *b2 = reinterpret_cast<const __nv_bfloat162 *>(&b);
+      uint4 r;
+      uint32_t *r2 = reinterpret_cast<uint32_t *>(&r);
 #pragma unroll
-    for (int j = 0; j < 4; ++j) {
-      const float2 fa = __bfloat1622float2(a2[j]), fb = __bfloat1622float2(b2[j]);
-      r2[j] = pack_bf16x2(fa.x + fb.x, fa.y + fb.y);
+      for (int j = 0; j < 4; ++j) {
+        const float2 fa = __bfloat1622float2(a2[j]), fb = __bfloat1622float2(b2[j]);
+        r2[j] = pack_bf16x2(fa.x + fb.x, fa.y + fb.y);
+        const float lo = __uint_as_float(r2[j] << 16), hi = __uint_as_float(r2[j] & 0xffff0000u);
+        sum += lo + hi;
+        sq = fmaf(lo, lo, fmaf(hi, hi, sq));
+      }
+      o[i] = r;
     }
-    o[i] = r;
+    if (stats) {
+#pragma unroll
+      for (int off = 8; off > 0; off >>= 1) {
+        sum += __shfl_xor_sync(0xffffffffu, sum, off);
+        sq += __shfl_xor_sync(0xffffffffu, sq, off);
+      }
+      const int seg = i0 / 16 + (lane >> 4);
+      if ((lane & 15) == 0 && seg < nseg) stats[(int64_t)warp * nseg + seg] = make_float2(sum, sq);
+    }
   }
 }
 
@@ -104,10 +123,10 @@ cudaError_t launch_embed_f32(const int64_t *ids, const float *wte, const float *
 }
 
 cudaError_t launch_embed_bf16(const int64_t *ids, const bf16 *wte, const bf16 *wpe, bf16 *x, int T, int S, int d,
-                              int V, int *status, cudaStream_t st) {
+                              int V, int *status, cudaStream_t st, float2 *stats) {
   if (d % 8) return cudaErrorInvalidValue;
   const int threads = 256, rows = threads / 32;
-  embed_bf16_kernel<<<(T + rows - 1) / rows, threads, 0, st>>>(ids, wte, wpe, x, T, S, d, V, status);
+  embed_bf16_kernel<<<(T + rows - 1) / rows, threads, 0, st>>>(ids, wte, wpe, x, T, S, d, V, status, stats);
   return cudaGetLastError();
 }
 
@@ -316,21 +335,25 @@ cudaError_t launch_layernorm_bf16_f32out(const bf16 *x, const float *g, const fl
 // ---------------------------------------------------------------------------
 // Weight packing (run once per weight load).
 // ---------------------------------------------------------------------------
+// kgain (optional): a factor per element of the K axis of the packed [N, K]
+// result (src columns without transpose, src rows with it), for the
+// gain-scaled weights of a folded LayerNorm.
 __global__ void pack_bf16_kernel(const float *__restrict__ src, bf16 *__restrict__ dst, int rows, int cols,
-                                 int transpose) {
+                                 int transpose, const float *__restrict__ kgain) {
   __shared__ float tile[32][33];
   const int bx = blockIdx.x * 32, by = blockIdx.y * 32;
   if (!transpose) {
     for (int i = threadIdx.y; i < 32; i += blockDim.y) {
       const int r = by + i, c = bx + threadIdx.x;
-      if (r < rows && c < cols) dst[(int64_t)r * cols + c] = __float2bfloat16_rn(src[(int64_t)r * cols + c]);
+      if (r < rows && c < cols)
+        dst[(int64_t)r * cols + c] = __float2bfloat16_rn(src[(int64_t)r * cols + c] * (kgain ? kgain[c] : 1.f));
     }
     return;
   }
   // dst[cols, rows] = src[rows, cols]^T
   for (int i = threadIdx.y; i < 32; i += blockDim.y) {
     const int r = by + i, c = bx + threadIdx.x;
-    tile[i][threadIdx.x] = (r < rows && c < cols) ? src[(int64_t)r * cols + c] : 0.f;
+    tile[i][threadIdx.x] = (r < rows && c < cols) ? src[(int64_t)r * cols + c] * (kgain ? kgain[r] : 1.f) : 0.f;
   }
   __syncthreads();
   for (int i = threadIdx.y; i < 32; i += blockDim.y) {
@@ -356,7 +379,49 @@ cudaError_t launch_e4m3_to_bf16(const uint8_t *src, bf16 *dst, int64_t n, cudaSt
 
 cudaError_t launch_pack_bf16(const float *src, bf16 *dst, int rows, int cols, int transpose, cudaStream_t st) {
   dim3 grid((cols + 31) / 32, (rows + 31) / 32), block(32, 8);
-  pack_bf16_kernel<<<grid, block, 0, st>>>(src, dst, rows, cols, transpose);
+  pack_bf16_kernel<<<grid, block, 0, st>>>(src, dst, rows, cols, transpose, nullptr);
+  return cudaGetLastError();
+}
+
+// c1[n] = sum_k Wp[n, k] (the bf16 gain-scaled weight the GEMM multiplies),
+// c2[n] = sum_k W[n, k] * shift[k] + bias[n] (the FP32 master weight), in
+// double; one warp per n, zeros in the padding up to npad.
+__global__ void ln_fold_vectors_kernel(const float *__restrict__ W, int w_kn, const float *__restrict__ shift,
+                                       const float *__restrict__ bias, const bf16 *__restrict__ Wp,
+                                       float *__restrict__ c1, float *__restrict__ c2, int N, int K, int npad) {
+  const int n = (blockIdx.x * blockDim.x + threadIdx.x) >> 5;
+  const int lane = threadIdx.x & 31;
+  if (n >= npad) return;
+  double a = 0.0, b = 0.0;
+  if (n < N) {
+    for (int k = lane; k < K; k += 32) {
+      a += (double)__bfloat162float(Wp[(int64_t)n * K + k]);
+      const float w = w_kn ? W[(int64_t)k * N + n] : W[(int64_t)n * K + k];
+      b += (double)w * (double)shift[k];
+    }
+  }
+#pragma unroll
+  for (int off = 16; off > 0; off >>= 1) {
+    a += __shfl_xor_sync(0xffffffffu, a, off);
+    b += __shfl_xor_sync(0xffffffffu, b, off);
+  }
+  if (lane == 0) {
+    c1[n] = n < N ? (float)a : 0.f;
+    c2[n] = n < N ? (float)(b + (bias ? (double)bias[n] : 0.0)) : 0.f;
+  }
+}
+
+cudaError_t launch_ln_fold_pack(const float *W, int w_kn, const float *gain, const float *shift, const float *bias,
+                                bf16 *Wp, float *c1, float *c2, int N, int K, cudaStream_t st) {
+  if (N <= 0 || K <= 0 || !W || !gain || !shift || !Wp || !c1 || !c2) return cudaErrorInvalidValue;
+  // Wp [N, K]: from W [K, N] transposed (w_kn) or W [N, K] as stored.
+  const int rows = w_kn ? K : N, cols = w_kn ? N : K;
+  dim3 grid((cols + 31) / 32, (rows + 31) / 32), block(32, 8);
+  pack_bf16_kernel<<<grid, block, 0, st>>>(W, Wp, rows, cols, w_kn, gain);
+  cudaError_t e = cudaGetLastError();
+  if (e != cudaSuccess) return e;
+  const int npad = (int)ln_vector_len(N);
+  ln_fold_vectors_kernel<<<(npad + 7) / 8, 256, 0, st>>>(W, w_kn, shift, bias, Wp, c1, c2, N, K, npad);
   return cudaGetLastError();
 }
 

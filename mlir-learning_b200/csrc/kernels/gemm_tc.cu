@@ -30,6 +30,7 @@
 #include <atomic>
 
 #include "../common.cuh"
+#include "../gemm_epi.cuh"
 #include "../kernels.h"
 
 namespace gpt2 {
@@ -64,8 +65,9 @@ __global__ void __launch_bounds__(NTHREADS, 1)
     gemm_tc_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constant__ CUtensorMap map_b,
                    const __grid_constant__ CUtensorMap map_c, void *C, int ldc, int M, int N, int K,
                    const float *__restrict__ bias, const bf16 *resid, int *status,
-                   const float *__restrict__ scale) {
+                   const float *__restrict__ scale, const LnFold ln) {
   using Cfg = TcCfg<BN>;
+  using Kind = EpiKind<EPI>;
   constexpr int STAGES = Cfg::STAGES;
   extern __shared__ unsigned char smem_raw[];
   unsigned char *smem = reinterpret_cast<unsigned char *>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
@@ -184,7 +186,7 @@ __global__ void __launch_bounds__(NTHREADS, 1)
       tile_coords(t, num_m, num_n, mb, nb);
       const int acc = local & 1;
       const uint32_t aph = (local >> 1) & 1;
-      if (EPI == EPI_BIAS_RESID && !OUT_F32) {
+      if (Kind::resid && !OUT_F32) {
         // Pull this row's residual into L2 while the tile's main loop runs,
         // so the chunked loads below do not wait on HBM (short-K GEMMs
         // would otherwise be bound by the epilogue).
@@ -196,18 +198,21 @@ __global__ void __launch_bounds__(NTHREADS, 1)
             if (nb * BN + i * 64 < N) asm volatile("prefetch.global.L2 [%0];" ::"l"(rp + i * 64));
         }
       }
+      const int row = mb * BM + row_in_tile;
+      const bool row_ok = row < M;
+      const int64_t row_off = (int64_t)row * ldc;
+      float ln_rstd = 0.f, ln_nmr = 0.f;  // folded LayerNorm of A's row, read while the main loop runs
+      if (Kind::ln && row_ok) ln_row_stats(ln, row, ln_rstd, ln_nmr);
+      RowStats rs;
       if (!mbar_wait(&tfull[acc], aph, abort_flag, status)) {
         set_status(status, GPT2_ERR_WAIT_TIMEOUT);
         *abort_flag = 1;
         break;
       }
       tc_fence_after();
-      const int row = mb * BM + row_in_tile;
-      const bool row_ok = row < M;
-      const int64_t row_off = (int64_t)row * ldc;
       uint4 res_cur[8], res_nxt[8];
       auto load_res = [&](uint4 (&dst)[8], int col0) {
-        if (EPI == EPI_BIAS_RESID && !OUT_F32 && row_ok && col0 + CH <= N) {
+        if (Kind::resid && !OUT_F32 && row_ok && col0 + CH <= N) {
           const uint4 *rp = reinterpret_cast<const uint4 *>(resid + row_off + col0);
 #pragma unroll
           for (int g = 0; g < 8; ++g) dst[g] = rp[g];
@@ -235,21 +240,25 @@ __global__ void __launch_bounds__(NTHREADS, 1)
           for (int j = 0; j < CH; ++j)
             r[j] = __float_as_uint(__uint_as_float(r[j]) * __shfl_sync(0xffffffffu, j < 32 ? s_lo : s_hi, j & 31));
         }
-        float bias_lo = 0.f, bias_hi = 0.f;
-        if (EPI != EPI_NONE) {
-          bias_lo = (col0 + lane < N) ? bias[col0 + lane] : 0.f;
-          if (CH == 64) bias_hi = (col0 + 32 + lane < N) ? bias[col0 + 32 + lane] : 0.f;
-        }
+        if (Kind::ln) {
+          ln_affine<CH, Kind::gelu_new>(v, ln, col0, ln_rstd, ln_nmr);
+        } else {
+          float bias_lo = 0.f, bias_hi = 0.f;
+          if (Kind::bias) {
+            bias_lo = (col0 + lane < N) ? bias[col0 + lane] : 0.f;
+            if (CH == 64) bias_hi = (col0 + 32 + lane < N) ? bias[col0 + 32 + lane] : 0.f;
+          }
 #pragma unroll
-        for (int j = 0; j < CH; ++j) {
-          float x = __uint_as_float(r[j]);
-          if (EPI != EPI_NONE) x += __shfl_sync(0xffffffffu, j < 32 ? bias_lo : bias_hi, j & 31);
-          if (EPI == EPI_BIAS_GELU) x = gelu_new_fast(x);
-          if (EPI == EPI_BIAS_GELU_ERF) x = gelu_erf_fast(x);
-          v[j] = x;
+          for (int j = 0; j < CH; ++j) {
+            float x = __uint_as_float(r[j]);
+            if (Kind::bias) x += __shfl_sync(0xffffffffu, j < 32 ? bias_lo : bias_hi, j & 31);
+            if (Kind::gelu_new) x = gelu_new_fast(x);
+            if (Kind::gelu_erf) x = gelu_erf_fast(x);
+            v[j] = x;
+          }
         }
         const bool full_chunk = col0 + CH <= N;
-        if (EPI == EPI_BIAS_RESID && !OUT_F32 && row_ok) {
+        if (Kind::resid && !OUT_F32 && row_ok) {
           if (full_chunk) {
 #pragma unroll
             for (int g = 0; g < 8; ++g) {
@@ -269,6 +278,12 @@ __global__ void __launch_bounds__(NTHREADS, 1)
 #pragma unroll
             for (int g = 0; g < 8; ++g) res_cur[g] = res_nxt[g];
           }
+        }
+        if (Kind::stats && !OUT_F32) {
+          // Statistics of the stored bf16 row, one LN_SEG-column segment per
+          // two chunks (BN is a multiple of LN_SEG); columns past N are 0.
+          rs.add_bf16<CH>(v);
+          if (c & 1) rs.flush(ln, row, (col0 + CH - LN_SEG) / LN_SEG, row_ok);
         }
         // 16-byte piece g of this row: 4 f32 or 8 bf16 values
         auto piece = [&](int g) -> uint4 {
@@ -374,7 +389,7 @@ int make_map_out(CUtensorMap *map, const void *base, int64_t rows, int64_t cols,
 
 template <int BN, int EPI, int OUT_F32, int TMA_STORE>
 cudaError_t launch_variant(const TcGemmPlan &p, void *C, int ldc, const float *bias, const bf16 *resid, int *status,
-                           int num_sms, cudaStream_t st, const float *scale) {
+                           int num_sms, cudaStream_t st, const float *scale, const LnFold &ln) {
   using Cfg = TcCfg<BN>;
   static std::atomic<uint64_t> attr_done{0};
   cudaError_t e = set_smem_once(gemm_tc_kernel<BN, EPI, OUT_F32, TMA_STORE>, Cfg::SMEM_BYTES, attr_done);
@@ -382,34 +397,42 @@ cudaError_t launch_variant(const TcGemmPlan &p, void *C, int ldc, const float *b
   const int tiles = ((p.M + BM - 1) / BM) * ((p.N + BN - 1) / BN);
   const int grid = tiles < num_sms ? tiles : num_sms;
   gemm_tc_kernel<BN, EPI, OUT_F32, TMA_STORE><<<grid, NTHREADS, Cfg::SMEM_BYTES, st>>>(
-      p.map_a, p.map_b, p.map_c, C, ldc, p.M, p.N, p.K, bias, resid, status, scale);
+      p.map_a, p.map_b, p.map_c, C, ldc, p.M, p.N, p.K, bias, resid, status, scale, ln);
   return cudaGetLastError();
 }
 
 template <int BN, int EPI, int OUT_F32>
 cudaError_t launch_store(const TcGemmPlan &p, void *C, int ldc, const float *bias, const bf16 *resid, int *status,
-                         int num_sms, cudaStream_t st, const float *scale) {
+                         int num_sms, cudaStream_t st, const float *scale, const LnFold &ln) {
   const bool tma = p.has_c && p.c_ptr == C && p.c_ld == ldc && p.c_f32 == OUT_F32;
-  if (tma) return launch_variant<BN, EPI, OUT_F32, 1>(p, C, ldc, bias, resid, status, num_sms, st, scale);
-  return launch_variant<BN, EPI, OUT_F32, 0>(p, C, ldc, bias, resid, status, num_sms, st, scale);
+  if (tma) return launch_variant<BN, EPI, OUT_F32, 1>(p, C, ldc, bias, resid, status, num_sms, st, scale, ln);
+  return launch_variant<BN, EPI, OUT_F32, 0>(p, C, ldc, bias, resid, status, num_sms, st, scale, ln);
 }
 
 template <int BN>
 cudaError_t dispatch_epi(const TcGemmPlan &p, void *C, int ldc, int out_f32, const float *bias, const bf16 *resid,
-                         int epi, int *status, int num_sms, cudaStream_t st, const float *scale) {
+                         int epi, int *status, int num_sms, cudaStream_t st, const float *scale, const LnFold &ln) {
+#define GPT2_TC_CASE(E, F) \
+  case E: return launch_store<BN, E, F>(p, C, ldc, bias, resid, status, num_sms, st, scale, ln)
   if (out_f32) {
-    if (epi == EPI_NONE) return launch_store<BN, EPI_NONE, 1>(p, C, ldc, bias, resid, status, num_sms, st, scale);
-    if (epi == EPI_BIAS) return launch_store<BN, EPI_BIAS, 1>(p, C, ldc, bias, resid, status, num_sms, st, scale);
+    switch (epi) {
+      GPT2_TC_CASE(EPI_NONE, 1);
+      GPT2_TC_CASE(EPI_BIAS, 1);
+      GPT2_TC_CASE(EPI_LN_BIAS, 1);
+    }
     return cudaErrorInvalidValue;
   }
   switch (epi) {
-    case EPI_NONE: return launch_store<BN, EPI_NONE, 0>(p, C, ldc, bias, resid, status, num_sms, st, scale);
-    case EPI_BIAS: return launch_store<BN, EPI_BIAS, 0>(p, C, ldc, bias, resid, status, num_sms, st, scale);
-    case EPI_BIAS_GELU: return launch_store<BN, EPI_BIAS_GELU, 0>(p, C, ldc, bias, resid, status, num_sms, st, scale);
-    case EPI_BIAS_RESID: return launch_store<BN, EPI_BIAS_RESID, 0>(p, C, ldc, bias, resid, status, num_sms, st, scale);
-    case EPI_BIAS_GELU_ERF:
-      return launch_store<BN, EPI_BIAS_GELU_ERF, 0>(p, C, ldc, bias, resid, status, num_sms, st, scale);
+    GPT2_TC_CASE(EPI_NONE, 0);
+    GPT2_TC_CASE(EPI_BIAS, 0);
+    GPT2_TC_CASE(EPI_BIAS_GELU, 0);
+    GPT2_TC_CASE(EPI_BIAS_RESID, 0);
+    GPT2_TC_CASE(EPI_BIAS_GELU_ERF, 0);
+    GPT2_TC_CASE(EPI_LN_BIAS, 0);
+    GPT2_TC_CASE(EPI_LN_BIAS_GELU, 0);
+    GPT2_TC_CASE(EPI_BIAS_RESID_STATS, 0);
   }
+#undef GPT2_TC_CASE
   return cudaErrorInvalidValue;
 }
 }  // namespace
@@ -437,17 +460,31 @@ int tc_gemm_set_output(TcGemmPlan *plan, const void *C, int ldc, int out_f32) {
   return plan->has_c;
 }
 
+bool ln_fold_valid(const TcGemmPlan &plan, int epi, int out_f32, const LnFold *ln) {
+  auto aligned16 = [](const void *p) { return (reinterpret_cast<uintptr_t>(p) & 15) == 0; };
+  if (epi == EPI_LN_BIAS || epi == EPI_LN_BIAS_GELU)
+    return ln && ln->c1 && ln->c2 && ln->stats_in && aligned16(ln->c1) && aligned16(ln->c2) && ln->k == plan.K &&
+           ln->nseg_in == ln_segments(plan.K) && ln->eps > 0.f && !(epi == EPI_LN_BIAS_GELU && out_f32);
+  if (epi == EPI_BIAS_RESID_STATS) return ln && ln->stats_out && ln->nseg_out == ln_segments(plan.N) && !out_f32;
+  return true;
+}
+
 cudaError_t launch_gemm_tc(const TcGemmPlan &plan, void *C, int ldc, int out_f32, const float *bias,
                            const bf16 *resid, int epi, int *status, int num_sms, cudaStream_t st,
-                           const float *scale) {
+                           const float *scale, const LnFold *ln) {
   if (ldc < plan.N || num_sms <= 0) return cudaErrorInvalidValue;
   if (!out_f32 && ldc % 8) return cudaErrorInvalidValue;
-  if (epi != EPI_NONE && !bias) return cudaErrorInvalidValue;
-  if (epi == EPI_BIAS_RESID && !resid) return cudaErrorInvalidValue;
+  const bool ln_epi = epi == EPI_LN_BIAS || epi == EPI_LN_BIAS_GELU;
+  if (epi != EPI_NONE && !ln_epi && !bias) return cudaErrorInvalidValue;
+  if ((epi == EPI_BIAS_RESID || epi == EPI_BIAS_RESID_STATS) && !resid) return cudaErrorInvalidValue;
+  if (!ln_fold_valid(plan, epi, out_f32, ln)) return cudaErrorInvalidValue;
+  const LnFold none;
+  const LnFold &lf = ln ? *ln : none;
   if (plan.two_sm && gemm_tc2sm_usable(plan, C, ldc, out_f32) && num_sms >= 2)
-    return launch_gemm_tc2sm(plan, C, ldc, out_f32, bias, resid, epi, status, num_sms, st, scale);
-  if (plan.bn == 256) return dispatch_epi<256>(plan, C, ldc, out_f32, bias, resid, epi, status, num_sms, st, scale);
-  return dispatch_epi<128>(plan, C, ldc, out_f32, bias, resid, epi, status, num_sms, st, scale);
+    return launch_gemm_tc2sm(plan, C, ldc, out_f32, bias, resid, epi, status, num_sms, st, scale, lf);
+  if (plan.bn == 256)
+    return dispatch_epi<256>(plan, C, ldc, out_f32, bias, resid, epi, status, num_sms, st, scale, lf);
+  return dispatch_epi<128>(plan, C, ldc, out_f32, bias, resid, epi, status, num_sms, st, scale, lf);
 }
 
 }  // namespace gpt2

@@ -41,20 +41,50 @@
 #include <atomic>
 
 #include "../common.cuh"
+#include "../gemm_epi.cuh"
 #include "../kernels.h"
 
 namespace gpt2 {
 
 namespace {
-constexpr int BM = 256, BN = 256, BK = 64, STAGES = 5, NTHREADS = 320, GROUP_M = 8;
+#ifndef GPT2_PAIR_STAGES
+#define GPT2_PAIR_STAGES 6
+#endif
+#ifndef GPT2_PAIR_NBUF
+#define GPT2_PAIR_NBUF 1
+#endif
+#ifndef GPT2_PAIR_STAGES_RESID
+#define GPT2_PAIR_STAGES_RESID 5
+#endif
+#ifndef GPT2_PAIR_NBUF_RESID
+#define GPT2_PAIR_NBUF_RESID 2
+#endif
+#ifndef GPT2_PAIR_GROUP_M_WIDE
+#define GPT2_PAIR_GROUP_M_WIDE 16
+#endif
+constexpr int BM = 256, BN = 256, BK = 64, NTHREADS = 320;
 constexpr int HALF_ROWS = 128;                   // rows of A (and of B) one CTA loads per tile
 constexpr int A_BYTES = HALF_ROWS * BK * 2;      // 16 KB
 constexpr int B_BYTES = HALF_ROWS * BK * 2;      // 16 KB
 constexpr int STAGE_BYTES = A_BYTES + B_BYTES;   // per CTA
 constexpr int EPI_WARPS = 8;
-constexpr int STAGING_BYTES = EPI_WARPS * 2 * 4096;  // 2 buffers x (32 rows x 128 bytes) per warp
-constexpr int SMEM_BYTES = 1024 + STAGES * STAGE_BYTES + STAGING_BYTES + 256;
 constexpr uint32_t TMEM_COLS = 512;              // two accumulators of BN columns
+
+// Shared memory split between the operand ring and the epilogue's store
+// staging (NBUF buffers of 32 rows x 128 bytes per epilogue warp).  Measured
+// on B200 at M = 65536: a 6-deep ring with one staging buffer is fastest for
+// the bias / GELU / no-epilogue shapes (QKV, fc, lm_head); the residual
+// epilogue, which also loads a tile of the residual, does better with 5
+// stages and 2 buffers.
+template <int EPI, int OUT_F32>
+struct PairCfg {
+  static constexpr bool RESID = EPI == EPI_BIAS_RESID || EPI == EPI_BIAS_RESID_STATS;
+  static constexpr int STAGES = RESID ? GPT2_PAIR_STAGES_RESID : GPT2_PAIR_STAGES;
+  static constexpr int NBUF = RESID ? GPT2_PAIR_NBUF_RESID : GPT2_PAIR_NBUF;
+  static constexpr int STAGING_BYTES = EPI_WARPS * NBUF * 4096;
+  static constexpr int SMEM_BYTES = 1024 + STAGES * STAGE_BYTES + STAGING_BYTES + 256;
+  static_assert(SMEM_BYTES <= 232448, "shared memory per CTA");
+};
 
 // ---- cluster / cta_group::2 helpers --------------------------------------
 __device__ __forceinline__ uint32_t cluster_ctarank() {
@@ -127,11 +157,13 @@ __device__ __forceinline__ void tc_commit_pair_self(uint64_t *bar) {
                : "memory");
 }
 
-__device__ __forceinline__ void tile_coords(int t, int num_m, int num_n, int &mb, int &nb) {
-  const int per_group = GROUP_M * num_n;
+// Tiles are walked in groups of group_m M-blocks, M fastest, so that a
+// group's A rows stay in L2 while every N-block of B passes once.
+__device__ __forceinline__ void tile_coords(int t, int num_m, int num_n, int group_m, int &mb, int &nb) {
+  const int per_group = group_m * num_n;
   const int group = t / per_group;
-  const int first_m = group * GROUP_M;
-  const int gsize = min(num_m - first_m, GROUP_M);
+  const int first_m = group * group_m;
+  const int gsize = min(num_m - first_m, group_m);
   const int in = t - group * per_group;
   mb = first_m + in % gsize;
   nb = in / gsize;
@@ -140,9 +172,12 @@ __device__ __forceinline__ void tile_coords(int t, int num_m, int num_n, int &mb
 template <int EPI, int OUT_F32>
 __global__ void __launch_bounds__(NTHREADS, 1)
     gemm_tc2sm_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constant__ CUtensorMap map_b,
-                      const __grid_constant__ CUtensorMap map_c, int ldc, int M, int N, int K,
+                      const __grid_constant__ CUtensorMap map_c, int ldc, int M, int N, int K, int group_m,
                       const float *__restrict__ bias, const bf16 *resid, int *status,
-                      const float *__restrict__ scale) {
+                      const float *__restrict__ scale, const LnFold ln) {
+  using Cfg = PairCfg<EPI, OUT_F32>;
+  using Kind = EpiKind<EPI>;
+  constexpr int STAGES = Cfg::STAGES, NBUF = Cfg::NBUF, STAGING_BYTES = Cfg::STAGING_BYTES;
   extern __shared__ unsigned char smem_raw[];
   unsigned char *smem = reinterpret_cast<unsigned char *>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   unsigned char *sa = smem;
@@ -195,7 +230,7 @@ __global__ void __launch_bounds__(NTHREADS, 1)
     bool ok = true;
     for (int t = pair; t < total && ok; t += npairs) {
       int mb, nb;
-      tile_coords(t, num_m, num_n, mb, nb);
+      tile_coords(t, num_m, num_n, group_m, mb, nb);
       for (int kb = 0; kb < num_k; ++kb, ++it) {
         const int s = it % STAGES;
         const uint32_t ph = (it / STAGES) & 1;
@@ -263,19 +298,22 @@ __global__ void __launch_bounds__(NTHREADS, 1)
     const int col_half = (warp - 2) >> 2;     // columns [col_half*128, +128) of the tile
     const int row_in_tile = static_cast<int>(rank) * HALF_ROWS + q * 32 + lane;
     const uint32_t tempty_leader = cluster_addr(smem_u32(tempty), 0);
-    unsigned char *stage_buf = staging + (warp - 2) * 2 * 4096;
+    unsigned char *stage_buf = staging + (warp - 2) * NBUF * 4096;
     uint32_t chunk_count = 0;
     int local = 0;
     for (int t = pair; t < total; t += npairs, ++local) {
       int mb, nb;
-      tile_coords(t, num_m, num_n, mb, nb);
+      tile_coords(t, num_m, num_n, group_m, mb, nb);
       const int acc = local & 1;
       const uint32_t aph = (local >> 1) & 1;
       const int row = mb * BM + row_in_tile;
       const bool row_ok = row < M;
       const int64_t row_off = (int64_t)row * ldc;
       const int tcol0 = nb * BN + col_half * (BN / 2);  // first column of this warp's half
-      if (EPI == EPI_BIAS_RESID && !OUT_F32 && row_ok) {
+      float ln_rstd = 0.f, ln_nmr = 0.f;  // folded LayerNorm of A's row, read while the main loop runs
+      if (Kind::ln && row_ok) ln_row_stats(ln, row, ln_rstd, ln_nmr);
+      RowStats rs;
+      if (Kind::resid && !OUT_F32 && row_ok) {
         // The residual row goes to L2 while the tile's main loop runs.
         const bf16 *rp = resid + row_off + tcol0;
 #pragma unroll
@@ -290,7 +328,7 @@ __global__ void __launch_bounds__(NTHREADS, 1)
       tc_fence_after();
       uint4 res_cur[8], res_nxt[8];
       auto load_res = [&](uint4 (&dst)[8], int col0) {
-        if (EPI == EPI_BIAS_RESID && !OUT_F32 && row_ok && col0 + CH <= N) {
+        if (Kind::resid && !OUT_F32 && row_ok && col0 + CH <= N) {
           const uint4 *rp = reinterpret_cast<const uint4 *>(resid + row_off + col0);
 #pragma unroll
           for (int g = 0; g < 8; ++g) dst[g] = rp[g];
@@ -319,20 +357,24 @@ __global__ void __launch_bounds__(NTHREADS, 1)
           for (int j = 0; j < CH; ++j)
             r[j] = __float_as_uint(__uint_as_float(r[j]) * __shfl_sync(0xffffffffu, j < 32 ? s_lo : s_hi, j & 31));
         }
-        float bias_lo = 0.f, bias_hi = 0.f;
-        if (EPI != EPI_NONE) {
-          bias_lo = (col0 + lane < N) ? bias[col0 + lane] : 0.f;
-          if (CH == 64) bias_hi = (col0 + 32 + lane < N) ? bias[col0 + 32 + lane] : 0.f;
-        }
+        if (Kind::ln) {
+          ln_affine<CH, Kind::gelu_new>(v, ln, col0, ln_rstd, ln_nmr);
+        } else {
+          float bias_lo = 0.f, bias_hi = 0.f;
+          if (Kind::bias) {
+            bias_lo = (col0 + lane < N) ? bias[col0 + lane] : 0.f;
+            if (CH == 64) bias_hi = (col0 + 32 + lane < N) ? bias[col0 + 32 + lane] : 0.f;
+          }
 #pragma unroll
-        for (int j = 0; j < CH; ++j) {
-          float x = __uint_as_float(r[j]);
-          if (EPI != EPI_NONE) x += __shfl_sync(0xffffffffu, j < 32 ? bias_lo : bias_hi, j & 31);
-          if (EPI == EPI_BIAS_GELU) x = gelu_new_fast(x);
-          if (EPI == EPI_BIAS_GELU_ERF) x = gelu_erf_fast(x);
-          v[j] = x;
+          for (int j = 0; j < CH; ++j) {
+            float x = __uint_as_float(r[j]);
+            if (Kind::bias) x += __shfl_sync(0xffffffffu, j < 32 ? bias_lo : bias_hi, j & 31);
+            if (Kind::gelu_new) x = gelu_new_fast(x);
+            if (Kind::gelu_erf) x = gelu_erf_fast(x);
+            v[j] = x;
+          }
         }
-        if (EPI == EPI_BIAS_RESID && !OUT_F32 && row_ok) {
+        if (Kind::resid && !OUT_F32 && row_ok) {
           if (col0 + CH <= N) {
 #pragma unroll
             for (int g = 0; g < 8; ++g) {
@@ -353,6 +395,12 @@ __global__ void __launch_bounds__(NTHREADS, 1)
             for (int g = 0; g < 8; ++g) res_cur[g] = res_nxt[g];
           }
         }
+        if (Kind::stats && !OUT_F32) {
+          // Statistics of the stored bf16 row: this warp's 128 columns are one
+          // LN_SEG segment (two chunks); columns past N are 0.
+          rs.add_bf16<CH>(v);
+          if (c == NCH - 1) rs.flush(ln, row, tcol0 / LN_SEG, row_ok);
+        }
         // 16-byte piece g of this row: 4 f32 or 8 bf16 values, written with
         // the 128-byte swizzle (piece g of row r at g ^ (r & 7)); the TMA
         // store clips the ragged M / N edges.
@@ -363,9 +411,9 @@ __global__ void __launch_bounds__(NTHREADS, 1)
           return make_uint4(pack_bf16x2(v[8 * g], v[8 * g + 1]), pack_bf16x2(v[8 * g + 2], v[8 * g + 3]),
                             pack_bf16x2(v[8 * g + 4], v[8 * g + 5]), pack_bf16x2(v[8 * g + 6], v[8 * g + 7]));
         };
-        unsigned char *buf = stage_buf + (chunk_count & 1) * 4096;
-        if (chunk_count >= 2) {
-          if (lane == 0) bulk_wait_read<1>();
+        unsigned char *buf = stage_buf + (chunk_count % NBUF) * 4096;
+        if (chunk_count >= NBUF) {
+          if (lane == 0) bulk_wait_read<NBUF - 1>();
           __syncwarp();
         }
 #pragma unroll
@@ -415,7 +463,7 @@ int pair_slots(int num_sms) {
   attr[0].val.clusterDim.z = 1;
   cfg.gridDim = dim3(static_cast<unsigned>(num_sms & ~1));
   cfg.blockDim = dim3(NTHREADS);
-  cfg.dynamicSmemBytes = SMEM_BYTES;
+  cfg.dynamicSmemBytes = PairCfg<EPI, OUT_F32>::SMEM_BYTES;
   cfg.attrs = attr;
   cfg.numAttrs = 1;
   if (cudaOccupancyMaxActiveClusters(&n, gemm_tc2sm_kernel<EPI, OUT_F32>, &cfg) != cudaSuccess || n <= 0) {
@@ -429,9 +477,9 @@ int pair_slots(int num_sms) {
 
 template <int EPI, int OUT_F32>
 cudaError_t launch_pair(const TcGemmPlan &p, int ldc, const float *bias, const bf16 *resid, int *status, int num_sms,
-                        cudaStream_t st, const float *scale) {
+                        cudaStream_t st, const float *scale, const LnFold &ln) {
   static std::atomic<uint64_t> attr_done{0};
-  cudaError_t e = set_smem_once(gemm_tc2sm_kernel<EPI, OUT_F32>, SMEM_BYTES, attr_done);
+  cudaError_t e = set_smem_once(gemm_tc2sm_kernel<EPI, OUT_F32>, PairCfg<EPI, OUT_F32>::SMEM_BYTES, attr_done);
   if (e != cudaSuccess) return e;
   const int tiles = ((p.M + BM - 1) / BM) * ((p.N + BN - 1) / BN);
   int pairs = pair_slots<EPI, OUT_F32>(num_sms);
@@ -445,12 +493,17 @@ cudaError_t launch_pair(const TcGemmPlan &p, int ldc, const float *bias, const b
   attr[0].val.clusterDim.z = 1;
   cfg.gridDim = dim3(static_cast<unsigned>(2 * pairs));
   cfg.blockDim = dim3(NTHREADS);
-  cfg.dynamicSmemBytes = SMEM_BYTES;
+  cfg.dynamicSmemBytes = PairCfg<EPI, OUT_F32>::SMEM_BYTES;
   cfg.stream = st;
   cfg.attrs = attr;
   cfg.numAttrs = 1;
+  // Wide outputs (the lm_head's vocabulary) take 16-block groups (4096 rows
+  // of A, 6 MB at d = 768, reused by every N-block while in L2); measured 2.5 %
+  // faster than 64-block groups and 4 % faster than 8-block groups.
+  const int num_n = (p.N + BN - 1) / BN;
+  const int group_m = num_n >= 64 ? GPT2_PAIR_GROUP_M_WIDE : 8;
   return cudaLaunchKernelEx(&cfg, gemm_tc2sm_kernel<EPI, OUT_F32>, p.map_a, p.map_b, p.map_c, ldc, p.M, p.N, p.K,
-                            bias, resid, status, scale);
+                            group_m, bias, resid, status, scale, ln);
 }
 }  // namespace
 
@@ -461,21 +514,30 @@ bool gemm_tc2sm_usable(const TcGemmPlan &plan, const void *C, int ldc, int out_f
 
 cudaError_t launch_gemm_tc2sm(const TcGemmPlan &plan, void *C, int ldc, int out_f32, const float *bias,
                               const bf16 *resid, int epi, int *status, int num_sms, cudaStream_t st,
-                              const float *scale) {
+                              const float *scale, const LnFold &ln) {
   if (!gemm_tc2sm_usable(plan, C, ldc, out_f32) || num_sms < 2) return cudaErrorInvalidValue;
+  if (!ln_fold_valid(plan, epi, out_f32, &ln)) return cudaErrorInvalidValue;
+#define GPT2_PAIR_CASE(E, F) \
+  case E: return launch_pair<E, F>(plan, ldc, bias, resid, status, num_sms, st, scale, ln)
   if (out_f32) {
-    if (epi == EPI_NONE) return launch_pair<EPI_NONE, 1>(plan, ldc, bias, resid, status, num_sms, st, scale);
-    if (epi == EPI_BIAS) return launch_pair<EPI_BIAS, 1>(plan, ldc, bias, resid, status, num_sms, st, scale);
+    switch (epi) {
+      GPT2_PAIR_CASE(EPI_NONE, 1);
+      GPT2_PAIR_CASE(EPI_BIAS, 1);
+      GPT2_PAIR_CASE(EPI_LN_BIAS, 1);
+    }
     return cudaErrorInvalidValue;
   }
   switch (epi) {
-    case EPI_NONE: return launch_pair<EPI_NONE, 0>(plan, ldc, bias, resid, status, num_sms, st, scale);
-    case EPI_BIAS: return launch_pair<EPI_BIAS, 0>(plan, ldc, bias, resid, status, num_sms, st, scale);
-    case EPI_BIAS_GELU: return launch_pair<EPI_BIAS_GELU, 0>(plan, ldc, bias, resid, status, num_sms, st, scale);
-    case EPI_BIAS_RESID: return launch_pair<EPI_BIAS_RESID, 0>(plan, ldc, bias, resid, status, num_sms, st, scale);
-    case EPI_BIAS_GELU_ERF:
-      return launch_pair<EPI_BIAS_GELU_ERF, 0>(plan, ldc, bias, resid, status, num_sms, st, scale);
+    GPT2_PAIR_CASE(EPI_NONE, 0);
+    GPT2_PAIR_CASE(EPI_BIAS, 0);
+    GPT2_PAIR_CASE(EPI_BIAS_GELU, 0);
+    GPT2_PAIR_CASE(EPI_BIAS_RESID, 0);
+    GPT2_PAIR_CASE(EPI_BIAS_GELU_ERF, 0);
+    GPT2_PAIR_CASE(EPI_LN_BIAS, 0);
+    GPT2_PAIR_CASE(EPI_LN_BIAS_GELU, 0);
+    GPT2_PAIR_CASE(EPI_BIAS_RESID_STATS, 0);
   }
+#undef GPT2_PAIR_CASE
   return cudaErrorInvalidValue;
 }
 

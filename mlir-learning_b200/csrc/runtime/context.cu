@@ -26,7 +26,7 @@ thread_local std::string g_err;
 Context *g_ctx = nullptr;
 
 void free_ws(Workspace &w) {
-  void *ptrs[] = {w.x, w.a, w.qkv, w.o, w.u, w.first_valid, w.key_valid, w.ids, w.mask};
+  void *ptrs[] = {w.x, w.a, w.qkv, w.o, w.u, w.stats, w.first_valid, w.key_valid, w.ids, w.mask};
   for (void *p : ptrs)
     if (p) cudaFree(p);
   if (w.logits) cudaFree(w.logits);
@@ -103,9 +103,13 @@ void destroy_context() {
   if (c->d_blob) cudaFree(c->d_blob);
   if (c->wte_h) cudaFree(c->wte_h);
   if (c->wpe_h) cudaFree(c->wpe_h);
+  if (c->wte_ln) cudaFree(c->wte_ln);
+  if (c->head_c1) cudaFree(c->head_c1);
+  if (c->head_c2) cudaFree(c->head_c2);
   for (auto &l : c->layers) {
     void *p[] = {l.qkv_wt, l.proj_wt, l.fc_wt, l.mproj_wt, l.qkv_q, l.proj_q, l.fc_q, l.mproj_q,
-                 l.qkv_s, l.proj_s, l.fc_s, l.mproj_s};
+                 l.qkv_s, l.proj_s, l.fc_s, l.mproj_s, l.qkv_lnw, l.fc_lnw, l.qkv_c1, l.qkv_c2,
+                 l.fc_c1, l.fc_c2};
     for (void *q : p)
       if (q) cudaFree(q);
   }
@@ -197,6 +201,17 @@ int load_blob(Context &c, const float *host_blob) {
         CK(launch_pack_bf16(w.proj_w, w.proj_wt, d, d, 1, c.stream));
         CK(launch_pack_bf16(w.fc_w, w.fc_wt, d, ff, 1, c.stream));
         CK(launch_pack_bf16(w.mproj_w, w.mproj_wt, ff, d, 1, c.stream));
+        // ln_1 into QKV and ln_2 into fc: gain-scaled copies and their c1 / c2
+        // (the unscaled copies above serve the decode step).
+        if (!w.qkv_lnw) CK(cudaMalloc(&w.qkv_lnw, sizeof(bf16) * (size_t)d * 3 * d));
+        if (!w.fc_lnw) CK(cudaMalloc(&w.fc_lnw, sizeof(bf16) * (size_t)d * ff));
+        float **vec[4] = {&w.qkv_c1, &w.qkv_c2, &w.fc_c1, &w.fc_c2};
+        const int vlen[4] = {3 * d, 3 * d, ff, ff};
+        for (int i = 0; i < 4; ++i)
+          if (!*vec[i]) CK(cudaMalloc(vec[i], sizeof(float) * ln_vector_len(vlen[i])));
+        CK(launch_ln_fold_pack(w.qkv_w, 1, w.ln1_g, w.ln1_b, w.qkv_b, w.qkv_lnw, w.qkv_c1, w.qkv_c2, 3 * d, d,
+                               c.stream));
+        CK(launch_ln_fold_pack(w.fc_w, 1, w.ln2_g, w.ln2_b, w.fc_b, w.fc_lnw, w.fc_c1, w.fc_c2, ff, d, c.stream));
         continue;
       }
       // Weight-only FP8: quantize on the host (per-output-channel scale), keep
@@ -224,6 +239,17 @@ int load_blob(Context &c, const float *host_blob) {
         CK(cudaMemcpy(*mt.sc, hs.data(), sizeof(float) * mt.N, cudaMemcpyHostToDevice));
         CK(launch_e4m3_to_bf16(*mt.q, mt.wt, (int64_t)n, c.stream));
       }
+    }
+    // BF16 folds ln_f into the lm_head: wte * ln_f gain, c2 = wte @ ln_f shift.
+    // Weight-only FP8 keeps its weights exactly on the E4M3 grid and runs the
+    // LayerNorm kernels instead.
+    c.ln_fold = c.dtype == 1;
+    if (c.ln_fold) {
+      if (!c.wte_ln) CK(cudaMalloc(&c.wte_ln, sizeof(bf16) * (size_t)m.vocab * d));
+      if (!c.head_c1) CK(cudaMalloc(&c.head_c1, sizeof(float) * ln_vector_len(m.vocab)));
+      if (!c.head_c2) CK(cudaMalloc(&c.head_c2, sizeof(float) * ln_vector_len(m.vocab)));
+      CK(launch_ln_fold_pack(c.wte, 0, c.lnf_g, c.lnf_b, nullptr, c.wte_ln, c.head_c1, c.head_c2, m.vocab, d,
+                             c.stream));
     }
     CK(cudaStreamSynchronize(c.stream));
   }
@@ -259,6 +285,7 @@ int ensure_workspace(Context &c, int B, int S) {
   CK(cudaMalloc(&w.qkv, es * Tn * 3 * d));
   CK(cudaMalloc(&w.o, es * Tn * d));
   CK(cudaMalloc(&w.u, es * Tn * ff));
+  if (c.dtype >= 1) CK(cudaMalloc(&w.stats, sizeof(float2) * Tn * ln_segments((int)d)));
   CK(cudaMalloc(&w.first_valid, sizeof(int) * Bn));
   CK(cudaMalloc(&w.key_valid, Tn));
   CK(cudaMalloc(&w.ids, sizeof(int64_t) * Tn));
@@ -277,8 +304,10 @@ int ensure_plans(Context &c, int64_t T) {
   const ModelDims &m = c.dims;
   const int d = m.n_embd, ff = m.n_inner;
   c.plans.resize(4 * m.n_layer + 1);
-  const bf16 *a = static_cast<const bf16 *>(c.ws.a), *o = static_cast<const bf16 *>(c.ws.o),
-             *u = static_cast<const bf16 *>(c.ws.u);
+  const bf16 *o = static_cast<const bf16 *>(c.ws.o), *u = static_cast<const bf16 *>(c.ws.u);
+  // With the LayerNorms folded, QKV, fc and the lm_head read the residual
+  // stream x itself and the gain-scaled weights.
+  const bf16 *a = static_cast<const bf16 *>(c.ln_fold ? c.ws.x : c.ws.a);
   auto pick_bn = [&](int N) {
     const int64_t tiles256 = ((T + 127) / 128) * ((N + 255) / 256);
     return tiles256 >= 2 * c.num_sms ? 256 : 128;
@@ -294,9 +323,9 @@ int ensure_plans(Context &c, int64_t T) {
   for (int l = 0; l < m.n_layer; ++l) {
     const LayerWeights &w = c.layers[l];
     TcGemmPlan *p = &c.plans[4 * l];
-    int r = tc_gemm_plan(&p[0], a, w.qkv_wt, (int)T, 3 * d, d, pick_tile(3 * d));
+    int r = tc_gemm_plan(&p[0], a, c.ln_fold ? w.qkv_lnw : w.qkv_wt, (int)T, 3 * d, d, pick_tile(3 * d));
     if (!r) r = tc_gemm_plan(&p[1], o, w.proj_wt, (int)T, d, d, pick_bn(d));
-    if (!r) r = tc_gemm_plan(&p[2], a, w.fc_wt, (int)T, ff, d, pick_tile(ff));
+    if (!r) r = tc_gemm_plan(&p[2], a, c.ln_fold ? w.fc_lnw : w.fc_wt, (int)T, ff, d, pick_tile(ff));
     if (!r) r = tc_gemm_plan(&p[3], u, w.mproj_wt, (int)T, d, ff, pick_tile(d));
     if (r) {
       set_error("TMA descriptor creation failed (%d)", r);
@@ -309,7 +338,7 @@ int ensure_plans(Context &c, int64_t T) {
   }
   c.head_tile = pick_tile(m.vocab);
   c.head_bn = pick_bn(m.vocab);
-  if (tc_gemm_plan(&c.plans[4 * m.n_layer], a, c.wte_h, (int)T, m.vocab, d, c.head_tile)) {
+  if (tc_gemm_plan(&c.plans[4 * m.n_layer], a, c.ln_fold ? c.wte_ln : c.wte_h, (int)T, m.vocab, d, c.head_tile)) {
     set_error("TMA descriptor creation failed (lm_head)");
     return -2;
   }
@@ -362,8 +391,10 @@ int profile_end(Profiler &p, double *ms, int64_t *count, int n) {
 }
 
 int forward_launch_count(const Context &c, int has_mask) {
-  // embed + 7 per layer + ln_f + lm_head; with a mask, seq_info + 1 per layer
-  return 3 + 7 * c.dims.n_layer + (has_mask ? 1 + c.dims.n_layer : 0);
+  // embed + 7 per layer + ln_f + lm_head; with a mask, seq_info + 1 per layer.
+  // With the LayerNorms folded into the GEMMs: embed + 5 per layer + lm_head.
+  const int base = c.ln_fold ? 2 + 5 * c.dims.n_layer : 3 + 7 * c.dims.n_layer;
+  return base + (has_mask ? 1 + c.dims.n_layer : 0);
 }
 
 // Buffers, TMA descriptors and output descriptor of a forward of (B, S) into
@@ -391,7 +422,8 @@ int prepare_forward(Context &c, int B, int S, float *d_logits, int64_t ld_logits
     const bool storable = !(reinterpret_cast<uintptr_t>(d_logits) & 15) && (ld_logits * 4) % 16 == 0;
     const int tile = storable ? c.head_tile : c.head_bn;
     if (head.two_sm != (tile == TC_TILE_PAIR) || (!head.two_sm && head.bn != tile)) {
-      if (tc_gemm_plan(&head, static_cast<const bf16 *>(w.a), c.wte_h, B * S, m.vocab, m.n_embd, tile)) {
+      if (tc_gemm_plan(&head, static_cast<const bf16 *>(c.ln_fold ? w.x : w.a), c.ln_fold ? c.wte_ln : c.wte_h,
+                       B * S, m.vocab, m.n_embd, tile)) {
         set_error("TMA descriptor creation failed (lm_head)");
         return -2;
       }
@@ -446,21 +478,67 @@ int launch_forward(Context &c, const int64_t *d_ids, const int64_t *d_mask, int 
   bf16 *x = static_cast<bf16 *>(w.x), *a = static_cast<bf16 *>(w.a), *qkv = static_cast<bf16 *>(w.qkv),
        *o = static_cast<bf16 *>(w.o), *u = static_cast<bf16 *>(w.u);
   const int ns = c.num_sms;
-  CKP(K_EMBED, launch_embed_bf16(d_ids, c.wte_h, c.wpe_h, x, (int)T, S, d, V, c.d_status, st));
-  for (int l = 0; l < m.n_layer; ++l) {
-    const LayerWeights &lw = c.layers[l];
-    const TcGemmPlan *p = &c.plans[4 * l];
-    CKP(K_LAYERNORM, launch_layernorm_bf16(x, lw.ln1_g, lw.ln1_b, a, (int)T, d, m.eps, st));
-    CKP(K_GEMM_QKV, launch_gemm_tc(p[0], qkv, 3 * d, 0, lw.qkv_b, nullptr, EPI_BIAS, c.d_status, ns, st, lw.qkv_s));
-    if (kv_fill) CK(launch_kv_store_bf16(qkv, static_cast<bf16 *>(c.dec.cache[l]), B, S, d, c.dec.max_len, 0, st));
-    CKP(K_ATTENTION, launch_attention_tc2(c.attn_plan, kv, o, c.d_status, st));
-    if (d_mask) CKP(K_MASKED_ROWS, launch_attn_masked_rows_bf16(qkv, w.first_valid, o, B, S, H, st));
-    CKP(K_GEMM_PROJ, launch_gemm_tc(p[1], x, d, 0, lw.proj_b, x, EPI_BIAS_RESID, c.d_status, ns, st, lw.proj_s));
-    CKP(K_LAYERNORM, launch_layernorm_bf16(x, lw.ln2_g, lw.ln2_b, a, (int)T, d, m.eps, st));
-    CKP(K_GEMM_FC, launch_gemm_tc(p[2], u, ff, 0, lw.fc_b, nullptr, EPI_BIAS_GELU, c.d_status, ns, st, lw.fc_s));
-    CKP(K_GEMM_MPROJ,
-        launch_gemm_tc(p[3], x, d, 0, lw.mproj_b, x, EPI_BIAS_RESID, c.d_status, ns, st, lw.mproj_s));
+  if (c.ln_fold) {
+    // Every LayerNorm folded into the GEMM after it: the embedding and the two
+    // residual GEMMs of each layer also write the row statistics of x, which
+    // the QKV / fc / lm_head epilogues turn into mean and 1/std.
+    LnFold stats_out;
+    stats_out.stats_out = w.stats;
+    stats_out.nseg_out = ln_segments(d);
+    auto fold = [&](const float *c1, const float *c2) {
+      LnFold f;
+      f.c1 = c1;
+      f.c2 = c2;
+      f.stats_in = w.stats;
+      f.nseg_in = ln_segments(d);
+      f.k = d;
+      f.eps = m.eps;
+      return f;
+    };
+    CKP(K_EMBED, launch_embed_bf16(d_ids, c.wte_h, c.wpe_h, x, (int)T, S, d, V, c.d_status, st, w.stats));
+    for (int l = 0; l < m.n_layer; ++l) {
+      const LayerWeights &lw = c.layers[l];
+      const TcGemmPlan *p = &c.plans[4 * l];
+      const LnFold ln1 = fold(lw.qkv_c1, lw.qkv_c2), ln2 = fold(lw.fc_c1, lw.fc_c2);
+      CKP(K_GEMM_QKV,
+          launch_gemm_tc(p[0], qkv, 3 * d, 0, nullptr, nullptr, EPI_LN_BIAS, c.d_status, ns, st, nullptr, &ln1));
+      if (kv_fill) CK(launch_kv_store_bf16(qkv, static_cast<bf16 *>(c.dec.cache[l]), B, S, d, c.dec.max_len, 0, st));
+      CKP(K_ATTENTION, launch_attention_tc2(c.attn_plan, kv, o, c.d_status, st));
+      if (d_mask) CKP(K_MASKED_ROWS, launch_attn_masked_rows_bf16(qkv, w.first_valid, o, B, S, H, st));
+      CKP(K_GEMM_PROJ, launch_gemm_tc(p[1], x, d, 0, lw.proj_b, x, EPI_BIAS_RESID_STATS, c.d_status, ns, st,
+                                      nullptr, &stats_out));
+      CKP(K_GEMM_FC,
+          launch_gemm_tc(p[2], u, ff, 0, nullptr, nullptr, EPI_LN_BIAS_GELU, c.d_status, ns, st, nullptr, &ln2));
+      CKP(K_GEMM_MPROJ, launch_gemm_tc(p[3], x, d, 0, lw.mproj_b, x, EPI_BIAS_RESID_STATS, c.d_status, ns, st,
+                                       nullptr, &stats_out));
+    }
+    if (!kv_fill) {
+      const LnFold lnf = fold(c.head_c1, c.head_c2);
+      const TcGemmPlan &head = c.plans[4 * m.n_layer];
+      CKP(K_LM_HEAD, launch_gemm_tc(head, d_logits, (int)ld_logits, 1, nullptr, nullptr, EPI_LN_BIAS, c.d_status,
+                                    ns, st, nullptr, &lnf));
+      return 0;
+    }
+  } else {
+    CKP(K_EMBED, launch_embed_bf16(d_ids, c.wte_h, c.wpe_h, x, (int)T, S, d, V, c.d_status, st));
+    for (int l = 0; l < m.n_layer; ++l) {
+      const LayerWeights &lw = c.layers[l];
+      const TcGemmPlan *p = &c.plans[4 * l];
+      CKP(K_LAYERNORM, launch_layernorm_bf16(x, lw.ln1_g, lw.ln1_b, a, (int)T, d, m.eps, st));
+      CKP(K_GEMM_QKV,
+          launch_gemm_tc(p[0], qkv, 3 * d, 0, lw.qkv_b, nullptr, EPI_BIAS, c.d_status, ns, st, lw.qkv_s));
+      if (kv_fill) CK(launch_kv_store_bf16(qkv, static_cast<bf16 *>(c.dec.cache[l]), B, S, d, c.dec.max_len, 0, st));
+      CKP(K_ATTENTION, launch_attention_tc2(c.attn_plan, kv, o, c.d_status, st));
+      if (d_mask) CKP(K_MASKED_ROWS, launch_attn_masked_rows_bf16(qkv, w.first_valid, o, B, S, H, st));
+      CKP(K_GEMM_PROJ, launch_gemm_tc(p[1], x, d, 0, lw.proj_b, x, EPI_BIAS_RESID, c.d_status, ns, st, lw.proj_s));
+      CKP(K_LAYERNORM, launch_layernorm_bf16(x, lw.ln2_g, lw.ln2_b, a, (int)T, d, m.eps, st));
+      CKP(K_GEMM_FC, launch_gemm_tc(p[2], u, ff, 0, lw.fc_b, nullptr, EPI_BIAS_GELU, c.d_status, ns, st, lw.fc_s));
+      CKP(K_GEMM_MPROJ,
+          launch_gemm_tc(p[3], x, d, 0, lw.mproj_b, x, EPI_BIAS_RESID, c.d_status, ns, st, lw.mproj_s));
+    }
   }
+  // ln_f over every row: the input of the lm_head, or (kv_fill) of the last
+  // position's logits.
   CKP(K_LAYERNORM, launch_layernorm_bf16(x, c.lnf_g, c.lnf_b, a, (int)T, d, m.eps, st));
   if (kv_fill) {
     bf16 *al = static_cast<bf16 *>(c.dec.a_last);

@@ -48,6 +48,10 @@ struct LayerWeights {
   // weight-only FP8: E4M3 codes [out, in] and per-output-channel scales
   uint8_t *qkv_q = nullptr, *proj_q = nullptr, *fc_q = nullptr, *mproj_q = nullptr;
   float *qkv_s = nullptr, *proj_s = nullptr, *fc_s = nullptr, *mproj_s = nullptr;
+  // BF16 with ln_1 / ln_2 folded into the QKV and fc GEMMs (LnFold): the
+  // gain-scaled weights [out, in] and the per-output vectors c1, c2
+  bf16 *qkv_lnw = nullptr, *fc_lnw = nullptr;
+  float *qkv_c1 = nullptr, *qkv_c2 = nullptr, *fc_c1 = nullptr, *fc_c2 = nullptr;
 };
 
 // Activation buffers of one forward, grown on demand.
@@ -56,6 +60,7 @@ struct Workspace {
   int B = 0;
   int S = 0;
   void *x = nullptr, *a = nullptr, *qkv = nullptr, *o = nullptr, *u = nullptr;
+  float2 *stats = nullptr;  // [T][ceil(d / LN_SEG)] row statistics of x for a folded LayerNorm
   int *first_valid = nullptr;
   uint8_t *key_valid = nullptr;
   int64_t *ids = nullptr, *mask = nullptr;  // staging for host-side entry points
@@ -154,6 +159,10 @@ struct Context {
   std::vector<TensorSpec> specs;
   const float *wte = nullptr, *wpe = nullptr, *lnf_g = nullptr, *lnf_b = nullptr;
   bf16 *wte_h = nullptr, *wpe_h = nullptr;  // BF16 copies
+  // BF16: ln_f folded into the lm_head (wte * ln_f gain, and its c1 / c2)
+  bf16 *wte_ln = nullptr;
+  float *head_c1 = nullptr, *head_c2 = nullptr;
+  bool ln_fold = false;  // the BF16 forward folds every LayerNorm into the next GEMM
   std::vector<LayerWeights> layers;
 
   Workspace ws;

@@ -114,6 +114,92 @@ def test_gemm_bf16_tcgen05(torch, M, N, K, epi, out_f32, bn, ldc):
         assert err <= 8e-3 * scale, (err, scale)
 
 
+def _row_stats(torch, x):
+    """Per row and 128-column segment: (sum, sum of squares) of x's values, float32 [M, nseg, 2]."""
+    M, K = x.shape
+    nseg = (K + pkg.LN_SEG - 1) // pkg.LN_SEG
+    xp = torch.zeros(M, nseg * pkg.LN_SEG, dtype=torch.float64, device=x.device)
+    xp[:, :K] = x.double()
+    xp = xp.view(M, nseg, pkg.LN_SEG)
+    return torch.stack([xp.sum(-1), (xp * xp).sum(-1)], -1).float().contiguous()
+
+
+def _vec_len(n):
+    return (n + 255) // 256 * 256
+
+
+@pytest.mark.parametrize("M,N,K,epi,out_f32,bn,ldc", [
+    (1000, 2304, 768, pkg.EPI_LN_BIAS, 0, 256, 2304),
+    (513, 3072, 768, pkg.EPI_LN_BIAS_GELU, 0, 2, 3072),
+    (513, 3072, 768, pkg.EPI_LN_BIAS_GELU, 0, 128, 3072),
+    (300, 50257, 768, pkg.EPI_LN_BIAS, 1, 2, 50304),    # the lm_head with ln_f folded in
+    (200, 1000, 768, pkg.EPI_LN_BIAS, 1, 128, 1000),
+    (77, 384, 1600, pkg.EPI_LN_BIAS_GELU, 0, 128, 384),  # K = 1600: a partial last segment
+])
+def test_gemm_layernorm_folded(torch, M, N, K, epi, out_f32, bn, ldc):
+    """LN(x) @ W + bias (then gelu_new) with the LayerNorm folded into the GEMM: gain-scaled bf16
+    weight, c1 / c2 vectors and row statistics, against LayerNorm then the linear layer in float64."""
+    g = torch.Generator(device="cuda").manual_seed(M + N + K + epi)
+    # rows with their own offset and scale, as in a residual stream
+    x = (torch.randn(M, K, device="cuda", generator=g) * (0.5 + torch.rand(M, 1, device="cuda", generator=g) * 3)
+         + torch.randn(M, 1, device="cuda", generator=g)).bfloat16()
+    gain = 1.0 + 0.2 * torch.randn(K, device="cuda", generator=g)
+    shift = 0.1 * torch.randn(K, device="cuda", generator=g)
+    W = 0.05 * torch.randn(K, N, device="cuda", generator=g)  # Conv1D layout [in, out]
+    bias = 0.1 * torch.randn(N, device="cuda", generator=g)
+    B = torch.empty(N, K, device="cuda", dtype=torch.bfloat16)
+    c1 = torch.full((_vec_len(N),), 9.0, device="cuda")
+    c2 = torch.full((_vec_len(N),), 9.0, device="cuda")
+    pkg.k_ln_fold_pack(W.data_ptr(), 1, gain.data_ptr(), shift.data_ptr(), bias.data_ptr(), B.data_ptr(),
+                       c1.data_ptr(), c2.data_ptr(), N, K, _stream(torch))
+    torch.cuda.synchronize()
+    assert torch.equal(B, (W.T * gain).bfloat16())
+    assert torch.allclose(c1[:N].double(), B.double().sum(1), rtol=1e-6, atol=1e-5)
+    assert torch.allclose(c2[:N].double(), W.double().T @ shift.double() + bias.double(), rtol=1e-6, atol=1e-5)
+    assert torch.all(c1[N:] == 0) and torch.all(c2[N:] == 0)
+    stats = _row_stats(torch, x)
+    C = torch.zeros(M, ldc, device="cuda", dtype=torch.float32 if out_f32 else torch.bfloat16)
+    eps = 1e-5
+    pkg.k_gemm_bf16_ln(x.data_ptr(), B.data_ptr(), C.data_ptr(), M, N, K, ldc, out_f32, None, None, epi, bn,
+                       c1.data_ptr(), c2.data_ptr(), stats.data_ptr(), None, eps, _stream(torch))
+    torch.cuda.synchronize()
+    xd = x.double()
+    mu = xd.mean(1, keepdim=True)
+    var = ((xd - mu) ** 2).mean(1, keepdim=True)
+    ln = (xd - mu) / torch.sqrt(var + eps) * gain.double() + shift.double()
+    ref = ln @ W.double() + bias.double()
+    if epi == pkg.EPI_LN_BIAS_GELU:
+        ref = 0.5 * ref * (1.0 + torch.tanh(0.7978845608028654 * (ref + 0.044715 * ref ** 3)))
+    got = C[:, :N].double()
+    scale = ref.abs().max().item()
+    err = (got - ref).abs().max().item()
+    # bf16 weights (W * gain rounded) and, for bf16 C, the output rounding
+    assert err <= 8e-3 * scale, (err, scale)
+    rel = ((got - ref).norm() / ref.norm()).item()
+    assert rel <= 4e-3, rel
+
+
+@pytest.mark.parametrize("M,N,K,bn", [(1000, 768, 768, 256), (513, 768, 3072, 2), (300, 1000, 512, 128),
+                                      (8192, 768, 3072, 2)])
+def test_gemm_residual_row_stats(torch, M, N, K, bn):
+    """EPI_BIAS_RESID_STATS: C = resid + A @ B^T + bias, and the per-segment sums of the stored bf16 C."""
+    g = torch.Generator(device="cuda").manual_seed(M * 7 + N + K)
+    A = torch.randn(M, K, device="cuda", generator=g).bfloat16()
+    Bw = (torch.randn(N, K, device="cuda", generator=g) * 0.05).bfloat16()
+    bias = torch.randn(N, device="cuda", generator=g)
+    C = (torch.randn(M, N, device="cuda", generator=g) * 3).bfloat16()
+    resid = C.clone()
+    nseg = (N + pkg.LN_SEG - 1) // pkg.LN_SEG
+    stats = torch.full((M, nseg, 2), 7.0, device="cuda")
+    pkg.k_gemm_bf16_ln(A.data_ptr(), Bw.data_ptr(), C.data_ptr(), M, N, K, N, 0, bias.data_ptr(), C.data_ptr(),
+                       pkg.EPI_BIAS_RESID_STATS, bn, None, None, None, stats.data_ptr(), 1e-5, _stream(torch))
+    torch.cuda.synchronize()
+    ref = resid.double() + A.double() @ Bw.double().T + bias.double()
+    assert (C.double() - ref).abs().max().item() <= 8e-3 * ref.abs().max().item()
+    want = _row_stats(torch, C).double()
+    assert torch.allclose(stats.double(), want, rtol=2e-5, atol=1e-3), (stats - want).abs().max()
+
+
 @pytest.mark.parametrize("T,d,dtype", [(1000, 768, 0), (33, 1600, 0), (1000, 768, 1), (5, 128, 1), (7, 1600, 1)])
 def test_layernorm(torch, T, d, dtype):
     g = torch.Generator(device="cuda").manual_seed(T + d)
