@@ -286,6 +286,11 @@ int gpt2k_gemm_bf16_ln(const void *A, const void *B, void *C, int M, int N, int 
 int gpt2k_ln_fold_pack(const float *W, int w_kn, const float *gain, const float *shift, const float *bias, void *B,
                        float *c1, float *c2, int N, int K, void *stream);
 
+/* Measured FP32 FFMA throughput of the current device in TFLOP/s (a
+ * microbenchmark of independent fma.rn.f32 chains on every SM, best of
+ * three launches): the roofline denominator of the exact-FP32 path. */
+int gpt2k_ffma_peak(float *tflops, void *stream);
+
 /* LayerNorm over rows of width d (FP32 statistics): dtype GPT2_DTYPE_F32
  * (x, y float) or GPT2_DTYPE_BF16 (x, y bf16); gain and shift are float. */
 int gpt2k_layernorm(const void *x, const float *gain, const float *shift, void *y, int T, int d, float eps,

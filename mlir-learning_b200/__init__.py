@@ -134,6 +134,7 @@ def lib() -> ctypes.CDLL:
     L.gpt2k_gemm_bf16_ln.argtypes = [vp, vp, vp, i32, i32, i32, i32, i32, vp, vp, i32, i32, vp, vp, vp, vp,
                                      ctypes.c_float, vp]
     L.gpt2k_ln_fold_pack.argtypes = [vp, i32, vp, vp, vp, vp, vp, vp, i32, i32, vp]
+    L.gpt2k_ffma_peak.argtypes = [P(ctypes.c_float), vp]
     L.gpt2k_layernorm.argtypes = [vp, vp, vp, vp, i32, i32, ctypes.c_float, i32, vp]
     L.gpt2k_attention_workspace_bytes.argtypes = [i32, i32]
     L.gpt2k_attention_workspace_bytes.restype = ctypes.c_size_t
@@ -402,6 +403,13 @@ def k_gemm_bf16_ln(A, B, C, M, N, K, ldc, out_f32=0, bias=None, resid=None, epi=
 
 def k_ln_fold_pack(W, w_kn, gain, shift, bias, B, c1, c2, N, K, stream=None):
     _check(lib().gpt2k_ln_fold_pack(W, w_kn, gain, shift, bias, B, c1, c2, N, K, stream), "gpt2k_ln_fold_pack")
+
+
+def k_ffma_peak(stream=None) -> float:
+    """Measured FP32 FFMA throughput of the current device, TFLOP/s."""
+    v = ctypes.c_float(0.0)
+    _check(lib().gpt2k_ffma_peak(ctypes.byref(v), stream), "gpt2k_ffma_peak")
+    return float(v.value)
 
 
 def k_layernorm(x, gain, shift, y, T, d, eps, dtype, stream=None):

@@ -444,11 +444,9 @@ int gpt2_generate(const int64_t *ids, int B, int S, int n_new, int64_t *out_toke
 }
 
 int gpt2_forward_launches(int B, int S, int has_mask) {
-  (void)B;
-  (void)S;
   Context *c = context();
   if (!c) return GPT2_ENOMODEL;
-  return forward_launch_count(*c, has_mask);
+  return forward_launch_count(*c, (int64_t)B * S, has_mask);
 }
 
 int gpt2_profile_begin(void) {
@@ -531,6 +529,10 @@ int gpt2k_ln_fold_pack(const float *W, int w_kn, const float *gain, const float 
   return ck(launch_ln_fold_pack(W, w_kn, gain, shift, bias, static_cast<bf16 *>(B), c1, c2, N, K,
                                 static_cast<cudaStream_t>(stream)),
             "gpt2k_ln_fold_pack");
+}
+
+int gpt2k_ffma_peak(float *tflops, void *stream) {
+  return ck(measure_ffma_peak(tflops, static_cast<cudaStream_t>(stream)), "gpt2k_ffma_peak");
 }
 
 int gpt2k_layernorm(const void *x, const float *gain, const float *shift, void *y, int T, int d, float eps,

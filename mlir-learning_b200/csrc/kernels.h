@@ -79,6 +79,9 @@ cudaError_t launch_ln_fold_pack(const float *W, int w_kn, const float *gain, con
 cudaError_t launch_seq_info(const int64_t *mask, int B, int S, int *first_valid, uint8_t *key_valid,
                             cudaStream_t st, int *kv_end = nullptr);
 
+// ---- FP32 SIMT throughput, measured (denominator of the exact-FP32 roofline) ----
+cudaError_t measure_ffma_peak(float *tflops, cudaStream_t st);
+
 // ---- embedding: x[t] = wte[ids[t]] + wpe[t % S] -------------------------------
 cudaError_t launch_embed_f32(const int64_t *ids, const float *wte, const float *wpe, float *x, int T, int S, int d,
                              int V, int *status, cudaStream_t st);

@@ -390,10 +390,11 @@ int profile_end(Profiler &p, double *ms, int64_t *count, int n) {
   return 0;
 }
 
-int forward_launch_count(const Context &c, int has_mask) {
+int forward_launch_count(const Context &c, int64_t T, int has_mask) {
   // embed + 7 per layer + ln_f + lm_head; with a mask, seq_info + 1 per layer.
   // With the LayerNorms folded into the GEMMs: embed + 5 per layer + lm_head.
-  const int base = c.ln_fold ? 2 + 5 * c.dims.n_layer : 3 + 7 * c.dims.n_layer;
+  const bool fold = c.ln_fold && T > kFewRows;
+  const int base = fold ? 2 + 5 * c.dims.n_layer : 3 + 7 * c.dims.n_layer;
   return base + (has_mask ? 1 + c.dims.n_layer : 0);
 }
 
@@ -403,6 +404,7 @@ int forward_launch_count(const Context &c, int has_mask) {
 int prepare_forward(Context &c, int B, int S, float *d_logits, int64_t ld_logits) {
   const ModelDims &m = c.dims;
   int r = ensure_workspace(c, B, S);
+  if (!r && c.dtype == 0 && (int64_t)B * S <= kFewRows) r = ensure_nk_f32(c);
   if (r || c.dtype == 0) return r;
   Workspace &w = c.ws;
   r = ensure_plans(c, (int64_t)B * S);
@@ -433,6 +435,76 @@ int prepare_forward(Context &c, int B, int S, float *d_logits, int64_t ld_logits
   return 0;
 }
 
+namespace {
+// The forward of at most kFewRows tokens (the reference host program's own
+// B1 x S5 call, short prompts): LayerNorm kernels and the split-K GEMV
+// kernels of the decode step, which spread each weight's stream over the
+// whole GPU, instead of the tiled GEMMs, which would give a handful of rows
+// one M-tile on a few SMs.  Same results contract as the tiled path.
+int launch_forward_few(Context &c, const int64_t *d_ids, const uint8_t *kv, const int64_t *d_mask, int B, int S,
+                       float *d_logits, int64_t ld_logits, cudaStream_t st, bool kv_fill) {
+  const ModelDims &m = c.dims;
+  const int T = B * S;
+  const int d = m.n_embd, ff = m.n_inner, H = m.n_head, V = m.vocab;
+  Workspace &w = c.ws;
+  if (c.dtype == 0) {
+    float *x = static_cast<float *>(w.x), *a = static_cast<float *>(w.a), *qkv = static_cast<float *>(w.qkv),
+          *o = static_cast<float *>(w.o), *u = static_cast<float *>(w.u);
+    CKP(K_EMBED, launch_embed_f32(d_ids, c.wte, c.wpe, x, T, S, d, V, c.d_status, st));
+    for (int l = 0; l < m.n_layer; ++l) {
+      const LayerWeights &lw = c.layers[l];
+      float *const *wt = &c.dec.wt[4 * l];
+      CKP(K_LAYERNORM, launch_layernorm_f32(x, lw.ln1_g, lw.ln1_b, a, T, d, m.eps, st));
+      CKP(K_GEMM_QKV, launch_gemv_f32(a, wt[0], qkv, T, 3 * d, d, 3 * d, lw.qkv_b, nullptr, EPI_BIAS, st));
+      if (kv_fill)
+        CK(launch_kv_store_f32(qkv, static_cast<float *>(c.dec.cache[l]), B, S, d, c.dec.max_len, 0, st));
+      CKP(K_ATTENTION, launch_attention_f32(qkv, kv, o, B, S, H, st));
+      if (d_mask) CKP(K_MASKED_ROWS, launch_attn_masked_rows_f32(qkv, w.first_valid, o, B, S, H, st));
+      CKP(K_GEMM_PROJ, launch_gemv_f32(o, wt[1], x, T, d, d, d, lw.proj_b, x, EPI_BIAS_RESID, st));
+      CKP(K_LAYERNORM, launch_layernorm_f32(x, lw.ln2_g, lw.ln2_b, a, T, d, m.eps, st));
+      CKP(K_GEMM_FC, launch_gemv_f32(a, wt[2], u, T, ff, d, ff, lw.fc_b, nullptr, EPI_BIAS_GELU, st));
+      CKP(K_GEMM_MPROJ, launch_gemv_f32(u, wt[3], x, T, d, ff, d, lw.mproj_b, x, EPI_BIAS_RESID, st));
+    }
+    CKP(K_LAYERNORM, launch_layernorm_f32(x, c.lnf_g, c.lnf_b, a, T, d, m.eps, st));
+    if (kv_fill) {
+      float *al = static_cast<float *>(c.dec.a_last);
+      CK(cudaMemcpy2DAsync(al, sizeof(float) * d, a + (int64_t)(S - 1) * d, sizeof(float) * S * d,
+                           sizeof(float) * d, B, cudaMemcpyDeviceToDevice, st));
+      CKP(K_LM_HEAD, launch_gemv_f32(al, c.wte, d_logits, B, V, d, (int)ld_logits, nullptr, nullptr, EPI_NONE, st));
+      return 0;
+    }
+    CKP(K_LM_HEAD, launch_gemv_f32(a, c.wte, d_logits, T, V, d, (int)ld_logits, nullptr, nullptr, EPI_NONE, st));
+    return 0;
+  }
+  bf16 *x = static_cast<bf16 *>(w.x), *a = static_cast<bf16 *>(w.a), *qkv = static_cast<bf16 *>(w.qkv),
+       *o = static_cast<bf16 *>(w.o), *u = static_cast<bf16 *>(w.u);
+  CKP(K_EMBED, launch_embed_bf16(d_ids, c.wte_h, c.wpe_h, x, T, S, d, V, c.d_status, st));
+  for (int l = 0; l < m.n_layer; ++l) {
+    const LayerWeights &lw = c.layers[l];
+    CKP(K_LAYERNORM, launch_layernorm_bf16(x, lw.ln1_g, lw.ln1_b, a, T, d, m.eps, st));
+    CKP(K_GEMM_QKV, launch_gemv_bf16(a, lw.qkv_wt, qkv, T, 3 * d, d, 3 * d, lw.qkv_b, nullptr, lw.qkv_s, EPI_BIAS, st));
+    if (kv_fill) CK(launch_kv_store_bf16(qkv, static_cast<bf16 *>(c.dec.cache[l]), B, S, d, c.dec.max_len, 0, st));
+    CKP(K_ATTENTION, launch_attention_tc2(c.attn_plan, kv, o, c.d_status, st));
+    if (d_mask) CKP(K_MASKED_ROWS, launch_attn_masked_rows_bf16(qkv, w.first_valid, o, B, S, H, st));
+    CKP(K_GEMM_PROJ, launch_gemv_bf16(o, lw.proj_wt, x, T, d, d, d, lw.proj_b, x, lw.proj_s, EPI_BIAS_RESID, st));
+    CKP(K_LAYERNORM, launch_layernorm_bf16(x, lw.ln2_g, lw.ln2_b, a, T, d, m.eps, st));
+    CKP(K_GEMM_FC, launch_gemv_bf16(a, lw.fc_wt, u, T, ff, d, ff, lw.fc_b, nullptr, lw.fc_s, EPI_BIAS_GELU, st));
+    CKP(K_GEMM_MPROJ,
+        launch_gemv_bf16(u, lw.mproj_wt, x, T, d, ff, d, lw.mproj_b, x, lw.mproj_s, EPI_BIAS_RESID, st));
+  }
+  CKP(K_LAYERNORM, launch_layernorm_bf16(x, c.lnf_g, c.lnf_b, a, T, d, m.eps, st));
+  if (kv_fill) {
+    bf16 *al = static_cast<bf16 *>(c.dec.a_last);
+    CK(cudaMemcpy2DAsync(al, sizeof(bf16) * d, a + (int64_t)(S - 1) * d, sizeof(bf16) * S * d, sizeof(bf16) * d, B,
+                         cudaMemcpyDeviceToDevice, st));
+    CKP(K_LM_HEAD, launch_gemv_bf16_f32out(al, c.wte_h, d_logits, B, V, d, (int)ld_logits, st));
+    return 0;
+  }
+  CKP(K_LM_HEAD, launch_gemv_bf16_f32out(a, c.wte_h, d_logits, T, V, d, (int)ld_logits, st));
+  return 0;
+}
+}  // namespace
+
 // Enqueues the forward's kernels on st (prepare_forward has run).  With
 // kv_fill, every layer's keys and values also go to the decode cache, and
 // only the last position's logits are computed, into d_logits [B, ld_logits].
@@ -447,6 +519,7 @@ int launch_forward(Context &c, const int64_t *d_ids, const int64_t *d_mask, int 
     CKP(K_SEQ_INFO, launch_seq_info(d_mask, B, S, w.first_valid, w.key_valid, st));
     kv = w.key_valid;
   }
+  if (T <= kFewRows) return launch_forward_few(c, d_ids, kv, d_mask, B, S, d_logits, ld_logits, st, kv_fill);
   if (c.dtype == 0) {
     float *x = static_cast<float *>(w.x), *a = static_cast<float *>(w.a), *qkv = static_cast<float *>(w.qkv),
           *o = static_cast<float *>(w.o), *u = static_cast<float *>(w.u);

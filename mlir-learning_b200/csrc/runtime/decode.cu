@@ -69,21 +69,27 @@ int kv_reserve(Context &c, int B, int max_len) {
   d.len = 0;
   CK(launch_set_int(d.d_pos, 0, c.stream));
   CK(cudaStreamSynchronize(c.stream));
-  if (c.dtype == 0 && d.wt.empty()) {
-    // The GEMV kernels read weights as [out, in]; the FP32 blob holds the
-    // Conv1D weights as [in, out].
-    d.wt.assign(4 * m.n_layer, nullptr);
-    for (int l = 0; l < m.n_layer; ++l) {
-      const LayerWeights &w = c.layers[l];
-      const float *src[4] = {w.qkv_w, w.proj_w, w.fc_w, w.mproj_w};
-      const int rows[4] = {(int)D, (int)D, (int)D, (int)ff}, cols[4] = {3 * (int)D, (int)D, (int)ff, (int)D};
-      for (int j = 0; j < 4; ++j) {
-        CK(cudaMalloc(&d.wt[4 * l + j], sizeof(float) * rows[j] * cols[j]));
-        CK(launch_transpose_f32(src[j], d.wt[4 * l + j], rows[j], cols[j], c.stream));
-      }
+  return ensure_nk_f32(c);
+}
+
+int ensure_nk_f32(Context &c) {
+  DecodeState &d = c.dec;
+  if (c.dtype != 0 || !d.wt.empty()) return 0;
+  // The GEMV kernels read weights as [out, in]; the FP32 blob holds the
+  // Conv1D weights as [in, out].
+  const ModelDims &m = c.dims;
+  const int D = m.n_embd, ff = m.n_inner;
+  d.wt.assign(4 * m.n_layer, nullptr);
+  for (int l = 0; l < m.n_layer; ++l) {
+    const LayerWeights &w = c.layers[l];
+    const float *src[4] = {w.qkv_w, w.proj_w, w.fc_w, w.mproj_w};
+    const int rows[4] = {D, D, D, ff}, cols[4] = {3 * D, D, ff, D};
+    for (int j = 0; j < 4; ++j) {
+      CK(cudaMalloc(&d.wt[4 * l + j], sizeof(float) * rows[j] * cols[j]));
+      CK(launch_transpose_f32(src[j], d.wt[4 * l + j], rows[j], cols[j], c.stream));
     }
-    CK(cudaStreamSynchronize(c.stream));
   }
+  CK(cudaStreamSynchronize(c.stream));
   return 0;
 }
 

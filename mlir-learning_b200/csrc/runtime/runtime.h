@@ -189,7 +189,12 @@ int ensure_workspace(Context &c, int B, int S);
 // Enqueues the forward on `st`; ids / mask are contiguous device arrays.
 int forward_device(Context &c, const int64_t *d_ids, const int64_t *d_mask, int B, int S, float *d_logits,
                    int64_t ld_logits, cudaStream_t st);
-int forward_launch_count(const Context &c, int has_mask);
+// A forward of at most this many tokens streams every weight for a handful
+// of rows: it runs the split-K GEMV kernels of the decode step.
+constexpr int64_t kFewRows = 16;
+int forward_launch_count(const Context &c, int64_t T, int has_mask);
+// The FP32 layer weights transposed to [out, in] for the GEMV kernels (once).
+int ensure_nk_f32(Context &c);
 int prepare_forward(Context &c, int B, int S, float *d_logits, int64_t ld_logits);
 int launch_forward(Context &c, const int64_t *d_ids, const int64_t *d_mask, int B, int S, float *d_logits,
                    int64_t ld_logits, cudaStream_t st, bool kv_fill);
