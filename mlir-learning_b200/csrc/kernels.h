@@ -204,12 +204,26 @@ cudaError_t launch_decode_embed_bf16(const int64_t *tok, const bf16 *wte, const 
                                      int V, const int *d_pos, int P, int *status, cudaStream_t st);
 // y[M, N] (row stride ldy) = epi(x[M, K] @ W[N, K]^T); resid has stride ldy;
 // scale (optional) multiplies the product per column before the epilogue.
+// ln (optional): a LayerNorm of x's rows (gain, shift over K, eps) applied
+// inside the kernel before the product; with EPI_NONE / EPI_BIAS /
+// EPI_BIAS_GELU only.
+struct GemvLn {
+  const float *gain = nullptr, *shift = nullptr;
+  float eps = 1e-5f;
+};
 cudaError_t launch_gemv_f32(const float *x, const float *W, float *y, int M, int N, int K, int ldy, const float *bias,
-                            const float *resid, int epi, cudaStream_t st);
+                            const float *resid, int epi, cudaStream_t st, const GemvLn *ln = nullptr);
 cudaError_t launch_gemv_bf16(const bf16 *x, const bf16 *W, bf16 *y, int M, int N, int K, int ldy, const float *bias,
-                             const bf16 *resid, const float *scale, int epi, cudaStream_t st);
+                             const bf16 *resid, const float *scale, int epi, cudaStream_t st,
+                             const GemvLn *ln = nullptr);
 cudaError_t launch_gemv_bf16_f32out(const bf16 *x, const bf16 *W, float *y, int M, int N, int K, int ldy,
-                                    cudaStream_t st);
+                                    cudaStream_t st, const GemvLn *ln = nullptr);
+// Attention of sequences of S <= 16 tokens (one warp per query row); rows
+// with no attendable key are left for launch_attn_masked_rows_*.
+cudaError_t launch_attention_short_f32(const float *qkv, const uint8_t *key_valid, float *o, int B, int S, int H,
+                                      int causal, cudaStream_t st);
+cudaError_t launch_attention_short_bf16(const bf16 *qkv, const uint8_t *key_valid, bf16 *o, int B, int S, int H,
+                                       int causal, cudaStream_t st);
 // cache [B][max_len][2D] (keys | values of every head) <- qkv rows of positions pos0 ..
 cudaError_t launch_kv_store_f32(const float *qkv, float *cache, int B, int S, int D, int max_len, int pos0,
                                 cudaStream_t st);

@@ -78,31 +78,94 @@ __global__ void decode_embed_kernel(const int64_t *__restrict__ tok, const T *__
   for (int i = lane; i < d; i += 32) x[(int64_t)b * d + i] = from_f<T>((ok ? to_f(e[i]) : 0.f) + to_f(p[i]));
 }
 
-// y[m, n] = epi(sum_k x[m, k] W[n, k]) for m < M <= 16: KS warps per output
-// column n stream W's row n (16-byte loads along k, each warp a 1/KS slice
-// of k) once for all M rows; x comes from L1 (it is tiny and shared by every
-// warp).  FP32 accumulation, warp-shuffle reduction, the KS partial sums
-// added through shared memory, the epilogue on lane m for row m.  KS > 1 puts
-// more warps (and loads in flight) on the narrow products.
-template <typename WT, typename AT, typename OT, int EPI, bool EXACT, int KS>
+// Butterfly reduce-scatter of 32 per-lane values over the warp: afterwards
+// lane j holds the warp's sum of value j (31 shuffles in all, where a full
+// reduction of each value would take 32 x 5).
+__device__ __forceinline__ float warp_reduce_scatter32(float (&v)[32]) {
+  const int lane = threadIdx.x & 31;
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) {
+    const bool upper = (lane & o) != 0;
+#pragma unroll
+    for (int i = 0; i < o; ++i) {
+      const float send = upper ? v[i] : v[i + o];
+      const float keep = upper ? v[i + o] : v[i];
+      v[i] = keep + __shfl_xor_sync(0xffffffffu, send, o);
+    }
+  }
+  return v[0];
+}
+
+// y[m, n] = epi(sum_k x[m, k] W[n, k]) for m < M <= MMAX: each warp streams
+// NC = 32 / MMAX rows of W (16-byte loads along k; the NC loads of a step are
+// issued together, each warp takes a 1/KS slice of k) for all M rows of x at
+// once, x coming from L1 (it is tiny and shared by every warp).  FP32
+// accumulation.  A lane's NC x MMAX partial sums are reduce-scattered over
+// the warp, leaving output (m, column) = (j % MMAX, j / MMAX) on lane j; the
+// KS slices are added through shared memory; the epilogue runs on that lane.
+// With LNP, x is first put through a LayerNorm (gain lng, shift lnb, biased
+// variance over K, FP32): each block computes its rows' mean and 1/std (two
+// passes per row, one warp per row) and normalises the x chunks as it reads
+// them, so the LayerNorm needs no launch and no output buffer of its own.
+template <typename WT, typename AT, typename OT, int EPI, bool EXACT, int MMAX, int KS, bool LNP>
 __global__ void __launch_bounds__(256) gemv_nk_kernel(const AT *__restrict__ x, const WT *__restrict__ W,
                                                       OT *__restrict__ y, int M, int N, int K, int ldy,
                                                       const float *__restrict__ bias, const OT *resid,
-                                                      const float *__restrict__ scale) {
-  constexpr int MMAX = 16;
-  __shared__ float part[8][MMAX];
-  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int n = blockIdx.x * (8 / KS) + warp / KS, ks = warp % KS;
+                                                      const float *__restrict__ scale, const float *__restrict__ lng,
+                                                      const float *__restrict__ lnb, float eps) {
+  constexpr int NC = 32 / MMAX;
   constexpr int WC = Chunk<WT>::N;  // weights per 16-byte chunk
-  float acc[MMAX];
+  __shared__ float part[8][32];
+  __shared__ float s_mean[16], s_rstd[16];
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int n0 = (blockIdx.x * (8 / KS) + warp / KS) * NC, ks = warp % KS;
+  float mean[MMAX], rstd[MMAX];
+  if (LNP) {
+    for (int m = warp; m < M; m += 8) {
+      const AT *xr = x + (int64_t)m * K;
+      float sum = 0.f;
+      for (int k = lane; k < K; k += 32) sum += to_f(xr[k]);
+      const float mu = warp_sum(sum) / K;
+      float sq = 0.f;
+      for (int k = lane; k < K; k += 32) {
+        const float t = to_f(xr[k]) - mu;
+        sq = fmaf(t, t, sq);
+      }
+      const float r = rsqrtf(warp_sum(sq) / K + eps);
+      if (lane == 0) {
+        s_mean[m] = mu;
+        s_rstd[m] = r;
+      }
+    }
+    __syncthreads();
 #pragma unroll
-  for (int m = 0; m < MMAX; ++m) acc[m] = 0.f;
-  if (n < N) {
-    const WT *wr = W + (int64_t)n * K;
-#pragma unroll 4
+    for (int m = 0; m < MMAX; ++m) {
+      mean[m] = m < M ? s_mean[m] : 0.f;
+      rstd[m] = m < M ? s_rstd[m] : 0.f;
+    }
+  }
+  float acc[32];
+#pragma unroll
+  for (int i = 0; i < 32; ++i) acc[i] = 0.f;
+  if (n0 < N) {
+    const WT *wr[NC];
+#pragma unroll
+    for (int c = 0; c < NC; ++c) wr[c] = W + (int64_t)(n0 + c < N ? n0 + c : n0) * K;  // past N: a valid row, unused
+#pragma unroll 1
     for (int k0 = (ks * 32 + lane) * WC; k0 < K; k0 += 32 * KS * WC) {
-      float w[WC];
-      load_chunk<WT>(wr + k0, w);
+      float w[NC][WC];
+#pragma unroll
+      for (int c = 0; c < NC; ++c) load_chunk<WT>(wr[c] + k0, w[c]);
+      float g[LNP ? WC : 1], b[LNP ? WC : 1];
+      if (LNP) {
+#pragma unroll
+        for (int j = 0; j < WC; j += 4) {
+          const float4 g4 = *reinterpret_cast<const float4 *>(lng + k0 + j);
+          const float4 b4 = *reinterpret_cast<const float4 *>(lnb + k0 + j);
+          g[j] = g4.x, g[j + 1] = g4.y, g[j + 2] = g4.z, g[j + 3] = g4.w;
+          b[j] = b4.x, b[j + 1] = b4.y, b[j + 2] = b4.z, b[j + 3] = b4.w;
+        }
+      }
 #pragma unroll
       for (int m = 0; m < MMAX; ++m) {
         if (m < M) {
@@ -111,43 +174,83 @@ __global__ void __launch_bounds__(256) gemv_nk_kernel(const AT *__restrict__ x, 
           for (int j = 0; j < WC; j += Chunk<AT>::N) {
             float xv[Chunk<AT>::N];
             load_chunk<AT>(xr + j, xv);
+            if (LNP) {
 #pragma unroll
-            for (int e = 0; e < Chunk<AT>::N; ++e) acc[m] = fmaf(xv[e], w[j + e], acc[m]);
+              for (int e = 0; e < Chunk<AT>::N; ++e)
+                xv[e] = fmaf((xv[e] - mean[m]) * rstd[m], g[LNP ? j + e : 0], b[LNP ? j + e : 0]);
+            }
+#pragma unroll
+            for (int c = 0; c < NC; ++c)
+#pragma unroll
+              for (int e = 0; e < Chunk<AT>::N; ++e) acc[c * MMAX + m] = fmaf(xv[e], w[c][j + e], acc[c * MMAX + m]);
           }
         }
       }
     }
   }
-#pragma unroll
-  for (int m = 0; m < MMAX; ++m) acc[m] = warp_sum(acc[m]);
+  float v = warp_reduce_scatter32(acc);
   if (KS > 1) {
-    if (lane == 0) {
-#pragma unroll
-      for (int m = 0; m < MMAX; ++m) part[warp][m] = acc[m];
-    }
+    part[warp][lane] = v;
     __syncthreads();
     if (ks != 0) return;
 #pragma unroll
-    for (int m = 0; m < MMAX; ++m) {
-      float t = part[warp][m];
-#pragma unroll
-      for (int i = 1; i < KS; ++i) t += part[warp + i][m];
-      acc[m] = t;
-    }
+    for (int i = 1; i < KS; ++i) v += part[warp + i][lane];
   }
-  if (n < N && lane < M) {
-    float v = 0.f;
-#pragma unroll
-    for (int m = 0; m < MMAX; ++m)
-      if (m == lane) v = acc[m];
+  const int m = lane % MMAX, n = n0 + lane / MMAX;
+  if (n < N && m < M) {
     if (scale) v *= scale[n];
     if (EPI != EPI_NONE) v += bias[n];
     if (EPI == EPI_BIAS_GELU) v = EXACT ? gelu_new_exact(v) : gelu_new_fast(v);
     if (EPI == EPI_BIAS_GELU_ERF) v = EXACT ? gelu_erf(v) : gelu_erf_fast(v);
-    const int64_t idx = (int64_t)lane * ldy + n;
+    const int64_t idx = (int64_t)m * ldy + n;
     if (EPI == EPI_BIAS_RESID) v += to_f(resid[idx]);
     y[idx] = from_f<OT>(v);
   }
+}
+
+// Attention of a short sequence (S <= 16, the few-token forward): one warp
+// per (sequence, head, query row), lane l holding dimensions l and l + 32 of
+// the head.  Scores q.k / 8 by warp reduction, softmax with max subtraction
+// (expf), O = P V.  Masked keys (causal future, key_valid 0) contribute
+// exactly 0; a row with no attendable key is left to the masked-rows kernel.
+template <typename T>
+__global__ void __launch_bounds__(128) attn_short_kernel(const T *__restrict__ qkv, const uint8_t *__restrict__ key_valid,
+                                                         T *__restrict__ o, int B, int S, int H, int causal) {
+  constexpr int DH = 64, SMAX = 16;
+  const int wid = (blockIdx.x * blockDim.x + threadIdx.x) >> 5, lane = threadIdx.x & 31;
+  if (wid >= B * H * S) return;
+  const int i = wid % S, h = (wid / S) % H, b = wid / (S * H);
+  const int D = H * DH;
+  const int64_t row = (int64_t)b * S;
+  const T *q = qkv + (row + i) * 3 * D + h * DH;
+  const float q0 = to_f(q[lane]) * 0.125f, q1 = to_f(q[lane + 32]) * 0.125f;
+  float sc[SMAX];
+  float mx = -INFINITY;
+#pragma unroll
+  for (int j = 0; j < SMAX; ++j) {
+    sc[j] = -INFINITY;
+    if (j < S && (!causal || j <= i) && (!key_valid || key_valid[row + j])) {
+      const T *k = qkv + (row + j) * 3 * D + D + h * DH;
+      const float s = warp_sum(fmaf(q0, to_f(k[lane]), q1 * to_f(k[lane + 32])));
+      sc[j] = s;
+      mx = fmaxf(mx, s);
+    }
+  }
+  if (mx == -INFINITY) return;
+  float l = 0.f, o0 = 0.f, o1 = 0.f;
+#pragma unroll
+  for (int j = 0; j < SMAX; ++j) {
+    if (sc[j] != -INFINITY) {
+      const float p = expf(sc[j] - mx);
+      const T *v = qkv + (row + j) * 3 * D + 2 * D + h * DH;
+      l += p;
+      o0 = fmaf(p, to_f(v[lane]), o0);
+      o1 = fmaf(p, to_f(v[lane + 32]), o1);
+    }
+  }
+  T *out = o + (row + i) * D + h * DH;
+  out[lane] = from_f<T>(o0 / l);
+  out[lane + 32] = from_f<T>(o1 / l);
 }
 
 // Copies the keys and values of S tokens per sequence (positions pos0 ..
@@ -308,14 +411,33 @@ __global__ void transpose_f32_kernel(const float *__restrict__ src, float *__res
   }
 }
 
-template <typename WT, typename AT, typename OT, bool EXACT, int KS>
+template <typename WT, typename AT, typename OT, bool EXACT, int MMAX, int KS>
 cudaError_t gemv_launch(const AT *x, const WT *W, OT *y, int M, int N, int K, int ldy, const float *bias,
-                        const OT *resid, const float *scale, int epi, cudaStream_t st) {
-  const int blocks = (N + 8 / KS - 1) / (8 / KS);
-#define GEMV_CASE(E)                                                                                              \
-  case E:                                                                                                         \
-    gemv_nk_kernel<WT, AT, OT, E, EXACT, KS><<<blocks, 256, 0, st>>>(x, W, y, M, N, K, ldy, bias, resid, scale); \
+                        const OT *resid, const float *scale, int epi, const GemvLn *ln, cudaStream_t st) {
+  constexpr int NC = 32 / MMAX, GROUPS_PER_BLOCK = 8 / KS;
+  const int groups = (N + NC - 1) / NC;
+  const int blocks = (groups + GROUPS_PER_BLOCK - 1) / GROUPS_PER_BLOCK;
+#define GEMV_CASE(E)                                                                                     \
+  case E:                                                                                                \
+    gemv_nk_kernel<WT, AT, OT, E, EXACT, MMAX, KS, false><<<blocks, 256, 0, st>>>(                       \
+        x, W, y, M, N, K, ldy, bias, resid, scale, nullptr, nullptr, 0.f);                               \
     break;
+#define GEMV_LN_CASE(E)                                                                                  \
+  case E:                                                                                                \
+    gemv_nk_kernel<WT, AT, OT, E, EXACT, MMAX, KS, true><<<blocks, 256, 0, st>>>(                        \
+        x, W, y, M, N, K, ldy, bias, resid, scale, ln->gain, ln->shift, ln->eps);                        \
+    break;
+  if (ln) {
+    // A LayerNorm ahead of the product: the QKV, fc and lm_head inputs.
+    switch (epi) {
+      GEMV_LN_CASE(EPI_NONE)
+      GEMV_LN_CASE(EPI_BIAS)
+      GEMV_LN_CASE(EPI_BIAS_GELU)
+      default:
+        return cudaErrorInvalidValue;
+    }
+    return cudaGetLastError();
+  }
   switch (epi) {
     GEMV_CASE(EPI_NONE)
     GEMV_CASE(EPI_BIAS)
@@ -326,17 +448,39 @@ cudaError_t gemv_launch(const AT *x, const WT *W, OT *y, int M, int N, int K, in
       return cudaErrorInvalidValue;
   }
 #undef GEMV_CASE
+#undef GEMV_LN_CASE
   return cudaGetLastError();
 }
 
-// Split k over up to 4 warps per column while the columns alone would not
-// give every SM several blocks.
+template <typename WT, typename AT, typename OT, bool EXACT, int MMAX>
+cudaError_t gemv_ks(const AT *x, const WT *W, OT *y, int M, int N, int K, int ldy, const float *bias,
+                    const OT *resid, const float *scale, int epi, const GemvLn *ln, cudaStream_t st) {
+  // Split k over KS warps until about 4096 warps stream the matrix (a few
+  // dozen per SM keep enough loads in flight), with at least one 16-byte step
+  // of k per lane for every warp.
+  constexpr int NC = 32 / MMAX;
+  const int groups = (N + NC - 1) / NC;
+  const int steps = (K + 32 * Chunk<WT>::N - 1) / (32 * Chunk<WT>::N);
+  int ks = 1;
+  while (ks < 8 && groups * ks < 4096 && 2 * ks <= steps) ks *= 2;
+  switch (ks) {
+    case 1: return gemv_launch<WT, AT, OT, EXACT, MMAX, 1>(x, W, y, M, N, K, ldy, bias, resid, scale, epi, ln, st);
+    case 2: return gemv_launch<WT, AT, OT, EXACT, MMAX, 2>(x, W, y, M, N, K, ldy, bias, resid, scale, epi, ln, st);
+    case 4: return gemv_launch<WT, AT, OT, EXACT, MMAX, 4>(x, W, y, M, N, K, ldy, bias, resid, scale, epi, ln, st);
+    default: return gemv_launch<WT, AT, OT, EXACT, MMAX, 8>(x, W, y, M, N, K, ldy, bias, resid, scale, epi, ln, st);
+  }
+}
+
+// Accumulators sized to the rows: 4, 8 or 16 (8, 4 or 2 columns per warp).
 template <typename WT, typename AT, typename OT, bool EXACT>
 cudaError_t gemv_dispatch(const AT *x, const WT *W, OT *y, int M, int N, int K, int ldy, const float *bias,
-                          const OT *resid, const float *scale, int epi, cudaStream_t st) {
-  if (N <= 1024) return gemv_launch<WT, AT, OT, EXACT, 4>(x, W, y, M, N, K, ldy, bias, resid, scale, epi, st);
-  if (N <= 4096) return gemv_launch<WT, AT, OT, EXACT, 2>(x, W, y, M, N, K, ldy, bias, resid, scale, epi, st);
-  return gemv_launch<WT, AT, OT, EXACT, 1>(x, W, y, M, N, K, ldy, bias, resid, scale, epi, st);
+                          const OT *resid, const float *scale, int epi, const GemvLn *ln, cudaStream_t st) {
+  if (ln && (!ln->gain || !ln->shift || K % 4 || !(ln->eps > 0.f) || (reinterpret_cast<uintptr_t>(ln->gain) & 15) ||
+             (reinterpret_cast<uintptr_t>(ln->shift) & 15)))
+    return cudaErrorInvalidValue;  // the gain and shift are read as 16-byte vectors
+  if (M <= 4) return gemv_ks<WT, AT, OT, EXACT, 4>(x, W, y, M, N, K, ldy, bias, resid, scale, epi, ln, st);
+  if (M <= 8) return gemv_ks<WT, AT, OT, EXACT, 8>(x, W, y, M, N, K, ldy, bias, resid, scale, epi, ln, st);
+  return gemv_ks<WT, AT, OT, EXACT, 16>(x, W, y, M, N, K, ldy, bias, resid, scale, epi, ln, st);
 }
 }  // namespace
 
@@ -352,19 +496,34 @@ cudaError_t launch_decode_embed_bf16(const int64_t *tok, const bf16 *wte, const 
 }
 
 cudaError_t launch_gemv_f32(const float *x, const float *W, float *y, int M, int N, int K, int ldy, const float *bias,
-                            const float *resid, int epi, cudaStream_t st) {
+                            const float *resid, int epi, cudaStream_t st, const GemvLn *ln) {
   if (M < 1 || M > 16 || K % 4 || ldy < N) return cudaErrorInvalidValue;
-  return gemv_dispatch<float, float, float, true>(x, W, y, M, N, K, ldy, bias, resid, nullptr, epi, st);
+  return gemv_dispatch<float, float, float, true>(x, W, y, M, N, K, ldy, bias, resid, nullptr, epi, ln, st);
 }
 cudaError_t launch_gemv_bf16(const bf16 *x, const bf16 *W, bf16 *y, int M, int N, int K, int ldy, const float *bias,
-                             const bf16 *resid, const float *scale, int epi, cudaStream_t st) {
+                             const bf16 *resid, const float *scale, int epi, cudaStream_t st, const GemvLn *ln) {
   if (M < 1 || M > 16 || K % 8 || ldy < N) return cudaErrorInvalidValue;
-  return gemv_dispatch<bf16, bf16, bf16, false>(x, W, y, M, N, K, ldy, bias, resid, scale, epi, st);
+  return gemv_dispatch<bf16, bf16, bf16, false>(x, W, y, M, N, K, ldy, bias, resid, scale, epi, ln, st);
 }
 cudaError_t launch_gemv_bf16_f32out(const bf16 *x, const bf16 *W, float *y, int M, int N, int K, int ldy,
-                                    cudaStream_t st) {
+                                    cudaStream_t st, const GemvLn *ln) {
   if (M < 1 || M > 16 || K % 8 || ldy < N) return cudaErrorInvalidValue;
-  return gemv_dispatch<bf16, bf16, float, false>(x, W, y, M, N, K, ldy, nullptr, nullptr, nullptr, EPI_NONE, st);
+  return gemv_dispatch<bf16, bf16, float, false>(x, W, y, M, N, K, ldy, nullptr, nullptr, nullptr, EPI_NONE, ln, st);
+}
+
+cudaError_t launch_attention_short_f32(const float *qkv, const uint8_t *key_valid, float *o, int B, int S, int H,
+                                      int causal, cudaStream_t st) {
+  if (S < 1 || S > 16) return cudaErrorInvalidValue;
+  const int warps = B * H * S;
+  attn_short_kernel<float><<<(warps + 3) / 4, 128, 0, st>>>(qkv, key_valid, o, B, S, H, causal);
+  return cudaGetLastError();
+}
+cudaError_t launch_attention_short_bf16(const bf16 *qkv, const uint8_t *key_valid, bf16 *o, int B, int S, int H,
+                                       int causal, cudaStream_t st) {
+  if (S < 1 || S > 16) return cudaErrorInvalidValue;
+  const int warps = B * H * S;
+  attn_short_kernel<bf16><<<(warps + 3) / 4, 128, 0, st>>>(qkv, key_valid, o, B, S, H, causal);
+  return cudaGetLastError();
 }
 
 cudaError_t launch_kv_store_f32(const float *qkv, float *cache, int B, int S, int D, int max_len, int pos0,

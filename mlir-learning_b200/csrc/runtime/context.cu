@@ -393,7 +393,8 @@ int profile_end(Profiler &p, double *ms, int64_t *count, int n) {
 int forward_launch_count(const Context &c, int64_t T, int has_mask) {
   // embed + 7 per layer + ln_f + lm_head; with a mask, seq_info + 1 per layer.
   // With the LayerNorms folded into the GEMMs: embed + 5 per layer + lm_head.
-  const bool fold = c.ln_fold && T > kFewRows;
+  // A few-token forward: embed + 5 per layer (LayerNorms inside the GEMVs) + lm_head.
+  const bool fold = T <= kFewRows || c.ln_fold;
   const int base = fold ? 2 + 5 * c.dims.n_layer : 3 + 7 * c.dims.n_layer;
   return base + (has_mask ? 1 + c.dims.n_layer : 0);
 }
@@ -447,60 +448,63 @@ int launch_forward_few(Context &c, const int64_t *d_ids, const uint8_t *kv, cons
   const int T = B * S;
   const int d = m.n_embd, ff = m.n_inner, H = m.n_head, V = m.vocab;
   Workspace &w = c.ws;
+  const GemvLn lnf{c.lnf_g, c.lnf_b, m.eps};
+  // ln_1, ln_2 and ln_f run inside the GEMVs that read them (GemvLn); the
+  // attention of these short sequences is one warp per query row.
   if (c.dtype == 0) {
-    float *x = static_cast<float *>(w.x), *a = static_cast<float *>(w.a), *qkv = static_cast<float *>(w.qkv),
-          *o = static_cast<float *>(w.o), *u = static_cast<float *>(w.u);
+    float *x = static_cast<float *>(w.x), *qkv = static_cast<float *>(w.qkv), *o = static_cast<float *>(w.o),
+          *u = static_cast<float *>(w.u);
     CKP(K_EMBED, launch_embed_f32(d_ids, c.wte, c.wpe, x, T, S, d, V, c.d_status, st));
     for (int l = 0; l < m.n_layer; ++l) {
       const LayerWeights &lw = c.layers[l];
       float *const *wt = &c.dec.wt[4 * l];
-      CKP(K_LAYERNORM, launch_layernorm_f32(x, lw.ln1_g, lw.ln1_b, a, T, d, m.eps, st));
-      CKP(K_GEMM_QKV, launch_gemv_f32(a, wt[0], qkv, T, 3 * d, d, 3 * d, lw.qkv_b, nullptr, EPI_BIAS, st));
+      const GemvLn ln1{lw.ln1_g, lw.ln1_b, m.eps}, ln2{lw.ln2_g, lw.ln2_b, m.eps};
+      CKP(K_GEMM_QKV, launch_gemv_f32(x, wt[0], qkv, T, 3 * d, d, 3 * d, lw.qkv_b, nullptr, EPI_BIAS, st, &ln1));
       if (kv_fill)
         CK(launch_kv_store_f32(qkv, static_cast<float *>(c.dec.cache[l]), B, S, d, c.dec.max_len, 0, st));
-      CKP(K_ATTENTION, launch_attention_f32(qkv, kv, o, B, S, H, st));
+      CKP(K_ATTENTION, launch_attention_short_f32(qkv, kv, o, B, S, H, 1, st));
       if (d_mask) CKP(K_MASKED_ROWS, launch_attn_masked_rows_f32(qkv, w.first_valid, o, B, S, H, st));
       CKP(K_GEMM_PROJ, launch_gemv_f32(o, wt[1], x, T, d, d, d, lw.proj_b, x, EPI_BIAS_RESID, st));
-      CKP(K_LAYERNORM, launch_layernorm_f32(x, lw.ln2_g, lw.ln2_b, a, T, d, m.eps, st));
-      CKP(K_GEMM_FC, launch_gemv_f32(a, wt[2], u, T, ff, d, ff, lw.fc_b, nullptr, EPI_BIAS_GELU, st));
+      CKP(K_GEMM_FC, launch_gemv_f32(x, wt[2], u, T, ff, d, ff, lw.fc_b, nullptr, EPI_BIAS_GELU, st, &ln2));
       CKP(K_GEMM_MPROJ, launch_gemv_f32(u, wt[3], x, T, d, ff, d, lw.mproj_b, x, EPI_BIAS_RESID, st));
     }
-    CKP(K_LAYERNORM, launch_layernorm_f32(x, c.lnf_g, c.lnf_b, a, T, d, m.eps, st));
     if (kv_fill) {
-      float *al = static_cast<float *>(c.dec.a_last);
-      CK(cudaMemcpy2DAsync(al, sizeof(float) * d, a + (int64_t)(S - 1) * d, sizeof(float) * S * d,
+      float *xl = static_cast<float *>(c.dec.a_last);
+      CK(cudaMemcpy2DAsync(xl, sizeof(float) * d, x + (int64_t)(S - 1) * d, sizeof(float) * S * d,
                            sizeof(float) * d, B, cudaMemcpyDeviceToDevice, st));
-      CKP(K_LM_HEAD, launch_gemv_f32(al, c.wte, d_logits, B, V, d, (int)ld_logits, nullptr, nullptr, EPI_NONE, st));
+      CKP(K_LM_HEAD,
+          launch_gemv_f32(xl, c.wte, d_logits, B, V, d, (int)ld_logits, nullptr, nullptr, EPI_NONE, st, &lnf));
       return 0;
     }
-    CKP(K_LM_HEAD, launch_gemv_f32(a, c.wte, d_logits, T, V, d, (int)ld_logits, nullptr, nullptr, EPI_NONE, st));
+    CKP(K_LM_HEAD,
+        launch_gemv_f32(x, c.wte, d_logits, T, V, d, (int)ld_logits, nullptr, nullptr, EPI_NONE, st, &lnf));
     return 0;
   }
-  bf16 *x = static_cast<bf16 *>(w.x), *a = static_cast<bf16 *>(w.a), *qkv = static_cast<bf16 *>(w.qkv),
-       *o = static_cast<bf16 *>(w.o), *u = static_cast<bf16 *>(w.u);
+  bf16 *x = static_cast<bf16 *>(w.x), *qkv = static_cast<bf16 *>(w.qkv), *o = static_cast<bf16 *>(w.o),
+       *u = static_cast<bf16 *>(w.u);
   CKP(K_EMBED, launch_embed_bf16(d_ids, c.wte_h, c.wpe_h, x, T, S, d, V, c.d_status, st));
   for (int l = 0; l < m.n_layer; ++l) {
     const LayerWeights &lw = c.layers[l];
-    CKP(K_LAYERNORM, launch_layernorm_bf16(x, lw.ln1_g, lw.ln1_b, a, T, d, m.eps, st));
-    CKP(K_GEMM_QKV, launch_gemv_bf16(a, lw.qkv_wt, qkv, T, 3 * d, d, 3 * d, lw.qkv_b, nullptr, lw.qkv_s, EPI_BIAS, st));
+    const GemvLn ln1{lw.ln1_g, lw.ln1_b, m.eps}, ln2{lw.ln2_g, lw.ln2_b, m.eps};
+    CKP(K_GEMM_QKV, launch_gemv_bf16(x, lw.qkv_wt, qkv, T, 3 * d, d, 3 * d, lw.qkv_b, nullptr, lw.qkv_s, EPI_BIAS,
+                                     st, &ln1));
     if (kv_fill) CK(launch_kv_store_bf16(qkv, static_cast<bf16 *>(c.dec.cache[l]), B, S, d, c.dec.max_len, 0, st));
-    CKP(K_ATTENTION, launch_attention_tc2(c.attn_plan, kv, o, c.d_status, st));
+    CKP(K_ATTENTION, launch_attention_short_bf16(qkv, kv, o, B, S, H, 1, st));
     if (d_mask) CKP(K_MASKED_ROWS, launch_attn_masked_rows_bf16(qkv, w.first_valid, o, B, S, H, st));
     CKP(K_GEMM_PROJ, launch_gemv_bf16(o, lw.proj_wt, x, T, d, d, d, lw.proj_b, x, lw.proj_s, EPI_BIAS_RESID, st));
-    CKP(K_LAYERNORM, launch_layernorm_bf16(x, lw.ln2_g, lw.ln2_b, a, T, d, m.eps, st));
-    CKP(K_GEMM_FC, launch_gemv_bf16(a, lw.fc_wt, u, T, ff, d, ff, lw.fc_b, nullptr, lw.fc_s, EPI_BIAS_GELU, st));
+    CKP(K_GEMM_FC,
+        launch_gemv_bf16(x, lw.fc_wt, u, T, ff, d, ff, lw.fc_b, nullptr, lw.fc_s, EPI_BIAS_GELU, st, &ln2));
     CKP(K_GEMM_MPROJ,
         launch_gemv_bf16(u, lw.mproj_wt, x, T, d, ff, d, lw.mproj_b, x, lw.mproj_s, EPI_BIAS_RESID, st));
   }
-  CKP(K_LAYERNORM, launch_layernorm_bf16(x, c.lnf_g, c.lnf_b, a, T, d, m.eps, st));
   if (kv_fill) {
-    bf16 *al = static_cast<bf16 *>(c.dec.a_last);
-    CK(cudaMemcpy2DAsync(al, sizeof(bf16) * d, a + (int64_t)(S - 1) * d, sizeof(bf16) * S * d, sizeof(bf16) * d, B,
+    bf16 *xl = static_cast<bf16 *>(c.dec.a_last);
+    CK(cudaMemcpy2DAsync(xl, sizeof(bf16) * d, x + (int64_t)(S - 1) * d, sizeof(bf16) * S * d, sizeof(bf16) * d, B,
                          cudaMemcpyDeviceToDevice, st));
-    CKP(K_LM_HEAD, launch_gemv_bf16_f32out(al, c.wte_h, d_logits, B, V, d, (int)ld_logits, st));
+    CKP(K_LM_HEAD, launch_gemv_bf16_f32out(xl, c.wte_h, d_logits, B, V, d, (int)ld_logits, st, &lnf));
     return 0;
   }
-  CKP(K_LM_HEAD, launch_gemv_bf16_f32out(a, c.wte_h, d_logits, T, V, d, (int)ld_logits, st));
+  CKP(K_LM_HEAD, launch_gemv_bf16_f32out(x, c.wte_h, d_logits, T, V, d, (int)ld_logits, st, &lnf));
   return 0;
 }
 }  // namespace
