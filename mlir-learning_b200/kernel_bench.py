@@ -106,8 +106,20 @@ def main():
         bias = torch.randn(N, device="cuda", generator=g)
         ldc = (N + 7) // 8 * 8
         C = torch.zeros(M, ldc, device="cuda", dtype=torch.float32 if args.out_f32 else torch.bfloat16)
-        fn = lambda: pkg.k_gemm_bf16(A.data_ptr(), Bw.data_ptr(), C.data_ptr(), M, N, K, ldc, args.out_f32,  # noqa
-                                     bias.data_ptr(), C.data_ptr(), args.epi, args.bn, st)
+        if args.epi in (pkg.EPI_LN_BIAS, pkg.EPI_LN_BIAS_GELU, pkg.EPI_BIAS_RESID_STATS):
+            # the folded-LayerNorm epilogues: c1 / c2 vectors and A's row statistics, or C's
+            nv = (N + 255) // 256 * 256
+            c1 = torch.randn(nv, device="cuda", generator=g)
+            c2 = torch.randn(nv, device="cuda", generator=g)
+            nseg = (max(K, N) + pkg.LN_SEG - 1) // pkg.LN_SEG
+            stats = torch.rand(M, nseg, 2, device="cuda", generator=g) + 1.0
+            fn = lambda: pkg.k_gemm_bf16_ln(A.data_ptr(), Bw.data_ptr(), C.data_ptr(), M, N, K, ldc,  # noqa
+                                            args.out_f32, bias.data_ptr(), C.data_ptr(), args.epi, args.bn,
+                                            c1.data_ptr(), c2.data_ptr(), stats.data_ptr(), stats.data_ptr(),
+                                            1e-5, st)
+        else:
+            fn = lambda: pkg.k_gemm_bf16(A.data_ptr(), Bw.data_ptr(), C.data_ptr(), M, N, K, ldc,  # noqa
+                                         args.out_f32, bias.data_ptr(), C.data_ptr(), args.epi, args.bn, st)
         ms = _time(torch, fn, args.warmup, args.iters)
         out.update(M=M, N=N, K=K, epi=args.epi, bn=args.bn, out_f32=args.out_f32, ms=ms,
                    tflops=2.0 * M * N * K / ms / 1e9)
