@@ -380,6 +380,20 @@ __device__ __forceinline__ void named_bar_sync(int id, int count) {
   asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(count) : "memory");
 }
 
+// Programmatic dependent launch.  pdl_wait() blocks until the grids this one
+// depends on have completed and their writes are visible (it returns at once
+// when the grid was launched without a programmatic dependency);
+// pdl_trigger() lets the next grid on the stream start launching once every
+// CTA of this one has issued it or exited.
+__device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+__device__ __forceinline__ void pdl_trigger() { asm volatile("griddepcontrol.launch_dependents;" ::: "memory"); }
+
+// Bulk prefetch of [p, p + bytes) into L2 by the calling thread (p 16-byte
+// aligned, bytes a multiple of 16): a hint, no data returns.
+__device__ __forceinline__ void prefetch_l2_bulk(const void *p, uint32_t bytes) {
+  asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(p), "r"(bytes) : "memory");
+}
+
 __device__ __forceinline__ float warp_sum(float v) {
 #pragma unroll
   for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);

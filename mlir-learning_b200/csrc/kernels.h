@@ -211,19 +211,27 @@ struct GemvLn {
   const float *gain = nullptr, *shift = nullptr;
   float eps = 1e-5f;
 };
+//
+// pdl (here and in the short / decode attention launchers): launch as a
+// programmatic dependent of the previous kernel on st (which must be a
+// kernel): the grid may start while that kernel runs, prefetches its weights
+// into L2, and waits (griddepcontrol.wait) for the previous grid to complete
+// before it reads anything that grid or an earlier one wrote.  Environment
+// GPT2_PDL=0 turns it off.
 cudaError_t launch_gemv_f32(const float *x, const float *W, float *y, int M, int N, int K, int ldy, const float *bias,
-                            const float *resid, int epi, cudaStream_t st, const GemvLn *ln = nullptr);
+                            const float *resid, int epi, cudaStream_t st, const GemvLn *ln = nullptr,
+                            bool pdl = false);
 cudaError_t launch_gemv_bf16(const bf16 *x, const bf16 *W, bf16 *y, int M, int N, int K, int ldy, const float *bias,
                              const bf16 *resid, const float *scale, int epi, cudaStream_t st,
-                             const GemvLn *ln = nullptr);
+                             const GemvLn *ln = nullptr, bool pdl = false);
 cudaError_t launch_gemv_bf16_f32out(const bf16 *x, const bf16 *W, float *y, int M, int N, int K, int ldy,
-                                    cudaStream_t st, const GemvLn *ln = nullptr);
+                                    cudaStream_t st, const GemvLn *ln = nullptr, bool pdl = false);
 // Attention of sequences of S <= 16 tokens (one warp per query row); rows
 // with no attendable key are left for launch_attn_masked_rows_*.
 cudaError_t launch_attention_short_f32(const float *qkv, const uint8_t *key_valid, float *o, int B, int S, int H,
-                                      int causal, cudaStream_t st);
+                                      int causal, cudaStream_t st, bool pdl = false);
 cudaError_t launch_attention_short_bf16(const bf16 *qkv, const uint8_t *key_valid, bf16 *o, int B, int S, int H,
-                                       int causal, cudaStream_t st);
+                                       int causal, cudaStream_t st, bool pdl = false);
 // cache [B][max_len][2D] (keys | values of every head) <- qkv rows of positions pos0 ..
 cudaError_t launch_kv_store_f32(const float *qkv, float *cache, int B, int S, int D, int max_len, int pos0,
                                 cudaStream_t st);
@@ -233,9 +241,9 @@ cudaError_t launch_kv_store_bf16(const bf16 *qkv, bf16 *cache, int B, int S, int
 // positions 0 .. pos - 1 plus its own key / value, which it appends; a
 // position at or past max_len records status 3 and changes nothing.
 cudaError_t launch_attn_decode_f32(const float *qkv, float *cache, float *out, int B, int H, const int *d_pos,
-                                   int max_len, int *status, cudaStream_t st);
+                                   int max_len, int *status, cudaStream_t st, bool pdl = false);
 cudaError_t launch_attn_decode_bf16(const bf16 *qkv, bf16 *cache, bf16 *out, int B, int H, const int *d_pos,
-                                    int max_len, int *status, cudaStream_t st);
+                                    int max_len, int *status, cudaStream_t st, bool pdl = false);
 cudaError_t launch_set_int(int *p, int v, cudaStream_t st);
 cudaError_t launch_add_int(int *p, int v, cudaStream_t st);
 // hist[(*d_pos - base) * B + b] = cur[b] for b < B (bounded by cap entries)

@@ -9,6 +9,7 @@
 // values.  Results equal the last position of the full forward on the same
 // sequence (up to accumulation order).
 #include <math.h>
+#include <stdlib.h>
 
 #include "../common.cuh"
 #include "../kernels.h"
@@ -35,6 +36,36 @@ __device__ __forceinline__ float from_f<float>(float v) {
 template <>
 __device__ __forceinline__ bf16 from_f<bf16>(float v) {
   return __float2bfloat16_rn(v);
+}
+
+// Programmatic dependent launch of the few-token chain (GEMV, short and
+// decode attention): on unless the environment sets GPT2_PDL=0.
+bool pdl_enabled() {
+  static const bool on = [] {
+    const char *e = getenv("GPT2_PDL");
+    return !(e && e[0] == '0');
+  }();
+  return on;
+}
+
+// kern<<<grid, block, smem, st>>>(args...), as a programmatic dependent of
+// the previous kernel on st when pdl is set (the kernel calls pdl_wait()
+// before it reads anything an earlier kernel wrote).
+template <typename... KArgs, typename... Args>
+cudaError_t launch_k(void (*kern)(KArgs...), dim3 grid, dim3 block, size_t smem, cudaStream_t st, bool pdl,
+                     Args... args) {
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = grid;
+  cfg.blockDim = block;
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = st;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = pdl && pdl_enabled() ? 1 : 0;
+  cudaError_t e = cudaLaunchKernelEx(&cfg, kern, static_cast<KArgs>(args)...);
+  return e != cudaSuccess ? e : cudaGetLastError();
 }
 
 // 16-byte chunk of a row as floats: 4 (f32) or 8 (bf16) values.
@@ -64,6 +95,7 @@ template <typename T>
 __global__ void decode_embed_kernel(const int64_t *__restrict__ tok, const T *__restrict__ wte,
                                     const T *__restrict__ wpe, T *__restrict__ x, int B, int d, int V,
                                     const int *__restrict__ d_pos, int P, int *status) {
+  pdl_trigger();  // the first GEMV may start streaming its weights
   const int b = (blockIdx.x * blockDim.x + threadIdx.x) >> 5, lane = threadIdx.x & 31;
   if (b >= B) return;
   const int64_t id = tok[b];
@@ -119,6 +151,22 @@ __global__ void __launch_bounds__(256) gemv_nk_kernel(const AT *__restrict__ x, 
   __shared__ float s_mean[16], s_rstd[16];
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int n0 = (blockIdx.x * (8 / KS) + warp / KS) * NC, ks = warp % KS;
+  {
+    // The block's weight rows (contiguous: 8 / KS column groups of NC rows)
+    // depend on no earlier kernel: they go to L2 while the previous kernel
+    // of a programmatic launch finishes, in 4 KB pieces spread over the
+    // threads.  K * sizeof(WT) is a multiple of 16, so every piece is too.
+    constexpr int ROWS = (8 / KS) * NC;
+    const int nb0 = blockIdx.x * ROWS;
+    if (nb0 < N) {
+      const char *base = reinterpret_cast<const char *>(W + (int64_t)nb0 * K);
+      const uint32_t bytes = static_cast<uint32_t>(min(ROWS, N - nb0)) * static_cast<uint32_t>(K) * sizeof(WT);
+      for (uint32_t off = threadIdx.x * 4096u; off < bytes; off += 256u * 4096u)
+        prefetch_l2_bulk(base + off, min(4096u, bytes - off));
+    }
+  }
+  pdl_wait();     // x, resid and y belong to earlier kernels
+  pdl_trigger();  // the next kernel may start its own weight prefetch
   float mean[MMAX], rstd[MMAX];
   if (LNP) {
     for (int m = warp; m < M; m += 8) {
@@ -217,6 +265,8 @@ template <typename T>
 __global__ void __launch_bounds__(128) attn_short_kernel(const T *__restrict__ qkv, const uint8_t *__restrict__ key_valid,
                                                          T *__restrict__ o, int B, int S, int H, int causal) {
   constexpr int DH = 64, SMAX = 16;
+  pdl_wait();
+  pdl_trigger();
   const int wid = (blockIdx.x * blockDim.x + threadIdx.x) >> 5, lane = threadIdx.x & 31;
   if (wid >= B * H * S) return;
   const int i = wid % S, h = (wid / S) % H, b = wid / (S * H);
@@ -277,6 +327,8 @@ __global__ void __launch_bounds__(128) attn_decode_kernel(const T *__restrict__ 
                                                           int max_len, int *status) {
   constexpr int DH = 64;
   extern __shared__ float sc[];  // max(max_len, 1024) floats: the scores, then partial output rows
+  pdl_wait();
+  pdl_trigger();
   const int h = blockIdx.x, b = blockIdx.y, tid = threadIdx.x;
   const int pos = *d_pos;
   if (pos < 0 || pos >= max_len) {  // the cache is full: report, touch nothing
@@ -413,20 +465,18 @@ __global__ void transpose_f32_kernel(const float *__restrict__ src, float *__res
 
 template <typename WT, typename AT, typename OT, bool EXACT, int MMAX, int KS>
 cudaError_t gemv_launch(const AT *x, const WT *W, OT *y, int M, int N, int K, int ldy, const float *bias,
-                        const OT *resid, const float *scale, int epi, const GemvLn *ln, cudaStream_t st) {
+                        const OT *resid, const float *scale, int epi, const GemvLn *ln, cudaStream_t st, bool pdl) {
   constexpr int NC = 32 / MMAX, GROUPS_PER_BLOCK = 8 / KS;
   const int groups = (N + NC - 1) / NC;
   const int blocks = (groups + GROUPS_PER_BLOCK - 1) / GROUPS_PER_BLOCK;
-#define GEMV_CASE(E)                                                                                     \
-  case E:                                                                                                \
-    gemv_nk_kernel<WT, AT, OT, E, EXACT, MMAX, KS, false><<<blocks, 256, 0, st>>>(                       \
-        x, W, y, M, N, K, ldy, bias, resid, scale, nullptr, nullptr, 0.f);                               \
-    break;
-#define GEMV_LN_CASE(E)                                                                                  \
-  case E:                                                                                                \
-    gemv_nk_kernel<WT, AT, OT, E, EXACT, MMAX, KS, true><<<blocks, 256, 0, st>>>(                        \
-        x, W, y, M, N, K, ldy, bias, resid, scale, ln->gain, ln->shift, ln->eps);                        \
-    break;
+#define GEMV_CASE(E)                                                                                          \
+  case E:                                                                                                     \
+    return launch_k(gemv_nk_kernel<WT, AT, OT, E, EXACT, MMAX, KS, false>, dim3(blocks), dim3(256), 0, st, pdl, \
+                    x, W, y, M, N, K, ldy, bias, resid, scale, nullptr, nullptr, 0.f);
+#define GEMV_LN_CASE(E)                                                                                       \
+  case E:                                                                                                     \
+    return launch_k(gemv_nk_kernel<WT, AT, OT, E, EXACT, MMAX, KS, true>, dim3(blocks), dim3(256), 0, st, pdl,  \
+                    x, W, y, M, N, K, ldy, bias, resid, scale, ln->gain, ln->shift, ln->eps);
   if (ln) {
     // A LayerNorm ahead of the product: the QKV, fc and lm_head inputs.
     switch (epi) {
@@ -436,7 +486,6 @@ cudaError_t gemv_launch(const AT *x, const WT *W, OT *y, int M, int N, int K, in
       default:
         return cudaErrorInvalidValue;
     }
-    return cudaGetLastError();
   }
   switch (epi) {
     GEMV_CASE(EPI_NONE)
@@ -449,12 +498,11 @@ cudaError_t gemv_launch(const AT *x, const WT *W, OT *y, int M, int N, int K, in
   }
 #undef GEMV_CASE
 #undef GEMV_LN_CASE
-  return cudaGetLastError();
 }
 
 template <typename WT, typename AT, typename OT, bool EXACT, int MMAX>
 cudaError_t gemv_ks(const AT *x, const WT *W, OT *y, int M, int N, int K, int ldy, const float *bias,
-                    const OT *resid, const float *scale, int epi, const GemvLn *ln, cudaStream_t st) {
+                    const OT *resid, const float *scale, int epi, const GemvLn *ln, cudaStream_t st, bool pdl) {
   // Split k over KS warps until about 4096 warps stream the matrix (a few
   // dozen per SM keep enough loads in flight), with at least one 16-byte step
   // of k per lane for every warp.
@@ -464,23 +512,28 @@ cudaError_t gemv_ks(const AT *x, const WT *W, OT *y, int M, int N, int K, int ld
   int ks = 1;
   while (ks < 8 && groups * ks < 4096 && 2 * ks <= steps) ks *= 2;
   switch (ks) {
-    case 1: return gemv_launch<WT, AT, OT, EXACT, MMAX, 1>(x, W, y, M, N, K, ldy, bias, resid, scale, epi, ln, st);
-    case 2: return gemv_launch<WT, AT, OT, EXACT, MMAX, 2>(x, W, y, M, N, K, ldy, bias, resid, scale, epi, ln, st);
-    case 4: return gemv_launch<WT, AT, OT, EXACT, MMAX, 4>(x, W, y, M, N, K, ldy, bias, resid, scale, epi, ln, st);
-    default: return gemv_launch<WT, AT, OT, EXACT, MMAX, 8>(x, W, y, M, N, K, ldy, bias, resid, scale, epi, ln, st);
+    case 1:
+      return gemv_launch<WT, AT, OT, EXACT, MMAX, 1>(x, W, y, M, N, K, ldy, bias, resid, scale, epi, ln, st, pdl);
+    case 2:
+      return gemv_launch<WT, AT, OT, EXACT, MMAX, 2>(x, W, y, M, N, K, ldy, bias, resid, scale, epi, ln, st, pdl);
+    case 4:
+      return gemv_launch<WT, AT, OT, EXACT, MMAX, 4>(x, W, y, M, N, K, ldy, bias, resid, scale, epi, ln, st, pdl);
+    default:
+      return gemv_launch<WT, AT, OT, EXACT, MMAX, 8>(x, W, y, M, N, K, ldy, bias, resid, scale, epi, ln, st, pdl);
   }
 }
 
 // Accumulators sized to the rows: 4, 8 or 16 (8, 4 or 2 columns per warp).
 template <typename WT, typename AT, typename OT, bool EXACT>
 cudaError_t gemv_dispatch(const AT *x, const WT *W, OT *y, int M, int N, int K, int ldy, const float *bias,
-                          const OT *resid, const float *scale, int epi, const GemvLn *ln, cudaStream_t st) {
+                          const OT *resid, const float *scale, int epi, const GemvLn *ln, cudaStream_t st,
+                          bool pdl) {
   if (ln && (!ln->gain || !ln->shift || K % 4 || !(ln->eps > 0.f) || (reinterpret_cast<uintptr_t>(ln->gain) & 15) ||
              (reinterpret_cast<uintptr_t>(ln->shift) & 15)))
     return cudaErrorInvalidValue;  // the gain and shift are read as 16-byte vectors
-  if (M <= 4) return gemv_ks<WT, AT, OT, EXACT, 4>(x, W, y, M, N, K, ldy, bias, resid, scale, epi, ln, st);
-  if (M <= 8) return gemv_ks<WT, AT, OT, EXACT, 8>(x, W, y, M, N, K, ldy, bias, resid, scale, epi, ln, st);
-  return gemv_ks<WT, AT, OT, EXACT, 16>(x, W, y, M, N, K, ldy, bias, resid, scale, epi, ln, st);
+  if (M <= 4) return gemv_ks<WT, AT, OT, EXACT, 4>(x, W, y, M, N, K, ldy, bias, resid, scale, epi, ln, st, pdl);
+  if (M <= 8) return gemv_ks<WT, AT, OT, EXACT, 8>(x, W, y, M, N, K, ldy, bias, resid, scale, epi, ln, st, pdl);
+  return gemv_ks<WT, AT, OT, EXACT, 16>(x, W, y, M, N, K, ldy, bias, resid, scale, epi, ln, st, pdl);
 }
 }  // namespace
 
@@ -496,34 +549,36 @@ cudaError_t launch_decode_embed_bf16(const int64_t *tok, const bf16 *wte, const 
 }
 
 cudaError_t launch_gemv_f32(const float *x, const float *W, float *y, int M, int N, int K, int ldy, const float *bias,
-                            const float *resid, int epi, cudaStream_t st, const GemvLn *ln) {
+                            const float *resid, int epi, cudaStream_t st, const GemvLn *ln, bool pdl) {
   if (M < 1 || M > 16 || K % 4 || ldy < N) return cudaErrorInvalidValue;
-  return gemv_dispatch<float, float, float, true>(x, W, y, M, N, K, ldy, bias, resid, nullptr, epi, ln, st);
+  return gemv_dispatch<float, float, float, true>(x, W, y, M, N, K, ldy, bias, resid, nullptr, epi, ln, st, pdl);
 }
 cudaError_t launch_gemv_bf16(const bf16 *x, const bf16 *W, bf16 *y, int M, int N, int K, int ldy, const float *bias,
-                             const bf16 *resid, const float *scale, int epi, cudaStream_t st, const GemvLn *ln) {
+                             const bf16 *resid, const float *scale, int epi, cudaStream_t st, const GemvLn *ln,
+                             bool pdl) {
   if (M < 1 || M > 16 || K % 8 || ldy < N) return cudaErrorInvalidValue;
-  return gemv_dispatch<bf16, bf16, bf16, false>(x, W, y, M, N, K, ldy, bias, resid, scale, epi, ln, st);
+  return gemv_dispatch<bf16, bf16, bf16, false>(x, W, y, M, N, K, ldy, bias, resid, scale, epi, ln, st, pdl);
 }
 cudaError_t launch_gemv_bf16_f32out(const bf16 *x, const bf16 *W, float *y, int M, int N, int K, int ldy,
-                                    cudaStream_t st, const GemvLn *ln) {
+                                    cudaStream_t st, const GemvLn *ln, bool pdl) {
   if (M < 1 || M > 16 || K % 8 || ldy < N) return cudaErrorInvalidValue;
-  return gemv_dispatch<bf16, bf16, float, false>(x, W, y, M, N, K, ldy, nullptr, nullptr, nullptr, EPI_NONE, ln, st);
+  return gemv_dispatch<bf16, bf16, float, false>(x, W, y, M, N, K, ldy, nullptr, nullptr, nullptr, EPI_NONE, ln, st,
+                                                 pdl);
 }
 
 cudaError_t launch_attention_short_f32(const float *qkv, const uint8_t *key_valid, float *o, int B, int S, int H,
-                                      int causal, cudaStream_t st) {
+                                      int causal, cudaStream_t st, bool pdl) {
   if (S < 1 || S > 16) return cudaErrorInvalidValue;
   const int warps = B * H * S;
-  attn_short_kernel<float><<<(warps + 3) / 4, 128, 0, st>>>(qkv, key_valid, o, B, S, H, causal);
-  return cudaGetLastError();
+  return launch_k(attn_short_kernel<float>, dim3((warps + 3) / 4), dim3(128), 0, st, pdl, qkv, key_valid, o, B, S, H,
+                  causal);
 }
 cudaError_t launch_attention_short_bf16(const bf16 *qkv, const uint8_t *key_valid, bf16 *o, int B, int S, int H,
-                                       int causal, cudaStream_t st) {
+                                       int causal, cudaStream_t st, bool pdl) {
   if (S < 1 || S > 16) return cudaErrorInvalidValue;
   const int warps = B * H * S;
-  attn_short_kernel<bf16><<<(warps + 3) / 4, 128, 0, st>>>(qkv, key_valid, o, B, S, H, causal);
-  return cudaGetLastError();
+  return launch_k(attn_short_kernel<bf16>, dim3((warps + 3) / 4), dim3(128), 0, st, pdl, qkv, key_valid, o, B, S, H,
+                  causal);
 }
 
 cudaError_t launch_kv_store_f32(const float *qkv, float *cache, int B, int S, int D, int max_len, int pos0,
@@ -538,20 +593,18 @@ cudaError_t launch_kv_store_bf16(const bf16 *qkv, bf16 *cache, int B, int S, int
 }
 
 cudaError_t launch_attn_decode_f32(const float *qkv, float *cache, float *out, int B, int H, const int *d_pos,
-                                   int max_len, int *status, cudaStream_t st) {
+                                   int max_len, int *status, cudaStream_t st, bool pdl) {
   if (max_len < 1 || max_len > 8192) return cudaErrorInvalidValue;
   const int sm = max_len > 1024 ? max_len : 1024;  // scores, then the key groups' partial rows
-  attn_decode_kernel<float, true><<<dim3(H, B), 128, sizeof(float) * sm, st>>>(qkv, cache, out, H, d_pos, max_len,
-                                                                                status);
-  return cudaGetLastError();
+  return launch_k(attn_decode_kernel<float, true>, dim3(H, B), dim3(128), sizeof(float) * sm, st, pdl, qkv, cache,
+                  out, H, d_pos, max_len, status);
 }
 cudaError_t launch_attn_decode_bf16(const bf16 *qkv, bf16 *cache, bf16 *out, int B, int H, const int *d_pos,
-                                    int max_len, int *status, cudaStream_t st) {
+                                    int max_len, int *status, cudaStream_t st, bool pdl) {
   if (max_len < 1 || max_len > 8192) return cudaErrorInvalidValue;
   const int sm = max_len > 1024 ? max_len : 1024;  // scores, then the key groups' partial rows
-  attn_decode_kernel<bf16, false><<<dim3(H, B), 128, sizeof(float) * sm, st>>>(qkv, cache, out, H, d_pos, max_len,
-                                                                               status);
-  return cudaGetLastError();
+  return launch_k(attn_decode_kernel<bf16, false>, dim3(H, B), dim3(128), sizeof(float) * sm, st, pdl, qkv, cache,
+                  out, H, d_pos, max_len, status);
 }
 
 namespace {

@@ -52,6 +52,7 @@ cudaError_t launch_seq_info(const int64_t *mask, int B, int S, int *first_valid,
 __global__ void embed_f32_kernel(const int64_t *__restrict__ ids, const float *__restrict__ wte,
                                  const float *__restrict__ wpe, float *__restrict__ x, int T, int S, int d, int V,
                                  int *status) {
+  pdl_trigger();  // a programmatic dependent (the first GEMV of a few-token forward) may start
   const int warp = (blockIdx.x * blockDim.x + threadIdx.x) >> 5;
   const int lane = threadIdx.x & 31;
   if (warp >= T) return;
@@ -70,6 +71,7 @@ __global__ void embed_f32_kernel(const int64_t *__restrict__ ids, const float *_
 __global__ void embed_bf16_kernel(const int64_t *__restrict__ ids, const bf16 *__restrict__ wte,
                                   const bf16 *__restrict__ wpe, bf16 *__restrict__ x, int T, int S, int d, int V,
                                   int *status, float2 *__restrict__ stats) {
+  pdl_trigger();  // a programmatic dependent (the first GEMV of a few-token forward) may start
   const int warp = (blockIdx.x * blockDim.x + threadIdx.x) >> 5;
   const int lane = threadIdx.x & 31;
   if (warp >= T) return;

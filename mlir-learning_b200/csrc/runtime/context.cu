@@ -451,6 +451,10 @@ int launch_forward_few(Context &c, const int64_t *d_ids, const uint8_t *kv, cons
   const GemvLn lnf{c.lnf_g, c.lnf_b, m.eps};
   // ln_1, ln_2 and ln_f run inside the GEMVs that read them (GemvLn); the
   // attention of these short sequences is one warp per query row.
+  // Every GEMV and attention launch here follows a kernel, so it can be a
+  // programmatic dependent of it (its weight prefetch overlaps the previous
+  // kernel); not in a profiled step, whose events bracket each kernel.
+  const bool pdl = !c.prof.on;
   if (c.dtype == 0) {
     float *x = static_cast<float *>(w.x), *qkv = static_cast<float *>(w.qkv), *o = static_cast<float *>(w.o),
           *u = static_cast<float *>(w.u);
@@ -459,14 +463,14 @@ int launch_forward_few(Context &c, const int64_t *d_ids, const uint8_t *kv, cons
       const LayerWeights &lw = c.layers[l];
       float *const *wt = &c.dec.wt[4 * l];
       const GemvLn ln1{lw.ln1_g, lw.ln1_b, m.eps}, ln2{lw.ln2_g, lw.ln2_b, m.eps};
-      CKP(K_GEMM_QKV, launch_gemv_f32(x, wt[0], qkv, T, 3 * d, d, 3 * d, lw.qkv_b, nullptr, EPI_BIAS, st, &ln1));
+      CKP(K_GEMM_QKV, launch_gemv_f32(x, wt[0], qkv, T, 3 * d, d, 3 * d, lw.qkv_b, nullptr, EPI_BIAS, st, &ln1, pdl));
       if (kv_fill)
         CK(launch_kv_store_f32(qkv, static_cast<float *>(c.dec.cache[l]), B, S, d, c.dec.max_len, 0, st));
-      CKP(K_ATTENTION, launch_attention_short_f32(qkv, kv, o, B, S, H, 1, st));
+      CKP(K_ATTENTION, launch_attention_short_f32(qkv, kv, o, B, S, H, 1, st, pdl));
       if (d_mask) CKP(K_MASKED_ROWS, launch_attn_masked_rows_f32(qkv, w.first_valid, o, B, S, H, st));
-      CKP(K_GEMM_PROJ, launch_gemv_f32(o, wt[1], x, T, d, d, d, lw.proj_b, x, EPI_BIAS_RESID, st));
-      CKP(K_GEMM_FC, launch_gemv_f32(x, wt[2], u, T, ff, d, ff, lw.fc_b, nullptr, EPI_BIAS_GELU, st, &ln2));
-      CKP(K_GEMM_MPROJ, launch_gemv_f32(u, wt[3], x, T, d, ff, d, lw.mproj_b, x, EPI_BIAS_RESID, st));
+      CKP(K_GEMM_PROJ, launch_gemv_f32(o, wt[1], x, T, d, d, d, lw.proj_b, x, EPI_BIAS_RESID, st, nullptr, pdl));
+      CKP(K_GEMM_FC, launch_gemv_f32(x, wt[2], u, T, ff, d, ff, lw.fc_b, nullptr, EPI_BIAS_GELU, st, &ln2, pdl));
+      CKP(K_GEMM_MPROJ, launch_gemv_f32(u, wt[3], x, T, d, ff, d, lw.mproj_b, x, EPI_BIAS_RESID, st, nullptr, pdl));
     }
     if (kv_fill) {
       float *xl = static_cast<float *>(c.dec.a_last);
@@ -477,7 +481,7 @@ int launch_forward_few(Context &c, const int64_t *d_ids, const uint8_t *kv, cons
       return 0;
     }
     CKP(K_LM_HEAD,
-        launch_gemv_f32(x, c.wte, d_logits, T, V, d, (int)ld_logits, nullptr, nullptr, EPI_NONE, st, &lnf));
+        launch_gemv_f32(x, c.wte, d_logits, T, V, d, (int)ld_logits, nullptr, nullptr, EPI_NONE, st, &lnf, pdl));
     return 0;
   }
   bf16 *x = static_cast<bf16 *>(w.x), *qkv = static_cast<bf16 *>(w.qkv), *o = static_cast<bf16 *>(w.o),
@@ -487,15 +491,15 @@ int launch_forward_few(Context &c, const int64_t *d_ids, const uint8_t *kv, cons
     const LayerWeights &lw = c.layers[l];
     const GemvLn ln1{lw.ln1_g, lw.ln1_b, m.eps}, ln2{lw.ln2_g, lw.ln2_b, m.eps};
     CKP(K_GEMM_QKV, launch_gemv_bf16(x, lw.qkv_wt, qkv, T, 3 * d, d, 3 * d, lw.qkv_b, nullptr, lw.qkv_s, EPI_BIAS,
-                                     st, &ln1));
+                                     st, &ln1, pdl));
     if (kv_fill) CK(launch_kv_store_bf16(qkv, static_cast<bf16 *>(c.dec.cache[l]), B, S, d, c.dec.max_len, 0, st));
-    CKP(K_ATTENTION, launch_attention_short_bf16(qkv, kv, o, B, S, H, 1, st));
+    CKP(K_ATTENTION, launch_attention_short_bf16(qkv, kv, o, B, S, H, 1, st, pdl));
     if (d_mask) CKP(K_MASKED_ROWS, launch_attn_masked_rows_bf16(qkv, w.first_valid, o, B, S, H, st));
-    CKP(K_GEMM_PROJ, launch_gemv_bf16(o, lw.proj_wt, x, T, d, d, d, lw.proj_b, x, lw.proj_s, EPI_BIAS_RESID, st));
+    CKP(K_GEMM_PROJ, launch_gemv_bf16(o, lw.proj_wt, x, T, d, d, d, lw.proj_b, x, lw.proj_s, EPI_BIAS_RESID, st, nullptr, pdl));
     CKP(K_GEMM_FC,
-        launch_gemv_bf16(x, lw.fc_wt, u, T, ff, d, ff, lw.fc_b, nullptr, lw.fc_s, EPI_BIAS_GELU, st, &ln2));
+        launch_gemv_bf16(x, lw.fc_wt, u, T, ff, d, ff, lw.fc_b, nullptr, lw.fc_s, EPI_BIAS_GELU, st, &ln2, pdl));
     CKP(K_GEMM_MPROJ,
-        launch_gemv_bf16(u, lw.mproj_wt, x, T, d, ff, d, lw.mproj_b, x, lw.mproj_s, EPI_BIAS_RESID, st));
+        launch_gemv_bf16(u, lw.mproj_wt, x, T, d, ff, d, lw.mproj_b, x, lw.mproj_s, EPI_BIAS_RESID, st, nullptr, pdl));
   }
   if (kv_fill) {
     bf16 *xl = static_cast<bf16 *>(c.dec.a_last);
@@ -504,7 +508,7 @@ int launch_forward_few(Context &c, const int64_t *d_ids, const uint8_t *kv, cons
     CKP(K_LM_HEAD, launch_gemv_bf16_f32out(xl, c.wte_h, d_logits, B, V, d, (int)ld_logits, st, &lnf));
     return 0;
   }
-  CKP(K_LM_HEAD, launch_gemv_bf16_f32out(x, c.wte_h, d_logits, T, V, d, (int)ld_logits, st, &lnf));
+  CKP(K_LM_HEAD, launch_gemv_bf16_f32out(x, c.wte_h, d_logits, T, V, d, (int)ld_logits, st, &lnf, pdl));
   return 0;
 }
 }  // namespace

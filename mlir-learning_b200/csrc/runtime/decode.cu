@@ -117,6 +117,9 @@ int launch_step(Context &c, const int64_t *d_tokens, int B, float *d_logits, int
   DecodeState &d = c.dec;
   const int D = m.n_embd, ff = m.n_inner, H = m.n_head, V = m.vocab;
   const int *dp = d.d_pos;
+  // Each GEMV and attention launch follows a kernel: a programmatic
+  // dependent of it (not in a profiled step, whose events bracket each kernel).
+  const bool pdl = !c.prof.on;
 
   if (c.dtype == 0) {
     float *x = static_cast<float *>(d.x), *qkv = static_cast<float *>(d.qkv),
@@ -127,15 +130,15 @@ int launch_step(Context &c, const int64_t *d_tokens, int B, float *d_logits, int
       const LayerWeights &lw = c.layers[l];
       float *const *wt = &d.wt[4 * l];
       const GemvLn ln1{lw.ln1_g, lw.ln1_b, m.eps}, ln2{lw.ln2_g, lw.ln2_b, m.eps};
-      CKP(K_GEMM_QKV, launch_gemv_f32(x, wt[0], qkv, B, 3 * D, D, 3 * D, lw.qkv_b, nullptr, EPI_BIAS, st, &ln1));
+      CKP(K_GEMM_QKV, launch_gemv_f32(x, wt[0], qkv, B, 3 * D, D, 3 * D, lw.qkv_b, nullptr, EPI_BIAS, st, &ln1, pdl));
       CKP(K_ATTENTION,
-          launch_attn_decode_f32(qkv, static_cast<float *>(d.cache[l]), o, B, H, dp, d.max_len, c.d_status, st));
-      CKP(K_GEMM_PROJ, launch_gemv_f32(o, wt[1], x, B, D, D, D, lw.proj_b, x, EPI_BIAS_RESID, st));
-      CKP(K_GEMM_FC, launch_gemv_f32(x, wt[2], u, B, ff, D, ff, lw.fc_b, nullptr, EPI_BIAS_GELU, st, &ln2));
-      CKP(K_GEMM_MPROJ, launch_gemv_f32(u, wt[3], x, B, D, ff, D, lw.mproj_b, x, EPI_BIAS_RESID, st));
+          launch_attn_decode_f32(qkv, static_cast<float *>(d.cache[l]), o, B, H, dp, d.max_len, c.d_status, st, pdl));
+      CKP(K_GEMM_PROJ, launch_gemv_f32(o, wt[1], x, B, D, D, D, lw.proj_b, x, EPI_BIAS_RESID, st, nullptr, pdl));
+      CKP(K_GEMM_FC, launch_gemv_f32(x, wt[2], u, B, ff, D, ff, lw.fc_b, nullptr, EPI_BIAS_GELU, st, &ln2, pdl));
+      CKP(K_GEMM_MPROJ, launch_gemv_f32(u, wt[3], x, B, D, ff, D, lw.mproj_b, x, EPI_BIAS_RESID, st, nullptr, pdl));
     }
     const GemvLn lnf{c.lnf_g, c.lnf_b, m.eps};
-    CKP(K_LM_HEAD, launch_gemv_f32(x, c.wte, d_logits, B, V, D, (int)ld, nullptr, nullptr, EPI_NONE, st, &lnf));
+    CKP(K_LM_HEAD, launch_gemv_f32(x, c.wte, d_logits, B, V, D, (int)ld, nullptr, nullptr, EPI_NONE, st, &lnf, pdl));
   } else {
     bf16 *x = static_cast<bf16 *>(d.x), *qkv = static_cast<bf16 *>(d.qkv),
          *o = static_cast<bf16 *>(d.o), *u = static_cast<bf16 *>(d.u);
@@ -144,16 +147,16 @@ int launch_step(Context &c, const int64_t *d_tokens, int B, float *d_logits, int
       const LayerWeights &lw = c.layers[l];
       const GemvLn ln1{lw.ln1_g, lw.ln1_b, m.eps}, ln2{lw.ln2_g, lw.ln2_b, m.eps};
       CKP(K_GEMM_QKV, launch_gemv_bf16(x, lw.qkv_wt, qkv, B, 3 * D, D, 3 * D, lw.qkv_b, nullptr, lw.qkv_s, EPI_BIAS,
-                                       st, &ln1));
-      CKP(K_ATTENTION, launch_attn_decode_bf16(qkv, static_cast<bf16 *>(d.cache[l]), o, B, H, dp, d.max_len, c.d_status, st));
-      CKP(K_GEMM_PROJ, launch_gemv_bf16(o, lw.proj_wt, x, B, D, D, D, lw.proj_b, x, lw.proj_s, EPI_BIAS_RESID, st));
+                                       st, &ln1, pdl));
+      CKP(K_ATTENTION, launch_attn_decode_bf16(qkv, static_cast<bf16 *>(d.cache[l]), o, B, H, dp, d.max_len, c.d_status, st, pdl));
+      CKP(K_GEMM_PROJ, launch_gemv_bf16(o, lw.proj_wt, x, B, D, D, D, lw.proj_b, x, lw.proj_s, EPI_BIAS_RESID, st, nullptr, pdl));
       CKP(K_GEMM_FC, launch_gemv_bf16(x, lw.fc_wt, u, B, ff, D, ff, lw.fc_b, nullptr, lw.fc_s, EPI_BIAS_GELU, st,
-                                      &ln2));
+                                      &ln2, pdl));
       CKP(K_GEMM_MPROJ,
-          launch_gemv_bf16(u, lw.mproj_wt, x, B, D, ff, D, lw.mproj_b, x, lw.mproj_s, EPI_BIAS_RESID, st));
+          launch_gemv_bf16(u, lw.mproj_wt, x, B, D, ff, D, lw.mproj_b, x, lw.mproj_s, EPI_BIAS_RESID, st, nullptr, pdl));
     }
     const GemvLn lnf{c.lnf_g, c.lnf_b, m.eps};
-    CKP(K_LM_HEAD, launch_gemv_bf16_f32out(x, c.wte_h, d_logits, B, V, D, (int)ld, st, &lnf));
+    CKP(K_LM_HEAD, launch_gemv_bf16_f32out(x, c.wte_h, d_logits, B, V, D, (int)ld, st, &lnf, pdl));
   }
   CK(launch_add_int(d.d_pos, 1, st));
   return 0;
