@@ -32,8 +32,11 @@
 //                scale folded in, running sum in FP32, P packed to bf16 pairs
 //                and stored into its TMEM columns; the epilogue divides O by
 //                the row sum and writes bf16 through shared memory and a TMA
-//                store.  The two tiles' exponential passes take turns on
-//                each sub-partition's MUFU unit.
+//                store.  The two tiles' softmax warps of a sub-partition
+//                issue independently: the kernel is bound by instruction
+//                issue and latency, not by the MUFU unit (measured: making
+//                them take turns on it, or moving a quarter of the
+//                exponentials to an FMA-pipe polynomial, was slower).
 // TMEM (512 columns): S0 [0,128), S1 [128,256), O0 [256,320), O1 [320,384),
 // P0 [384,448), P1 [448,512) (P: 128 bf16 per row = 64 columns).
 // Every barrier wait is bounded; a timeout records status 2 and unwinds.
@@ -60,8 +63,8 @@ struct Smem2 {
   static constexpr int OST = V + ST * TILE_BYTES;  // [tile][quarter] output staging (128-byte swizzle)
   static constexpr int BARS = OST + 8 * OST_BYTES;
   // q_full[2], q_empty[2], k_full[ST], v_full[ST], k_empty[ST], v_empty[ST], s_full[2], s_free[2], p_full[2],
-  // o_done[2], drain, mufu[2][4]
-  static constexpr int NBARS = 4 + 4 * ST + 8 + 1 + 8;
+  // o_done[2], drain
+  static constexpr int NBARS = 4 + 4 * ST + 8 + 1;
   static constexpr int MISC = BARS + NBARS * 8;
   static constexpr int TOTAL = MISC + 16;
   static constexpr int ALLOC = TOTAL + 1024;
@@ -72,33 +75,6 @@ __device__ __forceinline__ float ex2(float x) {
   asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
   return y;
 }
-// 2^x for a pair on the FMA pipe, to take load off the MUFU unit: Cody-Waite
-// split x = n + f with the round-to-nearest magic constant 1.5 * 2^23
-// (f in [-0.5, 0.5]), 2^f by a degree-3 polynomial fitted here for minimum
-// relative error on that interval (|rel err| < 1e-4, below the bf16 rounding
-// of P), 2^n added to the exponent field.  x <= -125 (masked or negligible
-// terms) gives exactly 0.
-constexpr int kPolyPairs = 4;  // of every 16 score pairs, this many take the polynomial path
-__device__ __forceinline__ uint64_t exp2_poly2(uint64_t x2) {
-  float x0, x1;
-  up2(x2, x0, x1);
-  const float c0 = fmaxf(x0, -126.f), c1 = fmaxf(x1, -126.f);
-  const uint64_t xc = pk2(c0, c1);
-  const uint64_t t = add2(xc, pk2(12582912.f, 12582912.f));
-  const uint64_t r = add2(t, pk2(-12582912.f, -12582912.f));
-  const uint64_t f = fma2(r, pk2(-1.f, -1.f), xc);
-  uint64_t p = fma2(pk2(0.0551716610789299f, 0.0551716610789299f), f, pk2(0.24261115491390228f, 0.24261115491390228f));
-  p = fma2(p, f, pk2(0.6932609677314758f, 0.6932609677314758f));
-  p = fma2(p, f, pk2(0.9999280571937561f, 0.9999280571937561f));
-  float t0, t1, p0, p1;
-  up2(t, t0, t1);
-  up2(p, p0, p1);
-  // (bits(t) - bits(1.5 * 2^23)) << 23 == bits(t) << 23 modulo 2^32
-  const float e0 = __uint_as_float(__float_as_uint(p0) + (__float_as_uint(t0) << 23));
-  const float e1 = __uint_as_float(__float_as_uint(p1) + (__float_as_uint(t1) << 23));
-  return pk2(x0 <= -125.f ? 0.f : e0, x1 <= -125.f ? 0.f : e1);
-}
-
 __device__ __forceinline__ float max3(float a, float b, float c) {
   float d;
   asm("max.f32 %0, %1, %2, %3;" : "=f"(d) : "f"(a), "f"(b), "f"(c));
@@ -142,7 +118,6 @@ __global__ void __launch_bounds__(NTHREADS, 1)
   uint64_t *k_full = bars + 4, *v_full = k_full + ST, *k_empty = v_full + ST, *v_empty = k_empty + ST;
   uint64_t *s_full = v_empty + ST, *s_free = s_full + 2, *p_full = s_free + 2, *o_done = p_full + 2;
   uint64_t *drain = o_done + 2;
-  uint64_t *mufu = drain + 1;  // [tile * 4 + quarter]: that warp finished issuing a step's exponentials
   uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(sm + Smem2::MISC);
   volatile int *abort_flag = reinterpret_cast<volatile int *>(sm + Smem2::MISC + 4);
 
@@ -167,7 +142,6 @@ __global__ void __launch_bounds__(NTHREADS, 1)
       mbar_init(&o_done[t], 1);
     }
     mbar_init(drain, 1);
-    for (int i = 0; i < 8; ++i) mbar_init(&mufu[i], 1);
     *abort_flag = 0;
     fence_mbar_init();
   }
@@ -342,7 +316,6 @@ __global__ void __launch_bounds__(NTHREADS, 1)
     const uint32_t p_tmem = tmem + lane_addr + kColP + t * 64;
     const float sl2 = 0.125f * 1.4426950408889634f;  // (1/sqrt(64)) * log2(e)
     unsigned char *ostage = sm + Smem2::OST + (t * 4 + qd) * OST_BYTES;
-    uint64_t *my_turn_done = &mufu[t * 4 + qd], *other_turn_done = &mufu[(t ^ 1) * 4 + qd];
     if (lane == 0) prefetch_tmap(&map_out);
     // A failed wait raises the abort flag; once it is up every later wait
     // returns at once, so the loop runs out without blocking.
@@ -357,12 +330,10 @@ __global__ void __launch_bounds__(NTHREADS, 1)
       __syncwarp();
       if (lane == 0) mbar_arrive(bar);
     };
-    int g_base = 0, g_other_base = 0;  // steps of this tile and of the other tile so far
+    int g_base = 0;  // steps of this tile so far
     for (int w = blockIdx.x; w < n_items; w += gridDim.x) {
       const AttnItem it = attn_item(w, S, B, H, causal, kv_end);
       const int n = it.n_kv[t];
-      const int g_other = g_other_base;
-      g_other_base += it.n_kv[t ^ 1];
       if (n == 0) continue;
       const int qrow = it.q0 + t * BQ + r;
       const uint8_t *kv_ok = key_valid ? key_valid + (int64_t)it.b * S : nullptr;
@@ -471,17 +442,6 @@ __global__ void __launch_bounds__(NTHREADS, 1)
           }
         }
         l_run *= alpha;
-        // The two tiles' exponential passes take turns on the MUFU unit of
-        // each SM sub-partition (it holds one softmax warp of each tile, the
-        // same TMEM quarter): tile 1's step j follows tile 0's step j, tile
-        // 0's step j follows tile 1's step j - 1, for the steps both tiles
-        // have.  A warp hands its turn over when three quarters of its
-        // exponentials are issued, so the other's wake-up overlaps the rest.
-        // Every step arrives once, so phase = the step's count over the
-        // launch; strict alternation keeps each side at most one phase ahead
-        // of the other's wait, so the parity waits cannot alias.
-        if (t == 1 && j < it.n_kv[0]) wait(other_turn_done, (g_other + j) & 1);
-        if (t == 0 && j > 0 && j - 1 < it.n_kv[1]) wait(other_turn_done, (g_other + j - 1) & 1);
         // p = 2^(s * scale * log2e - m): packed pairs for the scale and the sums,
         // bf16 pairs stored into P's TMEM columns 32 at a time.
         const uint64_t sl2x2 = pk2(sl2, sl2), negm2 = pk2(neg_m, neg_m);
@@ -493,19 +453,12 @@ __global__ void __launch_bounds__(NTHREADS, 1)
           for (int e2 = 0; e2 < 16; ++e2) {
             const int c = q4 * 32 + 2 * e2;
             const uint64_t x2 = fma2(pk2(__uint_as_float(sv[c]), __uint_as_float(sv[c + 1])), sl2x2, negm2);
-            float p0, p1;
-            if ((e2 & 3) * 4 >= 16 - kPolyPairs) {  // the last kPolyPairs / 4 of every 4 pairs
-              up2(exp2_poly2(x2), p0, p1);
-            } else {
-              float x0, x1;
-              up2(x2, x0, x1);
-              p0 = ex2(x0);
-              p1 = ex2(x1);
-            }
+            float x0, x1;
+            up2(x2, x0, x1);
+            const float p0 = ex2(x0), p1 = ex2(x1);
             rs2[e2 & 3] = add2(rs2[e2 & 3], pk2(p0, p1));
             pw[e2] = pack_bf16x2(p0, p1);
           }
-          if (q4 == 2) arrive(my_turn_done);
           tmem_st_32x32b_x16(p_tmem + q4 * 16, pw);
         }
         {

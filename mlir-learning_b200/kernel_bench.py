@@ -4,6 +4,7 @@ and small, single-kernel ncu captures.
 
   python mlir-learning_b200/kernel_bench.py attention --batch 64 --seq 1024 [--causal 0 --lengths uniform]
   python mlir-learning_b200/kernel_bench.py gemm --m 65536 --n 3072 --k 768 --epi 2
+  python mlir-learning_b200/kernel_bench.py gemm --dtype 0 --m 8192 --n 768 --k 3072 --epi 3
   python mlir-learning_b200/kernel_bench.py layernorm --rows 65536 --d 768
   python mlir-learning_b200/kernel_bench.py decode --batch 1 --seq 128 --new 64 --dtype 1
 
@@ -60,13 +61,15 @@ def main():
     ap.add_argument("--causal", type=int, default=1)
     ap.add_argument("--lengths", choices=["full", "uniform"], default="full",
                     help="uniform: right-padded, valid lengths uniform in [64, seq] (seeded)")
-    ap.add_argument("--dtype", type=int, default=1, help="0 f32, 1 bf16 tcgen05, 2 bf16 mma.sync (attention)")
+    ap.add_argument("--dtype", type=int, default=1,
+                    help="0 f32 (attention, gemm), 1 bf16 tcgen05, 2 bf16 mma.sync (attention)")
     ap.add_argument("--m", type=int, default=65536)
     ap.add_argument("--n", type=int, default=3072)
     ap.add_argument("--k", type=int, default=768)
     ap.add_argument("--epi", type=int, default=1)
     ap.add_argument("--bn", type=int, default=256)
     ap.add_argument("--out-f32", type=int, default=0)
+    ap.add_argument("--b-nk", type=int, default=0, help="gemm --dtype 0: B given as [N, K]")
     ap.add_argument("--rows", type=int, default=65536)
     ap.add_argument("--d", type=int, default=768)
     ap.add_argument("--warmup", type=int, default=3)
@@ -99,6 +102,18 @@ def main():
         flop = 4.0 * B * H * 64 * S * (S + 1) / 2 if args.causal else 4.0 * H * 64 * S * float(lens.sum())
         out.update(B=B, S=S, H=H, causal=args.causal, lengths=args.lengths, dtype=args.dtype, ms=ms,
                    tflops=flop / ms / 1e9, algorithmic_flop=flop)
+    elif args.kernel == "gemm" and args.dtype == 0:
+        # The exact-FP32 SIMT GEMM: B [K, N] as the FP32 forward's Conv1D weights (--b-nk 1: [N, K], the lm_head).
+        M, N, K = args.m, args.n, args.k
+        A = torch.randn(M, K, device="cuda", generator=g)
+        Bw = torch.randn(*((N, K) if args.b_nk else (K, N)), device="cuda", generator=g) * 0.05
+        bias = torch.randn(N, device="cuda", generator=g)
+        ldc = (N + 3) // 4 * 4
+        C = torch.zeros(M, ldc, device="cuda")
+        fn = lambda: pkg.k_gemm_f32(A.data_ptr(), Bw.data_ptr(), args.b_nk, C.data_ptr(), M, N, K, ldc,  # noqa
+                                    bias.data_ptr(), C.data_ptr(), args.epi, st)
+        ms = _time(torch, fn, args.warmup, args.iters)
+        out.update(M=M, N=N, K=K, epi=args.epi, b_nk=args.b_nk, dtype=0, ms=ms, tflops=2.0 * M * N * K / ms / 1e9)
     elif args.kernel == "gemm":
         M, N, K = args.m, args.n, args.k
         A = torch.randn(M, K, device="cuda", generator=g).bfloat16()

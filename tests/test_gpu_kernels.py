@@ -44,6 +44,11 @@ def _epi_ref(torch, acc, bias, resid, epi):
     (129, 3072, 768, 1, pkg.EPI_BIAS_GELU_ERF, 3072),
     (77, 50257, 768, 1, pkg.EPI_NONE, 50257),
     (64, 1000, 128, 1, pkg.EPI_NONE, 1008),
+    (130, 776, 136, 0, pkg.EPI_BIAS_RESID, 776),     # 64-wide tiles, ragged N, a half K step at the end
+    # enough tiles for 128-wide tiles: ragged M, both B layouts, a half K step
+    (9000, 2304, 768, 0, pkg.EPI_BIAS, 2304),
+    (4500, 3072, 768, 0, pkg.EPI_BIAS_GELU, 3072),
+    (9000, 1000, 136, 1, pkg.EPI_NONE, 1008),
 ])
 def test_gemm_f32(torch, M, N, K, b_nk, epi, ldc):
     g = torch.Generator(device="cuda").manual_seed(M * 7 + N)
