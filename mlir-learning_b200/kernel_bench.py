@@ -7,6 +7,7 @@ and small, single-kernel ncu captures.
   python mlir-learning_b200/kernel_bench.py gemm --dtype 0 --m 8192 --n 768 --k 3072 --epi 3
   python mlir-learning_b200/kernel_bench.py layernorm --rows 65536 --d 768
   python mlir-learning_b200/kernel_bench.py decode --batch 1 --seq 128 --new 64 --dtype 1
+  python mlir-learning_b200/kernel_bench.py forward --batch 1 --seq 5 --dtype 0
 
 Inputs are seeded random device tensors; each run does --warmup untimed and
 --iters timed launches between CUDA events on one stream and prints one JSON
@@ -53,7 +54,7 @@ def _time(torch, fn, warmup, iters):
 
 def main():
     ap = argparse.ArgumentParser()
-    ap.add_argument("kernel", choices=["attention", "gemm", "layernorm", "decode"])
+    ap.add_argument("kernel", choices=["attention", "gemm", "layernorm", "decode", "forward"])
     ap.add_argument("--new", type=int, default=64, help="decode: tokens generated per sequence")
     ap.add_argument("--batch", type=int, default=64)
     ap.add_argument("--seq", type=int, default=1024)
@@ -138,6 +139,18 @@ def main():
         ms = _time(torch, fn, args.warmup, args.iters)
         out.update(M=M, N=N, K=K, epi=args.epi, bn=args.bn, out_f32=args.out_f32, ms=ms,
                    tflops=2.0 * M * N * K / ms / 1e9)
+    elif args.kernel == "forward":
+        # The whole forward through the device entry point (repeat calls replay one CUDA graph), GPT-2 small
+        # with seeded weights; --dtype 0 FP32, 1 BF16.  Logits rows padded to a 16-byte multiple.
+        B, S = args.batch, args.seq
+        pkg.init(pkg.gpt2_small(args.dtype), 0)
+        pkg.init_seeded(1234, 0)
+        ids = torch.from_numpy(pkg.seeded_ids(B, S, 1234, 50257)).cuda()
+        ld = 50260
+        logits = torch.empty(B * S, ld, device="cuda")
+        fn = lambda: pkg.forward_device(ids.data_ptr(), None, B, S, logits.data_ptr(), ld, st)  # noqa
+        ms = _time(torch, fn, args.warmup, args.iters)
+        out.update(B=B, S=S, dtype=args.dtype, ms=ms, tokens_per_s=B * S / ms * 1e3)
     elif args.kernel == "decode":
         # Greedy generation with the KV cache on GPT-2 small (seeded weights): the time per
         # generated token is the difference between n_new and 1 new tokens, per step of B tokens.
