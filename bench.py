@@ -1,5 +1,5 @@
 """GPT-2 prefill throughput on B200: tokens/s of the GPT-2 small BF16 forward,
-batch 64 x seq 1024 (global batch; sharded over the ranks), logits resident
+batch 64 x seq 1024 (global batch, split over the ranks), logits resident
 on each shard.
 
   python bench.py [--gpus N --steps K --warmup W]        # this library
@@ -12,17 +12,22 @@ B8xS1024, 3: the BERT-base BF16 encoder B128xS512 with right-padded
 sequences of seeded lengths in [64, 512], 4: the GPT-2-XL shape with FP8
 weight-only GEMMs B32xS1024); the default is the headline workload.
 
-One step = one forward over this rank's B/N sequences (ids resident in HBM,
-FP32 logits written to HBM).  value = all ranks' tokens / max-over-ranks
-device time of the K timed steps (CUDA events on the launching stream).
-Every step reads and writes far more than the 126 MB L2 (the FP32 logits
-alone are 13.2 GB at N=1), so no separate L2 flush is done.
+One step = one forward over this rank's share of the configuration's batch
+(strong scaling by default: B/N sequences per rank; --scaling weak gives every
+rank the whole batch), ids resident in HBM, FP32 logits written to HBM.
+value = all ranks' tokens / max-over-ranks device time of the K timed steps
+(CUDA events on the launching stream).  Every step reads and writes far more
+than the 126 MB L2 (the FP32 logits alone are 13.2 GB at N=1), so no separate
+L2 flush is done.
 
 Also reported: a per-kernel event breakdown with the roofline of the
-dominant kernel, the end-to-end rate through the host-buffer C ABI
-(gpt2_forward_host: ids host->device and FP32 logits device->host inside
-the timed region), the SM clocks sampled during the timed steps, and (rank 0,
-N=1) the CPU oracle timed on one sequence of the same workload.
+dominant kernel (scaled to the timed step), the same forward with bf16
+logits, at N > 1 the forward plus the NCCL gather of every shard's logits
+into rank 0, the end-to-end rate through the drop-in gpt2_decoder (host ids
+in, a malloc'd FP32 result out, freed each step) and through
+gpt2_forward_host with pinned buffers, the SM clocks sampled during the
+timed steps, and (rank 0, N=1) the CPU oracle timed on one sequence of the
+same workload.
 """
 from __future__ import annotations
 
@@ -211,11 +216,16 @@ FP32_SIMT_NOMINAL_TFLOPS = 148 * 128 * 2 * 1.965e9 / 1e12
 
 
 def kernel_breakdown(prof: dict, work: dict, nprof: int, peaks: dict, config: int, tokens: int,
-                     ffma_tflops: float | None = None):
+                     ffma_tflops: float | None = None, timed_step_ms: float | None = None):
     """Per-kernel ms / share / rate of `nprof` profiled steps and the roofline of the dominant
-    kernel (achieved = algorithmic work per launch / average event-timed launch duration).  The
-    exact-FP32 workload (--config 1) runs on FFMA, not the tensor cores: its FLOP-bound
-    kernels are rated against the FP32 SIMT peak."""
+    kernel.  The exact-FP32 workload (--config 1) runs on FFMA, not the tensor cores: its
+    FLOP-bound kernels are rated against the FP32 SIMT peak.
+
+    The profiled steps bracket every launch with events and run at higher SM clocks than the
+    timed steps (which the 1000 W cap slows), so when timed_step_ms is given each kernel's
+    duration is also scaled to the timed step by its share of the profiled step
+    (`avg_launch_ms_at_timed_step`), and the roofline's `achieved` uses that scaled duration:
+    algorithmic work per launch / (share x timed step / launches per step)."""
     kernels = {}
     for k, (ms, n) in prof.items():
         if n == 0:
@@ -230,12 +240,18 @@ def kernel_breakdown(prof: dict, work: dict, nprof: int, peaks: dict, config: in
                 ent["gbs"] = amount / per_launch_s / 1e9
         kernels[k] = ent
     step_ms = sum(e["ms_per_step"] for e in kernels.values())
-    for e in kernels.values():
+    for k, e in kernels.items():
         e["share"] = e["ms_per_step"] / step_ms if step_ms else None
+        if timed_step_ms and step_ms:
+            e["avg_launch_ms_at_timed_step"] = e["share"] * timed_step_ms / max(1, e["launches_per_step"])
+            if k in work:
+                kind, amount = work[k]
+                rate = amount / (e["avg_launch_ms_at_timed_step"] / 1000.0)
+                e["tflops_at_timed_step" if kind == "flop" else "gbs_at_timed_step"] = rate / (1e12 if kind == "flop" else 1e9)
     dom = max(kernels, key=lambda k: kernels[k]["ms_per_step"])
     traffic = traffic_per_launch(config, dom, tokens)
     kind, amount = work.get(dom, ("flop", 0.0))
-    per_launch_s = kernels[dom]["avg_launch_ms"] / 1000.0
+    per_launch_s = kernels[dom].get("avg_launch_ms_at_timed_step", kernels[dom]["avg_launch_ms"]) / 1000.0
     if kind == "flop" and config == 1:
         achieved = amount / per_launch_s / 1e12
         peak = ffma_tflops or FP32_SIMT_NOMINAL_TFLOPS
@@ -248,7 +264,8 @@ def kernel_breakdown(prof: dict, work: dict, nprof: int, peaks: dict, config: in
         achieved = amount / per_launch_s / 1e12
         roof = {"bound": "tensor", "achieved": achieved, "peak": peaks["bf16_sus"], "unit": "TFLOP/s",
                 "frac": achieved / peaks["bf16_sus"], "traffic": traffic, "kernel": dom,
-                "peak_kind": f"bf16 sustained ({peaks['src']})", "algorithmic_per_launch": amount}
+                "peak_kind": f"bf16 sustained ({peaks['src']})", "algorithmic_per_launch": amount,
+                "time_basis": "profiled share x timed step" if timed_step_ms else "profiled launch events"}
     else:
         achieved = amount / per_launch_s / 1e9
         roof = {"bound": "hbm", "achieved": achieved, "peak": peaks["hbm_gbs"], "unit": "GB/s",
@@ -345,8 +362,13 @@ def run_reference(args, rank, world):
         "config": {"workload": CONFIGS[args.config][0], "global_batch": args.batch, "seq_len": S,
                    "sample_per_step": f"1 sequence x {S} tokens"
                    + (f" ({med} valid, the median length)" if args.config == 3 else "")},
+        # One sequence of the batch is timed per step and the rate is quoted per token: the full
+        # batch's time is extrapolated from it (sequences are independent and equally long).
+        "extrapolated": args.batch > 1,
         "cpu_baseline": {"value": value, "unit": "tokens/s", "cores": cores, "kind": "port",
-                         "sample": f"1 x {S} tokens per step; OpenBLAS sgemm ({O.blas_name().split('/')[-1]}) on "
+                         "extrapolated": args.batch > 1,
+                         "sample": f"1 x {S} tokens per step of the {args.batch}-sequence workload, extrapolated "
+                                   f"per token; OpenBLAS sgemm ({O.blas_name().split('/')[-1]}) on "
                                    f"all {cores} cores, loop nests single-threaded as the reference's CPU lowering"
                                    + (" (BERT-base encoder)" if args.config == 3 else "")},
         "e2e": {"value": value, "unit": "tokens/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
@@ -470,6 +492,128 @@ def run_bert(args, rank, world, local_rank, pkg, torch, dist):
         dist.destroy_process_group()
 
 
+def timed_steps(step, steps, stream, torch, dist, world):
+    """Runs `steps` calls of step() between CUDA events on `stream` (barrier and synchronize on
+    both sides); returns the max-over-ranks seconds."""
+    if world > 1:
+        dist.barrier()
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(stream)
+    for _ in range(steps):
+        step()
+    e1.record(stream)
+    torch.cuda.synchronize()
+    if world > 1:
+        dist.barrier()
+    return max_over_ranks(e0.elapsed_time(e1) / 1000.0, dist, "cuda")
+
+
+def e2e_decoder(pkg, ids_h, steps, dist, world):
+    """End to end through the drop-in symbol itself, called exactly as the reference's host program
+    calls it (src/gpt/gpt2_call.cpp:62-68, :93-94): decomposed int64 memrefs of host ids and an
+    all-ones mask in, a malloc'd FP32 logits memref out, read and freed by the caller every step.
+    Host wall clock (the call is synchronous), max over ranks.  Returns (seconds per step, one
+    result's checksum of its first and last logit rows)."""
+    import ctypes
+    P = ctypes.POINTER(ctypes.c_int64)
+    B, S = ids_h.shape
+    ids = np.ascontiguousarray(ids_h)
+    mask = np.ones_like(ids)
+    ip, mp = ids.ctypes.data_as(P), mask.ctypes.data_as(P)
+    lib = pkg.lib()
+
+    def call():
+        m = lib.gpt2_decoder(ip, ip, 0, B, S, S, 1, mp, mp, 0, B, S, S, 1)
+        if not m.allocated:
+            raise SystemExit("gpt2_decoder failed: " + pkg.last_error())
+        n = m.sizes[0] * m.sizes[1] * m.sizes[2]
+        view = np.ctypeslib.as_array(m.aligned, shape=(n,))
+        chk = float(view[:V].sum() + view[n - V:].sum())  # the caller reads its result
+        pkg._libc.free(ctypes.cast(m.allocated, ctypes.c_void_p))
+        return chk
+
+    chk = call()  # warm-up: staging buffers, graph capture
+    if world > 1:
+        dist.barrier()
+    t0 = time.perf_counter()
+    for _ in range(steps):
+        call()
+    et = time.perf_counter() - t0
+    return max_over_ranks(et, dist, "cuda") / steps, chk
+
+
+def e2e_pinned(pkg, ids_h, steps, dist, world):
+    """The companion host-buffer entry point gpt2_forward_host with pinned ids and logits (one DMA
+    each way, no staging); host wall clock, max over ranks.  Returns seconds per step."""
+    import ctypes
+    import torch
+    B, S = ids_h.shape
+    host_ids = torch.from_numpy(np.ascontiguousarray(ids_h)).pin_memory()
+    host_logits = torch.empty((B, S, V), dtype=torch.float32, pin_memory=True)
+    P = ctypes.POINTER
+    ip = host_ids.numpy().ctypes.data_as(P(ctypes.c_int64))
+    op = host_logits.numpy().ctypes.data_as(P(ctypes.c_float))
+    lib = pkg.lib()
+    if lib.gpt2_forward_host(ip, None, B, S, op) != 0:
+        raise SystemExit("gpt2_forward_host failed: " + pkg.last_error())
+    if world > 1:
+        dist.barrier()
+    t0 = time.perf_counter()
+    for _ in range(steps):
+        lib.gpt2_forward_host(ip, None, B, S, op)
+    et = time.perf_counter() - t0
+    del host_logits
+    return max_over_ranks(et, dist, "cuda") / steps
+
+
+def forward_plus_gather(pkg, torch, dist, rank, world, ids, Bg, S, stream, logits_dtype, chunks, steps, warmup):
+    """One step = this rank's forward and the gather of every shard's logits into rank 0's
+    [Bg x S, LD_LOGITS] buffer, timed together (CUDA events on the compute stream, max over ranks).
+    The shard runs as `chunks` sub-batches; a shard's chunk goes to rank 0 (NCCL send on a
+    separate stream) as soon as its lm_head has written it, while the next chunk computes.  Rank 0
+    writes its own shard in place and posts every receive up front.  Returns seconds per step."""
+    B = ids.shape[0]
+    if B % chunks:
+        chunks = 1
+    bc = B // chunks
+    tdt = torch.float32 if logits_dtype == pkg.DTYPE_F32 else torch.bfloat16
+    if rank == 0:
+        full = torch.empty(Bg * S, LD_LOGITS, device="cuda", dtype=tdt)
+        outs = [full[k * bc * S:(k + 1) * bc * S] for k in range(chunks)]
+    else:
+        local = torch.empty(B * S, LD_LOGITS, device="cuda", dtype=tdt)
+        outs = [local[k * bc * S:(k + 1) * bc * S] for k in range(chunks)]
+    ids_k = [ids[k * bc:(k + 1) * bc] for k in range(chunks)]
+    comm = torch.cuda.Stream()
+    evs = [torch.cuda.Event() for _ in range(chunks)]
+
+    def step():
+        reqs = []
+        if rank == 0:
+            ops = [dist.P2POp(dist.irecv, full[(p * B + k * bc) * S:(p * B + (k + 1) * bc) * S], p)
+                   for p in range(1, world) for k in range(chunks)]
+            reqs = dist.batch_isend_irecv(ops)
+        for k in range(chunks):
+            pkg.forward_device(ids_k[k].data_ptr(), None, bc, S, outs[k].data_ptr(), LD_LOGITS, stream.cuda_stream,
+                               logits_dtype)
+            if rank != 0:
+                evs[k].record(stream)
+                with torch.cuda.stream(comm):
+                    comm.wait_event(evs[k])
+                    dist.send(outs[k], dst=0)
+        for r in reqs:
+            r.wait()
+        stream.wait_stream(comm)
+
+    with torch.cuda.stream(stream):
+        for _ in range(warmup):
+            step()
+        t = timed_steps(step, steps, stream, torch, dist, world)
+    del outs
+    return t / steps
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -479,15 +623,18 @@ def main():
     ap.add_argument("--config", type=int, default=2, choices=sorted(CONFIGS),
                     help="reference configuration (2 = the headline BF16 workload)")
     ap.add_argument("--batch", type=int, default=None,
-                    help="global batch (sequences); default: the config's batch per rank (weak scaling) or in "
-                         "total (strong)")
-    ap.add_argument("--scaling", default="weak", choices=["weak", "strong"],
-                    help="weak: every rank runs the configuration's batch (sequences are independent, so "
-                         "the shards need no collective); strong: the configuration's batch split over ranks")
+                    help="global batch (sequences); default: the config's batch in total (strong scaling) or "
+                         "per rank (weak)")
+    ap.add_argument("--scaling", default="strong", choices=["strong", "weak"],
+                    help="strong (default): the configuration's batch split over the ranks, as the "
+                         "configuration states it; weak: every rank runs the configuration's batch")
     ap.add_argument("--seq", type=int, default=None, help="default: the config's")
-    ap.add_argument("--e2e-steps", type=int, default=2)
+    ap.add_argument("--e2e-steps", type=int, default=5)
+    ap.add_argument("--gather-steps", type=int, default=5)
+    ap.add_argument("--gather-chunks", type=int, default=2,
+                    help="sub-batches per shard in the forward + gather step (1 = gather after the forward)")
     ap.add_argument("--no-cpu-baseline", action="store_true")
-    ap.add_argument("--no-gather", action="store_true", help="skip the NCCL logits gather (N > 1)")
+    ap.add_argument("--no-gather", action="store_true", help="skip the forward + logits gather step (N > 1)")
     ap.add_argument("--no-decode", action="store_true", help="skip the KV-cache decode measurement")
     args = ap.parse_args()
 
@@ -532,58 +679,20 @@ def main():
     def step():
         pkg.forward_device(ids.data_ptr(), None, B, S, logits.data_ptr(), LD_LOGITS, sp)
 
-    def barrier():
-        if world > 1:
-            dist.barrier()
-
     for _ in range(max(args.warmup, 3)):
         step()
     torch.cuda.synchronize()
     if pkg.status() != 0:
         raise SystemExit("device status word set during warm-up")
-    barrier()
-    torch.cuda.synchronize()
-    ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     with ClockSampler(local_rank) as clk:
-        ev0.record(stream)
-        for _ in range(args.steps):
-            step()
-        ev1.record(stream)
-        torch.cuda.synchronize()
-    barrier()
-    elapsed = ev0.elapsed_time(ev1) / 1000.0
-    t_max = max_over_ranks(elapsed, dist, "cuda")
+        t_max = timed_steps(step, args.steps, stream, torch, dist, world)
     value = args.batch * S * args.steps / t_max
+    step_ms = 1000.0 * t_max / args.steps
 
-    # The output step after the forward: every shard's FP32 logits into rank 0 with NCCL over
-    # NVLink, one peer after another into one reused buffer (rank 0's ingress is the bound either
-    # way, and rank 0 holds two shards of logits at most); reported beside `value`, not inside it.
-    gather = None
-    if world > 1 and not args.no_gather:
-        buf = torch.empty_like(logits) if rank == 0 else None
-
-        def move():
-            for src in range(1, world):
-                if rank == 0:
-                    dist.recv(buf, src=src)
-                elif rank == src:
-                    dist.send(logits, dst=0)
-        move()  # warm-up: sets up the peer connections
-        torch.cuda.synchronize()
-        dist.barrier()
-        g0, g1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-        g0.record(stream)
-        move()
-        g1.record(stream)
-        torch.cuda.synchronize()
-        gt = max_over_ranks(g0.elapsed_time(g1) / 1000.0, dist, "cuda")
-        gather = {"ms": 1000.0 * gt, "bytes_to_rank0": int(logits.numel() * 4 * (world - 1)),
-                  "gbs_into_rank0": logits.numel() * 4 * (world - 1) / gt / 1e9,
-                  "tokens_per_s_forward_plus_gather": args.batch * S / (t_max / args.steps + gt),
-                  "method": "NCCL send/recv, one peer at a time into one buffer on rank 0"}
-        del buf
-
-    # Per-kernel breakdown (separate, profiled steps of the same workload).
+    # Per-kernel breakdown (separate, profiled steps of the same workload: an event pair around
+    # every launch).  The profiled step runs at higher clocks than the timed one (the timed
+    # step is power-capped), so each kernel's time is also given scaled to the timed step by its
+    # share, and the roofline is computed from that scaled time.
     pkg.profile_begin()
     nprof = 2
     p0, p1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
@@ -596,48 +705,81 @@ def main():
     profiled_step_ms = p0.elapsed_time(p1) / nprof
     work = kernel_work(B, S, args.config)
     ffma = pkg.k_ffma_peak() if args.config == 1 else None
-    kernels, roof = kernel_breakdown(prof, work, nprof, _peaks(), args.config, T, ffma)
+    kernels, roof = kernel_breakdown(prof, work, nprof, _peaks(), args.config, T, ffma, timed_step_ms=step_ms)
     fl = kernel_work(B, S)
     total_flop = (fl["gemm_qkv"][1] + fl["gemm_proj"][1] + fl["gemm_fc"][1] + fl["gemm_mproj"][1]) * L \
         + fl["lm_head"][1] + fl["attention"][1] * L
     fwd_tflops = total_flop / (t_max / args.steps) / 1e12
 
-    # End to end through the host-buffer C ABI: ids from pinned host memory in, FP32 logits out to
-    # pinned host memory, per step, synchronised.
+    # The same forward with bf16 logits (the optional store of the lm_head epilogue): half the
+    # bytes written; reported beside the FP32 headline.
+    bf16_logits = None
+    if dtype_code >= 1:
+        lg16 = torch.empty(T, LD_LOGITS, device="cuda", dtype=torch.bfloat16)
+
+        def step16():
+            pkg.forward_device(ids.data_ptr(), None, B, S, lg16.data_ptr(), LD_LOGITS, sp, pkg.DTYPE_BF16)
+        for _ in range(3):
+            step16()
+        n16 = max(3, args.steps // 2)
+        t16 = timed_steps(step16, n16, stream, torch, dist, world)
+        pkg.profile_begin()
+        step16()
+        prof16 = pkg.profile_end()
+        torch.cuda.synchronize()
+        head_ms, _ = prof16["lm_head"]
+        bf16_logits = {"tokens_per_s": args.batch * S * n16 / t16, "ms_per_step": 1000.0 * t16 / n16,
+                       "lm_head_ms_profiled": head_ms, "steps": n16,
+                       "logits_bytes_per_rank": int(T * V * 2)}
+        del lg16
+
+    # Forward + gather of every shard's logits into rank 0 (NCCL over NVLink), FP32 and bf16.
+    gather = None
+    if world > 1 and not args.no_gather:
+        del logits
+        gather = {"method": f"NCCL send/recv into one [global batch x S, {LD_LOGITS}] buffer on rank 0; "
+                            "each shard in sub-batches, a sub-batch sent as soon as its lm_head is done"}
+        for lab, dt in (("f32", pkg.DTYPE_F32), ("bf16", pkg.DTYPE_BF16)):
+            if dt == pkg.DTYPE_BF16 and dtype_code == 0:
+                continue
+            for ch in sorted({1, args.gather_chunks}):
+                ts = forward_plus_gather(pkg, torch, dist, rank, world, ids, args.batch, S, stream, dt, ch,
+                                         args.gather_steps, 2)
+                gather[f"{lab}_chunks{ch}"] = {
+                    "ms_per_step": 1000.0 * ts, "tokens_per_s_forward_plus_gather": args.batch * S / ts,
+                    "bytes_to_rank0": int((args.batch - B) * S * V * (4 if dt == pkg.DTYPE_F32 else 2))}
+        best = max((v for k, v in gather.items() if k.startswith("f32_")),
+                   key=lambda v: v["tokens_per_s_forward_plus_gather"])
+        gather["tokens_per_s_forward_plus_gather"] = best["tokens_per_s_forward_plus_gather"]
+        logits = torch.empty(T, LD_LOGITS, device="cuda", dtype=torch.float32)
+
+    # End to end: through the drop-in gpt2_decoder (malloc'd result, as the reference's host program
+    # receives it) and through gpt2_forward_host with pinned buffers.  Host memory for the results
+    # is bounded by half of what is free, shared by this host's ranks; with little memory the
+    # end-to-end steps use fewer sequences per rank and say so.
     e2e = None
     if args.e2e_steps > 0:
-        # The host holds every local rank's FP32 logits in pinned memory.  Pin at most half of the
-        # host memory that is free (more would make the host swap or kill the job): with many
-        # ranks on a small host the end-to-end step runs on fewer sequences per rank, and says so.
         import psutil
         local_ranks = int(os.environ.get("LOCAL_WORLD_SIZE", str(world)))
         avail = psutil.virtual_memory().available
-        eB = max(1, min(B, int(avail // 2 // (S * V * 4 * local_ranks))))
-        eB = torch.tensor([eB], device="cuda")
+        eB = max(1, min(B, int(avail // 2 // (2 * S * V * 4 * local_ranks))))
+        eBt = torch.tensor([eB], device="cuda")
         if world > 1:
-            dist.all_reduce(eB, op=dist.ReduceOp.MIN)  # the same work on every rank
-        eB = int(eB.item())
-        host_ids = torch.from_numpy(np.ascontiguousarray(ids_h[:eB])).pin_memory()
-        host_logits = torch.empty((eB, S, V), dtype=torch.float32, pin_memory=True)
-        ids_np, out_np = host_ids.numpy(), host_logits.numpy()
-        import ctypes
-        P = ctypes.POINTER
-        lib = pkg.lib()
-        ip = ids_np.ctypes.data_as(P(ctypes.c_int64))
-        op = out_np.ctypes.data_as(P(ctypes.c_float))
-        rc = lib.gpt2_forward_host(ip, None, eB, S, op)  # warm-up (grows staging buffers)
-        if rc != 0:
-            raise SystemExit("gpt2_forward_host failed: " + pkg.last_error())
-        barrier()
-        t0 = time.perf_counter()
-        for _ in range(args.e2e_steps):
-            lib.gpt2_forward_host(ip, None, eB, S, op)
-        et = time.perf_counter() - t0
-        e2e = {"value": eB * world * S * args.e2e_steps / max_over_ranks(et, dist, "cuda"), "unit": "tokens/s",
-               "h2d_bytes_per_step": int(ids_np.nbytes * world), "d2h_bytes_per_step": int(out_np.nbytes * world),
-               "steps": args.e2e_steps, "per_rank_batch": eB,
-               "api": "gpt2_forward_host (C ABI, host buffers, synchronous)"}
-        del host_logits
+            dist.all_reduce(eBt, op=dist.ReduceOp.MIN)  # the same work on every rank
+        eB = int(eBt.item())
+        sub = ids_h[:eB]
+        t_dec, _ = e2e_decoder(pkg, sub, args.e2e_steps, dist, world)
+        t_pin = e2e_pinned(pkg, sub, args.e2e_steps, dist, world)
+        h2d = int(sub.nbytes * 2 * world)  # ids and the all-ones mask
+        d2h = int(eB * S * V * 4 * world)
+        e2e = {"value": eB * world * S / t_dec, "unit": "tokens/s", "h2d_bytes_per_step": h2d,
+               "d2h_bytes_per_step": d2h, "steps": args.e2e_steps, "per_rank_batch": eB,
+               "api": "gpt2_decoder (the drop-in symbol; decomposed memrefs, malloc'd FP32 result freed by the "
+                      "caller each step)",
+               "d2h_gbs": d2h / t_dec / 1e9,
+               "pinned": {"value": eB * world * S / t_pin, "unit": "tokens/s", "d2h_gbs": d2h / t_pin / 1e9,
+                          "api": "gpt2_forward_host (pinned host ids and logits)"},
+               "decoder_vs_pinned": t_pin / t_dec}
 
     # Incremental decoding on the same model (reported beside the prefill number): greedy
     # generation with the KV cache, 64 new tokens after a 128-token prompt, per-token time from the
@@ -656,8 +798,8 @@ def main():
             gen(64)
             t1 = min(gen(1) for _ in range(3))
             tn = min(gen(64) for _ in range(3))
-            step = (tn - t1) / 63
-            decode[f"B{db}"] = {"ms_per_token_step": 1e3 * step, "tokens_per_s": db / step, "prompt": 128,
+            dstep = (tn - t1) / 63
+            decode[f"B{db}"] = {"ms_per_token_step": 1e3 * dstep, "tokens_per_s": db / dstep, "prompt": 128,
                                 "new_tokens": 64}
         decode["api"] = "gpt2_generate (KV cache, one CUDA graph per step)"
 
@@ -665,9 +807,10 @@ def main():
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
         r, dt, cores = cpu_reference_rate(S, fp8=args.config == 4)
         O = _oracle()
-        cpu = {"value": r, "unit": "tokens/s", "cores": cores, "kind": "port",
-               "sample": f"1 sequence x {S} tokens ({dt:.1f} s{', repeated' if dt * r > 1.5 * S else ''}); OpenBLAS sgemm "
-                         f"({O.blas_name().split('/')[-1]}) on all {cores} cores, loop nests single-threaded"}
+        cpu = {"value": r, "unit": "tokens/s", "cores": cores, "kind": "port", "extrapolated": args.batch > 1,
+               "sample": f"1 sequence x {S} tokens ({dt:.1f} s{', repeated' if dt * r > 1.5 * S else ''}) of the "
+                         f"{args.batch}-sequence workload; OpenBLAS sgemm ({O.blas_name().split('/')[-1]}) on all "
+                         f"{cores} cores, loop nests single-threaded"}
 
     clocks = clk.summary()
     weight_bytes = (L * (12 * D * D + 13 * D) + (V + 1024) * D) * (4 if dtype_code == 0 else 2)
@@ -678,13 +821,13 @@ def main():
         line = {
             "metric": METRICS.get(args.config, "GPT-2 prefill tokens/s"),
             "value": value, "unit": "tokens/s", "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
-            "ms_per_step": 1000.0 * t_max / args.steps, "higher_is_better": True, "scaling": args.scaling,
+            "ms_per_step": step_ms, "higher_is_better": True, "scaling": args.scaling,
             "vs_baseline": value / PUBLISHED_B1S5_TOKENS_PER_S if args.config == 0 else None,
             "dtype": dtype_label,
             "data": "synthetic (seeded Philox weights N(0,0.02), LN gain 1, biases 0; uniform token ids)",
             "config": {"workload": f"{wl_name} with global batch {args.batch} x {S}, logits FP32 resident per shard",
                        "global_batch": args.batch, "seq_len": S, "per_rank_batch": B,
-                       "parallelism": f"batch-sharded dp{world}",
+                       "parallelism": f"batch-sharded dp{world} ({args.scaling} scaling)",
                        "l2": f"no flush: every step moves > {moved_gb:.2f} GB (weights + FP32 logits), "
                              "more than the 126 MB L2"},
             "forward_tflops": fwd_tflops,
@@ -693,6 +836,7 @@ def main():
             "kernels": kernels,
             "cpu_baseline": cpu,
             "e2e": e2e,
+            "bf16_logits": bf16_logits,
             "logits_gather": gather,
             "decode": decode,
             "clocks": clocks,

@@ -171,12 +171,17 @@ int gpt2_status(void);
 /* Device-resident forward (benchmarks and device callers)                  */
 /* ------------------------------------------------------------------------ */
 
-/* logits [B, S, vocab] (row stride ld_logits >= vocab floats) of the loaded
- * model, everything on the model's device.  Columns [vocab, ld_logits) of a
- * row may be overwritten up to the next 16-byte boundary.  d_ids / d_mask: contiguous
- * int64 [B, S] device arrays (d_mask may be NULL = all ones).  Enqueued on
- * `stream` (a cudaStream_t; NULL = the CUDA default stream); returns when
- * enqueued.  logits_dtype must be GPT2_DTYPE_F32. */
+/* logits [B, S, vocab] (row stride ld_logits >= vocab elements) of the
+ * loaded model, everything on the model's device.  Columns [vocab, ld_logits)
+ * of a row may be overwritten up to the next 16-byte boundary.  d_ids /
+ * d_mask: contiguous int64 [B, S] device arrays (d_mask may be NULL = all
+ * ones).  Enqueued on `stream` (a cudaStream_t; NULL = the CUDA default
+ * stream); returns when enqueued.
+ * logits_dtype GPT2_DTYPE_F32: FP32 logits, the reference's output type
+ * (memref<1x?x50257xf32>, src/gpt/gpt2_call.cpp:17-21).  GPT2_DTYPE_BF16:
+ * the same FP32-accumulated logits rounded once to bf16 in the lm_head
+ * epilogue (half the bytes written, moved over PCIe or NVLink); BF16 and
+ * FP8-weight models only, ld_logits a multiple of 8. */
 int gpt2_forward_device(const int64_t *d_ids, const int64_t *d_mask, int B, int S, void *d_logits,
                         int64_t ld_logits, int logits_dtype, void *stream);
 
@@ -264,6 +269,19 @@ int gpt2k_gemm_f32(const float *A, const float *B, int b_nk, float *C, int M, in
  * output tile; bn = 2: two SMs (a CTA pair) per 256 x 256 tile. */
 int gpt2k_gemm_bf16(const void *A, const void *B, void *C, int M, int N, int K, int ldc, int out_f32,
                     const float *bias, const void *resid, int epi, int bn, void *stream);
+
+/* Test hook of the kernels' bounded-wait error path; no counterpart in the
+ * reference, which has no error path at all (src/gpt/gpt2_call.cpp:42-46
+ * checks cuInit only).  Runs the single-SM tcgen05 GEMM of gpt2k_gemm_bf16
+ * (bn = 128, C bf16 [M, N] with row stride N, no epilogue) with CTA 0's TMA
+ * producer withholding the copy of its first stage, so that CTA 0's MMA
+ * thread waits for data that never comes.  That wait gives up after its
+ * limit (2 s); the kernel records status 2 (GPT2 "a barrier wait timed
+ * out") in *d_status, stops issuing, waits for the copies it issued, frees
+ * its tensor memory and returns, and the CUDA context stays usable.  C is
+ * left partly written.  Enqueued on `stream`; nothing faults or hangs. */
+int gpt2k_test_gemm_withheld_load(const void *A, const void *B, void *C, int M, int N, int K, int *d_status,
+                                  void *stream);
 
 /* The GEMM epilogues of the BF16 forward's folded LayerNorms (C bf16, or f32
  * for GPT2_EPI_LN_BIAS).  A LayerNorm LN(a) = (a - mean) * rstd * gain + shift

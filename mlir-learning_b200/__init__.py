@@ -131,6 +131,7 @@ def lib() -> ctypes.CDLL:
     L.gpt2_generate.argtypes = [P(i64), i32, i32, i32, P(i64)]
     L.gpt2k_gemm_f32.argtypes = [vp, vp, i32, vp, i32, i32, i32, i32, vp, vp, i32, vp]
     L.gpt2k_gemm_bf16.argtypes = [vp, vp, vp, i32, i32, i32, i32, i32, vp, vp, i32, i32, vp]
+    L.gpt2k_test_gemm_withheld_load.argtypes = [vp, vp, vp, i32, i32, i32, vp, vp]
     L.gpt2k_gemm_bf16_ln.argtypes = [vp, vp, vp, i32, i32, i32, i32, i32, vp, vp, i32, i32, vp, vp, vp, vp,
                                      ctypes.c_float, vp]
     L.gpt2k_ln_fold_pack.argtypes = [vp, i32, vp, vp, vp, vp, vp, vp, i32, i32, vp]
@@ -316,8 +317,9 @@ def forward_host(input_ids, attention_mask=None) -> np.ndarray:
 
 
 def forward_device(ids_ptr: int, mask_ptr: int | None, B: int, S: int, logits_ptr: int, ld_logits: int,
-                   stream_ptr: int | None = None) -> None:
-    _check(lib().gpt2_forward_device(ids_ptr, mask_ptr, B, S, logits_ptr, ld_logits, DTYPE_F32, stream_ptr),
+                   stream_ptr: int | None = None, logits_dtype: int = DTYPE_F32) -> None:
+    """gpt2_forward_device: logits_dtype DTYPE_F32 (default) or DTYPE_BF16 (ld_logits in elements)."""
+    _check(lib().gpt2_forward_device(ids_ptr, mask_ptr, B, S, logits_ptr, ld_logits, logits_dtype, stream_ptr),
            "gpt2_forward_device")
 
 
@@ -393,6 +395,11 @@ def k_gemm_f32(A, B, b_nk, C, M, N, K, ldc, bias=None, resid=None, epi=EPI_NONE,
 
 def k_gemm_bf16(A, B, C, M, N, K, ldc, out_f32=0, bias=None, resid=None, epi=EPI_NONE, bn=256, stream=None):
     _check(lib().gpt2k_gemm_bf16(A, B, C, M, N, K, ldc, out_f32, bias, resid, epi, bn, stream), "gpt2k_gemm_bf16")
+
+
+def k_test_gemm_withheld_load(A, B, C, M, N, K, status_ptr, stream=None):
+    """gpt2k_test_gemm_withheld_load: the tcgen05 GEMM with one TMA copy withheld (timeout-path test hook)."""
+    _check(lib().gpt2k_test_gemm_withheld_load(A, B, C, M, N, K, status_ptr, stream), "gpt2k_test_gemm_withheld_load")
 
 
 def k_gemm_bf16_ln(A, B, C, M, N, K, ldc, out_f32=0, bias=None, resid=None, epi=EPI_LN_BIAS, bn=256, c1=None,

@@ -13,6 +13,7 @@
 #include <vector>
 
 #include "../../../include/gpt2_b200.h"
+#include "../runtime/hostcopy.h"
 #include "../runtime/runtime.h"
 
 namespace gpt2 {
@@ -135,15 +136,12 @@ int forward_host_locked(const int64_t *ids, const int64_t *mask, int B, int S, f
     set_error("host-to-device copy of ids/mask failed");
     return GPT2_ECUDA;
   }
-  r = forward_device(c, w.ids, mask ? w.mask : nullptr, B, S, w.logits, ldl, st);
+  r = forward_device(c, w.ids, mask ? w.mask : nullptr, B, S, w.logits, ldl, 1, st);
   if (r) return r;
-  cudaError_t e = cudaMemcpy2DAsync(logits, sizeof(float) * V, w.logits, sizeof(float) * ldl, sizeof(float) * V, T,
-                                    cudaMemcpyDeviceToHost, st);
-  if (e == cudaSuccess) e = cudaStreamSynchronize(st);
-  if (e != cudaSuccess) {
-    set_error("forward failed: %s", cudaGetErrorString(e));
-    return GPT2_ECUDA;
-  }
+  // Pinned destinations take one strided DMA; pageable ones (the drop-in's
+  // malloc'd result) stream through pinned staging chunks.
+  r = copy_rows_to_host(w.logits, ldl, T, V, logits, st);
+  if (r) return r;
   const int s = read_status_locked(c);
   if (s) {
     set_error("device status %d after forward", s);
@@ -183,9 +181,10 @@ MemRef3D decoder_impl(const int64_t *ids_aligned, int64_t ids_off, int64_t is0, 
   if (r) return out;
   const int64_t V = context()->dims.vocab;
   const int64_t n = is0 * is1 * V;
-  float *buf = static_cast<float *>(malloc(sizeof(float) * n));
+  // Released by the caller with free() (src/gpt/gpt2_call.cpp:94).
+  float *buf = static_cast<float *>(alloc_host_output(sizeof(float) * n));
   if (!buf) {
-    set_error("gpt2_decoder: malloc of %lld floats failed", (long long)n);
+    set_error("gpt2_decoder: allocation of %lld floats of host memory failed", (long long)n);
     return out;
   }
   // An all-ones mask is the unmasked computation; skip its kernels.
@@ -338,7 +337,8 @@ int gpt2_get_config(Gpt2Config *out) {
 
 void gpt2_shutdown(void) {
   std::lock_guard<std::mutex> lk(g_api_mu);
-  destroy_context();
+  destroy_context();  // synchronises the device first
+  release_host_staging();
 }
 
 const char *gpt2_last_error(void) { return last_error_text(); }
@@ -360,12 +360,12 @@ int gpt2_forward_device(const int64_t *d_ids, const int64_t *d_mask, int B, int 
     set_error("gpt2_forward_device: no model loaded");
     return GPT2_ENOMODEL;
   }
-  if (logits_dtype != GPT2_DTYPE_F32 || !d_ids || !d_logits) {
-    set_error("gpt2_forward_device: need ids, logits and logits_dtype GPT2_DTYPE_F32");
+  if ((logits_dtype != GPT2_DTYPE_F32 && logits_dtype != GPT2_DTYPE_BF16) || !d_ids || !d_logits) {
+    set_error("gpt2_forward_device: need ids, logits and logits_dtype GPT2_DTYPE_F32 or GPT2_DTYPE_BF16");
     return GPT2_EINVAL;
   }
   cudaSetDevice(c->device);
-  return forward_device(*c, d_ids, d_mask, B, S, static_cast<float *>(d_logits), ld_logits,
+  return forward_device(*c, d_ids, d_mask, B, S, d_logits, ld_logits, logits_dtype == GPT2_DTYPE_F32,
                         static_cast<cudaStream_t>(stream));
 }
 
@@ -495,6 +495,25 @@ int gpt2k_gemm_bf16(const void *A, const void *B, void *C, int M, int N, int K, 
   return ck(launch_gemm_tc(plan, C, ldc, out_f32, bias, static_cast<const bf16 *>(resid), epi, nullptr, sms,
                            static_cast<cudaStream_t>(stream)),
             "gpt2k_gemm_bf16");
+}
+
+int gpt2k_test_gemm_withheld_load(const void *A, const void *B, void *C, int M, int N, int K, int *d_status,
+                                  void *stream) {
+  if (!A || !B || !C || !d_status) {
+    set_error("gpt2k_test_gemm_withheld_load: null operand or status");
+    return GPT2_EINVAL;
+  }
+  TcGemmPlan plan;
+  const int r = tc_gemm_plan(&plan, static_cast<const bf16 *>(A), static_cast<const bf16 *>(B), M, N, K, 128);
+  if (r || N % 8) {
+    set_error("gpt2k_test_gemm_withheld_load: bad operands (%d)", r);
+    return GPT2_EINVAL;
+  }
+  int dev = 0, sms = 148;
+  cudaGetDevice(&dev);
+  cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+  return ck(launch_gemm_tc_withheld_load(plan, C, d_status, sms, static_cast<cudaStream_t>(stream)),
+            "gpt2k_test_gemm_withheld_load");
 }
 
 int gpt2k_gemm_bf16_ln(const void *A, const void *B, void *C, int M, int N, int K, int ldc, int out_f32,

@@ -153,6 +153,13 @@ cudaError_t launch_gemm_tc(const TcGemmPlan &plan, void *C, int ldc, int out_f32
                            const bf16 *resid, int epi, int *status, int num_sms, cudaStream_t st,
                            const float *scale = nullptr, const LnFold *ln = nullptr);
 bool ln_fold_valid(const TcGemmPlan &plan, int epi, int out_f32, const LnFold *ln);
+// Test hook of the bounded-wait error path: the single-SM kernel (plan.bn =
+// 128, C bf16 [M, N] by direct stores, no epilogue) with CTA 0's producer
+// withholding its first stage, so that CTA 0's MMA thread waits for data that
+// never comes, gives up after GPT2_WAIT_TIMEOUT_NS, records status 2, and
+// every role unwinds (drains what it issued, frees TMEM, returns).
+cudaError_t launch_gemm_tc_withheld_load(const TcGemmPlan &plan, void *C, int *status, int num_sms,
+                                         cudaStream_t st);
 // The CTA-pair kernel (called by launch_gemm_tc for TC_TILE_PAIR plans).
 bool gemm_tc2sm_usable(const TcGemmPlan &plan, const void *C, int ldc, int out_f32);
 cudaError_t launch_gemm_tc2sm(const TcGemmPlan &plan, void *C, int ldc, int out_f32, const float *bias,

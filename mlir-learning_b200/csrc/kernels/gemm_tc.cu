@@ -65,7 +65,7 @@ __global__ void __launch_bounds__(NTHREADS, 1)
     gemm_tc_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constant__ CUtensorMap map_b,
                    const __grid_constant__ CUtensorMap map_c, void *C, int ldc, int M, int N, int K,
                    const float *__restrict__ bias, const bf16 *resid, int *status,
-                   const float *__restrict__ scale, const LnFold ln) {
+                   const float *__restrict__ scale, const LnFold ln, int withhold) {
   using Cfg = TcCfg<BN>;
   using Kind = EpiKind<EPI>;
   constexpr int STAGES = Cfg::STAGES;
@@ -121,6 +121,9 @@ __global__ void __launch_bounds__(NTHREADS, 1)
         const int s = it % STAGES;
         const uint32_t ph = (it / STAGES) & 1;
         if (!mbar_wait(&empty[s], ph ^ 1, abort_flag, status)) { ok = false; break; }
+        // Test hook of the timeout path (gpt2k_test_gemm_withheld_load): CTA 0
+        // never fills its first stage, so its MMA thread's wait runs out.
+        if (withhold >= 0 && blockIdx.x == 0 && it == withhold) continue;
         mbar_arrive_expect_tx(&full[s], Cfg::STAGE_BYTES);
         tma_load_2d(sa + s * Cfg::A_BYTES, &map_a, &full[s], kb * BK, mb * BM);
         tma_load_2d(sb + s * Cfg::B_BYTES, &map_b, &full[s], kb * BK, nb * BN);
@@ -389,7 +392,7 @@ int make_map_out(CUtensorMap *map, const void *base, int64_t rows, int64_t cols,
 
 template <int BN, int EPI, int OUT_F32, int TMA_STORE>
 cudaError_t launch_variant(const TcGemmPlan &p, void *C, int ldc, const float *bias, const bf16 *resid, int *status,
-                           int num_sms, cudaStream_t st, const float *scale, const LnFold &ln) {
+                           int num_sms, cudaStream_t st, const float *scale, const LnFold &ln, int withhold = -1) {
   using Cfg = TcCfg<BN>;
   static std::atomic<uint64_t> attr_done{0};
   cudaError_t e = set_smem_once(gemm_tc_kernel<BN, EPI, OUT_F32, TMA_STORE>, Cfg::SMEM_BYTES, attr_done);
@@ -397,7 +400,7 @@ cudaError_t launch_variant(const TcGemmPlan &p, void *C, int ldc, const float *b
   const int tiles = ((p.M + BM - 1) / BM) * ((p.N + BN - 1) / BN);
   const int grid = tiles < num_sms ? tiles : num_sms;
   gemm_tc_kernel<BN, EPI, OUT_F32, TMA_STORE><<<grid, NTHREADS, Cfg::SMEM_BYTES, st>>>(
-      p.map_a, p.map_b, p.map_c, C, ldc, p.M, p.N, p.K, bias, resid, status, scale, ln);
+      p.map_a, p.map_b, p.map_c, C, ldc, p.M, p.N, p.K, bias, resid, status, scale, ln, withhold);
   return cudaGetLastError();
 }
 
@@ -458,6 +461,13 @@ int tc_gemm_set_output(TcGemmPlan *plan, const void *C, int ldc, int out_f32) {
   plan->c_f32 = out_f32;
   plan->has_c = make_map_out(&plan->map_c, C, plan->M, plan->N, ldc, out_f32) == 0;
   return plan->has_c;
+}
+
+cudaError_t launch_gemm_tc_withheld_load(const TcGemmPlan &plan, void *C, int *status, int num_sms,
+                                         cudaStream_t st) {
+  if (plan.two_sm || plan.bn != 128 || !status || num_sms <= 0) return cudaErrorInvalidValue;
+  const LnFold none;
+  return launch_variant<128, EPI_NONE, 0, 0>(plan, C, plan.N, nullptr, nullptr, status, num_sms, st, nullptr, none, 0);
 }
 
 bool ln_fold_valid(const TcGemmPlan &plan, int epi, int out_f32, const LnFold *ln) {

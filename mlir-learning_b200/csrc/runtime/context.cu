@@ -402,7 +402,7 @@ int forward_launch_count(const Context &c, int64_t T, int has_mask) {
 // Buffers, TMA descriptors and output descriptor of a forward of (B, S) into
 // d_logits: everything that allocates or encodes on the host, done before
 // any launch (and outside any graph capture).
-int prepare_forward(Context &c, int B, int S, float *d_logits, int64_t ld_logits) {
+int prepare_forward(Context &c, int B, int S, void *d_logits, int64_t ld_logits, int logits_f32) {
   const ModelDims &m = c.dims;
   int r = ensure_workspace(c, B, S);
   if (!r && c.dtype == 0 && (int64_t)B * S <= kFewRows) r = ensure_nk_f32(c);
@@ -419,10 +419,11 @@ int prepare_forward(Context &c, int B, int S, float *d_logits, int64_t ld_logits
     }
   }
   TcGemmPlan &head = c.plans[4 * m.n_layer];
-  if (d_logits && (head.c_ptr != d_logits || head.c_ld != (int)ld_logits || !head.c_f32)) {
+  if (d_logits && (head.c_ptr != d_logits || head.c_ld != (int)ld_logits || head.c_f32 != logits_f32)) {
     // Logits rows that TMA cannot store (unaligned base or row stride) go
     // through the single-SM kernel's direct stores, with its own tile width.
-    const bool storable = !(reinterpret_cast<uintptr_t>(d_logits) & 15) && (ld_logits * 4) % 16 == 0;
+    const bool storable =
+        !(reinterpret_cast<uintptr_t>(d_logits) & 15) && (ld_logits * (logits_f32 ? 4 : 2)) % 16 == 0;
     const int tile = storable ? c.head_tile : c.head_bn;
     if (head.two_sm != (tile == TC_TILE_PAIR) || (!head.two_sm && head.bn != tile)) {
       if (tc_gemm_plan(&head, static_cast<const bf16 *>(c.ln_fold ? w.x : w.a), c.ln_fold ? c.wte_ln : c.wte_h,
@@ -431,7 +432,7 @@ int prepare_forward(Context &c, int B, int S, float *d_logits, int64_t ld_logits
         return -2;
       }
     }
-    tc_gemm_set_output(&head, d_logits, (int)ld_logits, 1);
+    tc_gemm_set_output(&head, d_logits, (int)ld_logits, logits_f32);
   }
   return 0;
 }
@@ -443,7 +444,8 @@ namespace {
 // whole GPU, instead of the tiled GEMMs, which would give a handful of rows
 // one M-tile on a few SMs.  Same results contract as the tiled path.
 int launch_forward_few(Context &c, const int64_t *d_ids, const uint8_t *kv, const int64_t *d_mask, int B, int S,
-                       float *d_logits, int64_t ld_logits, cudaStream_t st, bool kv_fill) {
+                       void *d_logits_v, int64_t ld_logits, cudaStream_t st, bool kv_fill, int logits_f32) {
+  float *d_logits = static_cast<float *>(d_logits_v);
   const ModelDims &m = c.dims;
   const int T = B * S;
   const int d = m.n_embd, ff = m.n_inner, H = m.n_head, V = m.vocab;
@@ -508,6 +510,11 @@ int launch_forward_few(Context &c, const int64_t *d_ids, const uint8_t *kv, cons
     CKP(K_LM_HEAD, launch_gemv_bf16_f32out(xl, c.wte_h, d_logits, B, V, d, (int)ld_logits, st, &lnf));
     return 0;
   }
+  if (!logits_f32) {
+    CKP(K_LM_HEAD, launch_gemv_bf16(x, c.wte_h, static_cast<bf16 *>(d_logits_v), T, V, d, (int)ld_logits, nullptr,
+                                    nullptr, nullptr, EPI_NONE, st, &lnf, pdl));
+    return 0;
+  }
   CKP(K_LM_HEAD, launch_gemv_bf16_f32out(x, c.wte_h, d_logits, T, V, d, (int)ld_logits, st, &lnf, pdl));
   return 0;
 }
@@ -516,8 +523,9 @@ int launch_forward_few(Context &c, const int64_t *d_ids, const uint8_t *kv, cons
 // Enqueues the forward's kernels on st (prepare_forward has run).  With
 // kv_fill, every layer's keys and values also go to the decode cache, and
 // only the last position's logits are computed, into d_logits [B, ld_logits].
-int launch_forward(Context &c, const int64_t *d_ids, const int64_t *d_mask, int B, int S, float *d_logits,
-                   int64_t ld_logits, cudaStream_t st, bool kv_fill) {
+int launch_forward(Context &c, const int64_t *d_ids, const int64_t *d_mask, int B, int S, void *d_logits_v,
+                   int64_t ld_logits, cudaStream_t st, bool kv_fill, int logits_f32) {
+  float *d_logits = static_cast<float *>(d_logits_v);
   const ModelDims &m = c.dims;
   const int64_t T = (int64_t)B * S;
   const int d = m.n_embd, ff = m.n_inner, H = m.n_head, V = m.vocab;
@@ -527,7 +535,8 @@ int launch_forward(Context &c, const int64_t *d_ids, const int64_t *d_mask, int 
     CKP(K_SEQ_INFO, launch_seq_info(d_mask, B, S, w.first_valid, w.key_valid, st));
     kv = w.key_valid;
   }
-  if (T <= kFewRows) return launch_forward_few(c, d_ids, kv, d_mask, B, S, d_logits, ld_logits, st, kv_fill);
+  if (T <= kFewRows)
+    return launch_forward_few(c, d_ids, kv, d_mask, B, S, d_logits_v, ld_logits, st, kv_fill, logits_f32);
   if (c.dtype == 0) {
     float *x = static_cast<float *>(w.x), *a = static_cast<float *>(w.a), *qkv = static_cast<float *>(w.qkv),
           *o = static_cast<float *>(w.o), *u = static_cast<float *>(w.u);
@@ -596,8 +605,8 @@ int launch_forward(Context &c, const int64_t *d_ids, const int64_t *d_mask, int 
     if (!kv_fill) {
       const LnFold lnf = fold(c.head_c1, c.head_c2);
       const TcGemmPlan &head = c.plans[4 * m.n_layer];
-      CKP(K_LM_HEAD, launch_gemm_tc(head, d_logits, (int)ld_logits, 1, nullptr, nullptr, EPI_LN_BIAS, c.d_status,
-                                    ns, st, nullptr, &lnf));
+      CKP(K_LM_HEAD, launch_gemm_tc(head, d_logits_v, (int)ld_logits, logits_f32, nullptr, nullptr, EPI_LN_BIAS,
+                                    c.d_status, ns, st, nullptr, &lnf));
       return 0;
     }
   } else {
@@ -629,13 +638,13 @@ int launch_forward(Context &c, const int64_t *d_ids, const int64_t *d_mask, int 
     return 0;
   }
   const TcGemmPlan &head = c.plans[4 * m.n_layer];
-  CKP(K_LM_HEAD, launch_gemm_tc(head, d_logits, (int)ld_logits, 1, nullptr, nullptr, EPI_NONE, c.d_status, ns,
-                    st));
+  CKP(K_LM_HEAD, launch_gemm_tc(head, d_logits_v, (int)ld_logits, logits_f32, nullptr, nullptr, EPI_NONE,
+                                c.d_status, ns, st));
   return 0;
 }
 
-int forward_device(Context &c, const int64_t *d_ids, const int64_t *d_mask, int B, int S, float *d_logits,
-                   int64_t ld_logits, cudaStream_t st) {
+int forward_device(Context &c, const int64_t *d_ids, const int64_t *d_mask, int B, int S, void *d_logits,
+                   int64_t ld_logits, int logits_f32, cudaStream_t st) {
   const ModelDims &m = c.dims;
   if (!c.loaded) {
     set_error("no weights loaded");
@@ -645,14 +654,22 @@ int forward_device(Context &c, const int64_t *d_ids, const int64_t *d_mask, int 
     set_error("bad forward shape B=%d S=%d (n_positions %d) ld_logits=%lld", B, S, m.n_pos, (long long)ld_logits);
     return -1;
   }
-  int r = prepare_forward(c, B, S, d_logits, ld_logits);
+  if (!logits_f32 && (c.dtype == 0 || ld_logits % 8)) {
+    set_error("bf16 logits need a BF16 or FP8-weight model and a row stride that is a multiple of 8 (got dtype %d, "
+              "ld_logits %lld)", c.dtype, (long long)ld_logits);
+    return -1;
+  }
+  int r = prepare_forward(c, B, S, d_logits, ld_logits, logits_f32);
   if (r) return r;
-  auto launch = [&](cudaStream_t s) { return launch_forward(c, d_ids, d_mask, B, S, d_logits, ld_logits, s, false); };
+  auto launch = [&](cudaStream_t s) {
+    return launch_forward(c, d_ids, d_mask, B, S, d_logits, ld_logits, s, false, logits_f32);
+  };
   if (c.prof.on) return launch(st);  // per-launch events need plain launches
-  const uintptr_t key[6] = {reinterpret_cast<uintptr_t>(d_ids), reinterpret_cast<uintptr_t>(d_mask),
+  const uintptr_t key[7] = {reinterpret_cast<uintptr_t>(d_ids), reinterpret_cast<uintptr_t>(d_mask),
                             reinterpret_cast<uintptr_t>(d_logits), static_cast<uintptr_t>(ld_logits),
-                            static_cast<uintptr_t>(B), static_cast<uintptr_t>(S)};
-  return run_with_graph(c.graph, &c.use_graphs, key, 6, c.stream, st, launch);
+                            static_cast<uintptr_t>(B), static_cast<uintptr_t>(S),
+                            static_cast<uintptr_t>(logits_f32)};
+  return run_with_graph(c.graph, &c.use_graphs, key, 7, c.stream, st, launch);
 }
 
 }  // namespace gpt2

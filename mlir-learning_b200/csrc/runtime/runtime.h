@@ -187,17 +187,19 @@ int load_blob(Context &c, const float *host_blob);
 int ensure_workspace(Context &c, int B, int S);
 
 // Enqueues the forward on `st`; ids / mask are contiguous device arrays.
-int forward_device(Context &c, const int64_t *d_ids, const int64_t *d_mask, int B, int S, float *d_logits,
-                   int64_t ld_logits, cudaStream_t st);
+// logits_f32 = 1: FP32 logits; 0: bf16 logits (BF16 / FP8-weight models
+// only), row stride ld_logits in elements of that type.
+int forward_device(Context &c, const int64_t *d_ids, const int64_t *d_mask, int B, int S, void *d_logits,
+                   int64_t ld_logits, int logits_f32, cudaStream_t st);
 // A forward of at most this many tokens streams every weight for a handful
 // of rows: it runs the split-K GEMV kernels of the decode step.
 constexpr int64_t kFewRows = 16;
 int forward_launch_count(const Context &c, int64_t T, int has_mask);
 // The FP32 layer weights transposed to [out, in] for the GEMV kernels (once).
 int ensure_nk_f32(Context &c);
-int prepare_forward(Context &c, int B, int S, float *d_logits, int64_t ld_logits);
-int launch_forward(Context &c, const int64_t *d_ids, const int64_t *d_mask, int B, int S, float *d_logits,
-                   int64_t ld_logits, cudaStream_t st, bool kv_fill);
+int prepare_forward(Context &c, int B, int S, void *d_logits, int64_t ld_logits, int logits_f32 = 1);
+int launch_forward(Context &c, const int64_t *d_ids, const int64_t *d_mask, int B, int S, void *d_logits,
+                   int64_t ld_logits, cudaStream_t st, bool kv_fill, int logits_f32 = 1);
 // Incremental decoding (B <= 16 sequences of up to max_len tokens).
 int kv_reserve(Context &c, int B, int max_len);
 // The forward over B x S ids that also fills the cache (positions 0 .. S-1)

@@ -270,6 +270,50 @@ def forward(shape: ModelShape, blob: np.ndarray, ids: np.ndarray, mask: np.ndarr
     return out
 
 
+def _top(x: np.ndarray, k: int) -> np.ndarray:
+    """Column indices of each row's k largest entries, largest first (ties: lower index first)."""
+    part = np.argpartition(-x, k - 1, axis=1)[:, :k]
+    vals = np.take_along_axis(x, part, axis=1)
+    order = np.lexsort((part, -vals), axis=1)
+    return np.take_along_axis(part, order, axis=1)
+
+
+def top5_report(ref: np.ndarray, got: np.ndarray, bound: float) -> dict:
+    """Top-5 agreement of logits `got` with the oracle's `ref` (both [..., V]) under a STATED
+    per-logit error bound (an absolute logit difference fixed by the caller, not measured on
+    these rows).
+
+    A position is checkable when each of the oracle's top five logits leads the next one (1st
+    over 2nd, ..., 5th over 6th) by more than 2 * bound: two logits that are each within
+    `bound` of the oracle cannot swap there, so a kernel that honours the bound must give the
+    same five ids in the same order.  Reported:
+      total, checked (checkable positions), identical (checkable positions whose top-5 ids and
+      order agree), top1 (fraction of ALL positions whose argmax agrees), overlap (mean size of
+      the intersection of the two top-5 sets over ALL positions, 0..5), exceed (fraction of all
+      logits farther than `bound` from the oracle), max_err, p999 (99.9th percentile of the
+      per-logit error) and the bound itself."""
+    V = ref.shape[-1]
+    r = np.ascontiguousarray(ref, dtype=np.float32).reshape(-1, V)
+    g = np.ascontiguousarray(got, dtype=np.float32).reshape(-1, V)
+    ri = _top(r, 6)
+    rv = np.take_along_axis(r, ri, axis=1)
+    checkable = (rv[:, :5] - rv[:, 1:6] > 2.0 * bound).all(axis=1)
+    gi = _top(g, 5)
+    same = (gi == ri[:, :5]).all(axis=1)
+    err = np.abs(g - r)
+    return {
+        "total": int(r.shape[0]),
+        "checked": int(checkable.sum()),
+        "identical": int((same & checkable).sum()),
+        "top1": float((gi[:, 0] == ri[:, 0]).mean()),
+        "overlap": float((gi[:, :, None] == ri[:, None, :5]).any(axis=2).sum(axis=1).mean()),
+        "exceed": float((err > bound).mean()),
+        "max_err": float(err.max()),
+        "p999": float(np.quantile(err, 0.999)),
+        "bound": float(bound),
+    }
+
+
 # ---------------------------------------------------------------------------
 # BERT encoder
 # ---------------------------------------------------------------------------

@@ -3,23 +3,33 @@
 
 FP32 path: within 1e-4 absolute of the golden fixtures (HF GPT2LMHeadModel)
 and of the oracle, the reference's own tolerance (src/compare_outputs.py:17).
-BF16 path: relative error bound BF16_RTOL on the logits (max |diff| over
-max |logit|) and top-5 identity wherever the oracle's top-5 is separated by
-more than twice the error observed at that position."""
+BF16 path (helpers.top5_check): every logit within BF16_MAX_REL of max |logit|;
+top-5 identity at every position whose oracle top-5 is separated by more than
+twice the stated bound BF16_TOP5_BOUND_REL * max |logit|; and floors on the
+fraction of positions that are checkable, on the top-1 agreement over all
+positions and on the mean top-5 overlap, so that a check that can no longer
+fail (no checkable positions) fails instead."""
 import os
 
 import numpy as np
 import pytest
 
-from helpers import (attendable_rows, golden_files, load_golden, load_oracle, load_pkg, shape_to_cfg,
-                     top1_fraction, top5_agreement)
+from helpers import (BF16_MAX_REL, BF16_TOP5_BOUND_REL, attendable_rows, golden_files, load_golden, load_oracle,
+                     load_pkg, shape_to_cfg, top5_check)
 
 pytestmark = pytest.mark.gpu
 pkg = load_pkg()
 O = load_oracle()
 
 FP32_ATOL = 1e-4
-BF16_RTOL = 0.03
+# Floors of the BF16 top-5 statistics (calibration on a B200 beside each): positions checkable under
+# the stated bound (headline workload 3.2 %, 2-layer models 9.3-9.4 %), top-1 agreement over all
+# positions (0.974-1.0) and mean top-5 overlap (4.90-5.0 of 5).  The checkable floor applies where a
+# comparison has at least 64 positions.
+MIN_CHECKED_LARGE = 0.05   # 2-layer fixtures with >= 64 positions
+MIN_CHECKED_HEADLINE = 0.02
+MIN_TOP1 = 0.95
+MIN_OVERLAP = 4.85
 
 
 @pytest.fixture(scope="module")
@@ -35,16 +45,11 @@ def _model(shape, blob, dtype):
     pkg.load_weights(blob)
 
 
-def _bf16_check(ref, got, label):
-    scale = float(np.abs(ref).max())
-    err = float(np.abs(got - ref).max())
-    bound = BF16_RTOL * scale
-    checked, agree, total = top5_agreement(ref, got)
-    top1 = top1_fraction(ref, got)
-    print(f"{label}: max|diff| {err:.4g} (scale {scale:.3g}, rel {err / scale:.4g}); top-5 checked {checked}/{total}, "
-          f"identical {agree}; top-1 agreement {top1:.3f}")
-    assert err <= bound, (err, bound)
-    assert agree == checked
+def _bf16_check(ref, got, label, min_checked=MIN_CHECKED_LARGE):
+    total = ref.size // ref.shape[-1]
+    return top5_check(label, ref, got, max_rel=BF16_MAX_REL, bound_rel=BF16_TOP5_BOUND_REL,
+                      min_checked=min_checked if total >= 64 else None, min_top1=MIN_TOP1,
+                      min_overlap=MIN_OVERLAP)
 
 
 @pytest.mark.parametrize("path", golden_files(), ids=lambda p: p.split("/")[-1])
@@ -138,15 +143,83 @@ def test_bf16_vs_oracle_and_batch_invariance_config2(torch):
     assert pkg.status() == 0
     one = torch.empty(S, 50304, device="cuda")
     O.set_loop_threads(8)
+    refs, gots = [], []
     for b in (0, 63):
         pkg.forward_device(ids[b:b + 1].contiguous().data_ptr(), None, 1, S, one.data_ptr(), 50304,
                            torch.cuda.current_stream().cuda_stream)
         torch.cuda.synchronize()
         assert torch.equal(logits[b * S:(b + 1) * S, :V], one[:, :V])
-        ref = O.forward(shape, blob, ids_h[b:b + 1])
-        _bf16_check(ref[0], one[:, :V].cpu().numpy(), f"bf16 B64xS1024 seq {b}")
+        refs.append(O.forward(shape, blob, ids_h[b:b + 1])[0])
+        gots.append(one[:, :V].cpu().numpy())
     O.set_loop_threads(1)
+    _bf16_check(np.concatenate(refs), np.concatenate(gots), "bf16 B64xS1024 sequences 0 and 63",
+                min_checked=MIN_CHECKED_HEADLINE)
     assert torch.isfinite(logits[:, :V]).all()
+
+
+@pytest.mark.parametrize("shape_name,B,S", [("GPT2_TINY", 3, 40), ("GPT2_TINY", 1, 5), ("GPT2_SMALL", 2, 1024)])
+def test_bf16_logits_are_the_fp32_logits_rounded_once(torch, shape_name, B, S):
+    """logits_dtype GPT2_DTYPE_BF16: the lm_head epilogue (tiled tcgen05 GEMM on one SM or on CTA pairs,
+    or the GEMV of a few-token forward) rounds the same FP32 value it would store, so the bf16 logits
+    equal the FP32 logits converted to bf16 (round to nearest even), bit for bit."""
+    shape = getattr(O, shape_name)
+    blob = O.seeded_blob(shape, 77, 1)
+    _model(shape, blob, pkg.DTYPE_BF16)
+    V = shape.vocab_size
+    ld = (V + 7) // 8 * 8
+    ids = torch.from_numpy(O.token_ids(B, S, 77, V)).cuda()
+    st = torch.cuda.current_stream().cuda_stream
+    f32 = torch.empty(B * S, ld, device="cuda")
+    b16 = torch.empty(B * S, ld, device="cuda", dtype=torch.bfloat16)
+    for _ in range(2):  # plain launch, then the captured graph
+        pkg.forward_device(ids.data_ptr(), None, B, S, f32.data_ptr(), ld, st)
+        pkg.forward_device(ids.data_ptr(), None, B, S, b16.data_ptr(), ld, st, pkg.DTYPE_BF16)
+        torch.cuda.synchronize()
+        assert pkg.status() == 0
+        assert torch.equal(b16[:, :V], f32[:, :V].bfloat16())
+    wide = torch.empty(B * S, ld + 1, device="cuda", dtype=torch.bfloat16)  # sized for the refused stride
+    with pytest.raises(pkg.Gpt2Error, match="multiple of 8"):
+        pkg.forward_device(ids.data_ptr(), None, B, S, wide.data_ptr(), ld + 1, st, pkg.DTYPE_BF16)
+
+
+def test_bf16_logits_rejected_for_the_fp32_model(torch):
+    shape = O.GPT2_TINY
+    _model(shape, O.seeded_blob(shape, 3, 0), pkg.DTYPE_F32)
+    ids = torch.zeros(1, 4, dtype=torch.int64, device="cuda")
+    out = torch.empty(4, 1000, device="cuda", dtype=torch.bfloat16)
+    with pytest.raises(pkg.Gpt2Error, match="bf16 logits"):
+        pkg.forward_device(ids.data_ptr(), None, 1, 4, out.data_ptr(), 1000, None, pkg.DTYPE_BF16)
+
+
+def test_decoder_result_streams_through_staging_bit_exact(torch):
+    """gpt2_decoder's malloc'd result (pageable host memory, larger than one 32 MiB staging chunk, with a
+    ragged last chunk) and gpt2_forward_host into pinned memory both equal the device entry point's FP32
+    logits bit for bit, with and without a mask."""
+    shape = O.GPT2_SMALL
+    blob = O.seeded_blob(shape, 99, 0)
+    _model(shape, blob, pkg.DTYPE_BF16)
+    B, S, V = 2, 300, shape.vocab_size  # 600 rows of 201 KB: 4 chunks of <= 166 rows
+    ids_h = O.token_ids(B, S, 99, V)
+    mask_h = np.ones_like(ids_h)
+    mask_h[1, :17] = 0
+    for mask in (None, mask_h):
+        got = pkg.gpt2_decoder(ids_h, mask)
+        ids = torch.from_numpy(ids_h).cuda()
+        m = torch.from_numpy(mask).cuda() if mask is not None else None
+        dev = torch.empty(B * S, V, device="cuda")
+        pkg.forward_device(ids.data_ptr(), m.data_ptr() if m is not None else None, B, S, dev.data_ptr(), V,
+                           torch.cuda.current_stream().cuda_stream)
+        torch.cuda.synchronize()
+        want = dev.view(B, S, V).cpu().numpy()
+        assert np.array_equal(got, want)
+        pinned = torch.empty((B, S, V), dtype=torch.float32, pin_memory=True)
+        import ctypes
+        P = ctypes.POINTER
+        ids_c = np.ascontiguousarray(ids_h)
+        mp = np.ascontiguousarray(mask).ctypes.data_as(P(ctypes.c_int64)) if mask is not None else None
+        assert pkg.lib().gpt2_forward_host(ids_c.ctypes.data_as(P(ctypes.c_int64)), mp, B, S,
+                                           pinned.numpy().ctypes.data_as(P(ctypes.c_float))) == 0
+        assert np.array_equal(pinned.numpy(), want)
 
 
 @pytest.mark.parametrize("dtype", [0, 1])

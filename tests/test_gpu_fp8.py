@@ -2,24 +2,23 @@
 MLP 6400; E4M3 Conv1D weights with per-output-channel scales, BF16
 activations, tied BF16 lm_head) on the GPU, through the C ABI.
 
-Two comparisons with the oracle on the same inputs:
+Two comparisons with the oracle on the same inputs (helpers.top5_check):
   * against the oracle run on the FP8-dequantized weights, which isolates the
-    kernels: the BF16 bound (BF16_RTOL of max |logit|) and top-5 identity;
+    kernels: every logit within FP8_DEQ_MAX_REL of max |logit|, top-5 identity
+    at every position checkable under the stated bound BF16_TOP5_BOUND_REL,
+    and floors on the checkable fraction, top-1 agreement and top-5 overlap;
   * against the oracle on the original FP32 weights (the reference's own
-    computation): FP8_RTOL of max |logit|.
-Both require identical top-5 wherever the oracle's top-5 is separated by more
-than twice the error observed at that position."""
+    computation, quantization error included): FP8_F32_MAX_REL of max |logit|
+    and floors on top-1 agreement and top-5 overlap (the quantized model is a
+    different model, so top-5 identity is not required here)."""
 import numpy as np
 import pytest
 
-from helpers import load_oracle, load_pkg, shape_to_cfg, top1_fraction, top5_agreement
+from helpers import BF16_TOP5_BOUND_REL, FP8_DEQ_MAX_REL, FP8_F32_MAX_REL, load_oracle, load_pkg, shape_to_cfg, top5_check
 
 pytestmark = pytest.mark.gpu
 pkg = load_pkg()
 O = load_oracle()
-
-BF16_RTOL = 0.03
-FP8_RTOL = 0.15  # observed 0.067 (2 layers) and 0.097 (48 layers) of max |logit|
 
 
 @pytest.fixture(scope="module")
@@ -28,18 +27,6 @@ def torch():
     assert t.cuda.is_available(), "GPU tests need a CUDA device"
     t.cuda.set_device(0)
     return t
-
-
-def _check(ref, got, rtol, label):
-    scale = float(np.abs(ref).max())
-    err = float(np.abs(got - ref).max())
-    bound = rtol * scale
-    checked, agree, total = top5_agreement(ref, got)
-    top1 = top1_fraction(ref, got)
-    print(f"{label}: max|diff| {err:.4g} (rel {err / scale:.4g}, bound {rtol}); top-5 checked {checked}/{total}, "
-          f"identical {agree}; top-1 agreement {top1:.3f}")
-    assert err <= bound, (err, bound)
-    assert agree == checked
 
 
 def _run(shape, seed, B, S, masked):
@@ -60,15 +47,23 @@ def _run(shape, seed, B, S, masked):
 
 
 def test_fp8w_xl_shape_two_layers(torch):
+    # calibration on a B200: vs dequantized max rel 6.8e-3, checkable 5.9 %, top-1 0.982, overlap 4.92;
+    # vs FP32 weights max rel 6.7e-2, top-1 0.862, overlap 4.46
     shape = O.ModelShape(n_layer=2, n_embd=1600, n_head=25, n_inner=6400)
     ref_q, ref_f, got = _run(shape, 4321, 2, 200, True)
-    _check(ref_q, got, BF16_RTOL, "fp8w XL-shape L2 vs oracle on dequantized weights")
-    _check(ref_f, got, FP8_RTOL, "fp8w XL-shape L2 vs oracle on FP32 weights")
+    top5_check("fp8w XL-shape L2 vs oracle on dequantized weights", ref_q, got, max_rel=FP8_DEQ_MAX_REL,
+               bound_rel=BF16_TOP5_BOUND_REL, min_checked=0.03, min_top1=0.95, min_overlap=4.85)
+    top5_check("fp8w XL-shape L2 vs oracle on FP32 weights", ref_f, got, max_rel=FP8_F32_MAX_REL, min_top1=0.8,
+               min_overlap=4.3)
 
 
 def test_fp8w_gpt2_xl_48_layers(torch):
-    """The FP8-weight workload's model (GPT-2 XL shape, 48 layers) on one short sequence."""
-    ref_q, ref_f, got = _run(O.GPT2_XL, 2024, 1, 128, False)
-    _check(ref_q, got, BF16_RTOL, "fp8w GPT-2 XL vs oracle on dequantized weights")
-    _check(ref_f, got, FP8_RTOL, "fp8w GPT-2 XL vs oracle on FP32 weights")
+    """The FP8-weight workload's model (GPT-2 XL shape, 48 layers) on two sequences of 256 tokens.
+    Calibration on one sequence of 128 tokens: vs dequantized max rel 1.7e-2, checkable 1.6 %, top-1
+    0.961, overlap 4.82; vs FP32 weights max rel 9.7e-2, top-1 0.695, overlap 3.93."""
+    ref_q, ref_f, got = _run(O.GPT2_XL, 2024, 2, 256, False)
+    top5_check("fp8w GPT-2 XL vs oracle on dequantized weights", ref_q, got, max_rel=FP8_DEQ_MAX_REL,
+               bound_rel=BF16_TOP5_BOUND_REL, min_checked=0.01, min_top1=0.93, min_overlap=4.7)
+    top5_check("fp8w GPT-2 XL vs oracle on FP32 weights", ref_f, got, max_rel=FP8_F32_MAX_REL, min_top1=0.6,
+               min_overlap=3.7)
     pkg.shutdown()

@@ -6,7 +6,7 @@ FP32, so only the accumulation order and the final rounding differ)."""
 import numpy as np
 import pytest
 
-from helpers import load_pkg
+from helpers import attention_ref, load_pkg
 
 pytestmark = pytest.mark.gpu
 pkg = load_pkg()
@@ -219,27 +219,6 @@ def test_layernorm(torch, T, d, dtype):
     ref = torch.nn.functional.layer_norm(x.double(), (d,), gain.double(), shift.double(), 1e-5)
     err = (y.double() - ref).abs().max().item()
     assert err <= (1e-5 if dtype == 0 else 2e-2 * ref.abs().max().item()), err
-
-
-def attention_ref(torch, qkv, mask, B, S, H, causal=True):
-    """float64 restatement of the oracle's attention semantics."""
-    D = H * 64
-    x = qkv.double().view(B, S, 3, H, 64)
-    q, k, v = x[:, :, 0].transpose(1, 2), x[:, :, 1].transpose(1, 2), x[:, :, 2].transpose(1, 2)
-    s = q @ k.transpose(-1, -2) * 0.125
-    ok = torch.ones(S, S, dtype=torch.bool, device=qkv.device)
-    if causal:
-        ok = ok.tril()
-    ok = ok[None, None]
-    if mask is not None:
-        ok = ok & (mask != 0)[:, None, None, :]
-    s = s.masked_fill(~ok, float("-inf"))
-    p = torch.softmax(s, dim=-1)
-    o = p @ v
-    none = ~ok.any(-1)  # [B,1|H,S]
-    mean_v = v.mean(dim=2, keepdim=True).expand_as(o)
-    o = torch.where(none[..., None].expand_as(o), mean_v, o)
-    return o.transpose(1, 2).reshape(B * S, D)
 
 
 @pytest.mark.parametrize("dtype", [0, 1, 2, 3])

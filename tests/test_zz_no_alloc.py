@@ -1,13 +1,18 @@
 """gpt2k_attention_noalloc, the attention entry point for callers that cannot
 allocate device memory at call time, against gpt2k_attention (which takes its
-mask scratch from a caller workspace): identical outputs on two calls in a row
-with different masks (the built-in scratch keeps the previous call's bytes),
-for the FP32 and the tcgen05 BF16 kernels, and a clear error past the size
-limit.  Collected last, and self-contained so it also passes alone in a fresh
-process."""
+mask scratch from a caller workspace).
+
+Both entry points run the same kernels on the same inputs, so their outputs
+must be identical bit for bit; a stale byte left in the built-in scratch by an
+earlier call would show up as a difference.  Two calls in a row use
+different masks, for the FP32 and the tcgen05 BF16 kernels, and each output
+is also held to the float64 attention with the tolerance of the kernel tests
+(2e-5 FP32, 3e-2 BF16).  A shape just past the scratch limit is refused with
+a message.  Collected last, and self-contained so it also passes alone in a
+fresh process."""
 import pytest
 
-from helpers import load_pkg
+from helpers import attention_ref, load_pkg
 
 pytestmark = pytest.mark.gpu
 pkg = load_pkg()
@@ -44,14 +49,24 @@ def test_noalloc_matches_workspace_entry_point(torch, dtype):
         pkg.k_attention(qkv.data_ptr(), mask.data_ptr(), ref.data_ptr(), B, S, H, dtype, ws.data_ptr(), st)
         pkg.k_attention_noalloc(qkv.data_ptr(), mask.data_ptr(), got.data_ptr(), B, S, H, dtype, st)
         torch.cuda.synchronize()
-        err = (got.double() - ref.double()).abs().max().item()
+        assert torch.equal(got, ref), (call, (got.double() - ref.double()).abs().max().item())
+        want = attention_ref(torch, qkv, mask, B, S, H)
+        err = (got.double() - want).abs().max().item()
         assert err <= (2e-5 if dtype == pkg.DTYPE_F32 else 3e-2), (call, err)
-        assert torch.isfinite(got.float()).all()
 
 
 def test_noalloc_rejects_shapes_past_its_scratch(torch):
-    B, S, H = 8192, 1024, 1  # 8 Mi key bytes > the 4 MiB array
-    mask = torch.ones(1, dtype=torch.int64, device="cuda")
+    """B=4200 x S=1000 needs 256 + 4*4200 + 4200*1000 = 4,217,056 scratch bytes, just over the 4 MiB
+    array.  Every buffer is sized for that shape, so if the size check ever failed the call would
+    compute an attention into valid memory rather than touch memory it does not own through these
+    arguments."""
+    B, S, H = 4200, 1000, 1
+    assert pkg.k_attention_workspace_bytes(B, S) == 4_217_056 > 4 << 20
+    qkv = torch.zeros(B * S, 3 * H * 64, dtype=torch.bfloat16, device="cuda")
+    o = torch.zeros(B * S, H * 64, dtype=torch.bfloat16, device="cuda")
+    mask = torch.ones(B, S, dtype=torch.int64, device="cuda")
     with pytest.raises(pkg.Gpt2Error, match="built-in array"):
-        pkg.k_attention_noalloc(0, mask.data_ptr(), 0, B, S, H, pkg.DTYPE_F32,
+        pkg.k_attention_noalloc(qkv.data_ptr(), mask.data_ptr(), o.data_ptr(), B, S, H, pkg.DTYPE_BF16,
                                 torch.cuda.current_stream().cuda_stream)
+    torch.cuda.synchronize()
+    assert not o.any()  # nothing ran
