@@ -601,7 +601,9 @@ def forward_plus_gather(pkg, torch, dist, rank, world, ids, Bg, S, stream, logit
                 evs[k].record(stream)
                 with torch.cuda.stream(comm):
                     comm.wait_event(evs[k])
-                    dist.send(outs[k], dst=0)
+                    # the same batched point-to-point API as rank 0's receives (one communicator for both)
+                    for r in dist.batch_isend_irecv([dist.P2POp(dist.isend, outs[k], 0)]):
+                        r.wait()
         for r in reqs:
             r.wait()
         stream.wait_stream(comm)
