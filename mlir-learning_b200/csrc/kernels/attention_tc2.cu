@@ -430,14 +430,17 @@ __global__ void __launch_bounds__(NTHREADS, 1)
         // P_t and O_t of the previous iteration must be consumed before they are touched.
         if (j > 0) wait(&o_done[t], (g - 1) & 1);
         tc_fence_after();
-        if (rescale) {
+        // The TMEM loads and stores are warp-wide: when any row of the warp
+        // rescales, every lane takes part, with a factor of 1 where its row does not.
+        if (__any_sync(0xffffffffu, rescale)) {
+          const float a = rescale ? alpha : 1.f;
 #pragma unroll 1
           for (int c = 0; c < 64; c += 16) {
             uint32_t ov[16];
             tmem_ld_32x32b_x16(o_tmem + c, ov);
             tc_wait_ld();
 #pragma unroll
-            for (int e = 0; e < 16; ++e) ov[e] = __float_as_uint(__uint_as_float(ov[e]) * alpha);
+            for (int e = 0; e < 16; ++e) ov[e] = __float_as_uint(__uint_as_float(ov[e]) * a);
             tmem_st_32x32b_x16(o_tmem + c, ov);
           }
         }
