@@ -22,12 +22,13 @@ pkg = load_pkg()
 O = load_oracle()
 
 FP32_ATOL = 1e-4
-# Floors of the BF16 top-5 statistics (calibration on a B200 beside each): positions checkable under
-# the stated bound (headline workload 3.2 %, 2-layer models 9.3-9.4 %), top-1 agreement over all
-# positions (0.974-1.0) and mean top-5 overlap (4.90-5.0 of 5).  The checkable floor applies where a
-# comparison has at least 64 positions.
+# Floors of the BF16 top-5 statistics (measured on a B200 beside each): positions checkable under
+# the stated bound (headline workload 2.2 % with the bound taken from the larger of its two
+# sequences' max logit, 2-layer models 7.4-10.9 %), top-1 agreement over all positions (0.974-1.0)
+# and mean top-5 overlap (4.90-5.0 of 5).  The checkable floor applies where a comparison has at
+# least 64 positions.
 MIN_CHECKED_LARGE = 0.05   # 2-layer fixtures with >= 64 positions
-MIN_CHECKED_HEADLINE = 0.02
+MIN_CHECKED_HEADLINE = 0.015
 MIN_TOP1 = 0.95
 MIN_OVERLAP = 4.85
 
