@@ -315,15 +315,11 @@ int gpt2k_layernorm(const void *x, const float *gain, const float *shift, void *
                     int dtype, void *stream);
 
 /* Causal attention of one layer, head dim 64: qkv [B*S, 3*H*64] (q | k | v),
- * o [B*S, H*64] (16-byte aligned for BF16), in dtype: GPT2_DTYPE_F32 (SIMT),
- * GPT2_DTYPE_BF16 (tcgen05: one thread per query row, P in tensor memory)
- * or GPT2K_ATTN_BF16_MMA_SYNC (a second, warp-level mma.sync BF16 kernel kept
- * as an independent cross-check).  d_mask: contiguous int64 [B, S] or NULL.
- * workspace: device memory of gpt2k_attention_workspace_bytes(B, S) bytes
- * (unused, may be NULL, when d_mask is NULL). */
-enum { GPT2K_ATTN_BF16_MMA_SYNC = 2,
-       GPT2K_ATTN_BF16_TC_SMEM_P = 3 /* an earlier tcgen05 kernel (two threads per query row, P through
-                                        shared memory), kept as a cross-check; gpt2k_attention_ex only */ };
+ * o [B*S, H*64] (16-byte aligned for BF16), in dtype: GPT2_DTYPE_F32 (SIMT)
+ * or GPT2_DTYPE_BF16 (tcgen05: one thread per query row, P in tensor
+ * memory).  d_mask: contiguous int64 [B, S] or NULL.  workspace: device
+ * memory of gpt2k_attention_workspace_bytes(B, S) bytes (unused, may be
+ * NULL, when d_mask is NULL). */
 size_t gpt2k_attention_workspace_bytes(int B, int S);
 int gpt2k_attention(const void *qkv, const int64_t *d_mask, void *o, int B, int S, int H, int dtype,
                     void *workspace, void *stream);

@@ -668,18 +668,13 @@ int gpt2k_attention(const void *qkv, const int64_t *d_mask, void *o, int B, int 
       r = ck(launch_attn_masked_rows_f32(static_cast<const float *>(qkv), first_valid, static_cast<float *>(o), B, S,
                                          H, st),
              "gpt2k_attention");
-  } else if (dtype == GPT2_DTYPE_BF16 || dtype == GPT2K_ATTN_BF16_MMA_SYNC) {
-    if (dtype == GPT2_DTYPE_BF16) {
-      AttnTcPlan plan;
-      if (attention_tc_plan(&plan, static_cast<const bf16 *>(qkv), B, S, H, static_cast<const bf16 *>(o))) {
-        set_error("gpt2k_attention: TMA descriptor creation failed (qkv and o must be 16-byte aligned)");
-        return GPT2_EINVAL;
-      }
-      r = ck(launch_attention_tc2(plan, key_valid, static_cast<bf16 *>(o), nullptr, st), "gpt2k_attention");
-    } else {
-      r = ck(launch_attention_bf16(static_cast<const bf16 *>(qkv), key_valid, static_cast<bf16 *>(o), B, S, H, st),
-             "gpt2k_attention");
+  } else if (dtype == GPT2_DTYPE_BF16) {
+    AttnTcPlan plan;
+    if (attention_tc_plan(&plan, static_cast<const bf16 *>(qkv), B, S, H, static_cast<const bf16 *>(o))) {
+      set_error("gpt2k_attention: TMA descriptor creation failed (qkv and o must be 16-byte aligned)");
+      return GPT2_EINVAL;
     }
+    r = ck(launch_attention_tc2(plan, key_valid, static_cast<bf16 *>(o), nullptr, st), "gpt2k_attention");
     if (!r && d_mask)
       r = ck(launch_attn_masked_rows_bf16(static_cast<const bf16 *>(qkv), first_valid, static_cast<bf16 *>(o), B, S,
                                           H, st),
@@ -722,20 +717,13 @@ int gpt2k_attention_ex(const void *qkv, const int64_t *d_mask, void *o, int B, i
              "gpt2k_attention_ex");
     return r;
   }
-  if (dtype == GPT2_DTYPE_BF16 || dtype == GPT2K_ATTN_BF16_TC_SMEM_P) {
+  if (dtype == GPT2_DTYPE_BF16) {
     AttnTcPlan plan;
     if (attention_tc_plan(&plan, static_cast<const bf16 *>(qkv), B, S, H, static_cast<const bf16 *>(o))) {
       set_error("gpt2k_attention_ex: TMA descriptor creation failed (qkv and o must be 16-byte aligned)");
       return GPT2_EINVAL;
     }
-    if (dtype == GPT2_DTYPE_BF16)
-      r = ck(launch_attention_tc2(plan, key_valid, static_cast<bf16 *>(o), nullptr, st, c, kv_end),
-             "gpt2k_attention_ex");
-    else
-      r = ck(launch_attention_tc(plan, key_valid, static_cast<bf16 *>(o), nullptr, st, c, kv_end),
-             "gpt2k_attention_ex");
-  } else if (dtype == GPT2K_ATTN_BF16_MMA_SYNC) {
-    r = ck(launch_attention_bf16(static_cast<const bf16 *>(qkv), key_valid, static_cast<bf16 *>(o), B, S, H, st, c),
+    r = ck(launch_attention_tc2(plan, key_valid, static_cast<bf16 *>(o), nullptr, st, c, kv_end),
            "gpt2k_attention_ex");
   } else {
     set_error("gpt2k_attention_ex: bad dtype");

@@ -173,8 +173,6 @@ cudaError_t launch_gemm_tc2sm(const TcGemmPlan &plan, void *C, int ldc, int out_
 // causal = 0: every key of the sequence is attendable (the BERT encoder).
 cudaError_t launch_attention_f32(const float *qkv, const uint8_t *key_valid, float *o, int B, int S, int H,
                                  cudaStream_t st, int causal = 1);
-cudaError_t launch_attention_bf16(const bf16 *qkv, const uint8_t *key_valid, bf16 *o, int B, int S, int H,
-                                  cudaStream_t st, int causal = 1);
 // tcgen05 attention: TMA descriptor over qkv viewed as [B][S][3*H*64].
 struct AttnTcPlan {
   CUtensorMap map_qkv;
@@ -185,13 +183,11 @@ struct AttnTcPlan {
 };
 // Builds the qkv descriptor and, when o is given, the output descriptor.
 int attention_tc_plan(AttnTcPlan *plan, const bf16 *qkv, int B, int S, int H, const bf16 *o = nullptr);
-// kv_end (optional, [B]): keys at or past kv_end[b] are all masked, so their
-// tiles are skipped (right padding costs no attention work).
-cudaError_t launch_attention_tc(const AttnTcPlan &plan, const uint8_t *key_valid, bf16 *o, int *status,
-                                cudaStream_t st, int causal = 1, const int *kv_end = nullptr);
-// The same attention with one softmax thread per query row and P kept in
+// tcgen05 attention with one softmax thread per query row and P kept in
 // tensor memory (the P.V MMA reads its A operand from TMEM); o must be the
-// output the plan was built with.
+// output the plan was built with.  kv_end (optional, [B]): keys at or past
+// kv_end[b] are all masked, so their tiles are skipped (right padding costs no
+// attention work).
 cudaError_t launch_attention_tc2(const AttnTcPlan &plan, const uint8_t *key_valid, bf16 *o, int *status,
                                  cudaStream_t st, int causal = 1, const int *kv_end = nullptr);
 // Rows without an attendable key get the mean of V over all S keys: with the

@@ -515,7 +515,57 @@ __global__ void __launch_bounds__(NTHREADS, 1)
     tmem_dealloc(tmem, 512);
   }
 }
+typedef CUresult (*EncodeTiledFn)(CUtensorMap *, CUtensorMapDataType, cuuint32_t, void *, const cuuint64_t *,
+                                  const cuuint64_t *, const cuuint32_t *, const cuuint32_t *, CUtensorMapInterleave,
+                                  CUtensorMapSwizzle, CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+
+EncodeTiledFn encode_fn_attn() {
+  static std::atomic<EncodeTiledFn> fn{nullptr};
+  EncodeTiledFn f = fn.load();
+  if (f) return f;
+  void *p = nullptr;
+  cudaDriverEntryPointQueryResult q;
+  if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) != cudaSuccess ||
+      q != cudaDriverEntryPointSuccess || !p)
+    return nullptr;
+  f = reinterpret_cast<EncodeTiledFn>(p);
+  fn.store(f);
+  return f;
+}
 }  // namespace
+
+int attention_tc_plan(AttnTcPlan *plan, const bf16 *qkv, int B, int S, int H, const bf16 *o) {
+  EncodeTiledFn f = encode_fn_attn();
+  if (!f) return -1;
+  if (reinterpret_cast<uintptr_t>(qkv) & 15) return -2;
+  const int64_t D3 = 3LL * H * DH;
+  const cuuint64_t dims[3] = {static_cast<cuuint64_t>(D3), static_cast<cuuint64_t>(S), static_cast<cuuint64_t>(B)};
+  const cuuint64_t strides[2] = {static_cast<cuuint64_t>(D3 * 2), static_cast<cuuint64_t>(D3 * 2 * S)};
+  const cuuint32_t box[3] = {64, 128, 1};
+  const cuuint32_t estr[3] = {1, 1, 1};
+  CUresult r = f(&plan->map_qkv, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 3, const_cast<bf16 *>(qkv), dims, strides, box,
+                 estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                 CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS) return -3;
+  plan->out = nullptr;
+  if (o) {
+    if (reinterpret_cast<uintptr_t>(o) & 15) return -2;
+    const int64_t D = (int64_t)H * DH;
+    const cuuint64_t odims[3] = {static_cast<cuuint64_t>(D), static_cast<cuuint64_t>(S), static_cast<cuuint64_t>(B)};
+    const cuuint64_t ostrides[2] = {static_cast<cuuint64_t>(D * 2), static_cast<cuuint64_t>(D * 2 * S)};
+    const cuuint32_t obox[3] = {64, 32, 1};
+    r = f(&plan->map_out, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 3, const_cast<bf16 *>(o), odims, ostrides, obox, estr,
+          CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_NONE,
+          CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    if (r != CUDA_SUCCESS) return -3;
+    plan->out = o;
+  }
+  plan->qkv = qkv;
+  plan->B = B;
+  plan->S = S;
+  plan->H = H;
+  return 0;
+}
 
 cudaError_t launch_attention_tc2(const AttnTcPlan &plan, const uint8_t *key_valid, bf16 *o, int *status,
                                  cudaStream_t st, int causal, const int *kv_end) {

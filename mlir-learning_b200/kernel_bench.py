@@ -63,7 +63,7 @@ def main():
     ap.add_argument("--lengths", choices=["full", "uniform"], default="full",
                     help="uniform: right-padded, valid lengths uniform in [64, seq] (seeded)")
     ap.add_argument("--dtype", type=int, default=1,
-                    help="0 f32 (attention, gemm), 1 bf16 tcgen05, 2 bf16 mma.sync (attention)")
+                    help="0 f32 (attention, gemm), 1 bf16 tcgen05")
     ap.add_argument("--m", type=int, default=65536)
     ap.add_argument("--n", type=int, default=3072)
     ap.add_argument("--k", type=int, default=768)
