@@ -674,7 +674,7 @@ int gpt2k_attention(const void *qkv, const int64_t *d_mask, void *o, int B, int 
       set_error("gpt2k_attention: TMA descriptor creation failed (qkv and o must be 16-byte aligned)");
       return GPT2_EINVAL;
     }
-    r = ck(launch_attention_tc2(plan, key_valid, static_cast<bf16 *>(o), nullptr, st), "gpt2k_attention");
+    r = ck(launch_attention_tc3(plan, key_valid, static_cast<bf16 *>(o), nullptr, st), "gpt2k_attention");
     if (!r && d_mask)
       r = ck(launch_attn_masked_rows_bf16(static_cast<const bf16 *>(qkv), first_valid, static_cast<bf16 *>(o), B, S,
                                           H, st),
@@ -723,7 +723,7 @@ int gpt2k_attention_ex(const void *qkv, const int64_t *d_mask, void *o, int B, i
       set_error("gpt2k_attention_ex: TMA descriptor creation failed (qkv and o must be 16-byte aligned)");
       return GPT2_EINVAL;
     }
-    r = ck(launch_attention_tc2(plan, key_valid, static_cast<bf16 *>(o), nullptr, st, c, kv_end),
+    r = ck(launch_attention_tc3(plan, key_valid, static_cast<bf16 *>(o), nullptr, st, c, kv_end),
            "gpt2k_attention_ex");
   } else {
     set_error("gpt2k_attention_ex: bad dtype");

@@ -183,12 +183,12 @@ struct AttnTcPlan {
 };
 // Builds the qkv descriptor and, when o is given, the output descriptor.
 int attention_tc_plan(AttnTcPlan *plan, const bf16 *qkv, int B, int S, int H, const bf16 *o = nullptr);
-// tcgen05 attention with one softmax thread per query row and P kept in
-// tensor memory (the P.V MMA reads its A operand from TMEM); o must be the
-// output the plan was built with.  kv_end (optional, [B]): keys at or past
-// kv_end[b] are all masked, so their tiles are skipped (right padding costs no
-// attention work).
-cudaError_t launch_attention_tc2(const AttnTcPlan &plan, const uint8_t *key_valid, bf16 *o, int *status,
+// tcgen05 attention: three independent 128-query-tile slots per SM over
+// 64-key blocks, one softmax thread per query row, P kept in tensor memory
+// (the P.V MMA reads its A operand from TMEM); o must be the output the plan
+// was built with.  kv_end (optional, [B]): keys at or past kv_end[b] are all
+// masked, so their blocks are skipped (right padding costs no attention work).
+cudaError_t launch_attention_tc3(const AttnTcPlan &plan, const uint8_t *key_valid, bf16 *o, int *status,
                                  cudaStream_t st, int causal = 1, const int *kv_end = nullptr);
 // Rows without an attendable key get the mean of V over all S keys: with the
 // causal mask the rows q < first_valid[b]; without it, every row of a

@@ -371,7 +371,7 @@ int bert_launch(BertContext &c, const int64_t *d_ids, const int64_t *d_tt, const
       const BertLayer &lw = c.layers[l];
       const TcGemmPlan *p = &c.plans[4 * l];
       CKP(K_GEMM_QKV, launch_gemm_tc(p[0], qkv, 3 * d, 0, lw.qkv_b, nullptr, EPI_BIAS, c.d_status, ns, st));
-      CKP(K_ATTENTION, launch_attention_tc2(c.attn_plan, kv, o, c.d_status, st, 0, kv_end));
+      CKP(K_ATTENTION, launch_attention_tc3(c.attn_plan, kv, o, c.d_status, st, 0, kv_end));
       if (d_mask) CKP(K_MASKED_ROWS, launch_attn_masked_rows_bf16(qkv, w.first_valid, o, B, S, H, st, 0));
       CKP(K_GEMM_PROJ, launch_gemm_tc(p[1], y, d, 0, lw.ao_b, x, EPI_BIAS_RESID, c.d_status, ns, st));
       CKP(K_LAYERNORM, launch_layernorm_bf16(y, lw.aoln_g, lw.aoln_b, h, (int)T, d, m.eps, st));

@@ -596,7 +596,7 @@ int launch_forward(Context &c, const int64_t *d_ids, const int64_t *d_mask, int 
       CKP(K_GEMM_QKV,
           launch_gemm_tc(p[0], qkv, 3 * d, 0, nullptr, nullptr, EPI_LN_BIAS, c.d_status, ns, st, nullptr, &ln1));
       if (kv_fill) CK(launch_kv_store_bf16(qkv, static_cast<bf16 *>(c.dec.cache[l]), B, S, d, c.dec.max_len, 0, st));
-      CKP(K_ATTENTION, launch_attention_tc2(c.attn_plan, kv, o, c.d_status, st));
+      CKP(K_ATTENTION, launch_attention_tc3(c.attn_plan, kv, o, c.d_status, st));
       if (d_mask) CKP(K_MASKED_ROWS, launch_attn_masked_rows_bf16(qkv, w.first_valid, o, B, S, H, st));
       CKP(K_GEMM_PROJ, launch_gemm_tc(p[1], x, d, 0, lw.proj_b, x, EPI_BIAS_RESID_STATS, c.d_status, ns, st,
                                       nullptr, &stats_out));
@@ -621,7 +621,7 @@ int launch_forward(Context &c, const int64_t *d_ids, const int64_t *d_mask, int 
       CKP(K_GEMM_QKV,
           launch_gemm_tc(p[0], qkv, 3 * d, 0, lw.qkv_b, nullptr, EPI_BIAS, c.d_status, ns, st, lw.qkv_s));
       if (kv_fill) CK(launch_kv_store_bf16(qkv, static_cast<bf16 *>(c.dec.cache[l]), B, S, d, c.dec.max_len, 0, st));
-      CKP(K_ATTENTION, launch_attention_tc2(c.attn_plan, kv, o, c.d_status, st));
+      CKP(K_ATTENTION, launch_attention_tc3(c.attn_plan, kv, o, c.d_status, st));
       if (d_mask) CKP(K_MASKED_ROWS, launch_attn_masked_rows_bf16(qkv, w.first_valid, o, B, S, H, st));
       CKP(K_GEMM_PROJ, launch_gemm_tc(p[1], x, d, 0, lw.proj_b, x, EPI_BIAS_RESID, c.d_status, ns, st, lw.proj_s));
       CKP(K_LAYERNORM, launch_layernorm_bf16(x, lw.ln2_g, lw.ln2_b, a, (int)T, d, m.eps, st));
