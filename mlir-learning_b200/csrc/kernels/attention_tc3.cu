@@ -98,8 +98,34 @@ __device__ __forceinline__ float max3(float a, float b, float c) {
   return d;
 }
 
+// Unsigned division by a divisor fixed for the launch, as a multiply-high
+// and shifts (Granlund and Montgomery, "Division by invariant integers using
+// multiplication", PLDI 1994, figure 4.1): l = ceil(log2 d),
+// m = floor(2^32 (2^l - d) / d) + 1, n / d = (t + ((n - t) >> 1)) >> (l - 1)
+// with t = umulhi(m, n), exact for every 32-bit n when d >= 2.  The tile
+// walk divides by the pair count and the head count on every tile; as
+// integer divisions those cost several hundred clocks per tile.
+struct FastDiv {
+  uint32_t d, m, l;
+};
+__device__ __forceinline__ FastDiv make_fastdiv(uint32_t d) {
+  FastDiv f;
+  f.d = d;
+  uint32_t l = 0;
+  while (l < 32 && (1ull << l) < d) ++l;
+  f.l = l;
+  f.m = static_cast<uint32_t>(((1ull << 32) * ((1ull << l) - d)) / d + 1);
+  return f;
+}
+__device__ __forceinline__ uint32_t fast_div(uint32_t n, const FastDiv &f) {
+  if (f.d == 1) return n;
+  const uint32_t t = __umulhi(n, f.m);
+  return (t + ((n - t) >> 1)) >> (f.l - 1);
+}
+
 struct Geo {
   int S, H, n_tiles, n_pairs, n_units, nk_total, causal, P;
+  FastDiv div_pairs, div_h;
   const int *kv_end;
 };
 struct Tile {
@@ -116,13 +142,15 @@ __device__ __forceinline__ Geo make_geo(int B, int S, int H, int causal, const i
   g.nk_total = (S + BK - 1) / BK;
   g.causal = causal;
   g.P = gridDim.x * NSLOT;
+  g.div_pairs = make_fastdiv(g.n_pairs);
+  g.div_h = make_fastdiv(H);
   g.kv_end = kv_end;
   return g;
 }
 // The slot's next tile after (u, sec): the second tile of the pair, or the
 // first of the slot's next pair-unit.
 __device__ __forceinline__ void next_tile(const Geo &g, int &u, int &sec) {
-  const int i = u % g.n_pairs;
+  const int i = u - static_cast<int>(fast_div(u, g.div_pairs)) * g.n_pairs;
   if (sec == 0 && g.n_tiles - 1 - i != i) {
     sec = 1;
   } else {
@@ -132,9 +160,9 @@ __device__ __forceinline__ void next_tile(const Geo &g, int &u, int &sec) {
 }
 __device__ __forceinline__ Tile tile_of(const Geo &g, int u, int sec) {
   Tile t;
-  const int i = u % g.n_pairs, bh = u / g.n_pairs;
-  t.b = bh / g.H;
-  t.h = bh % g.H;
+  const int bh = static_cast<int>(fast_div(u, g.div_pairs)), i = u - bh * g.n_pairs;
+  t.b = static_cast<int>(fast_div(bh, g.div_h));
+  t.h = bh - t.b * g.H;
   t.qs = (sec ? i : g.n_tiles - 1 - i) * BQ;
   int nk = g.nk_total;
   if (g.kv_end) nk = min(nk, max(1, (g.kv_end[t.b] + BK - 1) / BK));
@@ -225,9 +253,9 @@ __global__ void __launch_bounds__(NTHREADS, 1)
     // has completed once the softmax freed S(g) (S(g + 1) waited for that);
     // V(g + VST - 1) replaces V(g - 1), whose only reader P.V(g - 1) has
     // completed once the softmax stored P(g) (it waits for P.V(g - 1) first,
-    // and P.V(g) waited for P(g)).  The Q tile of the next
-    // tile goes out right after the P.V of a tile's first block: the softmax
-    // has written the previous tile's output from that buffer by then.
+    // and P.V(g) waited for P(g)).  The Q tile of the next tile goes out
+    // right after the P.V of a tile's first block: the softmax hands that
+    // buffer back (its output store has read it) just after that P.
     const int s = warp;
     SlotBars &b = sb[s];
     const bool leader = elect_one_sync();
@@ -522,12 +550,19 @@ __global__ void __launch_bounds__(NTHREADS, 1)
         tc_wait_st();  // P (and a rescaled O) are in TMEM before the MMA may read them
         tc_fence_before();
         arrive(&bb.p_full);
+        // The previous tile's output store has had a whole block to read its
+        // staging rows: hand that Q buffer back now.  The control warp asks
+        // for it only after this P, to load the tile after this one.
+        if (j == 0 && nt > 0) {
+          if (lane == 0) bulk_wait_read<0>();
+          arrive(&bb.q_empty[(nt - 1) & 1]);
+        }
       }
       // Epilogue: O / l in bf16, staged in this tile's Q buffer (all its
       // Q K^T products are done) with the 128-byte swizzle and written by one
       // TMA store per warp (32 rows x 64 columns); rows past the sequence end
-      // are clipped by the tensor map.  The buffer goes back to the producer
-      // once the store has read it.
+      // are clipped by the tensor map.  The buffer goes back to the control
+      // warp after the next tile's first P (above).
       wait(&bb.o_done, (gb - 1) & 1);
       tc_fence_after();
       uint32_t ov[64];
@@ -552,9 +587,8 @@ __global__ void __launch_bounds__(NTHREADS, 1)
       if (lane == 0) {
         tma_store_3d(&map_out, ostage, t.h * DH, t.qs + qd * 32, t.b);
         bulk_commit();
-        bulk_wait_read<0>();
       }
-      arrive(&bb.q_empty[nt & 1]);
+      __syncwarp();
     }
     if (lane == 0) bulk_wait_all();  // stores complete before the CTA (and its shared memory) goes away
     __syncwarp();
