@@ -104,11 +104,14 @@ __device__ __forceinline__ float max3(float a, float b, float c) {
 // m = floor(2^32 (2^l - d) / d) + 1, n / d = (t + ((n - t) >> 1)) >> (l - 1)
 // with t = umulhi(m, n), exact for every 32-bit n when d >= 2.  The tile
 // walk divides by the pair count and the head count on every tile; as
-// integer divisions those cost several hundred clocks per tile.
+// integer divisions those cost several hundred clocks per tile.  The
+// constants are made on the host and reach the kernel as parameters (made in
+// the kernel, the compiler recomputed their 64-bit division wherever it ran
+// short of registers).
 struct FastDiv {
   uint32_t d, m, l;
 };
-__device__ __forceinline__ FastDiv make_fastdiv(uint32_t d) {
+FastDiv make_fastdiv(uint32_t d) {
   FastDiv f;
   f.d = d;
   uint32_t l = 0;
@@ -132,7 +135,8 @@ struct Tile {
   int b, h, qs, n;  // batch, head, first query row, key blocks
 };
 
-__device__ __forceinline__ Geo make_geo(int B, int S, int H, int causal, const int *kv_end) {
+// The tile walk of one launch (host side; grid CTAs).
+Geo make_geo(int B, int S, int H, int causal, const int *kv_end, int grid) {
   Geo g;
   g.S = S;
   g.H = H;
@@ -141,7 +145,7 @@ __device__ __forceinline__ Geo make_geo(int B, int S, int H, int causal, const i
   g.n_units = B * H * g.n_pairs;
   g.nk_total = (S + BK - 1) / BK;
   g.causal = causal;
-  g.P = gridDim.x * NSLOT;
+  g.P = grid * NSLOT;
   g.div_pairs = make_fastdiv(g.n_pairs);
   g.div_h = make_fastdiv(H);
   g.kv_end = kv_end;
@@ -204,8 +208,7 @@ __device__ __forceinline__ void cursor_next_block(Cursor &c, const Geo &g) {
 
 __global__ void __launch_bounds__(NTHREADS, 1)
     attention_tc3_kernel(const __grid_constant__ CUtensorMap map_qkv, const __grid_constant__ CUtensorMap map_out,
-                         const uint8_t *__restrict__ key_valid, int B, int S, int H, int *status, int causal,
-                         const int *__restrict__ kv_end) {
+                         const uint8_t *__restrict__ key_valid, const Geo g, int *status) {
   extern __shared__ unsigned char smem_raw[];
   unsigned char *sm =
       reinterpret_cast<unsigned char *>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
@@ -215,7 +218,7 @@ __global__ void __launch_bounds__(NTHREADS, 1)
   volatile int *abort_flag = reinterpret_cast<volatile int *>(sm + Smem3::MISC + 4);
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const Geo g = make_geo(B, S, H, causal, kv_end);
+  const int S = g.S, H = g.H, causal = g.causal;
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < NSLOT; ++s) {
@@ -667,8 +670,8 @@ cudaError_t launch_attention_tc3(const AttnTcPlan &plan, const uint8_t *key_vali
   cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
   const int64_t ctas = (units + NSLOT - 1) / NSLOT;
   const int grid = static_cast<int>(ctas < sms ? ctas : sms);
-  attention_tc3_kernel<<<grid, NTHREADS, Smem3::ALLOC, st>>>(plan.map_qkv, plan.map_out, key_valid, plan.B, plan.S,
-                                                             plan.H, status, causal, kv_end);
+  const Geo g = make_geo(plan.B, plan.S, plan.H, causal ? 1 : 0, kv_end, grid);
+  attention_tc3_kernel<<<grid, NTHREADS, Smem3::ALLOC, st>>>(plan.map_qkv, plan.map_out, key_valid, g, status);
   return cudaGetLastError();
 }
 
