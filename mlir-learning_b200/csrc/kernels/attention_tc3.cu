@@ -257,8 +257,9 @@ __global__ void __launch_bounds__(NTHREADS, 1)
     // V(g + VST - 1) replaces V(g - 1), whose only reader P.V(g - 1) has
     // completed once the softmax stored P(g) (it waits for P.V(g - 1) first,
     // and P.V(g) waited for P(g)).  The Q tile of the next tile goes out
-    // right after the P.V of a tile's first block: the softmax hands that
-    // buffer back (its output store has read it) just after that P.
+    // right after the P.V of a tile's second block (its only block, if it
+    // has one): the softmax hands that buffer back (the previous tile's
+    // output store has read it) just after that P.
     const int s = warp;
     SlotBars &b = sb[s];
     const bool leader = elect_one_sync();
@@ -362,9 +363,9 @@ __global__ void __launch_bounds__(NTHREADS, 1)
       const bool q_first = cursor_valid(sc, g) && sc.j == 0 && s_tile >= nq;
       if (cursor_valid(sc, g) && !q_first) ok = issue_s();
       const int tile_of_pv = pv_tile;
-      const bool tile_start = pc.j == 0;
+      const bool q_block = pc.j == min(1, pc.n - 1);
       if (ok) ok = issue_pv();
-      if (ok && tile_start && nq == tile_of_pv + 1 && cursor_valid(qc, g)) ok = load_q();
+      if (ok && q_block && nq == tile_of_pv + 1 && cursor_valid(qc, g)) ok = load_q();
       if (ok && q_first) ok = issue_s();
       if (ok && cursor_valid(kcur, g)) ok = load_k();
       if (ok && cursor_valid(vcur, g)) ok = load_v();
@@ -413,6 +414,45 @@ __global__ void __launch_bounds__(NTHREADS, 1)
       __syncwarp();
       if (lane == 0) mbar_arrive(bar);
     };
+    // Output of a finished tile: O / l in bf16, staged (128-byte swizzle) in
+    // the tile's Q buffer, whose Q K^T products are all done, and written by
+    // one TMA store per warp (32 rows x 64 columns); rows past the sequence
+    // end are clipped by the tensor map.  O is read in two 32-column halves.
+    auto write_out = [&](float l, int ob, int oh, int oqs, int buf) {
+      const float inv = l > 0.f ? 1.0f / l : 0.f;
+      unsigned char *ostage = sm + Smem3::Q + (s * 2 + buf) * QBYTES + qd * 32 * 128;
+      unsigned char *row = ostage + lane * 128;
+#pragma unroll
+      for (int half = 0; half < 2; ++half) {
+        uint32_t ov[32];
+        tmem_ld_32x32b_x32(o_tmem + 32 * half, ov);
+        tc_wait_ld();
+#pragma unroll
+        for (int gi = 0; gi < 4; ++gi) {
+          const float *f = reinterpret_cast<const float *>(&ov[gi * 8]);
+          const int chunk = half * 4 + gi;
+          *reinterpret_cast<uint4 *>(row + ((chunk ^ (lane & 7)) << 4)) =
+              make_uint4(pack_bf16x2(f[0] * inv, f[1] * inv), pack_bf16x2(f[2] * inv, f[3] * inv),
+                         pack_bf16x2(f[4] * inv, f[5] * inv), pack_bf16x2(f[6] * inv, f[7] * inv));
+        }
+      }
+      tc_fence_before();
+      fence_proxy_async_smem();
+      __syncwarp();
+      if (lane == 0) {
+        tma_store_3d(&map_out, ostage, oh * DH, oqs + qd * 32, ob);
+        bulk_commit();
+      }
+      __syncwarp();
+    };
+    // A tile's output is written during the next tile's first block (after
+    // its exponentials, when the tile's last P.V is long done and before that
+    // block's P lets the next P.V overwrite O), so the wait for the last P.V
+    // hides behind the next tile's work; the slot's last tile is written
+    // after the loop.
+    bool has_prev = false;
+    float prev_l = 0.f;
+    int prev_b = 0, prev_h = 0, prev_qs = 0;
     int gb = 0, nt = 0;  // blocks and tiles of this slot so far
     int u = blockIdx.x * NSLOT + s, sec = 0;
     for (; u < g.n_units; next_tile(g, u, sec), ++nt) {
@@ -532,9 +572,11 @@ __global__ void __launch_bounds__(NTHREADS, 1)
           up2(add2(s01, s23), a0, a1);
           l_run = l_run * alpha + (a0 + a1);
         }
-        // The previous P.V must be done before P is overwritten and O rescaled.
-        if (j > 0) wait(&bb.o_done, (gb - 1) & 1);
+        // The previous P.V must be done before P is overwritten and O rescaled
+        // (or, at a tile's first block, before O of the previous tile is read).
+        if (j > 0 || has_prev) wait(&bb.o_done, (gb - 1) & 1);
         tc_fence_after();
+        if (j == 0 && has_prev) write_out(prev_l, prev_b, prev_h, prev_qs, (nt - 1) & 1);
         // The TMEM loads and stores are warp-wide: when any row of the warp
         // rescales, every lane takes part, with a factor of 1 where its row does not.
         if (__any_sync(0xffffffffu, rescale)) {
@@ -553,45 +595,25 @@ __global__ void __launch_bounds__(NTHREADS, 1)
         tc_wait_st();  // P (and a rescaled O) are in TMEM before the MMA may read them
         tc_fence_before();
         arrive(&bb.p_full);
-        // The previous tile's output store has had a whole block to read its
-        // staging rows: hand that Q buffer back now.  The control warp asks
-        // for it only after this P, to load the tile after this one.
-        if (j == 0 && nt > 0) {
+        // The previous tile's output store has read its staging rows by the
+        // end of this tile's second block (or of its only one): hand that Q
+        // buffer back.  The control warp asks for it only after this P, to
+        // load the tile after this one.
+        if (j == min(1, t.n - 1) && nt > 0) {
           if (lane == 0) bulk_wait_read<0>();
           arrive(&bb.q_empty[(nt - 1) & 1]);
         }
       }
-      // Epilogue: O / l in bf16, staged in this tile's Q buffer (all its
-      // Q K^T products are done) with the 128-byte swizzle and written by one
-      // TMA store per warp (32 rows x 64 columns); rows past the sequence end
-      // are clipped by the tensor map.  The buffer goes back to the control
-      // warp after the next tile's first P (above).
+      has_prev = true;
+      prev_l = l_run;
+      prev_b = t.b;
+      prev_h = t.h;
+      prev_qs = t.qs;
+    }
+    if (has_prev) {
       wait(&bb.o_done, (gb - 1) & 1);
       tc_fence_after();
-      uint32_t ov[64];
-      tmem_ld_32x32b_x32(o_tmem, *reinterpret_cast<uint32_t(*)[32]>(&ov[0]));
-      tmem_ld_32x32b_x32(o_tmem + 32, *reinterpret_cast<uint32_t(*)[32]>(&ov[32]));
-      tc_wait_ld();
-      tc_fence_before();
-      unsigned char *ostage = sm + Smem3::Q + (s * 2 + (nt & 1)) * QBYTES + qd * 32 * 128;
-      {
-        const float inv = l_run > 0.f ? 1.0f / l_run : 0.f;
-        unsigned char *row = ostage + lane * 128;
-#pragma unroll
-        for (int gi = 0; gi < 8; ++gi) {
-          const float *f = reinterpret_cast<const float *>(&ov[gi * 8]);
-          *reinterpret_cast<uint4 *>(row + ((gi ^ (lane & 7)) << 4)) =
-              make_uint4(pack_bf16x2(f[0] * inv, f[1] * inv), pack_bf16x2(f[2] * inv, f[3] * inv),
-                         pack_bf16x2(f[4] * inv, f[5] * inv), pack_bf16x2(f[6] * inv, f[7] * inv));
-        }
-      }
-      fence_proxy_async_smem();
-      __syncwarp();
-      if (lane == 0) {
-        tma_store_3d(&map_out, ostage, t.h * DH, t.qs + qd * 32, t.b);
-        bulk_commit();
-      }
-      __syncwarp();
+      write_out(prev_l, prev_b, prev_h, prev_qs, (nt - 1) & 1);
     }
     if (lane == 0) bulk_wait_all();  // stores complete before the CTA (and its shared memory) goes away
     __syncwarp();
