@@ -270,6 +270,20 @@ int gpt2k_gemm_f32(const float *A, const float *B, int b_nk, float *C, int M, in
 int gpt2k_gemm_bf16(const void *A, const void *B, void *C, int M, int N, int K, int ldc, int out_f32,
                     const float *bias, const void *resid, int epi, int bn, void *stream);
 
+/* The products of the few-token forward and of decode steps: y[M, N] =
+ * epi(LN(x)[M, K] @ W[N, K]^T) for M <= 16 rows, x, W and a bf16 y (row
+ * stride ldy; resid has the same stride and may alias y), or an FP32 y with
+ * out_f32 = 1 (epi GPT2_EPI_NONE).  ln_gain / ln_shift (FP32 [K], both or
+ * neither): a LayerNorm of x's rows (FP32 statistics, eps) applied before the
+ * product; not with GPT2_EPI_BIAS_RESID.  impl 0: one SIMT kernel (warp per
+ * few weight rows); impl 1: the tensor-core kernel (weights as the 128-row
+ * MMA operand, K a multiple of 64, 16-byte aligned x and W).  They replace
+ * the linalg.matmul calls the reference's decode loop re-runs per token
+ * (src/gpt/lower_gpt_model.py:190-198). */
+int gpt2k_gemv_bf16(const void *x, const void *W, void *y, int M, int N, int K, int ldy, const float *bias,
+                    const void *resid, int epi, const float *ln_gain, const float *ln_shift, float eps, int out_f32,
+                    int impl, void *stream);
+
 /* Test hook of the kernels' bounded-wait error path; no counterpart in the
  * reference, which has no error path at all (src/gpt/gpt2_call.cpp:42-46
  * checks cuInit only).  Runs the single-SM tcgen05 GEMM of gpt2k_gemm_bf16

@@ -131,6 +131,7 @@ def lib() -> ctypes.CDLL:
     L.gpt2_generate.argtypes = [P(i64), i32, i32, i32, P(i64)]
     L.gpt2k_gemm_f32.argtypes = [vp, vp, i32, vp, i32, i32, i32, i32, vp, vp, i32, vp]
     L.gpt2k_gemm_bf16.argtypes = [vp, vp, vp, i32, i32, i32, i32, i32, vp, vp, i32, i32, vp]
+    L.gpt2k_gemv_bf16.argtypes = [vp, vp, vp, i32, i32, i32, i32, vp, vp, i32, vp, vp, ctypes.c_float, i32, i32, vp]
     L.gpt2k_test_gemm_withheld_load.argtypes = [vp, vp, vp, i32, i32, i32, vp, vp]
     L.gpt2k_gemm_bf16_ln.argtypes = [vp, vp, vp, i32, i32, i32, i32, i32, vp, vp, i32, i32, vp, vp, vp, vp,
                                      ctypes.c_float, vp]
@@ -395,6 +396,13 @@ def k_gemm_f32(A, B, b_nk, C, M, N, K, ldc, bias=None, resid=None, epi=EPI_NONE,
 
 def k_gemm_bf16(A, B, C, M, N, K, ldc, out_f32=0, bias=None, resid=None, epi=EPI_NONE, bn=256, stream=None):
     _check(lib().gpt2k_gemm_bf16(A, B, C, M, N, K, ldc, out_f32, bias, resid, epi, bn, stream), "gpt2k_gemm_bf16")
+
+
+def k_gemv_bf16(x, W, y, M, N, K, ldy, bias=None, resid=None, epi=EPI_NONE, ln_gain=None, ln_shift=None,
+                eps=1e-5, out_f32=0, impl=1, stream=None):
+    """gpt2k_gemv_bf16: y = epi(LN(x) @ W^T) for M <= 16 rows; impl 0 SIMT, 1 tensor cores (device pointers)."""
+    _check(lib().gpt2k_gemv_bf16(x, W, y, M, N, K, ldy, bias, resid, epi, ln_gain, ln_shift, eps, out_f32, impl,
+                                 stream), "gpt2k_gemv_bf16")
 
 
 def k_test_gemm_withheld_load(A, B, C, M, N, K, status_ptr, stream=None):

@@ -497,6 +497,43 @@ int gpt2k_gemm_bf16(const void *A, const void *B, void *C, int M, int N, int K, 
             "gpt2k_gemm_bf16");
 }
 
+int gpt2k_gemv_bf16(const void *x, const void *W, void *y, int M, int N, int K, int ldy, const float *bias,
+                    const void *resid, int epi, const float *ln_gain, const float *ln_shift, float eps, int out_f32,
+                    int impl, void *stream) {
+  if (!x || !W || !y || M < 1 || M > 16 || N < 1 || K < 8 || ldy < N || (!ln_gain) != (!ln_shift)) {
+    set_error("gpt2k_gemv_bf16: bad operands (M=%d N=%d K=%d ldy=%d)", M, N, K, ldy);
+    return GPT2_EINVAL;
+  }
+  if (out_f32 && epi != GPT2_EPI_NONE) {
+    set_error("gpt2k_gemv_bf16: an FP32 output takes no epilogue");
+    return GPT2_EINVAL;
+  }
+  if (impl == 1 && !gemv_tc_supported(M, N, K, ldy)) {
+    set_error("gpt2k_gemv_bf16: the tensor-core kernel needs K a multiple of 64 (K=%d)", K);
+    return GPT2_EINVAL;
+  }
+  const GemvLn ln{ln_gain, ln_shift, eps};
+  const GemvLn *lp = ln_gain ? &ln : nullptr;
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  const bf16 *xb = static_cast<const bf16 *>(x), *wb = static_cast<const bf16 *>(W);
+  if (impl == 1) {
+    if (out_f32) return ck(launch_gemv_tc_bf16_f32out(xb, wb, static_cast<float *>(y), M, N, K, ldy, nullptr, st, lp),
+                           "gpt2k_gemv_bf16");
+    return ck(launch_gemv_tc_bf16(xb, wb, static_cast<bf16 *>(y), M, N, K, ldy, bias,
+                                  static_cast<const bf16 *>(resid), nullptr, epi, nullptr, st, lp),
+              "gpt2k_gemv_bf16");
+  }
+  if (impl != 0) {
+    set_error("gpt2k_gemv_bf16: impl must be 0 or 1");
+    return GPT2_EINVAL;
+  }
+  if (out_f32) return ck(launch_gemv_bf16_f32out(xb, wb, static_cast<float *>(y), M, N, K, ldy, st, lp),
+                         "gpt2k_gemv_bf16");
+  return ck(launch_gemv_bf16(xb, wb, static_cast<bf16 *>(y), M, N, K, ldy, bias, static_cast<const bf16 *>(resid),
+                             nullptr, epi, st, lp),
+            "gpt2k_gemv_bf16");
+}
+
 int gpt2k_test_gemm_withheld_load(const void *A, const void *B, void *C, int M, int N, int K, int *d_status,
                                   void *stream) {
   if (!A || !B || !C || !d_status) {

@@ -389,6 +389,25 @@ __device__ __forceinline__ float gelu_new_fast(float x) {
   return 0.5f * x * (1.0f + tanh_approx(k * (x + 0.044715f * x * x * x)));
 }
 
+// Thread-block cluster: every thread of every CTA of the cluster arrives
+// (release) and waits (acquire).  A hardware barrier, not a spin loop: callers
+// make sure no CTA can leave without reaching it.
+__device__ __forceinline__ void cluster_sync_all() {
+  asm volatile("barrier.cluster.arrive.release.aligned;\n\tbarrier.cluster.wait.acquire.aligned;" ::: "memory");
+}
+// Address of the same shared-memory location in the CTA of rank `rank` of this
+// cluster, and a 32-bit load from it (distributed shared memory).
+__device__ __forceinline__ uint32_t cluster_map_shared(uint32_t smem_addr, uint32_t rank) {
+  uint32_t r;
+  asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(r) : "r"(smem_addr), "r"(rank));
+  return r;
+}
+__device__ __forceinline__ float ld_shared_cluster_f32(uint32_t addr) {
+  float v;
+  asm volatile("ld.shared::cluster.f32 %0, [%1];" : "=f"(v) : "r"(addr) : "memory");
+  return v;
+}
+
 // Named barrier `id` (1..15) over `count` threads (a multiple of 32).
 __device__ __forceinline__ void named_bar_sync(int id, int count) {
   asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(count) : "memory");

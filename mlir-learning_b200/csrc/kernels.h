@@ -229,6 +229,29 @@ cudaError_t launch_gemv_bf16(const bf16 *x, const bf16 *W, bf16 *y, int M, int N
                              const GemvLn *ln = nullptr, bool pdl = false);
 cudaError_t launch_gemv_bf16_f32out(const bf16 *x, const bf16 *W, float *y, int M, int N, int K, int ldy,
                                     cudaStream_t st, const GemvLn *ln = nullptr, bool pdl = false);
+// Programmatic dependent launch of the few-token chain: on unless the
+// environment sets GPT2_PDL=0.
+bool pdl_enabled();
+// The same products on the tensor cores (gemv_tc.cu): bf16 weights W[N, K]
+// (16-byte aligned, K a multiple of 64 that splits into at most 8 slices of
+// at most 6 k-steps), x 16-byte aligned, M <= 16 rows.  Epilogues EPI_NONE,
+// EPI_BIAS, EPI_BIAS_GELU, EPI_BIAS_GELU_ERF (ln allowed) and
+// EPI_BIAS_RESID (no ln); a wait timeout records status 2 in *status.
+bool gemv_tc_supported(int M, int N, int K, int ldy);
+cudaError_t launch_gemv_tc_bf16(const bf16 *x, const bf16 *W, bf16 *y, int M, int N, int K, int ldy,
+                                const float *bias, const bf16 *resid, const float *scale, int epi, int *status,
+                                cudaStream_t st, const GemvLn *ln = nullptr, bool pdl = false);
+cudaError_t launch_gemv_tc_bf16_f32out(const bf16 *x, const bf16 *W, float *y, int M, int N, int K, int ldy,
+                                       int *status, cudaStream_t st, const GemvLn *ln = nullptr, bool pdl = false);
+// The few-token and decode products: the tensor-core kernel where
+// gemv_tc_supported, else launch_gemv_bf16 (environment GPT2_GEMV_TC=0: always
+// the SIMT kernel).
+bool gemv_tc_enabled();
+cudaError_t launch_gemv_bf16_auto(const bf16 *x, const bf16 *W, bf16 *y, int M, int N, int K, int ldy,
+                                  const float *bias, const bf16 *resid, const float *scale, int epi, int *status,
+                                  cudaStream_t st, const GemvLn *ln = nullptr, bool pdl = false);
+cudaError_t launch_gemv_bf16_f32out_auto(const bf16 *x, const bf16 *W, float *y, int M, int N, int K, int ldy,
+                                         int *status, cudaStream_t st, const GemvLn *ln = nullptr, bool pdl = false);
 // Attention of sequences of S <= 16 tokens (one warp per query row); rows
 // with no attendable key are left for launch_attn_masked_rows_*.
 cudaError_t launch_attention_short_f32(const float *qkv, const uint8_t *key_valid, float *o, int B, int S, int H,

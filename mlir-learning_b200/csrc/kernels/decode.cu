@@ -16,6 +16,16 @@
 
 namespace gpt2 {
 
+// Programmatic dependent launch of the few-token chain (GEMV, short and
+// decode attention): on unless the environment sets GPT2_PDL=0.
+bool pdl_enabled() {
+  static const bool on = [] {
+    const char *e = getenv("GPT2_PDL");
+    return !(e && e[0] == '0');
+  }();
+  return on;
+}
+
 namespace {
 template <typename T>
 __device__ __forceinline__ float to_f(T v);
@@ -38,15 +48,6 @@ __device__ __forceinline__ bf16 from_f<bf16>(float v) {
   return __float2bfloat16_rn(v);
 }
 
-// Programmatic dependent launch of the few-token chain (GEMV, short and
-// decode attention): on unless the environment sets GPT2_PDL=0.
-bool pdl_enabled() {
-  static const bool on = [] {
-    const char *e = getenv("GPT2_PDL");
-    return !(e && e[0] == '0');
-  }();
-  return on;
-}
 
 // kern<<<grid, block, smem, st>>>(args...), as a programmatic dependent of
 // the previous kernel on st when pdl is set (the kernel calls pdl_wait()

@@ -495,30 +495,30 @@ int launch_forward_few(Context &c, const int64_t *d_ids, const uint8_t *kv, cons
   for (int l = 0; l < m.n_layer; ++l) {
     const LayerWeights &lw = c.layers[l];
     const GemvLn ln1{lw.ln1_g, lw.ln1_b, m.eps}, ln2{lw.ln2_g, lw.ln2_b, m.eps};
-    CKP(K_GEMM_QKV, launch_gemv_bf16(x, lw.qkv_wt, qkv, T, 3 * d, d, 3 * d, lw.qkv_b, nullptr, lw.qkv_s, EPI_BIAS,
+    CKP(K_GEMM_QKV, launch_gemv_bf16_auto(x, lw.qkv_wt, qkv, T, 3 * d, d, 3 * d, lw.qkv_b, nullptr, lw.qkv_s, EPI_BIAS, c.d_status,
                                      st, &ln1, pdl));
     if (kv_fill) CK(launch_kv_store_bf16(qkv, static_cast<bf16 *>(c.dec.cache[l]), B, S, d, c.dec.max_len, 0, st));
     CKP(K_ATTENTION, launch_attention_short_bf16(qkv, kv, o, B, S, H, 1, st, pdl));
     if (d_mask) CKP(K_MASKED_ROWS, launch_attn_masked_rows_bf16(qkv, w.first_valid, o, B, S, H, st));
-    CKP(K_GEMM_PROJ, launch_gemv_bf16(o, lw.proj_wt, x, T, d, d, d, lw.proj_b, x, lw.proj_s, EPI_BIAS_RESID, st, nullptr, pdl));
+    CKP(K_GEMM_PROJ, launch_gemv_bf16_auto(o, lw.proj_wt, x, T, d, d, d, lw.proj_b, x, lw.proj_s, EPI_BIAS_RESID, c.d_status, st, nullptr, pdl));
     CKP(K_GEMM_FC,
-        launch_gemv_bf16(x, lw.fc_wt, u, T, ff, d, ff, lw.fc_b, nullptr, lw.fc_s, EPI_BIAS_GELU, st, &ln2, pdl));
+        launch_gemv_bf16_auto(x, lw.fc_wt, u, T, ff, d, ff, lw.fc_b, nullptr, lw.fc_s, EPI_BIAS_GELU, c.d_status, st, &ln2, pdl));
     CKP(K_GEMM_MPROJ,
-        launch_gemv_bf16(u, lw.mproj_wt, x, T, d, ff, d, lw.mproj_b, x, lw.mproj_s, EPI_BIAS_RESID, st, nullptr, pdl));
+        launch_gemv_bf16_auto(u, lw.mproj_wt, x, T, d, ff, d, lw.mproj_b, x, lw.mproj_s, EPI_BIAS_RESID, c.d_status, st, nullptr, pdl));
   }
   if (kv_fill) {
     bf16 *xl = static_cast<bf16 *>(c.dec.a_last);
     CK(cudaMemcpy2DAsync(xl, sizeof(bf16) * d, x + (int64_t)(S - 1) * d, sizeof(bf16) * S * d, sizeof(bf16) * d, B,
                          cudaMemcpyDeviceToDevice, st));
-    CKP(K_LM_HEAD, launch_gemv_bf16_f32out(xl, c.wte_h, d_logits, B, V, d, (int)ld_logits, st, &lnf));
+    CKP(K_LM_HEAD, launch_gemv_bf16_f32out_auto(xl, c.wte_h, d_logits, B, V, d, (int)ld_logits, c.d_status, st, &lnf));
     return 0;
   }
   if (!logits_f32) {
-    CKP(K_LM_HEAD, launch_gemv_bf16(x, c.wte_h, static_cast<bf16 *>(d_logits_v), T, V, d, (int)ld_logits, nullptr,
-                                    nullptr, nullptr, EPI_NONE, st, &lnf, pdl));
+    CKP(K_LM_HEAD, launch_gemv_bf16_auto(x, c.wte_h, static_cast<bf16 *>(d_logits_v), T, V, d, (int)ld_logits, nullptr,
+                                    nullptr, nullptr, EPI_NONE, c.d_status, st, &lnf, pdl));
     return 0;
   }
-  CKP(K_LM_HEAD, launch_gemv_bf16_f32out(x, c.wte_h, d_logits, T, V, d, (int)ld_logits, st, &lnf, pdl));
+  CKP(K_LM_HEAD, launch_gemv_bf16_f32out_auto(x, c.wte_h, d_logits, T, V, d, (int)ld_logits, c.d_status, st, &lnf, pdl));
   return 0;
 }
 }  // namespace
@@ -637,7 +637,7 @@ int launch_forward(Context &c, const int64_t *d_ids, const int64_t *d_mask, int 
     bf16 *al = static_cast<bf16 *>(c.dec.a_last);
     CK(cudaMemcpy2DAsync(al, sizeof(bf16) * d, a + (int64_t)(S - 1) * d, sizeof(bf16) * S * d, sizeof(bf16) * d, B,
                          cudaMemcpyDeviceToDevice, st));
-    CKP(K_LM_HEAD, launch_gemv_bf16_f32out(al, c.wte_h, d_logits, B, V, d, (int)ld_logits, st));
+    CKP(K_LM_HEAD, launch_gemv_bf16_f32out_auto(al, c.wte_h, d_logits, B, V, d, (int)ld_logits, c.d_status, st));
     return 0;
   }
   const TcGemmPlan &head = c.plans[4 * m.n_layer];

@@ -146,17 +146,17 @@ int launch_step(Context &c, const int64_t *d_tokens, int B, float *d_logits, int
     for (int l = 0; l < m.n_layer; ++l) {
       const LayerWeights &lw = c.layers[l];
       const GemvLn ln1{lw.ln1_g, lw.ln1_b, m.eps}, ln2{lw.ln2_g, lw.ln2_b, m.eps};
-      CKP(K_GEMM_QKV, launch_gemv_bf16(x, lw.qkv_wt, qkv, B, 3 * D, D, 3 * D, lw.qkv_b, nullptr, lw.qkv_s, EPI_BIAS,
+      CKP(K_GEMM_QKV, launch_gemv_bf16_auto(x, lw.qkv_wt, qkv, B, 3 * D, D, 3 * D, lw.qkv_b, nullptr, lw.qkv_s, EPI_BIAS, c.d_status,
                                        st, &ln1, pdl));
       CKP(K_ATTENTION, launch_attn_decode_bf16(qkv, static_cast<bf16 *>(d.cache[l]), o, B, H, dp, d.max_len, c.d_status, st, pdl));
-      CKP(K_GEMM_PROJ, launch_gemv_bf16(o, lw.proj_wt, x, B, D, D, D, lw.proj_b, x, lw.proj_s, EPI_BIAS_RESID, st, nullptr, pdl));
-      CKP(K_GEMM_FC, launch_gemv_bf16(x, lw.fc_wt, u, B, ff, D, ff, lw.fc_b, nullptr, lw.fc_s, EPI_BIAS_GELU, st,
+      CKP(K_GEMM_PROJ, launch_gemv_bf16_auto(o, lw.proj_wt, x, B, D, D, D, lw.proj_b, x, lw.proj_s, EPI_BIAS_RESID, c.d_status, st, nullptr, pdl));
+      CKP(K_GEMM_FC, launch_gemv_bf16_auto(x, lw.fc_wt, u, B, ff, D, ff, lw.fc_b, nullptr, lw.fc_s, EPI_BIAS_GELU, c.d_status, st,
                                       &ln2, pdl));
       CKP(K_GEMM_MPROJ,
-          launch_gemv_bf16(u, lw.mproj_wt, x, B, D, ff, D, lw.mproj_b, x, lw.mproj_s, EPI_BIAS_RESID, st, nullptr, pdl));
+          launch_gemv_bf16_auto(u, lw.mproj_wt, x, B, D, ff, D, lw.mproj_b, x, lw.mproj_s, EPI_BIAS_RESID, c.d_status, st, nullptr, pdl));
     }
     const GemvLn lnf{c.lnf_g, c.lnf_b, m.eps};
-    CKP(K_LM_HEAD, launch_gemv_bf16_f32out(x, c.wte_h, d_logits, B, V, D, (int)ld, st, &lnf, pdl));
+    CKP(K_LM_HEAD, launch_gemv_bf16_f32out_auto(x, c.wte_h, d_logits, B, V, D, (int)ld, c.d_status, st, &lnf, pdl));
   }
   CK(launch_add_int(d.d_pos, 1, st));
   return 0;

@@ -352,3 +352,60 @@ def test_blas_sgemm_lowering_call(torch, M, N, K, transB, where):
 
 def pkg_einval():
     return -1
+
+
+# The few-token / decode products (gpt2k_gemv_bf16): the SIMT kernel (impl 0)
+# and the tensor-core kernel (impl 1, weights as the 128-row MMA operand, K
+# split over a thread-block cluster) against a float64 reference.  A
+# LayerNorm'd row enters the tensor-core kernel as two bf16 operands (hi and
+# lo), so both kernels multiply FP32 rows by bf16 weights and are held to the
+# bf16 rounding of the output: 1 % of the largest |y|.
+@pytest.mark.parametrize("M,N,K,epi,ln,out_f32", [
+    (1, 768, 768, pkg.EPI_BIAS, True, 0),             # one row (B = 1 decode)
+    (5, 2304, 768, pkg.EPI_BIAS, True, 0),            # QKV with ln_1, few rows
+    (16, 3072, 768, pkg.EPI_BIAS_GELU, True, 0),      # MLP fc with ln_2
+    (16, 768, 768, pkg.EPI_BIAS_RESID, False, 0),     # attention out-proj (6 weight tiles: K split 6 ways)
+    (16, 768, 3072, pkg.EPI_BIAS_RESID, False, 0),    # MLP proj (K = 3072: split 8 ways)
+    (3, 3072, 768, pkg.EPI_BIAS_GELU_ERF, False, 0),  # BERT's GELU (the SIMT kernel has it without a LayerNorm)
+    (7, 1000, 128, pkg.EPI_NONE, False, 0),           # ragged N, two k-steps
+    (16, 50257, 768, pkg.EPI_NONE, True, 1),          # lm_head with ln_f, FP32 logits
+])
+def test_gemv_bf16_both_kernels(torch, M, N, K, epi, ln, out_f32):
+    g = torch.Generator(device="cuda").manual_seed(M * 131 + N + K)
+    x = torch.randn(M, K, device="cuda", generator=g).to(torch.bfloat16)
+    W = (torch.randn(N, K, device="cuda", generator=g) * 0.05).to(torch.bfloat16)
+    bias = torch.randn(N, device="cuda", generator=g) * 0.1
+    gain = (1.0 + 0.1 * torch.randn(K, device="cuda", generator=g)).float()
+    shift = (0.1 * torch.randn(K, device="cuda", generator=g)).float()
+    resid0 = torch.randn(M, N, device="cuda", generator=g).to(torch.bfloat16)
+    xd = x.double()
+    if ln:
+        mu = xd.mean(1, keepdim=True)
+        var = ((xd - mu) ** 2).mean(1, keepdim=True)
+        xd = (xd - mu) / torch.sqrt(var + 1e-5) * gain.double() + shift.double()
+    ref = _epi_ref(torch, xd @ W.double().T, bias, resid0, epi)
+    scale = ref.abs().max().item()
+    outs = []
+    for impl in (0, 1, 1):
+        y = resid0.clone() if not out_f32 else torch.zeros(M, N, device="cuda")
+        pkg.k_gemv_bf16(x.data_ptr(), W.data_ptr(), y.data_ptr(), M, N, K, N,
+                        bias.data_ptr() if epi != pkg.EPI_NONE else None,
+                        y.data_ptr() if epi == pkg.EPI_BIAS_RESID else None, epi,
+                        gain.data_ptr() if ln else None, shift.data_ptr() if ln else None, 1e-5,
+                        out_f32, impl, _stream(torch))
+        torch.cuda.synchronize()
+        err = (y.double() - ref).abs().max().item()
+        assert err <= 1e-2 * scale, (impl, err, scale)
+        outs.append(y)
+    # The split-K partial sums meet in a fixed order: repeated runs agree bit for bit.
+    assert torch.equal(outs[1], outs[2])
+
+
+def test_gemv_bf16_rejects_what_the_tensor_core_kernel_cannot_do(torch):
+    x = torch.zeros(4, 136, device="cuda", dtype=torch.bfloat16)
+    W = torch.zeros(64, 136, device="cuda", dtype=torch.bfloat16)
+    y = torch.zeros(4, 64, device="cuda", dtype=torch.bfloat16)
+    with pytest.raises(pkg.Gpt2Error, match="multiple of 64"):
+        pkg.k_gemv_bf16(x.data_ptr(), W.data_ptr(), y.data_ptr(), 4, 64, 136, 64, impl=1, stream=_stream(torch))
+    with pytest.raises(pkg.Gpt2Error, match="bad operands"):
+        pkg.k_gemv_bf16(x.data_ptr(), W.data_ptr(), y.data_ptr(), 17, 64, 136, 64, impl=0, stream=_stream(torch))
