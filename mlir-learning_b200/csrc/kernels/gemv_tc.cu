@@ -181,6 +181,20 @@ __global__ void __launch_bounds__(128, 1)
   fence_proxy_async_smem();  // the MMA reads these rows through the async proxy
   __syncthreads();
 
+  // The epilogue's inputs from memory (rank 0 only): residual, bias and scale
+  // are loaded now, so their latency overlaps the weight stream and the MMAs.
+  const int n_ep = n0 + threadIdx.x;
+  const bool ep = ks == 0 && n_ep < N;
+  float res[XROWS];
+  float sc = 1.f, bn = 0.f;
+  if (ep) {
+    if (scale) sc = scale[n_ep];
+    if (EPI != EPI_NONE) bn = bias[n_ep];
+#pragma unroll
+    for (int t = 0; t < XROWS; ++t)
+      res[t] = (EPI == EPI_BIAS_RESID && t < M) ? __bfloat162float(resid[(int64_t)t * ldy + n_ep]) : 0.f;
+  }
+
   if (threadIdx.x == 0) {
     constexpr uint32_t idesc = idesc_bf16_f32(TN, XROWS, 0);  // both operands K-major
     bool ok = true;
@@ -245,22 +259,17 @@ __global__ void __launch_bounds__(128, 1)
     }
     cluster_sync_all();
   }
-  if (ks == 0) {
-    const int n = n0 + threadIdx.x;
-    if (n < N) {
-      const float sc = scale ? scale[n] : 1.f;
-      const float bn = EPI != EPI_NONE ? bias[n] : 0.f;
+  if (ep) {
 #pragma unroll
-      for (int t = 0; t < XROWS; ++t) {
-        if (t >= M) break;
-        float o = fmaf(v[t], sc, bn);
-        if (EPI == EPI_BIAS_GELU) o = gelu_new_fast(o);
-        if (EPI == EPI_BIAS_GELU_ERF) o = gelu_erf_fast(o);
-        const int64_t idx = (int64_t)t * ldy + n;
-        if (EPI == EPI_BIAS_RESID) o += __bfloat162float(resid[idx]);
-        if (OUTF32) static_cast<float *>(y)[idx] = o;
-        else static_cast<bf16 *>(y)[idx] = __float2bfloat16_rn(o);
-      }
+    for (int t = 0; t < XROWS; ++t) {
+      if (t >= M) break;
+      float o = fmaf(v[t], sc, bn);
+      if (EPI == EPI_BIAS_GELU) o = gelu_new_fast(o);
+      if (EPI == EPI_BIAS_GELU_ERF) o = gelu_erf_fast(o);
+      if (EPI == EPI_BIAS_RESID) o += res[t];
+      const int64_t idx = (int64_t)t * ldy + n_ep;
+      if (OUTF32) static_cast<float *>(y)[idx] = o;
+      else static_cast<bf16 *>(y)[idx] = __float2bfloat16_rn(o);
     }
   }
   // Every weight copy has landed (the products waited for them, or gave up
