@@ -168,17 +168,50 @@ __global__ void __launch_bounds__(256) gemv_nk_kernel(const AT *__restrict__ x, 
   }
   pdl_wait();     // x, resid and y belong to earlier kernels
   pdl_trigger();  // the next kernel may start its own weight prefetch
+  // The epilogue's inputs from memory, loaded now so that their latency
+  // overlaps the product (same values and order of operations as loading
+  // them at the end).
+  const int m_out = lane % MMAX, n_out = n0 + lane / MMAX;
+  const bool out_ok = n_out < N && m_out < M && (KS == 1 || ks == 0);
+  float pre_scale = 1.f, pre_bias = 0.f, pre_res = 0.f;
+  if (out_ok) {
+    if (scale) pre_scale = scale[n_out];
+    if (EPI != EPI_NONE) pre_bias = bias[n_out];
+    if (EPI == EPI_BIAS_RESID) pre_res = to_f(resid[(int64_t)m_out * ldy + n_out]);
+  }
   float mean[MMAX], rstd[MMAX];
   if (LNP) {
+    constexpr int LNR = 32;  // row values a lane keeps in registers (K <= 1024)
     for (int m = warp; m < M; m += 8) {
       const AT *xr = x + (int64_t)m * K;
-      float sum = 0.f;
-      for (int k = lane; k < K; k += 32) sum += to_f(xr[k]);
-      const float mu = warp_sum(sum) / K;
-      float sq = 0.f;
-      for (int k = lane; k < K; k += 32) {
-        const float t = to_f(xr[k]) - mu;
-        sq = fmaf(t, t, sq);
+      float mu, sq = 0.f;
+      if (K <= 32 * LNR) {
+        // One pass over memory: the row stays in registers between the mean
+        // and the centred variance (same order of additions as two passes).
+        float xv[LNR];
+        float sum = 0.f;
+#pragma unroll
+        for (int i = 0; i < LNR; ++i) {
+          const int k = lane + 32 * i;
+          xv[i] = k < K ? to_f(xr[k]) : 0.f;
+          if (k < K) sum += xv[i];
+        }
+        mu = warp_sum(sum) / K;
+#pragma unroll
+        for (int i = 0; i < LNR; ++i) {
+          if (lane + 32 * i < K) {
+            const float t = xv[i] - mu;
+            sq = fmaf(t, t, sq);
+          }
+        }
+      } else {
+        float sum = 0.f;
+        for (int k = lane; k < K; k += 32) sum += to_f(xr[k]);
+        mu = warp_sum(sum) / K;
+        for (int k = lane; k < K; k += 32) {
+          const float t = to_f(xr[k]) - mu;
+          sq = fmaf(t, t, sq);
+        }
       }
       const float r = rsqrtf(warp_sum(sq) / K + eps);
       if (lane == 0) {
@@ -245,15 +278,13 @@ __global__ void __launch_bounds__(256) gemv_nk_kernel(const AT *__restrict__ x, 
 #pragma unroll
     for (int i = 1; i < KS; ++i) v += part[warp + i][lane];
   }
-  const int m = lane % MMAX, n = n0 + lane / MMAX;
-  if (n < N && m < M) {
-    if (scale) v *= scale[n];
-    if (EPI != EPI_NONE) v += bias[n];
+  if (n_out < N && m_out < M) {
+    if (scale) v *= pre_scale;
+    if (EPI != EPI_NONE) v += pre_bias;
     if (EPI == EPI_BIAS_GELU) v = EXACT ? gelu_new_exact(v) : gelu_new_fast(v);
     if (EPI == EPI_BIAS_GELU_ERF) v = EXACT ? gelu_erf(v) : gelu_erf_fast(v);
-    const int64_t idx = (int64_t)m * ldy + n;
-    if (EPI == EPI_BIAS_RESID) v += to_f(resid[idx]);
-    y[idx] = from_f<OT>(v);
+    if (EPI == EPI_BIAS_RESID) v += pre_res;
+    y[(int64_t)m_out * ldy + n_out] = from_f<OT>(v);
   }
 }
 
