@@ -67,3 +67,16 @@ def test_fp8w_gpt2_xl_48_layers(torch):
     top5_check("fp8w GPT-2 XL vs oracle on FP32 weights", ref_f, got, max_rel=FP8_F32_MAX_REL, min_top1=0.6,
                min_overlap=3.7)
     pkg.shutdown()
+
+
+@pytest.mark.parametrize("B,S", [(4, 3), (2, 5)])
+def test_fp8w_few_tokens_tensor_core_products(torch, B, S):
+    """Forwards of 8-16 tokens run their products on the tensor-core GEMV with the FP8 weights'
+    per-channel scales in its epilogue (K = 1600 split 5 ways over a cluster; the 6400-deep MLP
+    projection falls back to the SIMT GEMV).  Too few positions for fraction floors: every logit
+    within FP8_DEQ_MAX_REL of the oracle on the dequantized weights, top-5 identity wherever the
+    stated bound makes it checkable."""
+    shape = O.ModelShape(n_layer=2, n_embd=1600, n_head=25, n_inner=6400)
+    ref_q, _, got = _run(shape, 77 + B, B, S, True)
+    top5_check(f"fp8w XL-shape L2 B{B}xS{S} vs oracle on dequantized weights", ref_q, got, max_rel=FP8_DEQ_MAX_REL,
+               bound_rel=BF16_TOP5_BOUND_REL)
