@@ -38,6 +38,13 @@ inline cudaError_t set_smem_once(Kernel kernel, int bytes, std::atomic<uint64_t>
 //                  GEMM (LnFold below)
 //   EPI_BIAS_RESID_STATS  EPI_BIAS_RESID, and the row statistics of the bf16
 //                  C it stores for the LayerNorm folded into the next GEMM
+//   EPI_LN_BIAS_GELU_ERF  the erf GELU of EPI_LN_BIAS (BERT's intermediate
+//                  layer after its folded attention-output LayerNorm)
+//   EPI_LNRES_BIAS_RESID_STATS  EPI_BIAS_RESID_STATS with a LayerNorm applied
+//                  to the residual as it is read: C = LN(resid)[row, col] +
+//                  acc + bias[col], LN from the residual rows' statistics and
+//                  the gain / shift of LnFold (BERT's post-LN residual
+//                  stream, kept un-normalised in memory)
 enum Epilogue : int {
   EPI_NONE = 0,
   EPI_BIAS = 1,
@@ -47,6 +54,8 @@ enum Epilogue : int {
   EPI_LN_BIAS = 5,
   EPI_LN_BIAS_GELU = 6,
   EPI_BIAS_RESID_STATS = 7,
+  EPI_LN_BIAS_GELU_ERF = 8,
+  EPI_LNRES_BIAS_RESID_STATS = 9,
 };
 
 // A pre-LayerNorm folded into the GEMM that consumes it:
@@ -65,6 +74,9 @@ struct LnFold {
   float eps = 1e-5f;
   float2 *stats_out = nullptr;               // [M][nseg_out] of C's rows (EPI_BIAS_RESID_STATS)
   int nseg_out = 0;                          // ceil(N / LN_SEG)
+  // EPI_LNRES_BIAS_RESID_STATS: the residual's LayerNorm (width N).
+  const float2 *res_stats = nullptr;         // [M][nseg_out] statistics of the residual rows
+  const float *res_gain = nullptr, *res_shift = nullptr;  // [N], 16-byte aligned
 };
 inline int ln_segments(int width) { return (width + LN_SEG - 1) / LN_SEG; }
 inline int64_t ln_vector_len(int n) { return ((int64_t)n + 255) / 256 * 256; }

@@ -206,6 +206,8 @@ __global__ void __launch_bounds__(NTHREADS, 1)
       const int64_t row_off = (int64_t)row * ldc;
       float ln_rstd = 0.f, ln_nmr = 0.f;  // folded LayerNorm of A's row, read while the main loop runs
       if (Kind::ln && row_ok) ln_row_stats(ln, row, ln_rstd, ln_nmr);
+      float res_rstd = 0.f, res_nmr = 0.f;  // the residual's LayerNorm (EPI_LNRES_*)
+      if (Kind::lnres && row_ok) ln_res_row_stats(ln, row, N, res_rstd, res_nmr);
       RowStats rs;
       if (!mbar_wait(&tfull[acc], aph, abort_flag, status)) {
         set_status(status, GPT2_ERR_WAIT_TIMEOUT);
@@ -244,7 +246,7 @@ __global__ void __launch_bounds__(NTHREADS, 1)
             r[j] = __float_as_uint(__uint_as_float(r[j]) * __shfl_sync(0xffffffffu, j < 32 ? s_lo : s_hi, j & 31));
         }
         if (Kind::ln) {
-          ln_affine<CH, Kind::gelu_new>(v, ln, col0, ln_rstd, ln_nmr);
+          ln_affine<CH, Kind::ln_act>(v, ln, col0, ln_rstd, ln_nmr);
         } else {
           float bias_lo = 0.f, bias_hi = 0.f;
           if (Kind::bias) {
@@ -265,6 +267,13 @@ __global__ void __launch_bounds__(NTHREADS, 1)
           if (full_chunk) {
 #pragma unroll
             for (int g = 0; g < 8; ++g) {
+              if (Kind::lnres) {
+                float rr[8];
+                ln_res_piece(res_cur[g], ln, col0 + 8 * g, res_rstd, res_nmr, rr);
+#pragma unroll
+                for (int j = 0; j < 8; ++j) v[g * 8 + j] += rr[j];
+                continue;
+              }
               const __nv_bfloat162 *h = reinterpret_cast<const __nv_bfloat162 *>(&res_cur[g]);
 #pragma unroll
               for (int j = 0; j < 4; ++j) {
@@ -275,7 +284,11 @@ __global__ void __launch_bounds__(NTHREADS, 1)
             }
           } else {
             for (int j = 0; j < CH; ++j)
-              if (col0 + j < N) v[j] += __bfloat162float(resid[row_off + col0 + j]);
+              if (col0 + j < N) {
+                float rj = __bfloat162float(resid[row_off + col0 + j]);
+                if (Kind::lnres) rj = fmaf(fmaf(rj, res_rstd, res_nmr), ln.res_gain[col0 + j], ln.res_shift[col0 + j]);
+                v[j] += rj;
+              }
           }
           if (c + 1 < NCH) {
 #pragma unroll
@@ -434,6 +447,8 @@ cudaError_t dispatch_epi(const TcGemmPlan &p, void *C, int ldc, int out_f32, con
     GPT2_TC_CASE(EPI_LN_BIAS, 0);
     GPT2_TC_CASE(EPI_LN_BIAS_GELU, 0);
     GPT2_TC_CASE(EPI_BIAS_RESID_STATS, 0);
+    GPT2_TC_CASE(EPI_LN_BIAS_GELU_ERF, 0);
+    GPT2_TC_CASE(EPI_LNRES_BIAS_RESID_STATS, 0);
   }
 #undef GPT2_TC_CASE
   return cudaErrorInvalidValue;
@@ -472,10 +487,14 @@ cudaError_t launch_gemm_tc_withheld_load(const TcGemmPlan &plan, void *C, int *s
 
 bool ln_fold_valid(const TcGemmPlan &plan, int epi, int out_f32, const LnFold *ln) {
   auto aligned16 = [](const void *p) { return (reinterpret_cast<uintptr_t>(p) & 15) == 0; };
-  if (epi == EPI_LN_BIAS || epi == EPI_LN_BIAS_GELU)
+  if (epi == EPI_LN_BIAS || epi == EPI_LN_BIAS_GELU || epi == EPI_LN_BIAS_GELU_ERF)
     return ln && ln->c1 && ln->c2 && ln->stats_in && aligned16(ln->c1) && aligned16(ln->c2) && ln->k == plan.K &&
-           ln->nseg_in == ln_segments(plan.K) && ln->eps > 0.f && !(epi == EPI_LN_BIAS_GELU && out_f32);
+           ln->nseg_in == ln_segments(plan.K) && ln->eps > 0.f && !(epi != EPI_LN_BIAS && out_f32);
   if (epi == EPI_BIAS_RESID_STATS) return ln && ln->stats_out && ln->nseg_out == ln_segments(plan.N) && !out_f32;
+  if (epi == EPI_LNRES_BIAS_RESID_STATS)
+    return ln && ln->stats_out && ln->nseg_out == ln_segments(plan.N) && !out_f32 && ln->res_stats &&
+           ln->res_gain && ln->res_shift && aligned16(ln->res_gain) && aligned16(ln->res_shift) && ln->eps > 0.f &&
+           plan.N % 8 == 0;
   return true;
 }
 
@@ -484,9 +503,10 @@ cudaError_t launch_gemm_tc(const TcGemmPlan &plan, void *C, int ldc, int out_f32
                            const float *scale, const LnFold *ln) {
   if (ldc < plan.N || num_sms <= 0) return cudaErrorInvalidValue;
   if (!out_f32 && ldc % 8) return cudaErrorInvalidValue;
-  const bool ln_epi = epi == EPI_LN_BIAS || epi == EPI_LN_BIAS_GELU;
+  const bool ln_epi = epi == EPI_LN_BIAS || epi == EPI_LN_BIAS_GELU || epi == EPI_LN_BIAS_GELU_ERF;
   if (epi != EPI_NONE && !ln_epi && !bias) return cudaErrorInvalidValue;
-  if ((epi == EPI_BIAS_RESID || epi == EPI_BIAS_RESID_STATS) && !resid) return cudaErrorInvalidValue;
+  if ((epi == EPI_BIAS_RESID || epi == EPI_BIAS_RESID_STATS || epi == EPI_LNRES_BIAS_RESID_STATS) && !resid)
+    return cudaErrorInvalidValue;
   if (!ln_fold_valid(plan, epi, out_f32, ln)) return cudaErrorInvalidValue;
   const LnFold none;
   const LnFold &lf = ln ? *ln : none;

@@ -78,7 +78,7 @@ constexpr uint32_t TMEM_COLS = 512;              // two accumulators of BN colum
 // stages and 2 buffers.
 template <int EPI, int OUT_F32>
 struct PairCfg {
-  static constexpr bool RESID = EPI == EPI_BIAS_RESID || EPI == EPI_BIAS_RESID_STATS;
+  static constexpr bool RESID = EpiKind<EPI>::resid;
   static constexpr int STAGES = RESID ? GPT2_PAIR_STAGES_RESID : GPT2_PAIR_STAGES;
   static constexpr int NBUF = RESID ? GPT2_PAIR_NBUF_RESID : GPT2_PAIR_NBUF;
   static constexpr int STAGING_BYTES = EPI_WARPS * NBUF * 4096;
@@ -312,6 +312,8 @@ __global__ void __launch_bounds__(NTHREADS, 1)
       const int tcol0 = nb * BN + col_half * (BN / 2);  // first column of this warp's half
       float ln_rstd = 0.f, ln_nmr = 0.f;  // folded LayerNorm of A's row, read while the main loop runs
       if (Kind::ln && row_ok) ln_row_stats(ln, row, ln_rstd, ln_nmr);
+      float res_rstd = 0.f, res_nmr = 0.f;  // the residual's LayerNorm (EPI_LNRES_*)
+      if (Kind::lnres && row_ok) ln_res_row_stats(ln, row, N, res_rstd, res_nmr);
       RowStats rs;
       if (Kind::resid && !OUT_F32 && row_ok) {
         // The residual row goes to L2 while the tile's main loop runs.
@@ -358,7 +360,7 @@ __global__ void __launch_bounds__(NTHREADS, 1)
             r[j] = __float_as_uint(__uint_as_float(r[j]) * __shfl_sync(0xffffffffu, j < 32 ? s_lo : s_hi, j & 31));
         }
         if (Kind::ln) {
-          ln_affine<CH, Kind::gelu_new>(v, ln, col0, ln_rstd, ln_nmr);
+          ln_affine<CH, Kind::ln_act>(v, ln, col0, ln_rstd, ln_nmr);
         } else {
           float bias_lo = 0.f, bias_hi = 0.f;
           if (Kind::bias) {
@@ -378,6 +380,13 @@ __global__ void __launch_bounds__(NTHREADS, 1)
           if (col0 + CH <= N) {
 #pragma unroll
             for (int g = 0; g < 8; ++g) {
+              if (Kind::lnres) {
+                float rr[8];
+                ln_res_piece(res_cur[g], ln, col0 + 8 * g, res_rstd, res_nmr, rr);
+#pragma unroll
+                for (int j = 0; j < 8; ++j) v[g * 8 + j] += rr[j];
+                continue;
+              }
               const __nv_bfloat162 *h = reinterpret_cast<const __nv_bfloat162 *>(&res_cur[g]);
 #pragma unroll
               for (int j = 0; j < 4; ++j) {
@@ -388,7 +397,11 @@ __global__ void __launch_bounds__(NTHREADS, 1)
             }
           } else {
             for (int j = 0; j < CH; ++j)
-              if (col0 + j < N) v[j] += __bfloat162float(resid[row_off + col0 + j]);
+              if (col0 + j < N) {
+                float rj = __bfloat162float(resid[row_off + col0 + j]);
+                if (Kind::lnres) rj = fmaf(fmaf(rj, res_rstd, res_nmr), ln.res_gain[col0 + j], ln.res_shift[col0 + j]);
+                v[j] += rj;
+              }
           }
           if (c + 1 < NCH) {
 #pragma unroll
@@ -536,6 +549,8 @@ cudaError_t launch_gemm_tc2sm(const TcGemmPlan &plan, void *C, int ldc, int out_
     GPT2_PAIR_CASE(EPI_LN_BIAS, 0);
     GPT2_PAIR_CASE(EPI_LN_BIAS_GELU, 0);
     GPT2_PAIR_CASE(EPI_BIAS_RESID_STATS, 0);
+    GPT2_PAIR_CASE(EPI_LN_BIAS_GELU_ERF, 0);
+    GPT2_PAIR_CASE(EPI_LNRES_BIAS_RESID_STATS, 0);
   }
 #undef GPT2_PAIR_CASE
   return cudaErrorInvalidValue;

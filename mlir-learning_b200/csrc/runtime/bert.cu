@@ -23,7 +23,7 @@ namespace {
 BertContext *g_bert = nullptr;
 
 void free_bert_ws(BertWorkspace &w) {
-  void *ptrs[] = {w.x, w.qkv, w.o, w.y, w.h, w.u, w.first_valid, w.kv_end, w.key_valid,
+  void *ptrs[] = {w.x, w.qkv, w.o, w.y, w.h, w.u, w.stats_h, w.stats_y, w.first_valid, w.kv_end, w.key_valid,
                   w.ids, w.tt, w.pos, w.mask, w.hidden, w.pooled};
   for (void *p : ptrs)
     if (p) cudaFree(p);
@@ -99,7 +99,8 @@ void bert_destroy_context() {
   free_bert_ws(c->ws);
   if (c->d_blob) cudaFree(c->d_blob);
   for (auto &l : c->layers) {
-    void *p[] = {l.qkv_w, l.qkv_b, l.qkv_h, l.ao_h, l.i_h, l.o_h};
+    void *p[] = {l.qkv_w, l.qkv_b, l.qkv_h, l.ao_h, l.i_h, l.o_h, l.qkv_fold_h, l.i_fold_h, l.qkv_c1, l.qkv_c2,
+                 l.i_c1, l.i_c2};
     for (void *q : p)
       if (q) cudaFree(q);
   }
@@ -192,6 +193,21 @@ int bert_load_blob(BertContext &c, const float *host_blob) {
       CK(launch_pack_bf16(w.ao_w, w.ao_h, d, d, 0, c.stream));
       CK(launch_pack_bf16(w.i_w, w.i_h, ff, d, 0, c.stream));
       CK(launch_pack_bf16(w.o_w, w.o_h, d, ff, 0, c.stream));
+      // Folded LayerNorms: the intermediate layer takes this layer's
+      // attention-output LayerNorm; QKV (after the first layer) the previous
+      // layer's output LayerNorm.
+      if (!w.i_fold_h) CK(cudaMalloc(&w.i_fold_h, sizeof(bf16) * (size_t)ff * d));
+      if (!w.i_c1) CK(cudaMalloc(&w.i_c1, sizeof(float) * ln_vector_len(ff)));
+      if (!w.i_c2) CK(cudaMalloc(&w.i_c2, sizeof(float) * ln_vector_len(ff)));
+      CK(launch_ln_fold_pack(w.i_w, 0, w.aoln_g, w.aoln_b, w.i_b, w.i_fold_h, w.i_c1, w.i_c2, ff, d, c.stream));
+      if (l > 0) {
+        const BertLayer &prev = c.layers[l - 1];
+        if (!w.qkv_fold_h) CK(cudaMalloc(&w.qkv_fold_h, sizeof(bf16) * 3 * dd));
+        if (!w.qkv_c1) CK(cudaMalloc(&w.qkv_c1, sizeof(float) * ln_vector_len(3 * d)));
+        if (!w.qkv_c2) CK(cudaMalloc(&w.qkv_c2, sizeof(float) * ln_vector_len(3 * d)));
+        CK(launch_ln_fold_pack(w.qkv_w, 0, prev.oln_g, prev.oln_b, w.qkv_b, w.qkv_fold_h, w.qkv_c1, w.qkv_c2, 3 * d,
+                               d, c.stream));
+      }
     }
   }
   CK(cudaStreamSynchronize(c.stream));
@@ -218,6 +234,8 @@ int bert_ensure_workspace(BertContext &c, int B, int S) {
   CK(cudaMalloc(&w.y, es * Tn * d));
   CK(cudaMalloc(&w.h, es * Tn * d));
   CK(cudaMalloc(&w.u, es * Tn * ff));
+  CK(cudaMalloc(&w.stats_h, sizeof(float2) * Tn * ln_segments((int)d)));
+  CK(cudaMalloc(&w.stats_y, sizeof(float2) * Tn * ln_segments((int)d)));
   CK(cudaMalloc(&w.first_valid, sizeof(int) * Bn));
   CK(cudaMalloc(&w.kv_end, sizeof(int) * Bn));
   CK(cudaMalloc(&w.key_valid, Tn));
@@ -258,16 +276,22 @@ int bert_ensure_plans(BertContext &c, int64_t T) {
   for (int l = 0; l < m.n_layer; ++l) {
     const BertLayer &w = c.layers[l];
     TcGemmPlan *p = &c.plans[4 * l];
-    int r = tc_gemm_plan(&p[0], static_cast<const bf16 *>(ws.x), w.qkv_h, (int)T, 3 * d, d, pick_tile(3 * d));
-    if (!r) r = tc_gemm_plan(&p[1], static_cast<const bf16 *>(ws.o), w.ao_h, (int)T, d, d, pick_bn(d));
-    if (!r) r = tc_gemm_plan(&p[2], static_cast<const bf16 *>(ws.h), w.i_h, (int)T, ff, d, pick_tile(ff));
+    // The residual stream stays un-normalised in memory (h after the
+    // attention output, y after the layer; their LayerNorms are folded into
+    // the GEMMs that read them): QKV reads the embedding output x in the
+    // first layer and the previous layer's y after it.
+    const bool first = l == 0;
+    int r = tc_gemm_plan(&p[0], static_cast<const bf16 *>(first ? ws.x : ws.y), first ? w.qkv_h : w.qkv_fold_h,
+                         (int)T, 3 * d, d, pick_tile(3 * d));
+    if (!r) r = tc_gemm_plan(&p[1], static_cast<const bf16 *>(ws.o), w.ao_h, (int)T, d, d, pick_tile(d));
+    if (!r) r = tc_gemm_plan(&p[2], static_cast<const bf16 *>(ws.h), w.i_fold_h, (int)T, ff, d, pick_tile(ff));
     if (!r) r = tc_gemm_plan(&p[3], static_cast<const bf16 *>(ws.u), w.o_h, (int)T, d, ff, pick_tile(d));
     if (r) {
       set_error("TMA descriptor creation failed (%d)", r);
       return -2;
     }
     tc_gemm_set_output(&p[0], ws.qkv, 3 * d, 0);
-    tc_gemm_set_output(&p[1], ws.y, d, 0);
+    tc_gemm_set_output(&p[1], ws.h, d, 0);
     tc_gemm_set_output(&p[2], ws.u, ff, 0);
     tc_gemm_set_output(&p[3], ws.y, d, 0);
   }
@@ -277,8 +301,12 @@ int bert_ensure_plans(BertContext &c, int64_t T) {
 }  // namespace
 
 int bert_forward_launch_count(const BertContext &c, int has_mask, int has_pooler) {
-  // embedding + 7 per layer (+ pooler); with a mask, seq_info + 1 per layer
-  return 1 + 7 * c.dims.n_layer + (has_pooler ? 1 : 0) + (has_mask ? 1 + c.dims.n_layer : 0);
+  // embedding + per layer 7 (FP32: with two LayerNorm kernels) or 5 (BF16:
+  // LayerNorms folded into the GEMMs) + the BF16 path's final LayerNorm
+  // (+ pooler); with a mask, seq_info + 1 per layer
+  const int L = c.dims.n_layer;
+  const int body = c.dtype == 1 ? 5 * L + 1 : 7 * L;
+  return 1 + body + (has_pooler ? 1 : 0) + (has_mask ? 1 + L : 0);
 }
 
 namespace {
@@ -367,21 +395,72 @@ int bert_launch(BertContext &c, const int64_t *d_ids, const int64_t *d_tt, const
     const int ns = c.num_sms;
     CKP(K_EMBED, launch_bert_embed_ln_bf16(d_ids, d_tt, d_pos, c.word, c.pos, c.type, c.emb_g, c.emb_b, x, (int)T,
                                            S, d, m.vocab, m.n_pos, m.type_vocab, m.eps, c.d_status, st));
+    // Post-LN with the LayerNorms folded: h = LN_out_prev(y) + o Wo + bo (x in
+    // the first layer) and y = LN_att(h) + gelu(LN_att(h) Wi + bi) Wo2 + bo2
+    // are stored un-normalised with their row statistics; every GEMM that
+    // reads one applies its LayerNorm (as A: folded weights, EPI_LN_*; as the
+    // residual: EPI_LNRES_*).  Only the last layer's output is normalised by
+    // a kernel, into the FP32 hidden state.
+    const int nseg = ln_segments(d);
+    LnFold base;
+    base.eps = m.eps;
+    float2 *sh = w.stats_h, *sy = w.stats_y;
     for (int l = 0; l < L; ++l) {
       const BertLayer &lw = c.layers[l];
       const TcGemmPlan *p = &c.plans[4 * l];
-      CKP(K_GEMM_QKV, launch_gemm_tc(p[0], qkv, 3 * d, 0, lw.qkv_b, nullptr, EPI_BIAS, c.d_status, ns, st));
+      if (l == 0) {
+        CKP(K_GEMM_QKV, launch_gemm_tc(p[0], qkv, 3 * d, 0, lw.qkv_b, nullptr, EPI_BIAS, c.d_status, ns, st));
+      } else {
+        LnFold f = base;
+        f.c1 = lw.qkv_c1;
+        f.c2 = lw.qkv_c2;
+        f.stats_in = sy;
+        f.nseg_in = nseg;
+        f.k = d;
+        CKP(K_GEMM_QKV, launch_gemm_tc(p[0], qkv, 3 * d, 0, nullptr, nullptr, EPI_LN_BIAS, c.d_status, ns, st,
+                                       nullptr, &f));
+      }
       CKP(K_ATTENTION, launch_attention_tc3(c.attn_plan, kv, o, c.d_status, st, 0, kv_end));
       if (d_mask) CKP(K_MASKED_ROWS, launch_attn_masked_rows_bf16(qkv, w.first_valid, o, B, S, H, st, 0));
-      CKP(K_GEMM_PROJ, launch_gemm_tc(p[1], y, d, 0, lw.ao_b, x, EPI_BIAS_RESID, c.d_status, ns, st));
-      CKP(K_LAYERNORM, launch_layernorm_bf16(y, lw.aoln_g, lw.aoln_b, h, (int)T, d, m.eps, st));
-      CKP(K_GEMM_FC, launch_gemm_tc(p[2], u, ff, 0, lw.i_b, nullptr, EPI_BIAS_GELU_ERF, c.d_status, ns, st));
-      CKP(K_GEMM_MPROJ, launch_gemm_tc(p[3], y, d, 0, lw.o_b, h, EPI_BIAS_RESID, c.d_status, ns, st));
-      if (l == L - 1)
-        CKP(K_LAYERNORM, launch_layernorm_bf16_f32out(y, lw.oln_g, lw.oln_b, d_hidden, (int)T, d, m.eps, st));
-      else
-        CKP(K_LAYERNORM, launch_layernorm_bf16(y, lw.oln_g, lw.oln_b, x, (int)T, d, m.eps, st));
+      {
+        LnFold f = base;
+        f.stats_out = sh;
+        f.nseg_out = nseg;
+        if (l == 0) {
+          CKP(K_GEMM_PROJ, launch_gemm_tc(p[1], h, d, 0, lw.ao_b, x, EPI_BIAS_RESID_STATS, c.d_status, ns, st,
+                                          nullptr, &f));
+        } else {
+          const BertLayer &prev = c.layers[l - 1];
+          f.res_stats = sy;
+          f.res_gain = prev.oln_g;
+          f.res_shift = prev.oln_b;
+          CKP(K_GEMM_PROJ, launch_gemm_tc(p[1], h, d, 0, lw.ao_b, y, EPI_LNRES_BIAS_RESID_STATS, c.d_status, ns,
+                                          st, nullptr, &f));
+        }
+      }
+      {
+        LnFold f = base;
+        f.c1 = lw.i_c1;
+        f.c2 = lw.i_c2;
+        f.stats_in = sh;
+        f.nseg_in = nseg;
+        f.k = d;
+        CKP(K_GEMM_FC, launch_gemm_tc(p[2], u, ff, 0, nullptr, nullptr, EPI_LN_BIAS_GELU_ERF, c.d_status, ns, st,
+                                      nullptr, &f));
+      }
+      {
+        LnFold f = base;
+        f.stats_out = sy;
+        f.nseg_out = nseg;
+        f.res_stats = sh;
+        f.res_gain = lw.aoln_g;
+        f.res_shift = lw.aoln_b;
+        CKP(K_GEMM_MPROJ, launch_gemm_tc(p[3], y, d, 0, lw.o_b, h, EPI_LNRES_BIAS_RESID_STATS, c.d_status, ns, st,
+                                         nullptr, &f));
+      }
     }
+    const BertLayer &last = c.layers[L - 1];
+    CKP(K_LAYERNORM, launch_layernorm_bf16_f32out(y, last.oln_g, last.oln_b, d_hidden, (int)T, d, m.eps, st));
   }
   if (d_pooled) CKP(K_LM_HEAD, launch_bert_pooler(d_hidden, c.pool_w, c.pool_b, d_pooled, B, S, d, st));
   return 0;

@@ -27,12 +27,19 @@ struct BertLayer {
   float *qkv_w = nullptr, *qkv_b = nullptr;  // FP32 [3d, d] and [3d]: q, k, v stacked (owned)
   const float *ao_w, *ao_b, *aoln_g, *aoln_b, *i_w, *i_b, *o_w, *o_b, *oln_g, *oln_b;  // in the blob, [out, in]
   bf16 *qkv_h = nullptr, *ao_h = nullptr, *i_h = nullptr, *o_h = nullptr;             // BF16 [out, in]
+  // BF16 forward with the LayerNorms folded: QKV with the previous layer's
+  // output LayerNorm (layers after the first) and the intermediate layer with
+  // this layer's attention-output LayerNorm, as gain-scaled weights and their
+  // c1 / c2 vectors (see LnFold).
+  bf16 *qkv_fold_h = nullptr, *i_fold_h = nullptr;
+  float *qkv_c1 = nullptr, *qkv_c2 = nullptr, *i_c1 = nullptr, *i_c2 = nullptr;
 };
 
 struct BertWorkspace {
   int64_t T = 0;
   int B = 0;
   void *x = nullptr, *qkv = nullptr, *o = nullptr, *y = nullptr, *h = nullptr, *u = nullptr;
+  float2 *stats_h = nullptr, *stats_y = nullptr;  // row statistics of h and y (BF16 forward, folded LayerNorms)
   int *first_valid = nullptr, *kv_end = nullptr;
   uint8_t *key_valid = nullptr;
   int64_t *ids = nullptr, *tt = nullptr, *pos = nullptr, *mask = nullptr;  // staging of the host entry points
