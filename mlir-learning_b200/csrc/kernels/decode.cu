@@ -166,19 +166,45 @@ __global__ void __launch_bounds__(256) gemv_nk_kernel(const AT *__restrict__ x, 
         prefetch_l2_bulk(base + off, min(4096u, bytes - off));
     }
   }
-  pdl_wait();     // x, resid and y belong to earlier kernels
-  pdl_trigger();  // the next kernel may start its own weight prefetch
-  // The epilogue's inputs from memory, loaded now so that their latency
-  // overlaps the product (same values and order of operations as loading
-  // them at the end).
+  // The first k step's weights and LayerNorm gain / shift, and the
+  // epilogue's scale and bias, are parameters no kernel of the chain writes
+  // (a programmatic dependent overlaps only its predecessors in the chain,
+  // which write activations): with PRE they are loaded before the wait, so
+  // that their latency overlaps it and the LayerNorm statistics instead of
+  // following them.  Same values and order of operations either way.  Not
+  // for 16-row accumulators, where it measured slower (0.86 -> 0.91 ms for
+  // a 16-token FP32 forward; 2-6 % faster at 1-5 rows).
+  constexpr bool PRE = MMAX <= 8;
+  const int kfirst = (ks * 32 + lane) * WC;
+  const WT *wr[NC];
+#pragma unroll
+  for (int c = 0; c < NC; ++c) wr[c] = W + (int64_t)(n0 + c < N ? n0 + c : n0) * K;  // past N: a valid row, unused
+  auto load_step = [&](int k0, float (&w)[NC][WC], float *g, float *b) {
+#pragma unroll
+    for (int c = 0; c < NC; ++c) load_chunk<WT>(wr[c] + k0, w[c]);
+    if (LNP) {
+#pragma unroll
+      for (int j = 0; j < WC; j += 4) {
+        const float4 g4 = *reinterpret_cast<const float4 *>(lng + k0 + j);
+        const float4 b4 = *reinterpret_cast<const float4 *>(lnb + k0 + j);
+        g[j] = g4.x, g[j + 1] = g4.y, g[j + 2] = g4.z, g[j + 3] = g4.w;
+        b[j] = b4.x, b[j + 1] = b4.y, b[j + 2] = b4.z, b[j + 3] = b4.w;
+      }
+    }
+  };
+  float w0[NC][WC], g0[LNP ? WC : 1], b0[LNP ? WC : 1];
+  if (PRE && n0 < N && kfirst < K) load_step(kfirst, w0, g0, b0);
   const int m_out = lane % MMAX, n_out = n0 + lane / MMAX;
   const bool out_ok = n_out < N && m_out < M && (KS == 1 || ks == 0);
   float pre_scale = 1.f, pre_bias = 0.f, pre_res = 0.f;
   if (out_ok) {
     if (scale) pre_scale = scale[n_out];
     if (EPI != EPI_NONE) pre_bias = bias[n_out];
-    if (EPI == EPI_BIAS_RESID) pre_res = to_f(resid[(int64_t)m_out * ldy + n_out]);
   }
+  pdl_wait();     // x, resid and y belong to earlier kernels
+  pdl_trigger();  // the next kernel may start its own weight prefetch
+  // The residual, loaded now so that its latency overlaps the product.
+  if (out_ok && EPI == EPI_BIAS_RESID) pre_res = to_f(resid[(int64_t)m_out * ldy + n_out]);
   float mean[MMAX], rstd[MMAX];
   if (LNP) {
     constexpr int LNR = 32;  // row values a lane keeps in registers (K <= 1024)
@@ -229,45 +255,42 @@ __global__ void __launch_bounds__(256) gemv_nk_kernel(const AT *__restrict__ x, 
   float acc[32];
 #pragma unroll
   for (int i = 0; i < 32; ++i) acc[i] = 0.f;
-  if (n0 < N) {
-    const WT *wr[NC];
+  // One k step: acc += x[:, k0 .. k0 + WC) (LayerNorm applied) . w rows.
+  auto fma_step = [&](int k0, const float (&w)[NC][WC], const float *g, const float *b) {
 #pragma unroll
-    for (int c = 0; c < NC; ++c) wr[c] = W + (int64_t)(n0 + c < N ? n0 + c : n0) * K;  // past N: a valid row, unused
-#pragma unroll 1
-    for (int k0 = (ks * 32 + lane) * WC; k0 < K; k0 += 32 * KS * WC) {
-      float w[NC][WC];
+    for (int m = 0; m < MMAX; ++m) {
+      if (m < M) {
+        const AT *xr = x + (int64_t)m * K + k0;
 #pragma unroll
-      for (int c = 0; c < NC; ++c) load_chunk<WT>(wr[c] + k0, w[c]);
-      float g[LNP ? WC : 1], b[LNP ? WC : 1];
-      if (LNP) {
+        for (int j = 0; j < WC; j += Chunk<AT>::N) {
+          float xv[Chunk<AT>::N];
+          load_chunk<AT>(xr + j, xv);
+          if (LNP) {
 #pragma unroll
-        for (int j = 0; j < WC; j += 4) {
-          const float4 g4 = *reinterpret_cast<const float4 *>(lng + k0 + j);
-          const float4 b4 = *reinterpret_cast<const float4 *>(lnb + k0 + j);
-          g[j] = g4.x, g[j + 1] = g4.y, g[j + 2] = g4.z, g[j + 3] = g4.w;
-          b[j] = b4.x, b[j + 1] = b4.y, b[j + 2] = b4.z, b[j + 3] = b4.w;
-        }
-      }
-#pragma unroll
-      for (int m = 0; m < MMAX; ++m) {
-        if (m < M) {
-          const AT *xr = x + (int64_t)m * K + k0;
-#pragma unroll
-          for (int j = 0; j < WC; j += Chunk<AT>::N) {
-            float xv[Chunk<AT>::N];
-            load_chunk<AT>(xr + j, xv);
-            if (LNP) {
-#pragma unroll
-              for (int e = 0; e < Chunk<AT>::N; ++e)
-                xv[e] = fmaf((xv[e] - mean[m]) * rstd[m], g[LNP ? j + e : 0], b[LNP ? j + e : 0]);
-            }
-#pragma unroll
-            for (int c = 0; c < NC; ++c)
-#pragma unroll
-              for (int e = 0; e < Chunk<AT>::N; ++e) acc[c * MMAX + m] = fmaf(xv[e], w[c][j + e], acc[c * MMAX + m]);
+            for (int e = 0; e < Chunk<AT>::N; ++e) xv[e] = fmaf((xv[e] - mean[m]) * rstd[m], g[j + e], b[j + e]);
           }
+#pragma unroll
+          for (int c = 0; c < NC; ++c)
+#pragma unroll
+            for (int e = 0; e < Chunk<AT>::N; ++e) acc[c * MMAX + m] = fmaf(xv[e], w[c][j + e], acc[c * MMAX + m]);
         }
       }
+    }
+  };
+  if (n0 < N) {
+    // With PRE the first step runs from the values loaded before the wait
+    // (peeled, so they are dead before the loop).
+    int k0 = kfirst;
+    if (PRE && k0 < K) {
+      fma_step(k0, w0, g0, b0);
+      k0 += 32 * KS * WC;
+    }
+#pragma unroll 1
+    for (; k0 < K; k0 += 32 * KS * WC) {
+      float w[NC][WC];
+      float g[LNP ? WC : 1], b[LNP ? WC : 1];
+      load_step(k0, w, g, b);
+      fma_step(k0, w, g, b);
     }
   }
   float v = warp_reduce_scatter32(acc);
