@@ -328,15 +328,30 @@ __global__ void __launch_bounds__(128) attn_short_kernel(const T *__restrict__ q
   const int D = H * DH;
   const int64_t row = (int64_t)b * S;
   const T *q = qkv + (row + i) * 3 * D + h * DH;
+  // Every load of the row is issued before any is used (the query, the
+  // sequence's keys and values, the key mask), so the kernel waits for one
+  // L2 round trip instead of one per dependent step.
   const float q0 = to_f(q[lane]) * 0.125f, q1 = to_f(q[lane + 32]) * 0.125f;
+  float k0[SMAX], k1[SMAX], v0[SMAX], v1[SMAX];
+  bool use[SMAX];
+#pragma unroll
+  for (int j = 0; j < SMAX; ++j) {
+    use[j] = false;
+    k0[j] = k1[j] = v0[j] = v1[j] = 0.f;
+    if (j < S) {
+      const T *k = qkv + (row + j) * 3 * D + D + h * DH;
+      k0[j] = to_f(k[lane]), k1[j] = to_f(k[lane + 32]);
+      v0[j] = to_f(k[D + lane]), v1[j] = to_f(k[D + lane + 32]);
+      use[j] = (!causal || j <= i) && (!key_valid || key_valid[row + j]);
+    }
+  }
   float sc[SMAX];
   float mx = -INFINITY;
 #pragma unroll
   for (int j = 0; j < SMAX; ++j) {
     sc[j] = -INFINITY;
-    if (j < S && (!causal || j <= i) && (!key_valid || key_valid[row + j])) {
-      const T *k = qkv + (row + j) * 3 * D + D + h * DH;
-      const float s = warp_sum(fmaf(q0, to_f(k[lane]), q1 * to_f(k[lane + 32])));
+    if (use[j]) {
+      const float s = warp_sum(fmaf(q0, k0[j], q1 * k1[j]));
       sc[j] = s;
       mx = fmaxf(mx, s);
     }
@@ -347,10 +362,9 @@ __global__ void __launch_bounds__(128) attn_short_kernel(const T *__restrict__ q
   for (int j = 0; j < SMAX; ++j) {
     if (sc[j] != -INFINITY) {
       const float p = expf(sc[j] - mx);
-      const T *v = qkv + (row + j) * 3 * D + 2 * D + h * DH;
       l += p;
-      o0 = fmaf(p, to_f(v[lane]), o0);
-      o1 = fmaf(p, to_f(v[lane + 32]), o1);
+      o0 = fmaf(p, v0[j], o0);
+      o1 = fmaf(p, v1[j], o1);
     }
   }
   T *out = o + (row + i) * D + h * DH;
