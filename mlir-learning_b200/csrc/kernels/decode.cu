@@ -396,18 +396,35 @@ __global__ void __launch_bounds__(128) attn_decode_kernel(const T *__restrict__ 
                                                           int max_len, int *status) {
   constexpr int DH = 64;
   extern __shared__ float sc[];  // max(max_len, 1024) floats: the scores, then partial output rows
-  pdl_wait();
-  pdl_trigger();
+  pdl_trigger();  // the next GEMV may start its own early loads
   const int h = blockIdx.x, b = blockIdx.y, tid = threadIdx.x;
+  const int D = H * DH;
+  T *cb = cache + (int64_t)b * max_len * 2 * D;
+  // The position and the cached keys and values of positions 0 .. pos - 1
+  // were written before this step's chain began (a programmatic dependent
+  // overlaps only its predecessors in the chain, which write qkv): the
+  // cached rows are prefetched into L1 before the wait, so that the scores
+  // and P V after it read them without an L2 round trip.
   const int pos = *d_pos;
+  if (pos >= 0 && pos < max_len) {
+    for (int j = tid; j < pos; j += blockDim.x) {
+      const char *kr = reinterpret_cast<const char *>(cb + (int64_t)j * 2 * D + h * DH);
+      const char *vr = kr + sizeof(T) * D;
+#pragma unroll
+      for (int o = 0; o < DH * (int)sizeof(T); o += 128) {
+        asm volatile("prefetch.global.L1 [%0];" ::"l"(kr + o));
+        asm volatile("prefetch.global.L1 [%0];" ::"l"(vr + o));
+      }
+    }
+  }
+  pdl_wait();
   if (pos < 0 || pos >= max_len) {  // the cache is full: report, touch nothing
     if (tid == 0) set_status(status, GPT2_ERR_BAD_LAUNCH);
     return;
   }
-  const int D = H * DH, n = pos + 1;
+  const int n = pos + 1;
   const T *q = qkv + (int64_t)b * 3 * D + h * DH;
   const T *knew = q + D, *vnew = q + 2 * D;
-  T *cb = cache + (int64_t)b * max_len * 2 * D;
   __shared__ float qs[DH], red[2 * DH];
   __shared__ float stat[4];
   if (tid < DH) qs[tid] = to_f(q[tid]);
