@@ -140,8 +140,21 @@ __device__ __forceinline__ float warp_reduce_scatter32(float (&v)[32]) {
 // variance over K, FP32): each block computes its rows' mean and 1/std (two
 // passes per row, one warp per row) and normalises the x chunks as it reads
 // them, so the LayerNorm needs no launch and no output buffer of its own.
+// FP32 weights with 8-row accumulators (forwards of 5-8 tokens, the
+// reference host program's B1 x S5 call among them): at most 80 registers,
+// so three blocks fit an SM (the LayerNorm variants spill about 140 bytes of
+// the row kept for the statistics).  A whole wave of the fc product then
+// fits the GPU and the next kernel's blocks become resident sooner: that
+// forward went from 0.390 to 0.359 ms.  Other instances keep the compiler's
+// choice (the same bound measured slower for 4 and 16 rows, and spills
+// heavily for bf16 weights).
+template <typename WT, int MMAX>
+constexpr int gemv_min_blocks() {
+  return sizeof(WT) == 4 && MMAX == 8 ? 3 : 0;
+}
+
 template <typename WT, typename AT, typename OT, int EPI, bool EXACT, int MMAX, int KS, bool LNP>
-__global__ void __launch_bounds__(256) gemv_nk_kernel(const AT *__restrict__ x, const WT *__restrict__ W,
+__global__ void __launch_bounds__(256, (gemv_min_blocks<WT, MMAX>())) gemv_nk_kernel(const AT *__restrict__ x, const WT *__restrict__ W,
                                                       OT *__restrict__ y, int M, int N, int K, int ldy,
                                                       const float *__restrict__ bias, const OT *resid,
                                                       const float *__restrict__ scale, const float *__restrict__ lng,
